@@ -1,0 +1,1056 @@
+// CPU oracle for the evie-b200 test-suite and the CPU baseline leg of bench.py.
+//
+// TEST INFRASTRUCTURE ONLY. This is a C++ restatement of evie-core's CPU engine (Rust, which cannot be
+// built in this environment: no cargo/rustc, crates not vendored). Nothing in the product library links
+// or calls it; only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load it, as the checker.
+//
+// It follows, function by function (paths relative to the evie repository):
+//   crates/evie-core/src/kernels.rs:107-117   bf16 widening
+//   crates/evie-core/src/kernels.rs:138-268   matvec / matmul dispatch (n==1 dot_rows, n<8 multi_dot, else packed GEMM)
+//   crates/evie-core/src/kernels.rs:270-522   AVX2/FMA micro-kernels (load8, hsum, dot_rows, multi_dot, pack_panel, micro)
+//   crates/evie-core/src/kernels.rs:573-662   silu, sigmoid, softplus(thr 20), dot (8 lanes), rmsnorm, softmax, topk
+//   crates/evie-core/src/model.rs:217-284     Model::forward (segments batched for projections, hooks)
+//   crates/evie-core/src/model.rs:296-396     Model::deltanet (conv+SiLU, L2 norm, decay/beta, recurrence, gated norm)
+//   crates/evie-core/src/model.rs:398-479     Model::attention + rope
+//   crates/evie-core/src/model.rs:501-524     recur_body (loop order kept)
+//   crates/evie-core/src/steering.rs:150-210  Plan::begin / Plan::apply (add / mul / set, latching gates)
+//   crates/evie/src/worker.rs:97-121          Capture (sqrt-companded i8 frames, f16 residual)
+//   crates/evie-core/src/gpu/mod.rs:577-593   track_max semantics (max |a| over positions > 0)
+//
+// Floating point: build with -ffp-contract=off so that scalar `a += b * c` stays a rounded multiply followed
+// by a rounded add, as Rust compiles it; the AVX2 paths use explicit _mm256_fmadd_ps exactly where the
+// reference does. Transcendentals come from the same libm (expf, log1pf, sinf, cosf, powf, sqrtf).
+
+#include <immintrin.h>
+#include <stdint.h>
+#include <string.h>
+#include <math.h>
+#include <stdlib.h>
+#include <algorithm>
+#include <atomic>
+#include <condition_variable>
+#include <functional>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#define EXPORT extern "C" __attribute__((visibility("default")))
+
+// ------------------------------------------------------------------------------------------------
+// thread pool (stands in for rayon's global pool; results never depend on the thread count because
+// every output element is produced by exactly one task in a fixed order)
+
+namespace {
+
+class Pool {
+ public:
+  explicit Pool(int n) { resize(n); }
+  ~Pool() { stop_all(); }
+  int size() const { return (int)workers_.size() + 1; }
+  void resize(int n) {
+    stop_all();
+    if (n < 1) n = 1;
+    quit_ = false;
+    for (int i = 0; i < n - 1; i++) workers_.emplace_back([this] { loop(); });
+  }
+  // Runs f(i) for i in [0, n) over all threads, dynamic chunking.
+  void run(long n, const std::function<void(long)>& f) {
+    if (n <= 0) return;
+    if (workers_.empty() || n == 1) {
+      for (long i = 0; i < n; i++) f(i);
+      return;
+    }
+    std::unique_lock<std::mutex> lk(m_);
+    job_ = &f;
+    total_ = n;
+    next_.store(0);
+    pending_ = (int)workers_.size();
+    gen_++;
+    lk.unlock();
+    cv_.notify_all();
+    work();
+    lk.lock();
+    done_cv_.wait(lk, [this] { return pending_ == 0; });
+    job_ = nullptr;
+  }
+
+ private:
+  void work() {
+    for (;;) {
+      long i = next_.fetch_add(1);
+      if (i >= total_) break;
+      (*job_)(i);
+    }
+  }
+  void loop() {
+    long seen = 0;
+    for (;;) {
+      std::unique_lock<std::mutex> lk(m_);
+      cv_.wait(lk, [&] { return quit_ || gen_ != seen; });
+      if (quit_) return;
+      seen = gen_;
+      lk.unlock();
+      work();
+      lk.lock();
+      if (--pending_ == 0) done_cv_.notify_all();
+    }
+  }
+  void stop_all() {
+    {
+      std::lock_guard<std::mutex> lk(m_);
+      quit_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+    workers_.clear();
+  }
+  std::vector<std::thread> workers_;
+  std::mutex m_;
+  std::condition_variable cv_, done_cv_;
+  const std::function<void(long)>* job_ = nullptr;
+  long total_ = 0;
+  std::atomic<long> next_{0};
+  int pending_ = 0;
+  long gen_ = 0;
+  bool quit_ = false;
+};
+
+Pool& pool() {
+  static Pool p(1);
+  return p;
+}
+
+inline void par_for(long n, const std::function<void(long)>& f) { pool().run(n, f); }
+
+// ------------------------------------------------------------------------------------------------
+// scalar helpers (kernels.rs:106-117, 572-662)
+
+inline float bf16_to_f32(uint16_t x) {
+  uint32_t u = (uint32_t)x << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+inline float silu(float x) { return x / (1.0f + expf(-x)); }
+inline float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+inline float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// kernels.rs:589-603: eight lane accumulators, summed left to right, then the scalar remainder.
+inline float dot(const float* a, const float* b, size_t n) {
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  size_t full = n / 8 * 8;
+  for (size_t c = 0; c < full; c += 8)
+    for (int i = 0; i < 8; i++) acc[i] += a[c + i] * b[c + i];
+  float s = -0.0f;
+  for (int i = 0; i < 8; i++) s += acc[i];
+  for (size_t i = full; i < n; i++) s += a[i] * b[i];
+  return s;
+}
+
+// kernels.rs:607-613
+inline void rmsnorm(const float* x, const float* w, float eps, float* out, size_t n) {
+  float ms = dot(x, x, n) / (float)n;
+  float inv = 1.0f / sqrtf(ms + eps);
+  for (size_t i = 0; i < n; i++) out[i] = x[i] * inv * w[i];
+}
+
+void rmsnorm_rows(const float* x, const float* w, float eps, float* out, size_t d, long rows) {
+  par_for(rows, [&](long r) { rmsnorm(x + r * d, w, eps, out + r * d, d); });
+}
+
+void add_inplace(float* x, const float* y, size_t n) {
+  long chunks = (long)((n + (1 << 14) - 1) >> 14);
+  par_for(chunks, [&](long c) {
+    size_t a = (size_t)c << 14, b = std::min(n, a + (1 << 14));
+    for (size_t i = a; i < b; i++) x[i] += y[i];
+  });
+}
+
+// kernels.rs:628-639
+void softmax_inplace(float* x, size_t n) {
+  float m = -INFINITY;
+  for (size_t i = 0; i < n; i++) m = fmaxf(m, x[i]);
+  float s = 0.0f;
+  for (size_t i = 0; i < n; i++) {
+    x[i] = expf(x[i] - m);
+    s += x[i];
+  }
+  float inv = 1.0f / s;
+  for (size_t i = 0; i < n; i++) x[i] *= inv;
+}
+
+// kernels.rs:642-662: strict `>` against the floor, insertion after every entry >= v, so on ties the
+// lower index ranks first.
+int topk(const float* v, size_t n, int k, uint32_t* idx, float* val) {
+  if ((size_t)k > n) k = (int)n;
+  if (k <= 0) return 0;
+  std::vector<std::pair<uint32_t, float>> best;
+  best.reserve(k + 1);
+  float floor = -INFINITY;
+  for (size_t i = 0; i < n; i++) {
+    float x = v[i];
+    if ((int)best.size() < k || x > floor) {
+      size_t pos = 0;
+      {
+        size_t lo = 0, hi = best.size();
+        while (lo < hi) {  // partition_point(|b| b >= x)
+          size_t mid = (lo + hi) / 2;
+          if (best[mid].second >= x) lo = mid + 1; else hi = mid;
+        }
+        pos = lo;
+      }
+      best.insert(best.begin() + pos, {(uint32_t)i, x});
+      if ((int)best.size() > k) best.pop_back();
+      if ((int)best.size() == k) floor = best[k - 1].second;
+    }
+  }
+  for (size_t i = 0; i < best.size(); i++) {
+    idx[i] = best[i].first;
+    if (val) val[i] = best[i].second;
+  }
+  return (int)best.size();
+}
+
+// ------------------------------------------------------------------------------------------------
+// AVX2 matmul (kernels.rs:138-268, 270-522), bf16 weights only
+
+constexpr size_t KC = 256;
+constexpr size_t NR = 16;
+
+__attribute__((target("avx2,fma,f16c"))) inline __m256 load8(const uint16_t* p) {
+  __m128i v = _mm_loadu_si128((const __m128i*)p);
+  return _mm256_castsi256_ps(_mm256_slli_epi32(_mm256_cvtepu16_epi32(v), 16));
+}
+
+__attribute__((target("avx2,fma"))) inline float hsum(__m256 v) {
+  __m128 lo = _mm256_castps256_ps128(v);
+  __m128 hi = _mm256_extractf128_ps(v, 1);
+  __m128 s = _mm_add_ps(lo, hi);
+  s = _mm_add_ps(s, _mm_movehl_ps(s, s));
+  s = _mm_add_ss(s, _mm_shuffle_ps(s, s, 0x55));
+  return _mm_cvtss_f32(s);
+}
+
+// kernels.rs:303-362
+__attribute__((target("avx2,fma,f16c"))) void dot_rows(const uint16_t* w, size_t cols, size_t r0,
+                                                         const float* x, float* ys, size_t n) {
+  size_t i = 0;
+  while (i + 4 <= n) {
+    const uint16_t* p0 = w + (r0 + i) * cols;
+    const uint16_t *p1 = p0 + cols, *p2 = p0 + 2 * cols, *p3 = p0 + 3 * cols;
+    __m256 z = _mm256_setzero_ps();
+    __m256 a0 = z, a1 = z, a2 = z, a3 = z, b0 = z, b1 = z, b2 = z, b3 = z;
+    size_t k = 0;
+    while (k + 16 <= cols) {
+      __m256 x0 = _mm256_loadu_ps(x + k), x1 = _mm256_loadu_ps(x + k + 8);
+      a0 = _mm256_fmadd_ps(load8(p0 + k), x0, a0);
+      b0 = _mm256_fmadd_ps(load8(p0 + k + 8), x1, b0);
+      a1 = _mm256_fmadd_ps(load8(p1 + k), x0, a1);
+      b1 = _mm256_fmadd_ps(load8(p1 + k + 8), x1, b1);
+      a2 = _mm256_fmadd_ps(load8(p2 + k), x0, a2);
+      b2 = _mm256_fmadd_ps(load8(p2 + k + 8), x1, b2);
+      a3 = _mm256_fmadd_ps(load8(p3 + k), x0, a3);
+      b3 = _mm256_fmadd_ps(load8(p3 + k + 8), x1, b3);
+      k += 16;
+    }
+    float s[4] = {hsum(_mm256_add_ps(a0, b0)), hsum(_mm256_add_ps(a1, b1)), hsum(_mm256_add_ps(a2, b2)),
+                  hsum(_mm256_add_ps(a3, b3))};
+    while (k < cols) {
+      float xv = x[k];
+      s[0] += bf16_to_f32(p0[k]) * xv;
+      s[1] += bf16_to_f32(p1[k]) * xv;
+      s[2] += bf16_to_f32(p2[k]) * xv;
+      s[3] += bf16_to_f32(p3[k]) * xv;
+      k++;
+    }
+    memcpy(ys + i, s, sizeof s);
+    i += 4;
+  }
+  while (i < n) {
+    const uint16_t* p = w + (r0 + i) * cols;
+    __m256 a = _mm256_setzero_ps();
+    size_t k = 0;
+    while (k + 8 <= cols) {
+      a = _mm256_fmadd_ps(load8(p + k), _mm256_loadu_ps(x + k), a);
+      k += 8;
+    }
+    float s = hsum(a);
+    while (k < cols) {
+      s += bf16_to_f32(p[k]) * x[k];
+      k++;
+    }
+    ys[i] = s;
+    i++;
+  }
+}
+
+// kernels.rs:365-396
+template <int T>
+__attribute__((target("avx2,fma,f16c"))) void multi_dot(const uint16_t* w, size_t cols, size_t r0, size_t nr,
+                                                          const float* x, float* y, size_t ldy) {
+  for (size_t r = r0; r < r0 + nr; r++) {
+    const uint16_t* p = w + r * cols;
+    __m256 acc[T];
+    for (int t = 0; t < T; t++) acc[t] = _mm256_setzero_ps();
+    size_t k = 0;
+    while (k + 8 <= cols) {
+      __m256 wv = load8(p + k);
+      for (int t = 0; t < T; t++) acc[t] = _mm256_fmadd_ps(wv, _mm256_loadu_ps(x + t * cols + k), acc[t]);
+      k += 8;
+    }
+    for (int t = 0; t < T; t++) {
+      float s = hsum(acc[t]);
+      for (size_t kk = k; kk < cols; kk++) s += bf16_to_f32(p[kk]) * x[t * cols + kk];
+      y[t * ldy + r] = s;
+    }
+  }
+}
+
+// kernels.rs:427-464 (the packed values are exact f32 widenings; the 8x8 transpose only moves them)
+__attribute__((target("avx2,fma,f16c"))) void pack_panel(const uint16_t* w, size_t cols, size_t rows, size_t r0,
+                                                           size_t k0, size_t kc, float* pack) {
+  size_t nr = std::min(NR, rows - r0);
+  for (size_t k = 0; k < kc; k++)
+    for (size_t i = 0; i < NR; i++) pack[k * NR + i] = i < nr ? bf16_to_f32(w[(r0 + i) * cols + k0 + k]) : 0.0f;
+}
+
+// kernels.rs:466-521
+template <int M>
+__attribute__((target("avx2,fma"))) void micro(const float* pack, size_t kc, const float* x, size_t ldx, float* y,
+                                               size_t ldy, size_t nr, bool accumulate) {
+  __m256 acc[M][2];
+  for (int i = 0; i < M; i++) acc[i][0] = acc[i][1] = _mm256_setzero_ps();
+  if (accumulate) {
+    for (int i = 0; i < M; i++) {
+      const float* yr = y + i * ldy;
+      float tmp[NR] = {0};
+      for (size_t j = 0; j < nr; j++) tmp[j] = yr[j];
+      acc[i][0] = _mm256_loadu_ps(tmp);
+      acc[i][1] = _mm256_loadu_ps(tmp + 8);
+    }
+  }
+  for (size_t k = 0; k < kc; k++) {
+    __m256 w0 = _mm256_loadu_ps(pack + k * NR), w1 = _mm256_loadu_ps(pack + k * NR + 8);
+    for (int i = 0; i < M; i++) {
+      __m256 xb = _mm256_broadcast_ss(x + i * ldx + k);
+      acc[i][0] = _mm256_fmadd_ps(xb, w0, acc[i][0]);
+      acc[i][1] = _mm256_fmadd_ps(xb, w1, acc[i][1]);
+    }
+  }
+  for (int i = 0; i < M; i++) {
+    float tmp[NR];
+    _mm256_storeu_ps(tmp, acc[i][0]);
+    _mm256_storeu_ps(tmp + 8, acc[i][1]);
+    float* yr = y + i * ldy;
+    for (size_t j = 0; j < nr; j++) yr[j] = tmp[j];
+  }
+}
+
+int n_threads() { return pool().size(); }
+
+// kernels.rs:138-143
+void matvec(const uint16_t* w, size_t rows, size_t cols, const float* x, float* y) {
+  long chunk = (long)std::min<size_t>(512, std::max<size_t>(4, rows / (n_threads() * 6))) & ~3L;
+  if (chunk < 4) chunk = 4;
+  long nch = (long)((rows + chunk - 1) / chunk);
+  par_for(nch, [&](long ci) {
+    size_t r0 = ci * chunk, n = std::min<size_t>(chunk, rows - r0);
+    dot_rows(w, cols, r0, x, y + r0, n);
+  });
+}
+
+// kernels.rs:163-268
+void matmul(const uint16_t* w, size_t rows, size_t cols, const float* x, size_t n, float* y) {
+  if (n == 0) return;
+  if (n == 1) return matvec(w, rows, cols, x, y);
+  if (n < 8) {
+    size_t chunk = std::min<size_t>(512, std::max<size_t>(4, rows / (n_threads() * 6)));
+    long nch = (long)((rows + chunk - 1) / chunk);
+    par_for(nch, [&](long ci) {
+      size_t r0 = ci * chunk, nr = std::min(chunk, rows - r0);
+      switch (n) {
+        case 2: multi_dot<2>(w, cols, r0, nr, x, y, rows); break;
+        case 3: multi_dot<3>(w, cols, r0, nr, x, y, rows); break;
+        case 4: multi_dot<4>(w, cols, r0, nr, x, y, rows); break;
+        case 5: multi_dot<5>(w, cols, r0, nr, x, y, rows); break;
+        case 6: multi_dot<6>(w, cols, r0, nr, x, y, rows); break;
+        default: multi_dot<7>(w, cols, r0, nr, x, y, rows); break;
+      }
+    });
+    return;
+  }
+  size_t panels = (rows + NR - 1) / NR;
+  size_t tb_size = std::min<size_t>((std::max<size_t>((2u << 20) / (cols * 4), 6) / 6) * 6, 480);
+  for (size_t tb0 = 0; tb0 < n; tb0 += tb_size) {
+    size_t tb = std::min(tb_size, n - tb0);
+    par_for((long)panels, [&](long p) {
+      thread_local std::vector<float> pack;
+      pack.resize(KC * NR);
+      size_t r0 = p * NR, nr = std::min(NR, rows - r0);
+      for (size_t k0 = 0; k0 < cols; k0 += KC) {
+        size_t kc = std::min(KC, cols - k0);
+        pack_panel(w, cols, rows, r0, k0, kc, pack.data());
+        for (size_t t = 0; t < tb;) {
+          size_t m = std::min<size_t>(6, tb - t);
+          const float* xr = x + (tb0 + t) * cols + k0;
+          float* yr = y + (tb0 + t) * rows + r0;
+          bool acc = k0 > 0;
+          switch (m) {
+            case 6: micro<6>(pack.data(), kc, xr, cols, yr, rows, nr, acc); break;
+            case 5: micro<5>(pack.data(), kc, xr, cols, yr, rows, nr, acc); break;
+            case 4: micro<4>(pack.data(), kc, xr, cols, yr, rows, nr, acc); break;
+            case 3: micro<3>(pack.data(), kc, xr, cols, yr, rows, nr, acc); break;
+            case 2: micro<2>(pack.data(), kc, xr, cols, yr, rows, nr, acc); break;
+            default: micro<1>(pack.data(), kc, xr, cols, yr, rows, nr, acc); break;
+          }
+          t += m;
+        }
+      }
+    });
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// gated delta rule step (model.rs:501-524), loop order kept
+
+inline void recur_body(float* s, const float* q, const float* k, const float* v, float decay, float beta, float* kv,
+                       float* o, int dk, int dv) {
+  for (int j = 0; j < dv; j++) kv[j] = 0.0f;
+  for (int i = 0; i < dk; i++) {
+    const float* row = s + (size_t)i * dv;
+    float ki = k[i];
+    for (int j = 0; j < dv; j++) kv[j] += row[j] * ki;
+  }
+  for (int j = 0; j < dv; j++) kv[j] = (v[j] - decay * kv[j]) * beta;
+  for (int j = 0; j < dv; j++) o[j] = 0.0f;
+  for (int i = 0; i < dk; i++) {
+    float* row = s + (size_t)i * dv;
+    float ki = k[i], qi = q[i];
+    for (int j = 0; j < dv; j++) {
+      row[j] = row[j] * decay + ki * kv[j];
+      o[j] += row[j] * qi;
+    }
+  }
+}
+
+inline uint16_t f32_to_f16(float v) { return (uint16_t)_cvtss_sh(v, _MM_FROUND_TO_NEAREST_INT); }
+
+// worker.rs:97-112 companding: q = round(127 * sqrt(min(|v|, 1))), sign of v.
+inline int8_t compand(float v) {
+  float q = roundf(sqrtf(fminf(fabsf(v), 1.0f)) * 127.0f);
+  return v < 0.0f ? (int8_t)(-(int)q) : (int8_t)(int)q;
+}
+
+// ------------------------------------------------------------------------------------------------
+// model
+
+struct Mat {
+  const uint16_t* p = nullptr;
+  size_t rows = 0, cols = 0;
+};
+
+struct DeltaNetW {
+  Mat qkv, z, b, a, out;
+  std::vector<float> conv, neg_a, dt_bias, norm;
+};
+struct AttnW {
+  Mat q, k, v, o;
+  std::vector<float> q_norm, k_norm;
+};
+struct LayerW {
+  int kind = 0;  // 0 = linear (DeltaNet), 1 = full attention
+  std::vector<float> ln1, ln2;
+  DeltaNetW dn;
+  AttnW at;
+  Mat gate, up, down;
+};
+
+struct Cfg {
+  int hidden, intermediate, n_layers, vocab;
+  float eps;
+  int n_heads, n_kv_heads, head_dim, rotary_dim;
+  double rope_theta;
+  int conv_kernel, lin_k_heads, lin_v_heads, lin_k_dim, lin_v_dim;
+  int conv_dim() const { return 2 * lin_k_heads * lin_k_dim + lin_v_heads * lin_v_dim; }
+};
+
+struct Model {
+  Cfg cfg;
+  Mat embed, lm_head;
+  std::vector<LayerW> layers;
+  std::vector<float> final_norm, inv_freq;
+};
+
+struct LayerCache {
+  std::vector<float> conv, state;  // linear
+  std::vector<float> k, v;         // full: [pos][kv][hd]
+};
+struct Cache {
+  size_t pos = 0;
+  std::vector<LayerCache> layers;
+};
+
+// steering.rs:77-104, with the ops already compiled (Add values multiplied by the dose unit).
+struct Op {
+  int neuron, kind;  // kind 1 add, 2 mul, 3 set
+  float value;
+  int gate;  // -1 none
+};
+struct GateSpec {
+  float threshold;
+  int last_layer;
+};
+struct Plan {
+  std::vector<std::vector<Op>> ops;
+  std::vector<GateSpec> gates;
+  std::vector<std::vector<std::tuple<int, int, float>>> detectors;  // per layer: (gate, neuron, weight)
+};
+struct GateState {
+  std::vector<char> open;
+  std::vector<float> score;
+  std::vector<std::vector<float>> partial;
+  std::vector<int> opened_at;  // -1 = None
+};
+
+// steering.rs:151-160
+void plan_begin(const Plan& p, GateState& st, size_t rows) {
+  size_t g = p.gates.size();
+  if (st.open.size() != g) {
+    st.open.assign(g, 0);
+    st.score.assign(g, 0.0f);
+    st.partial.assign(g, {});
+    st.opened_at.assign(g, -1);
+  }
+  for (auto& v : st.partial) {
+    v.clear();
+    v.resize(rows, 0.0f);
+  }
+  for (auto& o : st.opened_at) o = -1;
+}
+
+// steering.rs:163-210
+void plan_apply(const Plan& p, int layer, float* acts, size_t n, size_t rows, GateState& st) {
+  if ((size_t)layer < p.detectors.size()) {
+    for (auto& [g, neuron, w] : p.detectors[layer])
+      for (size_t r = 0; r < rows; r++)
+        if (r < st.partial[g].size()) st.partial[g][r] += w * acts[r * n + neuron];
+    for (size_t g = 0; g < p.gates.size(); g++) {
+      if (p.gates[g].last_layer != layer || st.partial[g].empty()) continue;
+      st.score[g] = st.partial[g].back();
+      if (!st.open[g]) {
+        for (size_t r = 0; r < st.partial[g].size(); r++)
+          if (st.partial[g][r] > p.gates[g].threshold) {
+            st.opened_at[g] = (int)r;
+            st.open[g] = 1;
+            break;
+          }
+      }
+    }
+  }
+  if ((size_t)layer >= p.ops.size()) return;
+  for (const Op& op : p.ops[layer]) {
+    size_t from = 0;
+    if (op.gate >= 0) {
+      int g = op.gate;
+      if (!st.open[g]) continue;
+      if (st.opened_at[g] >= 0) {
+        if (p.gates[g].last_layer <= layer) from = (size_t)st.opened_at[g];
+        else continue;
+      }
+    }
+    for (size_t r = from; r < rows; r++) {
+      float& a = acts[r * n + op.neuron];
+      if (op.kind == 1) a += op.value;
+      else if (op.kind == 2) a *= op.value;
+      else if (op.kind == 3) a = op.value;
+    }
+  }
+}
+
+// One sequence of a forward call.
+struct SeqIO {
+  Cache* cache;
+  const uint32_t* tokens;
+  long n;
+  const Plan* plan;     // may be null
+  GateState* gate;      // required when plan != null
+  int8_t* frames;       // [n][layers*intermediate] or null
+  uint16_t* resid;      // [n][layers*hidden] f16 or null
+};
+
+void rope(const Model& m, float* x, size_t pos) {
+  int half = m.cfg.rotary_dim / 2;
+  for (int i = 0; i < half; i++) {
+    float ang = (float)pos * m.inv_freq[i];
+    float s = sinf(ang), c = cosf(ang);
+    float a = x[i], b = x[i + half];
+    x[i] = a * c - b * s;
+    x[i + half] = b * c + a * s;
+  }
+}
+
+// model.rs:296-396
+void deltanet(const Model& m, const DeltaNetW& dn, int li, const float* h, long total, SeqIO* seqs, int nseq,
+              const std::vector<long>& offs, float* out) {
+  const Cfg& cfg = m.cfg;
+  int c = cfg.conv_dim();
+  int hk = cfg.lin_k_heads, hv = cfg.lin_v_heads, dk = cfg.lin_k_dim, dv = cfg.lin_v_dim;
+  int key_dim = hk * dk, vd = hv * dv, kern = cfg.conv_kernel;
+  std::vector<float> qkv((size_t)total * c), z((size_t)total * vd), bb((size_t)total * hv), aa((size_t)total * hv);
+  matmul(dn.qkv.p, dn.qkv.rows, dn.qkv.cols, h, total, qkv.data());
+  matmul(dn.z.p, dn.z.rows, dn.z.cols, h, total, z.data());
+  matmul(dn.b.p, dn.b.rows, dn.b.cols, h, total, bb.data());
+  matmul(dn.a.p, dn.a.rows, dn.a.cols, h, total, aa.data());
+  std::vector<float> core((size_t)total * vd, 0.0f);
+  for (int s = 0; s < nseq; s++) {
+    long r0 = offs[s], nrows = offs[s + 1] - offs[s];
+    if (nrows == 0) continue;
+    LayerCache& lc = seqs[s].cache->layers[li];
+    float* rows = qkv.data() + (size_t)r0 * c;
+    std::vector<float> ext((size_t)(kern - 1 + nrows) * c);
+    memcpy(ext.data(), lc.conv.data(), sizeof(float) * (kern - 1) * c);
+    memcpy(ext.data() + (size_t)(kern - 1) * c, rows, sizeof(float) * nrows * c);
+    par_for(nrows, [&](long t) {
+      float* row = rows + (size_t)t * c;
+      for (int ch = 0; ch < c; ch++) {
+        const float* w = dn.conv.data() + (size_t)ch * kern;
+        float acc = 0.0f;
+        for (int j = 0; j < kern; j++) acc += w[j] * ext[(size_t)(t + j) * c + ch];
+        row[ch] = silu(acc);
+      }
+    });
+    memcpy(lc.conv.data(), ext.data() + (size_t)nrows * c, sizeof(float) * (kern - 1) * c);
+    float qscale = 1.0f / sqrtf((float)dk);
+    par_for(nrows, [&](long t) {
+      float* row = rows + (size_t)t * c;
+      for (int head = 0; head < hk; head++) {
+        int bases[2] = {head * dk, key_dim + head * dk};
+        float scales[2] = {qscale, 1.0f};
+        for (int u = 0; u < 2; u++) {
+          float* v = row + bases[u];
+          float inv = 1.0f / sqrtf(dot(v, v, dk) + 1e-6f);
+          float f = inv * scales[u];
+          for (int i = 0; i < dk; i++) v[i] *= f;
+        }
+      }
+    });
+    const float* bseg = bb.data() + (size_t)r0 * hv;
+    const float* aseg = aa.data() + (size_t)r0 * hv;
+    const float* zseg = z.data() + (size_t)r0 * vd;
+    int ratio = hv / hk;
+    float eps = cfg.eps;
+    par_for(hv, [&](long head) {
+      float* st = lc.state.data() + (size_t)head * dk * dv;
+      int kh = (int)head / ratio;
+      std::vector<float> kv(dv), o(dv);
+      for (long t = 0; t < nrows; t++) {
+        const float* row = rows + (size_t)t * c;
+        const float* q = row + kh * dk;
+        const float* k = row + key_dim + kh * dk;
+        const float* v = row + 2 * key_dim + head * dv;
+        float decay = expf(dn.neg_a[head] * softplus(aseg[t * hv + head] + dn.dt_bias[head]));
+        float beta = sigmoid(bseg[t * hv + head]);
+        recur_body(st, q, k, v, decay, beta, kv.data(), o.data(), dk, dv);
+        const float* zt = zseg + (size_t)t * vd + head * dv;
+        float inv = 1.0f / sqrtf(dot(o.data(), o.data(), dv) / (float)dv + eps);
+        float* dst = core.data() + (size_t)(r0 + t) * vd + head * dv;
+        for (int j = 0; j < dv; j++) dst[j] = o[j] * inv * dn.norm[j] * silu(zt[j]);
+      }
+    });
+  }
+  matmul(dn.out.p, dn.out.rows, dn.out.cols, core.data(), total, out);
+}
+
+// model.rs:398-467
+void attention(const Model& m, const AttnW& at, int li, const float* h, long total, SeqIO* seqs, int nseq,
+               const std::vector<long>& offs, float* out) {
+  const Cfg& cfg = m.cfg;
+  int nh = cfg.n_heads, nkv = cfg.n_kv_heads, hd = cfg.head_dim;
+  std::vector<float> qg((size_t)total * nh * hd * 2), kk((size_t)total * nkv * hd), vv((size_t)total * nkv * hd);
+  matmul(at.q.p, at.q.rows, at.q.cols, h, total, qg.data());
+  matmul(at.k.p, at.k.rows, at.k.cols, h, total, kk.data());
+  matmul(at.v.p, at.v.rows, at.v.cols, h, total, vv.data());
+  std::vector<float> o((size_t)total * nh * hd, 0.0f);
+  float scale = 1.0f / sqrtf((float)hd);
+  int group = nh / nkv;
+  for (int s = 0; s < nseq; s++) {
+    long r0 = offs[s], nrows = offs[s + 1] - offs[s];
+    if (nrows == 0) continue;
+    size_t pos0 = seqs[s].cache->pos;
+    par_for(nrows, [&](long t) {
+      float* row = qg.data() + (size_t)(r0 + t) * nh * hd * 2;
+      std::vector<float> tmp(hd);
+      for (int head = 0; head < nh; head++) {
+        float* q = row + (size_t)head * 2 * hd;
+        memcpy(tmp.data(), q, sizeof(float) * hd);
+        rmsnorm(tmp.data(), at.q_norm.data(), cfg.eps, q, hd);
+        rope(m, q, pos0 + t);
+      }
+    });
+    par_for(nrows, [&](long t) {
+      float* row = kk.data() + (size_t)(r0 + t) * nkv * hd;
+      std::vector<float> tmp(hd);
+      for (int head = 0; head < nkv; head++) {
+        float* k = row + (size_t)head * hd;
+        memcpy(tmp.data(), k, sizeof(float) * hd);
+        rmsnorm(tmp.data(), at.k_norm.data(), cfg.eps, k, hd);
+        rope(m, k, pos0 + t);
+      }
+    });
+    LayerCache& lc = seqs[s].cache->layers[li];
+    lc.k.insert(lc.k.end(), kk.begin() + (size_t)r0 * nkv * hd, kk.begin() + (size_t)(r0 + nrows) * nkv * hd);
+    lc.v.insert(lc.v.end(), vv.begin() + (size_t)r0 * nkv * hd, vv.begin() + (size_t)(r0 + nrows) * nkv * hd);
+    const float* kc = lc.k.data();
+    const float* vc = lc.v.data();
+    par_for(nrows * nh, [&](long i) {
+      long t = i / nh;
+      int head = (int)(i % nh);
+      int kvh = head / group;
+      const float* qrow = qg.data() + (size_t)(r0 + t) * nh * hd * 2;
+      const float* q = qrow + (size_t)head * 2 * hd;
+      const float* gate = q + hd;
+      size_t ctx = pos0 + t + 1;
+      std::vector<float> sc(ctx);
+      for (size_t j = 0; j < ctx; j++) sc[j] = dot(q, kc + (j * nkv + kvh) * hd, hd) * scale;
+      softmax_inplace(sc.data(), ctx);
+      float* oh = o.data() + (size_t)(r0 + t) * nh * hd + (size_t)head * hd;
+      for (int d = 0; d < hd; d++) oh[d] = 0.0f;
+      for (size_t j = 0; j < ctx; j++) {
+        const float* vr = vc + (j * nkv + kvh) * hd;
+        float p = sc[j];
+        for (int d = 0; d < hd; d++) oh[d] += p * vr[d];
+      }
+      for (int d = 0; d < hd; d++) oh[d] *= sigmoid(gate[d]);
+    });
+  }
+  matmul(at.o.p, at.o.rows, at.o.cols, o.data(), total, out);
+}
+
+// model.rs:217-294 (+ Probe hooks, worker.rs:130-152). Returns logits for the last row of each sequence
+// with rows (rows of sequences without tokens are left untouched).
+void forward(Model& m, SeqIO* seqs, int nseq, const float* act_scale, float* track_max, int want_logits,
+             float* logits) {
+  const Cfg& cfg = m.cfg;
+  size_t d = cfg.hidden, n = cfg.intermediate;
+  std::vector<long> offs(nseq + 1, 0);
+  for (int i = 0; i < nseq; i++) offs[i + 1] = offs[i] + seqs[i].n;
+  long total = offs[nseq];
+  if (total == 0) return;
+  std::vector<float> x((size_t)total * d), h((size_t)total * d), mixed((size_t)total * d);
+  std::vector<float> g((size_t)total * n), u((size_t)total * n);
+  {
+    std::vector<uint32_t> toks;
+    for (int i = 0; i < nseq; i++) toks.insert(toks.end(), seqs[i].tokens, seqs[i].tokens + seqs[i].n);
+    par_for(total, [&](long r) {
+      const uint16_t* e = m.embed.p + (size_t)toks[r] * m.embed.cols;
+      for (size_t i = 0; i < d; i++) x[r * d + i] = bf16_to_f32(e[i]);
+    });
+  }
+  for (int i = 0; i < nseq; i++)
+    if (seqs[i].plan) plan_begin(*seqs[i].plan, *seqs[i].gate, (size_t)seqs[i].n);
+  for (int li = 0; li < cfg.n_layers; li++) {
+    LayerW& layer = m.layers[li];
+    rmsnorm_rows(x.data(), layer.ln1.data(), cfg.eps, h.data(), d, total);
+    if (layer.kind == 0) deltanet(m, layer.dn, li, h.data(), total, seqs, nseq, offs, mixed.data());
+    else attention(m, layer.at, li, h.data(), total, seqs, nseq, offs, mixed.data());
+    add_inplace(x.data(), mixed.data(), x.size());
+    rmsnorm_rows(x.data(), layer.ln2.data(), cfg.eps, h.data(), d, total);
+    matmul(layer.gate.p, layer.gate.rows, layer.gate.cols, h.data(), total, g.data());
+    matmul(layer.up.p, layer.up.rows, layer.up.cols, h.data(), total, u.data());
+    {
+      size_t nn = g.size();
+      long chunks = (long)((nn + (1 << 14) - 1) >> 14);
+      par_for(chunks, [&](long c) {
+        size_t a = (size_t)c << 14, b = std::min(nn, a + (1 << 14));
+        for (size_t i = a; i < b; i++) g[i] = silu(g[i]) * u[i];
+      });
+    }
+    for (int s = 0; s < nseq; s++) {
+      SeqIO& sq = seqs[s];
+      long rows = offs[s + 1] - offs[s];
+      float* acts = g.data() + (size_t)offs[s] * n;
+      if (sq.plan) plan_apply(*sq.plan, li, acts, n, (size_t)rows, *sq.gate);
+      if (sq.frames) {
+        const float* sc = act_scale ? act_scale + (size_t)li * n : nullptr;
+        par_for(rows, [&](long r) {
+          int8_t* dst = sq.frames + (size_t)r * cfg.n_layers * n + (size_t)li * n;
+          const float* src = acts + (size_t)r * n;
+          for (size_t j = 0; j < n; j++) dst[j] = compand(sc ? src[j] / sc[j] : src[j]);
+        });
+      }
+      if (track_max) {
+        float* dst = track_max + (size_t)li * n;
+        for (long r = 0; r < rows; r++) {
+          if (sq.cache->pos + r == 0) continue;
+          const float* src = acts + (size_t)r * n;
+          for (size_t j = 0; j < n; j++) dst[j] = fmaxf(dst[j], fabsf(src[j]));
+        }
+      }
+    }
+    matmul(layer.down.p, layer.down.rows, layer.down.cols, g.data(), total, mixed.data());
+    add_inplace(x.data(), mixed.data(), x.size());
+    for (int s = 0; s < nseq; s++) {
+      SeqIO& sq = seqs[s];
+      if (!sq.resid) continue;
+      long rows = offs[s + 1] - offs[s];
+      for (long r = 0; r < rows; r++) {
+        uint16_t* dst = sq.resid + (size_t)r * cfg.n_layers * d + (size_t)li * d;
+        const float* src = x.data() + (size_t)(offs[s] + r) * d;
+        for (size_t i = 0; i < d; i++) dst[i] = f32_to_f16(src[i]);
+      }
+    }
+  }
+  for (int s = 0; s < nseq; s++) seqs[s].cache->pos += seqs[s].n;
+  if (!want_logits) return;
+  std::vector<int> live;
+  for (int s = 0; s < nseq; s++)
+    if (seqs[s].n > 0) live.push_back(s);
+  std::vector<float> last(live.size() * d), normed(live.size() * d);
+  for (size_t i = 0; i < live.size(); i++) {
+    long r = offs[live[i] + 1] - 1;
+    memcpy(last.data() + i * d, x.data() + (size_t)r * d, sizeof(float) * d);
+  }
+  rmsnorm_rows(last.data(), m.final_norm.data(), cfg.eps, normed.data(), d, (long)live.size());
+  size_t v = m.lm_head.rows;
+  std::vector<float> out(live.size() * v);
+  matmul(m.lm_head.p, m.lm_head.rows, m.lm_head.cols, normed.data(), live.size(), out.data());
+  for (size_t i = 0; i < live.size(); i++) memcpy(logits + (size_t)live[i] * v, out.data() + i * v, sizeof(float) * v);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------
+// C ABI for the ctypes wrapper (oracle/__init__.py)
+
+EXPORT void oracle_set_threads(int n) { pool().resize(n); }
+EXPORT int oracle_threads() { return n_threads(); }
+
+EXPORT void oracle_matmul(const uint16_t* w, long rows, long cols, const float* x, long n, float* y) {
+  matmul(w, rows, cols, x, n, y);
+}
+EXPORT int oracle_topk(const float* v, long n, int k, uint32_t* idx, float* val) { return topk(v, n, k, idx, val); }
+EXPORT void oracle_softmax(float* x, long n) { softmax_inplace(x, n); }
+EXPORT float oracle_dot(const float* a, const float* b, long n) { return dot(a, b, n); }
+
+// Gated DeltaNet single decode step over B*H independent heads (model.rs:374-376 + recur_body).
+// S: [B][H][dk][dv] f32 (updated in place); q,k: [B][H][dk] bf16; v: [B][H][dv] bf16;
+// g (log decay) and beta: [B][H] f32; o: [B][H][dv] f32 = S_new^T q.
+EXPORT void oracle_gdn_decode(int B, int H, int dk, int dv, float* S, const uint16_t* q, const uint16_t* k,
+                              const uint16_t* v, const float* g, const float* beta, float* o) {
+  par_for((long)B * H, [&](long bh) {
+    std::vector<float> qf(dk), kf(dk), vf(dv), kv(dv);
+    for (int i = 0; i < dk; i++) qf[i] = bf16_to_f32(q[bh * dk + i]), kf[i] = bf16_to_f32(k[bh * dk + i]);
+    for (int j = 0; j < dv; j++) vf[j] = bf16_to_f32(v[bh * dv + j]);
+    recur_body(S + (size_t)bh * dk * dv, qf.data(), kf.data(), vf.data(), expf(g[bh]), beta[bh], kv.data(),
+               o + (size_t)bh * dv, dk, dv);
+  });
+}
+
+// Gated DeltaNet prefill, token-sequential exactly as evie-core runs it (it has no chunked form).
+// q,k: [B][T][H][dk] bf16; v: [B][T][H][dv] bf16; g, beta: [B][T][H] f32; S: [B][H][dk][dv] (in: initial,
+// out: final); o: [B][T][H][dv] f32.
+EXPORT void oracle_gdn_prefill(int B, int T, int H, int dk, int dv, float* S, const uint16_t* q, const uint16_t* k,
+                               const uint16_t* v, const float* g, const float* beta, float* o) {
+  par_for((long)B * H, [&](long bh) {
+    long b = bh / H, h = bh % H;
+    std::vector<float> qf(dk), kf(dk), vf(dv), kv(dv);
+    float* st = S + (size_t)bh * dk * dv;
+    for (long t = 0; t < T; t++) {
+      size_t row = ((size_t)b * T + t) * H + h;
+      for (int i = 0; i < dk; i++) qf[i] = bf16_to_f32(q[row * dk + i]), kf[i] = bf16_to_f32(k[row * dk + i]);
+      for (int j = 0; j < dv; j++) vf[j] = bf16_to_f32(v[row * dv + j]);
+      recur_body(st, qf.data(), kf.data(), vf.data(), expf(g[row]), beta[row], kv.data(), o + row * dv, dk, dv);
+    }
+  });
+}
+
+// Gated GQA decode attention core (model.rs:445-464) over a paged KV cache.
+// q, gate (logits): [B][Hq][hd] bf16; pages: [num_pages][Hkv][page_size][hd] bf16; page_table: [B][max_pages];
+// ctx: [B]; out: [B][Hq][hd] f32 = softmax(q.K^T * scale) V * sigmoid(gate).
+EXPORT void oracle_gqa_decode(int B, int Hq, int Hkv, int hd, int page_size, const uint16_t* q, const uint16_t* kp,
+                              const uint16_t* vp, const int32_t* page_table, int max_pages, const int32_t* ctx,
+                              const uint16_t* gate, float scale, float* out) {
+  int group = Hq / Hkv;
+  par_for((long)B * Hq, [&](long bh) {
+    long b = bh / Hq;
+    int head = (int)(bh % Hq), kvh = head / group;
+    long n = ctx[b];
+    std::vector<float> qf(hd), kf(hd), sc(n > 0 ? n : 1);
+    for (int i = 0; i < hd; i++) qf[i] = bf16_to_f32(q[bh * hd + i]);
+    auto row_of = [&](const uint16_t* pages, long j) {
+      long page = page_table[b * max_pages + j / page_size];
+      return pages + (((size_t)page * Hkv + kvh) * page_size + (size_t)(j % page_size)) * hd;
+    };
+    for (long j = 0; j < n; j++) {
+      const uint16_t* kr = row_of(kp, j);
+      for (int i = 0; i < hd; i++) kf[i] = bf16_to_f32(kr[i]);
+      sc[j] = dot(qf.data(), kf.data(), hd) * scale;
+    }
+    float* oh = out + (size_t)bh * hd;
+    for (int i = 0; i < hd; i++) oh[i] = 0.0f;
+    if (n > 0) softmax_inplace(sc.data(), n);
+    for (long j = 0; j < n; j++) {
+      const uint16_t* vr = row_of(vp, j);
+      float p = sc[j];
+      for (int i = 0; i < hd; i++) oh[i] += p * bf16_to_f32(vr[i]);
+    }
+    for (int i = 0; i < hd; i++) oh[i] *= sigmoid(bf16_to_f32(gate[bh * hd + i]));
+  });
+}
+
+// ---- model ----
+
+struct oracle_cfg {
+  int hidden, intermediate, n_layers, vocab;
+  float eps;
+  int n_heads, n_kv_heads, head_dim, rotary_dim;
+  double rope_theta;
+  int conv_kernel, lin_k_heads, lin_v_heads, lin_k_dim, lin_v_dim;
+};
+
+EXPORT void* oracle_model_new(const oracle_cfg* c, const int* kinds) {
+  Model* m = new Model();
+  m->cfg = Cfg{c->hidden,     c->intermediate, c->n_layers,    c->vocab,       c->eps,
+               c->n_heads,    c->n_kv_heads,   c->head_dim,    c->rotary_dim,  c->rope_theta,
+               c->conv_kernel, c->lin_k_heads, c->lin_v_heads, c->lin_k_dim,   c->lin_v_dim};
+  m->layers.resize(c->n_layers);
+  for (int i = 0; i < c->n_layers; i++) m->layers[i].kind = kinds[i];
+  int half = c->rotary_dim / 2;
+  for (int i = 0; i < half; i++)
+    m->inv_freq.push_back(1.0f / powf((float)c->rope_theta, (float)(2 * i) / (float)c->rotary_dim));
+  return m;
+}
+EXPORT void oracle_model_free(void* p) { delete (Model*)p; }
+
+// Registers one tensor. Matrices are bf16 views (the caller keeps the memory alive); vectors are copied
+// as f32 with the load-time transforms of model.rs:148,171 (1+w norms, -exp(A_log)).
+// slot codes: matrices 1 embed, 2 lm_head, 10 qkv, 11 z, 12 b, 13 a, 14 out, 20 q, 21 k, 22 v, 23 o, 30 gate,
+// 31 up, 32 down; vectors 40 ln1(+1), 41 ln2(+1), 42 final_norm(+1), 43 q_norm(+1), 44 k_norm(+1),
+// 45 conv, 46 A_log(->-exp), 47 dt_bias, 48 gated norm (as is).
+EXPORT int oracle_model_set(void* p, int layer, int slot, const void* data, int is_bf16, long rows, long cols) {
+  Model* m = (Model*)p;
+  if (slot < 40) {
+    if (!is_bf16) return -1;
+    Mat mat{(const uint16_t*)data, (size_t)rows, (size_t)cols};
+    if (slot == 1) { m->embed = mat; return 0; }
+    if (slot == 2) { m->lm_head = mat; return 0; }
+    if (layer < 0 || layer >= (int)m->layers.size()) return -2;
+    LayerW& L = m->layers[layer];
+    switch (slot) {
+      case 10: L.dn.qkv = mat; break;
+      case 11: L.dn.z = mat; break;
+      case 12: L.dn.b = mat; break;
+      case 13: L.dn.a = mat; break;
+      case 14: L.dn.out = mat; break;
+      case 20: L.at.q = mat; break;
+      case 21: L.at.k = mat; break;
+      case 22: L.at.v = mat; break;
+      case 23: L.at.o = mat; break;
+      case 30: L.gate = mat; break;
+      case 31: L.up = mat; break;
+      case 32: L.down = mat; break;
+      default: return -3;
+    }
+    return 0;
+  }
+  size_t n = (size_t)rows * (size_t)cols;
+  std::vector<float> v(n);
+  for (size_t i = 0; i < n; i++)
+    v[i] = is_bf16 ? bf16_to_f32(((const uint16_t*)data)[i]) : ((const float*)data)[i];
+  if (slot == 40 || slot == 41 || slot == 42 || slot == 43 || slot == 44)
+    for (auto& x : v) x = 1.0f + x;
+  if (slot == 46)
+    for (auto& x : v) x = -expf(x);
+  if (slot == 42) { m->final_norm = v; return 0; }
+  if (layer < 0 || layer >= (int)m->layers.size()) return -2;
+  LayerW& L = m->layers[layer];
+  switch (slot) {
+    case 40: L.ln1 = v; break;
+    case 41: L.ln2 = v; break;
+    case 43: L.at.q_norm = v; break;
+    case 44: L.at.k_norm = v; break;
+    case 45: L.dn.conv = v; break;
+    case 46: L.dn.neg_a = v; break;
+    case 47: L.dn.dt_bias = v; break;
+    case 48: L.dn.norm = v; break;
+    default: return -3;
+  }
+  return 0;
+}
+
+// model.rs:92-106
+EXPORT void* oracle_cache_new(void* p) {
+  Model* m = (Model*)p;
+  const Cfg& c = m->cfg;
+  Cache* cache = new Cache();
+  cache->layers.resize(c.n_layers);
+  for (int i = 0; i < c.n_layers; i++)
+    if (m->layers[i].kind == 0) {
+      cache->layers[i].conv.assign((size_t)(c.conv_kernel - 1) * c.conv_dim(), 0.0f);
+      cache->layers[i].state.assign((size_t)c.lin_v_heads * c.lin_k_dim * c.lin_v_dim, 0.0f);
+    }
+  return cache;
+}
+EXPORT void oracle_cache_free(void* c) { delete (Cache*)c; }
+EXPORT void* oracle_cache_clone(void* c) { return new Cache(*(Cache*)c); }
+EXPORT long oracle_cache_pos(void* c) { return (long)((Cache*)c)->pos; }
+// Copies one linear layer's recurrent state ([hv][dk][dv] f32) or conv window out of a cache.
+EXPORT long oracle_cache_read(void* c, int layer, int which, float* dst, long cap) {
+  LayerCache& lc = ((Cache*)c)->layers[layer];
+  std::vector<float>& v = which == 0 ? lc.state : which == 1 ? lc.conv : which == 2 ? lc.k : lc.v;
+  long n = (long)v.size();
+  if (dst && cap >= n) memcpy(dst, v.data(), sizeof(float) * n);
+  return n;
+}
+
+EXPORT void* oracle_plan_new(int n_layers) {
+  Plan* p = new Plan();
+  p->ops.resize(n_layers);
+  p->detectors.resize(n_layers);
+  return p;
+}
+EXPORT void oracle_plan_free(void* p) { delete (Plan*)p; }
+EXPORT void oracle_plan_add_op(void* p, int layer, int neuron, int kind, float value, int gate) {
+  ((Plan*)p)->ops[layer].push_back(Op{neuron, kind, value, gate});
+}
+EXPORT int oracle_plan_add_gate(void* p, float threshold, int last_layer) {
+  Plan* pl = (Plan*)p;
+  pl->gates.push_back(GateSpec{threshold, last_layer});
+  return (int)pl->gates.size() - 1;
+}
+EXPORT void oracle_plan_add_detector(void* p, int gate, int layer, int neuron, float weight) {
+  ((Plan*)p)->detectors[layer].emplace_back(gate, neuron, weight);
+}
+EXPORT void* oracle_gate_state_new() { return new GateState(); }
+EXPORT void oracle_gate_state_free(void* s) { delete (GateState*)s; }
+EXPORT int oracle_gate_state_open(void* s, int g) {
+  GateState* st = (GateState*)s;
+  return g < (int)st->open.size() ? st->open[g] : 0;
+}
+// Runs Plan::begin + Plan::apply on a plain activation block (steering.rs unit tests).
+EXPORT void oracle_plan_begin(void* p, void* s, long rows) { plan_begin(*(Plan*)p, *(GateState*)s, rows); }
+EXPORT void oracle_plan_apply(void* p, int layer, float* acts, long n, long rows, void* s) {
+  plan_apply(*(Plan*)p, layer, acts, n, rows, *(GateState*)s);
+}
+
+struct oracle_seq {
+  void* cache;
+  const uint32_t* tokens;
+  long n;
+  void* plan;
+  void* gate;
+  int8_t* frames;
+  uint16_t* resid;
+};
+
+EXPORT void oracle_forward(void* p, oracle_seq* seqs, int nseq, const float* act_scale, float* track_max,
+                           int want_logits, float* logits) {
+  std::vector<SeqIO> io(nseq);
+  for (int i = 0; i < nseq; i++)
+    io[i] = SeqIO{(Cache*)seqs[i].cache, seqs[i].tokens, seqs[i].n, (const Plan*)seqs[i].plan,
+                  (GateState*)seqs[i].gate, seqs[i].frames, seqs[i].resid};
+  forward(*(Model*)p, io.data(), nseq, act_scale, track_max, want_logits, logits);
+}
+
+EXPORT int8_t oracle_compand(float v) { return compand(v); }
+EXPORT uint16_t oracle_f32_to_f16(float v) { return f32_to_f16(v); }
