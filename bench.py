@@ -1,0 +1,466 @@
+"""Benchmark of the evie-b200 hot path: one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Workloads (per GPU; with N GPUs each rank runs its own share: weak scaling, no data-path collective):
+  gdn_decode   Gated DeltaNet decode step, B=64 sequences x 16 heads, dk=dv=128, fp32 state (config 1)
+  gqa_decode   gated GQA decode attention, B=64, 16 q / 4 kv heads, hd 256, ctx ~ U[1024, 32768], 256-token pages
+               (config 3)
+  gdn_prefill  Gated DeltaNet prefill, B=8, T=8192, 16 heads (config 2)
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the launching stream; L2 is
+flushed (a 256 MiB write) between timed steps whenever a step's working set fits in L2. The K-step region is
+bracketed by a barrier and torch.cuda.synchronize() on both sides; the reported time is the max over ranks.
+`e2e` repeats the step through the C ABI from pinned host buffers with the host<->device copies inside the timed
+region. `cpu_baseline` (rank 0, N=1) times the CPU oracle (a C++ restatement of evie-core's CPU path) on a
+bounded sample of the same workload. `--impl reference` times that CPU path alone, with every host thread.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s/GPU (batch 64) + prefill tok/s; % of HBM/tensor roofline at 1/2/4/8"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        d["source"] = "measured"
+        return d
+    return dict(FALLBACK_PEAKS)
+
+
+def profiled_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if one exists."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(kernel)
+    return None
+
+
+# ------------------------------------------------------------------------------------------------------------
+# clocks during the timed region
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------------------
+# workloads
+
+class Workload:
+    name = ""
+    unit = "tokens/s"
+    dtype = "f32"
+    kernel = ""            # dominant kernel name (ncu)
+    bound = "hbm"
+    flush_l2 = False
+    tokens_per_step = 0    # units of the metric per step per GPU
+
+    def config(self) -> dict:
+        raise NotImplementedError
+
+    def setup(self, dev):
+        raise NotImplementedError
+
+    def step(self):
+        """Enqueues one step on the current stream. Returns the number of our kernel launches."""
+        raise NotImplementedError
+
+    def algorithmic(self) -> float:
+        """Bytes (hbm) or FLOPs (tensor) of the dominant kernel per step."""
+        raise NotImplementedError
+
+    def e2e_step(self):
+        """One step through the C ABI with host buffers (H2D inputs, D2H result). Returns (h2d, d2h) bytes."""
+        raise NotImplementedError
+
+    def cpu_sample(self, threads: int) -> dict:
+        raise NotImplementedError
+
+
+class GdnDecode(Workload):
+    name = "gdn_decode"
+    kernel = "gdn_decode_step_kernel"
+    flush_l2 = True  # the 64 MiB state fits in the 126 MB L2
+
+    def __init__(self, B=64, H=16, d=128):
+        self.B, self.H, self.d = B, H, d
+        self.tokens_per_step = B
+
+    def config(self):
+        return {"workload": f"gdn_decode_step B={self.B} H={self.H} dk=dv={self.d} fp32 state (config 1)",
+                "global_batch": self.B, "heads": self.H, "l2": "flushed between timed steps"}
+
+    def algorithmic(self):
+        B, H, d = self.B, self.H, self.d
+        return 2 * B * H * d * d * 4 + B * H * 3 * d * 2 + B * H * 8 + B * H * d * 4
+
+    def setup(self, dev):
+        import torch
+        from tests._inputs import gdn_decode_inputs
+
+        x = gdn_decode_inputs(self.B, self.H, 2)
+        self.x = {k: v.to(dev) for k, v in x.items()}
+        self.o = torch.empty(self.B, self.H, self.d, device=dev)
+        self.host = {k: v.pin_memory() for k, v in x.items() if k != "S"}
+        self.dev_in = {k: torch.empty_like(v, device=dev) for k, v in self.host.items()}
+        self.o_host = torch.empty(self.B, self.H, self.d).pin_memory()
+
+    def step(self):
+        from evie_b200 import ops
+
+        x = self.x
+        ops.gdn_decode_step(x["q"], x["k"], x["v"], x["g"], x["beta"], x["S"], self.o)
+        return 1
+
+    def e2e_step(self):
+        from evie_b200 import ops
+
+        h2d = 0
+        for k, v in self.host.items():
+            self.dev_in[k].copy_(v, non_blocking=True)
+            h2d += v.numel() * v.element_size()
+        d = self.dev_in
+        ops.gdn_decode_step(d["q"], d["k"], d["v"], d["g"], d["beta"], self.x["S"], self.o)
+        self.o_host.copy_(self.o, non_blocking=True)
+        return h2d, self.o.numel() * 4
+
+    def cpu_sample(self, threads):
+        import oracle
+        from tests._inputs import bf16_bits, gdn_decode_inputs
+
+        oracle.set_threads(threads)
+        x = gdn_decode_inputs(self.B, self.H, 2)
+        S = x["S"].numpy().copy()
+        args = (bf16_bits(x["q"]), bf16_bits(x["k"]), bf16_bits(x["v"]), x["g"].numpy(), x["beta"].numpy())
+        oracle.gdn_decode(S, *args)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 and n < 2000:
+            oracle.gdn_decode(S, *args)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        return {"value": self.B / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": f"{n} full decode steps (B={self.B}, H={self.H}) of the oracle's recur_body restatement"}
+
+
+class GqaDecode(Workload):
+    name = "gqa_decode"
+    kernel = "gqa_decode_kernel"
+
+    def __init__(self, B=64, Hq=16, Hkv=4, hd=256, page=256):
+        import torch
+
+        self.B, self.Hq, self.Hkv, self.hd, self.page = B, Hq, Hkv, hd, page
+        g = torch.Generator().manual_seed(4)
+        self.ctx = torch.randint(1024, 32769, (B,), generator=g).tolist()
+        self.tokens_per_step = B
+
+    def config(self):
+        return {"workload": f"gqa_decode B={self.B} Hq={self.Hq} Hkv={self.Hkv} hd={self.hd} ctx~U[1024,32768] "
+                            f"(sum {sum(self.ctx)}) page={self.page} bf16 KV (config 3)",
+                "global_batch": self.B, "l2": f"inputs larger than L2 ({self.algorithmic() / 1e9:.2f} GB)"}
+
+    def algorithmic(self):
+        """K and V rows read once, q and gate (bf16) read, out (f32) written, page tables and lengths read."""
+        kv = sum(self.ctx) * self.Hkv * self.hd * 2 * 2
+        pages = sum((c + self.page - 1) // self.page for c in self.ctx)
+        return kv + self.B * self.Hq * self.hd * (2 + 2 + 4) + (pages + self.B) * 4
+
+    def setup(self, dev):
+        import torch
+        from tests._inputs import gqa_inputs
+
+        x = gqa_inputs(self.B, self.Hq, self.Hkv, self.ctx, 4, hd=self.hd, page=self.page)
+        self.x = {k: v.to(dev) for k, v in x.items()}
+        self.out = torch.empty(self.B, self.Hq, self.hd, device=dev)
+        self.host = {k: x[k].pin_memory() for k in ("q", "gate")}
+        self.dev_in = {k: torch.empty_like(v, device=dev) for k, v in self.host.items()}
+        self.out_host = torch.empty(self.B, self.Hq, self.hd).pin_memory()
+
+    def step(self):
+        from evie_b200 import ops
+
+        x = self.x
+        ops.gqa_decode_paged(x["q"], x["gate"], x["kp"], x["vp"], x["pt"], x["ctx"], 1 / 16, self.out)
+        return 1
+
+    def e2e_step(self):
+        from evie_b200 import ops
+
+        h2d = 0
+        for k, v in self.host.items():
+            self.dev_in[k].copy_(v, non_blocking=True)
+            h2d += v.numel() * v.element_size()
+        x = self.x
+        ops.gqa_decode_paged(self.dev_in["q"], self.dev_in["gate"], x["kp"], x["vp"], x["pt"], x["ctx"], 1 / 16,
+                             self.out)
+        self.out_host.copy_(self.out, non_blocking=True)
+        return h2d, self.out.numel() * 4
+
+    def cpu_sample(self, threads):
+        import oracle
+        from tests._inputs import bf16_bits, gqa_inputs
+
+        oracle.set_threads(threads)
+        nb = 8
+        x = gqa_inputs(nb, self.Hq, self.Hkv, self.ctx[:nb], 4, hd=self.hd, page=self.page)
+        args = (bf16_bits(x["q"]), bf16_bits(x["kp"]), bf16_bits(x["vp"]), x["pt"].numpy(), x["ctx"].numpy(),
+                bf16_bits(x["gate"]), 1 / 16)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 and n < 100:
+            oracle.gqa_decode(*args)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        # scale to the full batch by context length
+        per_tok = dt / sum(self.ctx[:nb])
+        full = per_tok * sum(self.ctx)
+        return {"value": self.B / full, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": f"{n} calls on the first {nb} sequences (ctx {sum(self.ctx[:nb])} tokens), "
+                          f"scaled to the batch by context length"}
+
+
+WORKLOADS = {"gdn_decode": GdnDecode, "gqa_decode": GqaDecode}
+
+
+def make_workload(args):
+    cls = WORKLOADS[args.workload]
+    return cls(B=args.batch) if args.batch else cls()
+DEFAULT_WORKLOAD = "gdn_decode"
+
+
+# ------------------------------------------------------------------------------------------------------------
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    w = make_workload(args)
+    threads = os.cpu_count() or 1
+    vals = []
+    for _ in range(args.warmup):
+        w.cpu_sample(threads)
+    for _ in range(args.steps):
+        vals.append(w.cpu_sample(threads))
+    v = statistics.median(x["value"] for x in vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": vals[0]["unit"], "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * w.tokens_per_step / v,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+        "config": w.config(),
+        "cpu_baseline": {"value": v, "unit": vals[0]["unit"], "cores": threads, "kind": "port",
+                         "sample": vals[0]["sample"]},
+        "e2e": {"value": v, "unit": vals[0]["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import evie_b200
+
+    rank, world, local = dist_env()
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    evie_b200.lib()
+    w = make_workload(args)
+    w.setup(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if w.flush_l2 else None
+    stream = torch.cuda.current_stream()
+
+    for _ in range(max(args.warmup, 3)):
+        w.step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    launches = 0
+    with Clocks(local) as clk:
+        barrier()
+        t_wall = time.perf_counter()
+        for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(i & 0xFF)
+            ev[i][0].record(stream)
+            launches += w.step()
+            ev[i][1].record(stream)
+        barrier()
+        t_wall = time.perf_counter() - t_wall
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = sum(step_ms)
+    clocks = clk.summary()
+
+    # e2e through the C ABI with host buffers
+    for _ in range(2):
+        w.e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    h2d = d2h = 0
+    for i in range(args.steps):
+        if flush is not None:
+            flush.fill_(i & 0xFF)
+        h2d, d2h = w.e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if flush is not None:  # take the flushes out of the e2e time
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms -= f0.elapsed_time(f1)
+
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = t.tolist()
+
+    pk = peaks()
+    avg_s = total_ms / 1000.0 / args.steps
+    units = w.tokens_per_step * world
+    line = {
+        "metric": METRIC,
+        "value": units / avg_s,
+        "unit": w.unit,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": w.dtype,
+        "data": "synthetic",
+        "config": dict(w.config(), parallelism=f"dp{world}"),
+        "clocks": clocks,
+        "e2e": {"value": units / (e2e_ms / 1000.0 / args.steps), "unit": w.unit, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "wall_s": t_wall,
+    }
+    alg = w.algorithmic()
+    if w.bound == "hbm":
+        ach = alg / avg_s / 1e9
+        line["roofline"] = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                            "frac": ach / pk["hbm_gbs"], "traffic": profiled_traffic(w.kernel),
+                            "kernel": w.kernel, "algorithmic_bytes": alg, "peak_source": pk["source"]}
+    else:
+        ach = alg / avg_s / 1e12
+        line["roofline"] = {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                            "frac": ach / pk["bf16_tflops"], "traffic": profiled_traffic(w.kernel),
+                            "kernel": w.kernel, "algorithmic_flops": alg, "peak_source": pk["source"]}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = w.cpu_sample(int(os.environ.get("EVIE_CPU_THREADS", os.cpu_count() or 1)))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--batch", type=int, default=0, help="override the batch size (small profiling cases)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

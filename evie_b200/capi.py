@@ -1,0 +1,62 @@
+"""ctypes declarations of every entry point in include/evie_cuda.h."""
+from __future__ import annotations
+
+import ctypes as C
+
+
+class Seq(C.Structure):
+    """evie_seq"""
+    _fields_ = [("slot", C.c_int32), ("pos0", C.c_int32), ("tokens", C.c_void_p), ("n_tokens", C.c_int32)]
+
+
+class Op(C.Structure):
+    """evie_op"""
+    _fields_ = [("layer", C.c_int32), ("neuron", C.c_int32), ("mode", C.c_int32), ("value", C.c_float)]
+
+
+class ModelInfo(C.Structure):
+    """evie_model_info"""
+    _fields_ = [
+        ("hidden", C.c_int32), ("intermediate", C.c_int32), ("n_layers", C.c_int32), ("vocab", C.c_int32),
+        ("n_linear_layers", C.c_int32), ("n_full_layers", C.c_int32), ("slots", C.c_int32), ("max_ctx", C.c_int32),
+        ("max_rows", C.c_int32), ("max_ops", C.c_int32), ("weight_bytes", C.c_int64), ("cache_bytes", C.c_int64),
+    ]
+
+
+P, I, F, SZ = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+
+SIGNATURES = {
+    "evie_create": (I, [C.c_char_p, I, I, I, I, C.POINTER(P)]),
+    "evie_destroy": (None, [P]),
+    "evie_last_error": (C.c_char_p, [P]),
+    "evie_last_global_error": (C.c_char_p, []),
+    "evie_info": (I, [P, C.POINTER(ModelInfo)]),
+    "evie_forward": (I, [P, P, I, I, I, P, P, P, P]),
+    "evie_set_ops": (I, [P, I, P, I]),
+    "evie_reset_slot": (I, [P, I]),
+    "evie_set_scale": (I, [P, P, SZ]),
+    "evie_track_max": (I, [P, I]),
+    "evie_read_max": (I, [P, P, SZ]),
+    "evie_gdn_decode_step": (I, [P, P, P, P, P, P, P, I, I, I, I, P]),
+    "evie_gdn_chunk_prefill": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, P]),
+    "evie_gqa_decode_paged": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, F, P]),
+}
+
+
+def declare(L) -> None:
+    """Sets restype/argtypes for every exported function that the library has."""
+    for name, (res, args) in SIGNATURES.items():
+        f = getattr(L, name, None)
+        if f is None:
+            continue
+        f.restype = res
+        f.argtypes = args
+
+
+def header_functions(header_path: str) -> list:
+    """Names of every function the C header declares (used to check that the library exports all of them)."""
+    import re
+
+    with open(header_path) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"EVIE_API\s+[\w\s\*]+?\b(evie_\w+)\s*\(", text)))

@@ -1,0 +1,371 @@
+// Gated GQA softmax attention, decode (one query row per sequence), over a paged bf16 KV cache, for sm_100a.
+//
+// Semantics follow the attention core of evie-core's Model::attention (crates/evie-core/src/model.rs:445-464):
+//   scores_j = scale * q . k_j (j < ctx);  p = softmax(scores);  o = sum_j p_j v_j;  o *= sigmoid(gate)
+// for every query head h, with KV head h / (Hq / Hkv) (model.rs:447).
+//
+// Design (HBM-bound: every K/V byte is read exactly once; ~4 flop per byte at GQA group 4):
+//   * one CTA per (sequence b, KV head, split of kSplit tokens) serves all GROUP query heads of that KV head, so
+//     K/V are streamed once, not GROUP times;
+//   * a warp reads a token's 512-byte K (or V) row with one 16-byte load per lane (8 head dims per lane) —
+//     fully coalesced, and kTokIter rows are in flight per lane before any use;
+//   * q.k partial dots for kTokIter tokens x GROUP heads (= 32 values) are finished with one 31-shuffle
+//     reduce-scatter, leaving one score per lane;
+//   * the softmax of the split is exact (two passes over the scores held in shared memory); P.V accumulates
+//     GROUP x 8 values per lane and is reduced across warps in shared memory;
+//   * splits are merged in-kernel: every CTA publishes (m, l, O) for its split, takes a ticket with atomicAdd,
+//     and the CTA that takes the last ticket combines them (no spin-wait, no second launch). A sequence that fits
+//     one split writes its output directly.
+#include <map>
+#include <mutex>
+
+#include "common.h"
+#include "gqa_decode.h"
+
+namespace evie {
+
+namespace {
+
+constexpr int kHD = 256;
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kSplit = 512;                   // tokens per CTA
+constexpr int kTokPerWarp = kSplit / kWarps;  // 64
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Scratch {
+  float* o;        // [B][Hkv][max_splits][GROUP][HD] unnormalised split outputs
+  float* ml;       // [B][Hkv][max_splits][GROUP][2]  split max (log2 domain) and sum
+  int* tickets;    // [B][Hkv]
+  int max_splits;
+};
+
+template <int GROUP>
+__global__ void __launch_bounds__(kThreads, 2)
+    gqa_decode_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ gate,
+                      const __nv_bfloat16* __restrict__ kp, const __nv_bfloat16* __restrict__ vp,
+                      const int32_t* __restrict__ page_table, const int32_t* __restrict__ ctx_lens,
+                      float* __restrict__ out, int Hkv, int page_size, int max_pages, float scale, Scratch scr) {
+  constexpr int kTokIter = 32 / GROUP;  // tokens per reduce-scatter round
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int Hq = Hkv * GROUP;
+  const int ctx = min(ctx_lens[b], max_pages * page_size);
+  const int n_splits = (ctx + kSplit - 1) / kSplit;
+  const int t0 = split * kSplit;
+
+  float* outb = out + ((size_t)b * Hq + (size_t)kvh * GROUP) * kHD;
+  const __nv_bfloat16* gateb = gate + ((size_t)b * Hq + (size_t)kvh * GROUP) * kHD;
+  if (ctx <= 0) {
+    if (split == 0)
+      for (int i = tid; i < GROUP * kHD; i += kThreads) outb[i] = 0.0f * sigmoidf_(__bfloat162float(gateb[i]));
+    return;
+  }
+  if (split >= n_splits) return;
+
+  __shared__ float s_p[kSplit][GROUP];       // scores, then probabilities (token-major for broadcast reads)
+  __shared__ float s_red[kWarps][GROUP][kHD];
+  __shared__ float s_stat[kWarps][GROUP];
+  __shared__ float s_m[GROUP], s_l[GROUP];
+  __shared__ int s_last;
+
+  // q for this KV head's query heads, 8 dims per lane, pre-scaled into the log2 domain.
+  float qr[GROUP][8];
+  {
+    const float f = scale * kLog2e;
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) {
+      const uint4 u = *reinterpret_cast<const uint4*>(q + ((size_t)b * Hq + kvh * GROUP + h) * kHD + lane * 8);
+      bf16x8_to_f32(u, qr[h]);
+#pragma unroll
+      for (int d = 0; d < 8; d++) qr[h][d] *= f;
+    }
+  }
+  const int32_t* pt = page_table + (size_t)b * max_pages;
+  auto row_ptr = [&](const __nv_bfloat16* pages, int j) {
+    const int page = pt[j / page_size];
+    return pages + (((size_t)page * Hkv + kvh) * page_size + (j % page_size)) * kHD + lane * 8;
+  };
+
+  // ---- scores
+  const int wt0 = t0 + warp * kTokPerWarp;
+  for (int it = 0; it < kTokPerWarp; it += kTokIter) {
+    uint4 kr[kTokIter];
+#pragma unroll
+    for (int t = 0; t < kTokIter; t++) {
+      const int j = wt0 + it + t;
+      kr[t] = j < ctx ? *reinterpret_cast<const uint4*>(row_ptr(kp, j)) : make_uint4(0, 0, 0, 0);
+    }
+    float vals[32];
+#pragma unroll
+    for (int t = 0; t < kTokIter; t++) {
+      float kf[8];
+      bf16x8_to_f32(kr[t], kf);
+#pragma unroll
+      for (int h = 0; h < GROUP; h++) {
+        float a = 0.f;
+#pragma unroll
+        for (int d = 0; d < 8; d++) a = fmaf(qr[h][d], kf[d], a);
+        vals[t * GROUP + h] = a;
+      }
+    }
+    // reduce-scatter: afterwards lane l holds the full sum of value index l
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < off; i++) {
+        const float send = upper ? vals[i] : vals[i + off];
+        const float keep = upper ? vals[i + off] : vals[i];
+        vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+    const int tl = it + lane / GROUP;  // token within the warp's range
+    const int j = wt0 + tl;
+    s_p[warp * kTokPerWarp + tl][lane % GROUP] = j < ctx ? vals[0] : -INFINITY;
+  }
+  __syncthreads();
+
+  // ---- softmax over the split (max, exp2, sum), per query head
+  {
+    float mx[GROUP];
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) mx[h] = -INFINITY;
+    for (int t = tid; t < kSplit; t += kThreads)
+#pragma unroll
+      for (int h = 0; h < GROUP; h++) mx[h] = fmaxf(mx[h], s_p[t][h]);
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) {
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
+      if (lane == 0) s_stat[warp][h] = mx[h];
+    }
+    __syncthreads();
+    if (tid < GROUP) {
+      float m = s_stat[0][tid];
+      for (int w = 1; w < kWarps; w++) m = fmaxf(m, s_stat[w][tid]);
+      s_m[tid] = m;
+    }
+    __syncthreads();
+    float sm[GROUP];
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) sm[h] = 0.f;
+    for (int t = tid; t < kSplit; t += kThreads)
+#pragma unroll
+      for (int h = 0; h < GROUP; h++) {
+        const float p = exp2f(s_p[t][h] - s_m[h]);
+        s_p[t][h] = p;
+        sm[h] += p;
+      }
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) {
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) sm[h] += __shfl_xor_sync(0xffffffffu, sm[h], off);
+    }
+    __syncthreads();  // everyone has read s_stat (max) before it is reused for sums
+    if (lane == 0)
+#pragma unroll
+      for (int h = 0; h < GROUP; h++) s_stat[warp][h] = sm[h];
+    __syncthreads();
+    if (tid < GROUP) {
+      float l = 0.f;
+      for (int w = 0; w < kWarps; w++) l += s_stat[w][tid];
+      s_l[tid] = l;
+    }
+  }
+
+  // ---- P.V
+  float acc[GROUP][8];
+#pragma unroll
+  for (int h = 0; h < GROUP; h++)
+#pragma unroll
+    for (int d = 0; d < 8; d++) acc[h][d] = 0.f;
+  constexpr int kVIter = 8;
+  for (int it = 0; it < kTokPerWarp; it += kVIter) {
+    uint4 vr[kVIter];
+#pragma unroll
+    for (int t = 0; t < kVIter; t++) {
+      const int j = wt0 + it + t;
+      vr[t] = j < ctx ? *reinterpret_cast<const uint4*>(row_ptr(vp, j)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int t = 0; t < kVIter; t++) {
+      float vf[8];
+      bf16x8_to_f32(vr[t], vf);
+      const int tl = warp * kTokPerWarp + it + t;
+#pragma unroll
+      for (int h = 0; h < GROUP; h++) {
+        const float p = s_p[tl][h];
+#pragma unroll
+        for (int d = 0; d < 8; d++) acc[h][d] = fmaf(p, vf[d], acc[h][d]);
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < GROUP; h++) {
+    float4* dst = reinterpret_cast<float4*>(&s_red[warp][h][lane * 8]);
+    dst[0] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    dst[1] = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+  }
+  __syncthreads();
+
+  // ---- publish or finish
+  constexpr int kOutPerThread = GROUP * kHD / kThreads;
+  float osum[kOutPerThread];
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) {
+    const int e = tid + i * kThreads;
+    const int h = e / kHD, d = e % kHD;
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) a += s_red[w][h][d];
+    osum[i] = a;
+  }
+  if (n_splits == 1) {
+#pragma unroll
+    for (int i = 0; i < kOutPerThread; i++) {
+      const int e = tid + i * kThreads;
+      const int h = e / kHD;
+      outb[e] = osum[i] / s_l[h] * sigmoidf_(__bfloat162float(gateb[e]));
+    }
+    return;
+  }
+  const size_t bh = (size_t)b * Hkv + kvh;
+  float* po = scr.o + (bh * scr.max_splits + split) * GROUP * kHD;
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) __stcg(po + tid + i * kThreads, osum[i]);
+  if (tid < GROUP) {
+    float* pml = scr.ml + ((bh * scr.max_splits + split) * GROUP + tid) * 2;
+    __stcg(pml, s_m[tid]);
+    __stcg(pml + 1, s_l[tid]);
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(scr.tickets + bh, 1) == n_splits - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  // Last CTA of this (b, KV head): merge the splits. Per-split weights first (reuse s_p as scratch).
+  float* s_w = &s_p[0][0];  // [GROUP][n_splits]  (n_splits <= kSplit)
+  if (tid < GROUP) {
+    const float* ml = scr.ml + (bh * scr.max_splits) * GROUP * 2;
+    float M = -INFINITY;
+    for (int s = 0; s < n_splits; s++) M = fmaxf(M, __ldcg(ml + ((size_t)s * GROUP + tid) * 2));
+    float L = 0.f;
+    for (int s = 0; s < n_splits; s++) {
+      const float w = exp2f(__ldcg(ml + ((size_t)s * GROUP + tid) * 2) - M);
+      s_w[tid * n_splits + s] = w;
+      L += w * __ldcg(ml + ((size_t)s * GROUP + tid) * 2 + 1);
+    }
+    for (int s = 0; s < n_splits; s++) s_w[tid * n_splits + s] /= L;
+  }
+  __syncthreads();
+  const float* pob = scr.o + bh * scr.max_splits * GROUP * kHD;
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) {
+    const int e = tid + i * kThreads;
+    const int h = e / kHD;
+    float a = 0.f;
+    for (int s = 0; s < n_splits; s++) a += s_w[h * n_splits + s] * __ldcg(pob + (size_t)s * GROUP * kHD + e);
+    outb[e] = a * sigmoidf_(__bfloat162float(gateb[e]));
+  }
+  if (tid == 0) scr.tickets[bh] = 0;  // ready for the next call
+}
+
+// Split scratch per (device, stream), grown on demand and kept for the process lifetime, so that calls on
+// different streams never share tickets or partials.
+struct DeviceScratch {
+  void* base = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_scratch_mu;
+std::map<std::pair<int, cudaStream_t>, DeviceScratch> g_scratch;
+
+evie_status get_scratch(int B, int Hkv, int group, int max_splits, Scratch* s, cudaStream_t st) {
+  int dev = 0;
+  EVIE_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  const size_t n_o = (size_t)B * Hkv * max_splits * group * kHD;
+  const size_t n_ml = (size_t)B * Hkv * max_splits * group * 2;
+  const size_t n_t = (size_t)B * Hkv;
+  const size_t need = (n_o + n_ml) * sizeof(float) + n_t * sizeof(int) + 256;
+  DeviceScratch& d = g_scratch[{dev, st}];
+  if (d.bytes < need) {
+    if (d.base) {
+      EVIE_CUDA_TRY(cudaStreamSynchronize(st));
+      EVIE_CUDA_TRY(cudaFree(d.base));
+      d.base = nullptr;
+      d.bytes = 0;
+    }
+    if (cudaMalloc(&d.base, need) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(EVIE_ERR_OOM, "evie_gqa_decode_paged: cannot allocate %zu bytes of split scratch", need);
+    }
+    EVIE_CUDA_TRY(cudaMemsetAsync(d.base, 0, need, st));  // tickets start at zero; each merge resets its own
+    d.bytes = need;
+  }
+  char* p = (char*)d.base;
+  s->tickets = (int*)p;
+  p += (n_t * sizeof(int) + 255) / 256 * 256;
+  s->ml = (float*)p;
+  p += n_ml * sizeof(float);
+  s->o = (float*)p;
+  s->max_splits = max_splits;
+  return EVIE_OK;
+}
+
+}  // namespace
+
+evie_status launch_gqa_decode_bf16(const void* q, const void* gate, const void* kp, const void* vp,
+                                   const int32_t* page_table, const int32_t* ctx_lens, float* out, int B, int Hq,
+                                   int Hkv, int page_size, int max_pages, float scale, cudaStream_t st) {
+  const int group = Hq / Hkv;
+  const long max_tokens = (long)max_pages * page_size;
+  const int max_splits = (int)((max_tokens + kSplit - 1) / kSplit);
+  if (B == 0 || max_splits == 0) {
+    if (B > 0) {  // no context at all: outputs are zero
+      EVIE_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(float) * (size_t)B * Hq * kHD, st));
+    }
+    return EVIE_OK;
+  }
+  Scratch scr;
+  evie_status rc = get_scratch(B, Hkv, group, max_splits, &scr, st);
+  if (rc != EVIE_OK) return rc;
+  dim3 grid(max_splits, Hkv, B);
+  auto* qq = (const __nv_bfloat16*)q;
+  auto* gg = (const __nv_bfloat16*)gate;
+  auto* kk = (const __nv_bfloat16*)kp;
+  auto* vv = (const __nv_bfloat16*)vp;
+  switch (group) {
+    case 2: gqa_decode_kernel<2><<<grid, kThreads, 0, st>>>(qq, gg, kk, vv, page_table, ctx_lens, out, Hkv, page_size, max_pages, scale, scr); break;
+    case 4: gqa_decode_kernel<4><<<grid, kThreads, 0, st>>>(qq, gg, kk, vv, page_table, ctx_lens, out, Hkv, page_size, max_pages, scale, scr); break;
+    default: return fail(EVIE_ERR_ARG, "GQA group %d not supported (2, 4)", group);
+  }
+  EVIE_CHECK_LAUNCH("gqa_decode_kernel");
+  return EVIE_OK;
+}
+
+}  // namespace evie
+
+extern "C" evie_status evie_gqa_decode_paged(const void* q, const void* gate, const void* k_pages, const void* v_pages,
+                                             const int32_t* page_table, const int32_t* ctx_lens, float* out, int B,
+                                             int Hq, int Hkv, int hd, int page_size, int max_pages, float scale,
+                                             void* stream) {
+  EVIE_ARG(hd == 256, "evie_gqa_decode_paged: head_dim 256 required (got %d)", hd);
+  EVIE_ARG(B >= 0 && Hkv > 0 && Hq > 0 && Hq % Hkv == 0, "evie_gqa_decode_paged: bad head counts %d/%d", Hq, Hkv);
+  const int group = Hq / Hkv;
+  EVIE_ARG(group == 2 || group == 4, "evie_gqa_decode_paged: GQA group %d unsupported (2 or 4)", group);
+  EVIE_ARG(page_size > 0 && page_size % 64 == 0, "evie_gqa_decode_paged: page_size must be a multiple of 64");
+  EVIE_ARG(max_pages >= 0 && (long)max_pages * page_size <= evie::kGqaMaxContext,
+           "evie_gqa_decode_paged: max_pages * page_size exceeds %ld tokens", (long)evie::kGqaMaxContext);
+  EVIE_ARG(B <= 65535 && Hkv <= 65535, "evie_gqa_decode_paged: grid too large");
+  EVIE_ARG(B == 0 || (q && gate && k_pages && v_pages && page_table && ctx_lens && out),
+           "evie_gqa_decode_paged: null pointer");
+  EVIE_ARG((((uintptr_t)q | (uintptr_t)k_pages | (uintptr_t)v_pages) & 15) == 0,
+           "evie_gqa_decode_paged: q and the KV pages must be 16-byte aligned");
+  return evie::launch_gqa_decode_bf16(q, gate, k_pages, v_pages, page_table, ctx_lens, out, B, Hq, Hkv, page_size,
+                                      max_pages, scale, (cudaStream_t)stream);
+}

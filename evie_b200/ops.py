@@ -1,0 +1,58 @@
+"""Isolated hot-path ops on torch CUDA tensors, through the C ABI of libevie_cuda.so.
+
+torch provides device memory and the stream; the computation is the library's sm_100a kernels.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import check, lib
+
+
+def _ptr(t: torch.Tensor) -> int:
+    assert t.is_cuda and t.is_contiguous(), "expected a contiguous CUDA tensor"
+    return t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def gdn_decode_step(q, k, v, g, beta, state, o=None):
+    """One Gated DeltaNet recurrent step (evie_gdn_decode_step). state [B,H,128,128] f32 is updated in place.
+
+    q, k: [B,H,128] bf16; v: [B,H,128] bf16; g (log decay), beta: [B,H] f32. Returns o [B,H,128] f32."""
+    B, H, dk, dv = state.shape
+    assert q.dtype == k.dtype == v.dtype == torch.bfloat16 and state.dtype == torch.float32
+    if o is None:
+        o = torch.empty(B, H, dv, device=state.device, dtype=torch.float32)
+    check(lib().evie_gdn_decode_step(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state), _ptr(o), B, H,
+                                     dk, dv, _stream()))
+    return o
+
+
+def gdn_chunk_prefill(q, k, v, g, beta, state, o=None, chunk: int = 64):
+    """Chunked Gated DeltaNet prefill (evie_gdn_chunk_prefill). q,k,v: [B,T,H,128] bf16; g,beta: [B,T,H] f32;
+    state [B,H,128,128] f32: initial in, final out. Returns o [B,T,H,128] bf16."""
+    B, T, H, dk = q.shape
+    dv = v.shape[-1]
+    if o is None:
+        o = torch.empty(B, T, H, dv, device=q.device, dtype=torch.bfloat16)
+    check(lib().evie_gdn_chunk_prefill(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state), _ptr(o), B, T,
+                                       H, dk, dv, chunk, _stream()))
+    return o
+
+
+def gqa_decode_paged(q, gate, k_pages, v_pages, page_table, ctx_lens, scale, out=None):
+    """Gated GQA decode attention over a paged bf16 KV cache (evie_gqa_decode_paged).
+
+    q, gate: [B,Hq,256] bf16; k_pages, v_pages: [P,Hkv,page,256] bf16; page_table [B,max_pages] int32;
+    ctx_lens [B] int32. Returns out [B,Hq,256] f32."""
+    B, Hq, hd = q.shape
+    _, Hkv, page, _ = k_pages.shape
+    if out is None:
+        out = torch.empty(B, Hq, hd, device=q.device, dtype=torch.float32)
+    check(lib().evie_gqa_decode_paged(_ptr(q), _ptr(gate), _ptr(k_pages), _ptr(v_pages), _ptr(page_table),
+                                      _ptr(ctx_lens), _ptr(out), B, Hq, Hkv, hd, page, page_table.shape[1],
+                                      float(scale), _stream()))
+    return out

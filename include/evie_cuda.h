@@ -1,0 +1,126 @@
+/* evie_cuda.h — C ABI of libevie_cuda.so, a B200 (sm_100a) implementation of the Qwen3.5 token-mixing hot path
+ * of the evie neuron-steering engine.
+ *
+ * The ABI mirrors evie-core's GPU backend (`GpuModel`, crates/evie-core/src/gpu/mod.rs) so that evie-core's
+ * forward loop, caches and per-neuron hooks can call it through a Rust `extern "C"` block: plain pointers,
+ * sizes and status codes; no C++ or CUDA types cross the boundary. Every function returns a status and never
+ * aborts the process; the message for the last failure is available from `evie_last_error` (per context) or
+ * `evie_last_global_error` (calls without a context, and context creation).
+ *
+ * Threading: one context per GPU; a context is not re-entrant (drive it from one host thread, as evie's
+ * inference thread drives `GpuModel`, crates/evie/src/worker.rs:209-237). Isolated-op entry points may be
+ * called from any thread; they enqueue work on the stream they are given.
+ */
+#ifndef EVIE_CUDA_H
+#define EVIE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define EVIE_API __attribute__((visibility("default")))
+#else
+#define EVIE_API
+#endif
+
+typedef int evie_status;
+#define EVIE_OK 0
+#define EVIE_ERR_ARG 1     /* invalid argument or size limit (the reference's `ensure!` limits) */
+#define EVIE_ERR_CUDA 2    /* CUDA / cuBLAS runtime error */
+#define EVIE_ERR_IO 3      /* checkpoint could not be read or parsed */
+#define EVIE_ERR_OOM 4     /* device allocation failed */
+#define EVIE_ERR_TIMEOUT 5 /* a bounded device-side wait gave up */
+
+typedef struct evie_ctx evie_ctx;
+
+/* One sequence in a forward call (GpuSeq, gpu/mod.rs:147-154). `tokens` is a host pointer. */
+typedef struct {
+  int32_t slot;            /* cache slot, 0..slots-1 */
+  int32_t pos0;            /* absolute position of the first new token */
+  const uint32_t* tokens;  /* n_tokens token ids */
+  int32_t n_tokens;
+} evie_seq;
+
+/* One steering op for a slot (the tuple of GpuModel::set_ops, gpu/mod.rs:555-565).
+ * mode 1 = add `value` (already dose x unit, engine.rs:102-108), 2 = multiply by `value`, 3 = set to `value`. */
+typedef struct {
+  int32_t layer;
+  int32_t neuron;
+  int32_t mode;
+  float value;
+} evie_op;
+
+/* Model dimensions, for sizing host buffers. */
+typedef struct {
+  int32_t hidden, intermediate, n_layers, vocab;
+  int32_t n_linear_layers, n_full_layers;
+  int32_t slots, max_ctx, max_rows, max_ops;
+  int64_t weight_bytes, cache_bytes;
+} evie_model_info;
+
+/* Creates a context on `device` and uploads the checkpoint in `ckpt_dir` (config.json + *.safetensors, bf16).
+ * Replaces GpuModel::new(model, max_ctx) (gpu/mod.rs:226). `slots` sequences can be cached at once, each up
+ * to `max_ctx` positions; one forward call carries at most `max_rows` new tokens in total. */
+EVIE_API evie_status evie_create(const char* ckpt_dir, int device, int slots, int max_ctx, int max_rows, evie_ctx** out);
+EVIE_API void evie_destroy(evie_ctx* ctx);
+EVIE_API const char* evie_last_error(const evie_ctx* ctx);
+EVIE_API const char* evie_last_global_error(void);
+EVIE_API evie_status evie_info(const evie_ctx* ctx, evie_model_info* out);
+
+/* Runs the new tokens of `n_seqs` sequences (GpuModel::forward, gpu/mod.rs:615). All output pointers are host
+ * buffers and may be NULL when not wanted:
+ *   logits       [n_seqs][vocab] f32, next-token logits of each sequence's last new token (if want_logits);
+ *   frames       [rows][layers*intermediate] i8 sqrt-companded activations after steering (if capture);
+ *   resid        [rows][layers*hidden] f16 bits, residual stream leaving each layer (if capture);
+ *   next_tokens  [n_seqs] greedy token id = first index of the maximum logit (topk(logits, 1), sampling.rs:60).
+ * rows are the concatenation of every sequence's new tokens, in call order. */
+EVIE_API evie_status evie_forward(evie_ctx* ctx, const evie_seq* seqs, int n_seqs, int want_logits, int capture, float* logits,
+                         int8_t* frames, uint16_t* resid, uint32_t* next_tokens);
+
+/* Replaces a slot's steering ops (GpuModel::set_ops, gpu/mod.rs:556). Ops apply in the given order. */
+EVIE_API evie_status evie_set_ops(evie_ctx* ctx, int slot, const evie_op* ops, int n_ops);
+/* Zeroes a slot's recurrent and conv state (GpuModel::reset_slot, gpu/mod.rs:568). */
+EVIE_API evie_status evie_reset_slot(evie_ctx* ctx, int slot);
+/* Per-neuron activation scales used to normalise captured frames, layer-major (gpu/mod.rs:549). */
+EVIE_API evie_status evie_set_scale(evie_ctx* ctx, const float* scale, size_t n);
+/* Track the max |activation| of every neuron over positions > 0 across later calls (gpu/mod.rs:578). */
+EVIE_API evie_status evie_track_max(evie_ctx* ctx, int on);
+/* Reads the tracked maxima, layer-major (gpu/mod.rs:590). */
+EVIE_API evie_status evie_read_max(evie_ctx* ctx, float* out, size_t n);
+
+/* ---- isolated ops: device pointers, enqueued on `stream` (a cudaStream_t, NULL = legacy default) ---- */
+
+/* One Gated DeltaNet recurrent decode step over B*H heads (recur_step, crates/evie-core/src/model.rs:501-541;
+ * the `deltanet` WGSL kernel, gpu/kernels.wgsl:379-442):
+ *   kv = S^T k; delta = (v - exp(g) kv) beta; S <- exp(g) S + k delta^T; o = S^T q (updated S).
+ * q,k: [B][H][dk] bf16; v: [B][H][dv] bf16; g (log decay), beta: [B][H] f32; state: [B][H][dk][dv] f32 updated
+ * in place; o: [B][H][dv] f32. dk = dv = 128. */
+EVIE_API evie_status evie_gdn_decode_step(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                                 float* state, float* o, int B, int H, int dk, int dv, void* stream);
+
+/* Gated DeltaNet prefill over T tokens, chunked (chunk = 64) on tcgen05 tensor cores. Same recurrence as
+ * evie-core's token-sequential loop (model.rs:362-387). q,k: [B][T][H][dk] bf16; v: [B][T][H][dv] bf16;
+ * g, beta: [B][T][H] f32; state: [B][H][dk][dv] f32, initial state in, final state out; o: [B][T][H][dv] bf16. */
+EVIE_API evie_status evie_gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                                   float* state, void* o, int B, int T, int H, int dk, int dv, int chunk,
+                                   void* stream);
+
+/* Gated GQA softmax attention decode over a paged bf16 KV cache (the attention core of Model::attention,
+ * model.rs:445-464; WGSL attn_scores/attn_out, gpu/kernels.wgsl:508-589), split-KV with an in-kernel combine:
+ *   out[b,h] = softmax(scale * q[b,h] . K[b, 0..ctx_b)) V[b, 0..ctx_b) * sigmoid(gate[b,h]).
+ * q, gate (logits): [B][Hq][hd] bf16; k_pages, v_pages: [num_pages][Hkv][page_size][hd] bf16;
+ * page_table: [B][max_pages] int32; ctx_lens: [B] int32 (0 <= ctx_b <= max_pages*page_size);
+ * out: [B][Hq][hd] f32. hd = 256, Hq/Hkv in {2,4}, page_size a multiple of 64, max_pages*page_size <= 262144.
+ * Scratch for the split partials is allocated by the library on first use, per (device, stream), and kept. */
+EVIE_API evie_status evie_gqa_decode_paged(const void* q, const void* gate, const void* k_pages, const void* v_pages,
+                                  const int32_t* page_table, const int32_t* ctx_lens, float* out, int B, int Hq,
+                                  int Hkv, int hd, int page_size, int max_pages, float scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EVIE_CUDA_H */
