@@ -21,6 +21,7 @@
 
 #include "common.h"
 #include "gqa_decode.h"
+#include "model_kernels.h"
 
 namespace evie {
 
@@ -33,6 +34,83 @@ constexpr int kSplit = 512;                   // tokens per CTA
 constexpr int kTokPerWarp = kSplit / kWarps;  // 64
 constexpr float kLog2e = 1.4426950408889634f;
 
+// One lane's 8 consecutive head dims of a K or V row.
+template <typename KV>
+struct KVRow;
+template <>
+struct KVRow<__nv_bfloat16> {
+  using Raw = uint4;
+  __device__ __forceinline__ static void load(Raw& r, const __nv_bfloat16* p) {
+    r = p ? *reinterpret_cast<const uint4*>(p) : make_uint4(0, 0, 0, 0);
+  }
+  __device__ __forceinline__ static void widen(const Raw& r, float* f) { bf16x8_to_f32(r, f); }
+};
+template <>
+struct KVRow<float> {
+  struct Raw {
+    float4 a, b;
+  };
+  __device__ __forceinline__ static void load(Raw& r, const float* p) {
+    if (p) {
+      r.a = *reinterpret_cast<const float4*>(p);
+      r.b = *reinterpret_cast<const float4*>(p + 4);
+    } else {
+      r.a = r.b = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  __device__ __forceinline__ static void widen(const Raw& r, float* f) {
+    f[0] = r.a.x; f[1] = r.a.y; f[2] = r.a.z; f[3] = r.a.w; f[4] = r.b.x; f[5] = r.b.y; f[6] = r.b.z; f[7] = r.b.w;
+  }
+};
+
+// Inputs/outputs of the isolated op: bf16 q and gate logits [B][Hq][hd], f32 out, caller's page table.
+struct IsoIO {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* gate_logits;
+  float* out;
+  const int32_t* page_table;
+  const int32_t* ctx_lens;
+  int Hq, max_pages;
+  __device__ __forceinline__ int ctx_of(int b) const { return ctx_lens[b]; }
+  __device__ __forceinline__ const int32_t* page_row(int b) const { return page_table + (size_t)b * max_pages; }
+  __device__ __forceinline__ void load_q(int b, int h, int lane, float* f) const {
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(q + ((size_t)b * Hq + h) * kHD + lane * 8), f);
+  }
+  __device__ __forceinline__ float gate(int b, int h, int d) const {
+    return __bfloat162float(gate_logits[((size_t)b * Hq + h) * kHD + d]);
+  }
+  __device__ __forceinline__ void store(int b, int h, int d, float v) const { out[((size_t)b * Hq + h) * kHD + d] = v; }
+};
+
+// Inputs/outputs inside the model: one query per row (ctx = pos + 1), f32 rotated q [R][nh][hd], gate logits
+// from the q projection planes (per head [q | gate]), output written as the split operand of o_proj.
+struct ModelIO {
+  const float* q_rot;
+  const float* Y2;
+  size_t yplane;
+  int ldy;
+  __nv_bfloat16* X2;
+  size_t xplane;
+  const RowInfo* rows;
+  const int* page_table;
+  int pages_per_slot, Hq;
+  __device__ __forceinline__ int ctx_of(int b) const { return rows[b].pos + 1; }
+  __device__ __forceinline__ const int32_t* page_row(int b) const {
+    return page_table + (size_t)rows[b].slot * pages_per_slot;
+  }
+  __device__ __forceinline__ void load_q(int b, int h, int lane, float* f) const {
+    const float4* p = reinterpret_cast<const float4*>(q_rot + ((size_t)b * Hq + h) * kHD + lane * 8);
+    const float4 a = p[0], c = p[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = c.x; f[5] = c.y; f[6] = c.z; f[7] = c.w;
+  }
+  __device__ __forceinline__ float gate(int b, int h, int d) const {
+    return load_y(Y2, yplane, (size_t)b * ldy + (size_t)h * 2 * kHD + kHD + d);
+  }
+  __device__ __forceinline__ void store(int b, int h, int d, float v) const {
+    store_split(X2, xplane, (size_t)b * Hq * kHD + (size_t)h * kHD + d, v);
+  }
+};
+
 struct Scratch {
   float* o;        // [B][Hkv][max_splits][GROUP][HD] unnormalised split outputs
   float* ml;       // [B][Hkv][max_splits][GROUP][2]  split max (log2 domain) and sum
@@ -40,27 +118,23 @@ struct Scratch {
   int max_splits;
 };
 
-template <int GROUP>
+template <int GROUP, typename KV, class IO>
 __global__ void __launch_bounds__(kThreads, 2)
-    gqa_decode_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ gate,
-                      const __nv_bfloat16* __restrict__ kp, const __nv_bfloat16* __restrict__ vp,
-                      const int32_t* __restrict__ page_table, const int32_t* __restrict__ ctx_lens,
-                      float* __restrict__ out, int Hkv, int page_size, int max_pages, float scale, Scratch scr) {
+    gqa_decode_kernel(IO io, const KV* __restrict__ kp, const KV* __restrict__ vp, int Hkv, int page_size,
+                      int max_pages, float scale, Scratch scr) {
   constexpr int kTokIter = 32 / GROUP;  // tokens per reduce-scatter round
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
   const int b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int Hq = Hkv * GROUP;
-  const int ctx = min(ctx_lens[b], max_pages * page_size);
+  const int ctx = min(io.ctx_of(b), max_pages * page_size);
   const int n_splits = (ctx + kSplit - 1) / kSplit;
   const int t0 = split * kSplit;
 
-  float* outb = out + ((size_t)b * Hq + (size_t)kvh * GROUP) * kHD;
-  const __nv_bfloat16* gateb = gate + ((size_t)b * Hq + (size_t)kvh * GROUP) * kHD;
+  const int h0 = kvh * GROUP;  // first query head of this KV head
   if (ctx <= 0) {
     if (split == 0)
-      for (int i = tid; i < GROUP * kHD; i += kThreads) outb[i] = 0.0f * sigmoidf_(__bfloat162float(gateb[i]));
+      for (int i = tid; i < GROUP * kHD; i += kThreads) io.store(b, h0 + i / kHD, i % kHD, 0.0f);
     return;
   }
   if (split >= n_splits) return;
@@ -77,14 +151,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     const float f = scale * kLog2e;
 #pragma unroll
     for (int h = 0; h < GROUP; h++) {
-      const uint4 u = *reinterpret_cast<const uint4*>(q + ((size_t)b * Hq + kvh * GROUP + h) * kHD + lane * 8);
-      bf16x8_to_f32(u, qr[h]);
+      io.load_q(b, h0 + h, lane, qr[h]);
 #pragma unroll
       for (int d = 0; d < 8; d++) qr[h][d] *= f;
     }
   }
-  const int32_t* pt = page_table + (size_t)b * max_pages;
-  auto row_ptr = [&](const __nv_bfloat16* pages, int j) {
+  const int32_t* pt = io.page_row(b);
+  auto row_ptr = [&](const KV* pages, int j) {
     const int page = pt[j / page_size];
     return pages + (((size_t)page * Hkv + kvh) * page_size + (j % page_size)) * kHD + lane * 8;
   };
@@ -92,17 +165,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---- scores
   const int wt0 = t0 + warp * kTokPerWarp;
   for (int it = 0; it < kTokPerWarp; it += kTokIter) {
-    uint4 kr[kTokIter];
+    typename KVRow<KV>::Raw kr[kTokIter];
 #pragma unroll
     for (int t = 0; t < kTokIter; t++) {
       const int j = wt0 + it + t;
-      kr[t] = j < ctx ? *reinterpret_cast<const uint4*>(row_ptr(kp, j)) : make_uint4(0, 0, 0, 0);
+      KVRow<KV>::load(kr[t], j < ctx ? row_ptr(kp, j) : nullptr);
     }
     float vals[32];
 #pragma unroll
     for (int t = 0; t < kTokIter; t++) {
       float kf[8];
-      bf16x8_to_f32(kr[t], kf);
+      KVRow<KV>::widen(kr[t], kf);
 #pragma unroll
       for (int h = 0; h < GROUP; h++) {
         float a = 0.f;
@@ -184,16 +257,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int d = 0; d < 8; d++) acc[h][d] = 0.f;
   constexpr int kVIter = 8;
   for (int it = 0; it < kTokPerWarp; it += kVIter) {
-    uint4 vr[kVIter];
+    typename KVRow<KV>::Raw vr[kVIter];
 #pragma unroll
     for (int t = 0; t < kVIter; t++) {
       const int j = wt0 + it + t;
-      vr[t] = j < ctx ? *reinterpret_cast<const uint4*>(row_ptr(vp, j)) : make_uint4(0, 0, 0, 0);
+      KVRow<KV>::load(vr[t], j < ctx ? row_ptr(vp, j) : nullptr);
     }
 #pragma unroll
     for (int t = 0; t < kVIter; t++) {
       float vf[8];
-      bf16x8_to_f32(vr[t], vf);
+      KVRow<KV>::widen(vr[t], vf);
       const int tl = warp * kTokPerWarp + it + t;
 #pragma unroll
       for (int h = 0; h < GROUP; h++) {
@@ -227,8 +300,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int i = 0; i < kOutPerThread; i++) {
       const int e = tid + i * kThreads;
-      const int h = e / kHD;
-      outb[e] = osum[i] / s_l[h] * sigmoidf_(__bfloat162float(gateb[e]));
+      const int h = e / kHD, d = e % kHD;
+      io.store(b, h0 + h, d, osum[i] / s_l[h] * sigmoidf_(io.gate(b, h0 + h, d)));
     }
     return;
   }
@@ -267,10 +340,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
   for (int i = 0; i < kOutPerThread; i++) {
     const int e = tid + i * kThreads;
-    const int h = e / kHD;
+    const int h = e / kHD, d = e % kHD;
     float a = 0.f;
     for (int s = 0; s < n_splits; s++) a += s_w[h * n_splits + s] * __ldcg(pob + (size_t)s * GROUP * kHD + e);
-    outb[e] = a * sigmoidf_(__bfloat162float(gateb[e]));
+    io.store(b, h0 + h, d, a * sigmoidf_(io.gate(b, h0 + h, d)));
   }
   if (tid == 0) scr.tickets[bh] = 0;  // ready for the next call
 }
@@ -317,7 +390,31 @@ evie_status get_scratch(int B, int Hkv, int group, int max_splits, Scratch* s, c
   return EVIE_OK;
 }
 
+
+template <typename KV, class IO>
+evie_status launch_gqa(const IO& io, const KV* kp, const KV* vp, int B, int Hq, int Hkv, int page_size, int max_pages,
+                       int max_ctx, float scale, const Scratch& scr, cudaStream_t st) {
+  const int group = Hq / Hkv;
+  const int max_splits = (max_ctx + kSplit - 1) / kSplit;
+  dim3 grid(max_splits > 0 ? max_splits : 1, Hkv, B);
+  switch (group) {
+    case 2: gqa_decode_kernel<2, KV, IO><<<grid, kThreads, 0, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale, scr); break;
+    case 4: gqa_decode_kernel<4, KV, IO><<<grid, kThreads, 0, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale, scr); break;
+    default: return fail(EVIE_ERR_ARG, "GQA group %d not supported (2, 4)", group);
+  }
+  EVIE_CHECK_LAUNCH("gqa_decode_kernel");
+  return EVIE_OK;
+}
+
 }  // namespace
+
+size_t gqa_scratch_bytes(int rows, int Hkv, int group, int max_ctx) {
+  const size_t max_splits = (size_t)(max_ctx + kSplit - 1) / kSplit;
+  const size_t n_o = (size_t)rows * Hkv * max_splits * group * kHD;
+  const size_t n_ml = (size_t)rows * Hkv * max_splits * group * 2;
+  const size_t n_t = (size_t)rows * Hkv;
+  return (n_t * sizeof(int) + 255) / 256 * 256 + (n_ml + n_o) * sizeof(float) + 256;
+}
 
 evie_status launch_gqa_decode_bf16(const void* q, const void* gate, const void* kp, const void* vp,
                                    const int32_t* page_table, const int32_t* ctx_lens, float* out, int B, int Hq,
@@ -334,19 +431,37 @@ evie_status launch_gqa_decode_bf16(const void* q, const void* gate, const void* 
   Scratch scr;
   evie_status rc = get_scratch(B, Hkv, group, max_splits, &scr, st);
   if (rc != EVIE_OK) return rc;
-  dim3 grid(max_splits, Hkv, B);
-  auto* qq = (const __nv_bfloat16*)q;
-  auto* gg = (const __nv_bfloat16*)gate;
-  auto* kk = (const __nv_bfloat16*)kp;
-  auto* vv = (const __nv_bfloat16*)vp;
-  switch (group) {
-    case 2: gqa_decode_kernel<2><<<grid, kThreads, 0, st>>>(qq, gg, kk, vv, page_table, ctx_lens, out, Hkv, page_size, max_pages, scale, scr); break;
-    case 4: gqa_decode_kernel<4><<<grid, kThreads, 0, st>>>(qq, gg, kk, vv, page_table, ctx_lens, out, Hkv, page_size, max_pages, scale, scr); break;
-    default: return fail(EVIE_ERR_ARG, "GQA group %d not supported (2, 4)", group);
-  }
-  EVIE_CHECK_LAUNCH("gqa_decode_kernel");
-  return EVIE_OK;
+  IsoIO io{(const __nv_bfloat16*)q, (const __nv_bfloat16*)gate, out, page_table, ctx_lens, Hq, max_pages};
+  return launch_gqa<__nv_bfloat16>(io, (const __nv_bfloat16*)kp, (const __nv_bfloat16*)vp, B, Hq, Hkv, page_size,
+                                   max_pages, (int)max_tokens, scale, scr, st);
 }
+
+template <typename KV>
+evie_status launch_gqa_model(const float* q_rot, const float* Y2, size_t yplane, int ldy, __nv_bfloat16* X2,
+                             size_t xplane, const RowInfo* rows, int R, const int* page_table, int pages_per_slot,
+                             const KV* kc, const KV* vc, int Hq, int Hkv, int page_size, int max_ctx, float scale,
+                             void* scratch, int ticket_rows, cudaStream_t st) {
+  if (R == 0) return EVIE_OK;
+  const int group = Hq / Hkv;
+  const int max_splits = (max_ctx + kSplit - 1) / kSplit;
+  Scratch scr;
+  char* p = (char*)scratch;
+  scr.tickets = (int*)p;  // fixed-size region: tickets of unused rows stay zero across calls
+  p += ((size_t)ticket_rows * Hkv * sizeof(int) + 255) / 256 * 256;
+  scr.ml = (float*)p;
+  p += (size_t)R * Hkv * max_splits * group * 2 * sizeof(float);
+  scr.o = (float*)p;
+  scr.max_splits = max_splits;
+  ModelIO io{q_rot, Y2, yplane, ldy, X2, xplane, rows, page_table, pages_per_slot, Hq};
+  return launch_gqa<KV>(io, kc, vc, R, Hq, Hkv, page_size, pages_per_slot, max_ctx, scale, scr, st);
+}
+template evie_status launch_gqa_model<__nv_bfloat16>(const float*, const float*, size_t, int, __nv_bfloat16*, size_t,
+                                                     const RowInfo*, int, const int*, int, const __nv_bfloat16*,
+                                                     const __nv_bfloat16*, int, int, int, int, float, void*, int,
+                                                     cudaStream_t);
+template evie_status launch_gqa_model<float>(const float*, const float*, size_t, int, __nv_bfloat16*, size_t,
+                                             const RowInfo*, int, const int*, int, const float*, const float*, int, int,
+                                             int, int, float, void*, int, cudaStream_t);
 
 }  // namespace evie
 

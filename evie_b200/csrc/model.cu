@@ -1,0 +1,730 @@
+// Host runtime of the full-model path: the C ABI that mirrors evie-core's GpuModel (crates/evie-core/src/gpu/mod.rs).
+//
+//   evie_create   GpuModel::new (gpu/mod.rs:226-262): config.json + safetensors -> device weights, slot caches
+//   evie_forward  GpuModel::forward (gpu/mod.rs:615-706) = Model::forward (model.rs:217-284) on device
+//   evie_set_ops / evie_reset_slot / evie_set_scale / evie_track_max / evie_read_max  (gpu/mod.rs:549-593)
+//
+// Device memory (all owned by the context):
+//   weights   bf16; per layer the projections that read the same input are fused row-wise into one matrix:
+//             DeltaNet [qkv; z; b; a] x d, attention [q(+gate); k; v] x d, MLP [gate; up] x d
+//   caches    conv window [slot][lin layer][K-1][conv_dim] f32, recurrent state [slot][lin layer][hv][dk][dv] f32,
+//             KV pages [full layer][slot * pages_per_slot][nkv][256][hd] (bf16, or f32 with EVIE_KV_F32=1),
+//             a fixed page table per slot (slot s owns pages s*pps .. s*pps+pps-1)
+//   activations sized for max_rows: residual x f32, split operand planes X2 bf16, projection outputs Y2 f32
+#include <cublas_v2.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <dirent.h>
+#include <fstream>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "gqa_decode.h"
+#include "json.h"
+#include "model_kernels.h"
+
+using evie::RowInfo;
+using evie::SegInfo;
+
+namespace {
+
+constexpr int kPage = 256;
+constexpr int kMaxOps = 64;
+
+struct Tensor {
+  std::string dtype;
+  std::vector<int64_t> shape;
+  const char* data = nullptr;
+  size_t bytes = 0;
+};
+
+// weights.rs:33-123: every *.safetensors in the directory, memory-mapped.
+struct SafeTensors {
+  struct Map {
+    void* p = MAP_FAILED;
+    size_t n = 0;
+  };
+  std::vector<Map> maps;
+  std::map<std::string, Tensor> t;
+  ~SafeTensors() {
+    for (auto& m : maps)
+      if (m.p != MAP_FAILED) munmap(m.p, m.n);
+  }
+  std::string open_dir(const std::string& dir) {
+    DIR* d = opendir(dir.c_str());
+    if (!d) return "cannot open " + dir;
+    std::vector<std::string> files;
+    while (dirent* e = readdir(d)) {
+      std::string n = e->d_name;
+      if (n.size() > 12 && n.substr(n.size() - 12) == ".safetensors") files.push_back(dir + "/" + n);
+    }
+    closedir(d);
+    std::sort(files.begin(), files.end());
+    if (files.empty()) return "no .safetensors files in " + dir;
+    for (auto& f : files) {
+      int fd = open(f.c_str(), O_RDONLY);
+      if (fd < 0) return "cannot open " + f;
+      struct stat st;
+      fstat(fd, &st);
+      Map m;
+      m.n = (size_t)st.st_size;
+      m.p = mmap(nullptr, m.n, PROT_READ, MAP_PRIVATE, fd, 0);
+      close(fd);
+      if (m.p == MAP_FAILED || m.n < 8) return f + " is too small or unmappable";
+      maps.push_back(m);
+      const char* base = (const char*)m.p;
+      uint64_t hn;
+      memcpy(&hn, base, 8);
+      if (8 + hn > m.n) return f + ": bad header length";
+      evie::json::Value h;
+      try {
+        h = evie::json::parse(base + 8, hn);
+      } catch (std::exception& e) {
+        return f + ": " + e.what();
+      }
+      const char* data = base + 8 + hn;
+      for (auto& kv : h.obj) {
+        if (kv.first == "__metadata__") continue;
+        Tensor x;
+        x.dtype = kv.second["dtype"].string();
+        for (auto& s : kv.second["shape"].arr) x.shape.push_back(s.integer());
+        const auto& off = kv.second["data_offsets"].arr;
+        size_t a = (size_t)off[0].integer(), b = (size_t)off[1].integer();
+        if (8 + hn + b > m.n) return f + ": tensor " + kv.first + " out of range";
+        x.data = data + a;
+        x.bytes = b - a;
+        t[kv.first] = x;
+      }
+    }
+    return "";
+  }
+  const Tensor* get(const std::string& n) const {
+    auto it = t.find(n);
+    return it == t.end() ? nullptr : &it->second;
+  }
+};
+
+float bf16_bits_to_f32(uint16_t b) {
+  uint32_t u = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+float half_bits_to_f32(uint16_t h) {
+  const uint32_t s = (h >> 15) & 1, e = (h >> 10) & 31, m = h & 1023;
+  float v;
+  if (e == 0) v = std::ldexp((float)m, -24);
+  else if (e == 31) v = m ? NAN : INFINITY;
+  else v = std::ldexp((float)(m | 1024), (int)e - 25);
+  return s ? -v : v;
+}
+
+struct Layer {
+  int kind = 0;  // 0 DeltaNet, 1 full attention
+  int idx = 0;   // index among layers of the same kind
+  float* ln1 = nullptr;
+  float* ln2 = nullptr;
+  __nv_bfloat16* w_in = nullptr;   // fused input projection
+  __nv_bfloat16* w_out = nullptr;  // out_proj / o_proj [d][vd or nh*hd]
+  __nv_bfloat16* w_gu = nullptr;   // [2n][d]
+  __nv_bfloat16* w_down = nullptr; // [d][n]
+  float *conv = nullptr, *neg_a = nullptr, *dt_bias = nullptr, *norm = nullptr;  // DeltaNet
+  float *q_norm = nullptr, *k_norm = nullptr;                                    // attention
+};
+
+}  // namespace
+
+struct evie_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  cublasHandle_t blas = nullptr;
+  void* blas_ws = nullptr;
+  evie::ModelShape s{};
+  std::vector<int> kinds;
+  int n_lin = 0, n_full = 0;
+  int slots = 0, max_ctx = 0, max_rows = 0, pages_per_slot = 0;
+  bool kv_f32 = false;
+  std::vector<void*> allocs;
+  size_t weight_bytes = 0, cache_bytes = 0;
+  // weights
+  __nv_bfloat16* embed = nullptr;  // [V][d] (also the LM head when tied)
+  __nv_bfloat16* lm_head = nullptr;
+  float* final_norm = nullptr;
+  float* inv_freq = nullptr;
+  std::vector<Layer> layers;
+  // caches
+  float* conv_state = nullptr;
+  float* rec_state = nullptr;
+  void* k_cache = nullptr;
+  void* v_cache = nullptr;
+  int* page_table = nullptr;
+  // steering / capture
+  evie_op* ops = nullptr;      // [slots][kMaxOps]
+  int* op_range = nullptr;     // [slots][L][2]
+  float* scale = nullptr;      // [L][n]
+  uint32_t* maxbuf = nullptr;  // [L][n]
+  bool track = false;
+  // activations
+  float* x = nullptr;
+  __nv_bfloat16* X2 = nullptr;
+  float* Y2 = nullptr;
+  float* act = nullptr;
+  float* q_rot = nullptr;
+  int8_t* frames = nullptr;
+  uint16_t* resid = nullptr;
+  float* L2 = nullptr;
+  float* logits = nullptr;
+  unsigned long long* best = nullptr;
+  uint32_t* next = nullptr;
+  void* attn_scratch = nullptr;
+  RowInfo* d_rows = nullptr;
+  SegInfo* d_segs = nullptr;
+  RowInfo* h_rows = nullptr;  // pinned
+  SegInfo* h_segs = nullptr;  // pinned
+  std::string err;
+
+  template <typename T>
+  evie_status alloc(T** p, size_t count, bool zero = true) {
+    void* q = nullptr;
+    if (cudaMalloc(&q, std::max<size_t>(count * sizeof(T), 16)) != cudaSuccess) {
+      cudaGetLastError();
+      return evie::fail(EVIE_ERR_OOM, "cannot allocate %zu bytes on device %d", count * sizeof(T), device);
+    }
+    allocs.push_back(q);
+    if (zero) EVIE_CUDA_TRY(cudaMemset(q, 0, std::max<size_t>(count * sizeof(T), 16)));
+    *p = (T*)q;
+    return EVIE_OK;
+  }
+};
+
+namespace {
+
+#define TRY(expr)                        \
+  do {                                   \
+    evie_status rc_ = (expr);            \
+    if (rc_ != EVIE_OK) return rc_;      \
+  } while (0)
+
+evie_status upload_f32(evie_ctx* c, const SafeTensors& st, const std::string& name, size_t expect, float** out,
+                       float add = 0.0f, bool neg_exp = false) {
+  const Tensor* t = st.get(name);
+  if (!t) return evie::fail(EVIE_ERR_IO, "missing tensor %s", name.c_str());
+  std::vector<float> v;
+  if (t->dtype == "F32") {
+    v.resize(t->bytes / 4);
+    memcpy(v.data(), t->data, t->bytes);
+  } else if (t->dtype == "BF16" || t->dtype == "F16") {
+    v.resize(t->bytes / 2);
+    for (size_t i = 0; i < v.size(); i++) {
+      uint16_t b;
+      memcpy(&b, t->data + 2 * i, 2);
+      v[i] = t->dtype == "BF16" ? bf16_bits_to_f32(b) : half_bits_to_f32(b);
+    }
+  } else {
+    return evie::fail(EVIE_ERR_IO, "%s: unsupported dtype %s", name.c_str(), t->dtype.c_str());
+  }
+  if (v.size() != expect) return evie::fail(EVIE_ERR_IO, "%s: %zu values, expected %zu", name.c_str(), v.size(), expect);
+  for (auto& x : v) {
+    x = x + add;
+    if (neg_exp) x = -expf(x);  // model.rs:171: A_log -> -exp(A_log)
+  }
+  TRY(c->alloc(out, v.size(), false));
+  EVIE_CUDA_TRY(cudaMemcpy(*out, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+  c->weight_bytes += v.size() * 4;
+  return EVIE_OK;
+}
+
+// Concatenates bf16 matrices row-wise into one device matrix of `cols` columns.
+evie_status upload_rows(evie_ctx* c, const SafeTensors& st, const std::vector<std::pair<std::string, int64_t>>& parts,
+                        int64_t cols, __nv_bfloat16** out) {
+  int64_t rows = 0;
+  for (auto& p : parts) rows += p.second;
+  TRY(c->alloc(out, (size_t)rows * cols, false));
+  int64_t r0 = 0;
+  for (auto& p : parts) {
+    const Tensor* t = st.get(p.first);
+    if (!t) return evie::fail(EVIE_ERR_IO, "missing tensor %s", p.first.c_str());
+    if (t->dtype != "BF16") return evie::fail(EVIE_ERR_IO, "%s: expected BF16, got %s", p.first.c_str(), t->dtype.c_str());
+    if ((int64_t)t->bytes != p.second * cols * 2)
+      return evie::fail(EVIE_ERR_IO, "%s: size %zu does not match %lld x %lld", p.first.c_str(), t->bytes,
+                        (long long)p.second, (long long)cols);
+    EVIE_CUDA_TRY(cudaMemcpy(*out + r0 * cols, t->data, t->bytes, cudaMemcpyHostToDevice));
+    r0 += p.second;
+  }
+  c->weight_bytes += (size_t)rows * cols * 2;
+  return EVIE_OK;
+}
+
+evie_status read_config(evie_ctx* c, const std::string& dir) {
+  std::ifstream f(dir + "/config.json");
+  if (!f) return evie::fail(EVIE_ERR_IO, "cannot read %s/config.json", dir.c_str());
+  std::stringstream ss;
+  ss << f.rdbuf();
+  try {
+    evie::json::Value root = evie::json::parse(ss.str());
+    const evie::json::Value& t = root.has("text_config") ? root["text_config"] : root;  // config.rs:82
+    auto I = [&](const char* k) {
+      if (!t.has(k)) throw std::runtime_error(std::string("missing ") + k);
+      return (int)t[k].integer();
+    };
+    auto& s = c->s;
+    s.d = I("hidden_size");
+    s.n = I("intermediate_size");
+    s.L = I("num_hidden_layers");
+    s.V = I("vocab_size");
+    s.eps = (float)t["rms_norm_eps"].number();
+    s.nh = I("num_attention_heads");
+    s.nkv = I("num_key_value_heads");
+    s.hd = I("head_dim");
+    s.K = I("linear_conv_kernel_dim");
+    s.dk = I("linear_key_head_dim");
+    s.hk = I("linear_num_key_heads");
+    s.hv = I("linear_num_value_heads");
+    s.dv = I("linear_value_head_dim");
+    double theta = 10000000.0, partial = 1.0;  // config.rs:85-88
+    if (t.has("rope_parameters")) {
+      theta = t["rope_parameters"]["rope_theta"].number();
+      if (t["rope_parameters"].has("partial_rotary_factor")) partial = t["rope_parameters"]["partial_rotary_factor"].number();
+    } else {
+      if (t.has("rope_theta")) theta = t["rope_theta"].number();
+      if (t.has("partial_rotary_factor")) partial = t["partial_rotary_factor"].number();
+    }
+    s.rot = (int)std::round(s.hd * partial);  // config.rs:116
+    for (auto& lt : t["layer_types"].arr) {
+      if (lt.string() == "linear_attention") c->kinds.push_back(0);
+      else if (lt.string() == "full_attention") c->kinds.push_back(1);
+      else throw std::runtime_error("unsupported layer type " + lt.string());
+    }
+    if ((int)c->kinds.size() != s.L) throw std::runtime_error("layer_types does not match num_hidden_layers");
+    s.conv_dim = 2 * s.hk * s.dk + s.hv * s.dv;  // config.rs:144-146
+    s.vd = s.hv * s.dv;
+    s.key_dim = s.hk * s.dk;
+    s.in_dn = s.conv_dim + s.vd + 2 * s.hv;
+    s.in_at = (2 * s.nh + 2 * s.nkv) * s.hd;
+    std::vector<float> inv(s.rot / 2);
+    for (int i = 0; i < s.rot / 2; i++) inv[i] = 1.0f / powf((float)theta, (float)(2 * i) / (float)s.rot);  // model.rs:198-201
+    TRY(c->alloc(&c->inv_freq, inv.size() + 1, false));
+    EVIE_CUDA_TRY(cudaMemcpy(c->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice));
+  } catch (std::exception& e) {
+    return evie::fail(EVIE_ERR_IO, "config.json: %s", e.what());
+  }
+  // Limits of these kernels (gpu/mod.rs:267-269 states the same shape limits for the wgpu backend).
+  auto& s = c->s;
+  if (s.dk != 128 || s.dv != 128) return evie::fail(EVIE_ERR_ARG, "DeltaNet heads must be 128 wide");
+  if (s.hd != 256) return evie::fail(EVIE_ERR_ARG, "attention head_dim must be 256");
+  if (s.rot > s.hd || s.rot % 2) return evie::fail(EVIE_ERR_ARG, "bad rotary dim %d", s.rot);
+  if (s.nh % s.nkv || (s.nh / s.nkv != 2 && s.nh / s.nkv != 4)) return evie::fail(EVIE_ERR_ARG, "GQA group must be 2 or 4");
+  if (s.hv % s.hk) return evie::fail(EVIE_ERR_ARG, "value heads must be a multiple of key heads");
+  if (s.K < 1 || s.K > 16) return evie::fail(EVIE_ERR_ARG, "conv kernel %d out of range", s.K);
+  return EVIE_OK;
+}
+
+evie_status load_weights(evie_ctx* c, const std::string& dir) {
+  SafeTensors st;
+  std::string e = st.open_dir(dir);
+  if (!e.empty()) return evie::fail(EVIE_ERR_IO, "%s", e.c_str());
+  std::string p;  // model.rs:140-146
+  if (st.get("model.language_model.embed_tokens.weight")) p = "model.language_model.";
+  else if (st.get("model.embed_tokens.weight")) p = "model.";
+  else return evie::fail(EVIE_ERR_IO, "unrecognised checkpoint layout in %s", dir.c_str());
+  auto& s = c->s;
+  const Tensor* emb = st.get(p + "embed_tokens.weight");
+  if (emb->shape.size() != 2 || emb->shape[0] < s.V || emb->shape[1] != s.d)
+    return evie::fail(EVIE_ERR_IO, "embedding shape does not match config");
+  s.V = (int)emb->shape[0];  // the LM head has as many rows as the embedding (model.rs:279)
+  TRY(upload_rows(c, st, {{p + "embed_tokens.weight", s.V}}, s.d, &c->embed));
+  c->lm_head = c->embed;
+  {
+    // config.rs:101-104 + model.rs:151: a separate lm_head only when present and embeddings are not tied
+    std::ifstream f(dir + "/config.json");
+    std::stringstream ss;
+    ss << f.rdbuf();
+    evie::json::Value root = evie::json::parse(ss.str());
+    const evie::json::Value& t = root.has("text_config") ? root["text_config"] : root;
+    bool tie = false;
+    if (t["tie_word_embeddings"].kind == evie::json::Value::Bool) tie = t["tie_word_embeddings"].b;
+    else if (root["tie_word_embeddings"].kind == evie::json::Value::Bool) tie = root["tie_word_embeddings"].b;
+    if (st.get("lm_head.weight") && !tie) TRY(upload_rows(c, st, {{"lm_head.weight", s.V}}, s.d, &c->lm_head));
+  }
+  c->layers.resize(s.L);
+  for (int i = 0; i < s.L; i++) {
+    Layer& L = c->layers[i];
+    const std::string l = p + "layers." + std::to_string(i) + ".";
+    L.kind = c->kinds[i];
+    L.idx = L.kind == 0 ? c->n_lin++ : c->n_full++;
+    TRY(upload_f32(c, st, l + "input_layernorm.weight", s.d, &L.ln1, 1.0f));
+    TRY(upload_f32(c, st, l + "post_attention_layernorm.weight", s.d, &L.ln2, 1.0f));
+    if (L.kind == 0) {
+      const std::string a = l + "linear_attn.";
+      TRY(upload_rows(c, st,
+                      {{a + "in_proj_qkv.weight", s.conv_dim}, {a + "in_proj_z.weight", s.vd},
+                       {a + "in_proj_b.weight", s.hv}, {a + "in_proj_a.weight", s.hv}},
+                      s.d, &L.w_in));
+      TRY(upload_rows(c, st, {{a + "out_proj.weight", s.d}}, s.vd, &L.w_out));
+      TRY(upload_f32(c, st, a + "conv1d.weight", (size_t)s.conv_dim * s.K, &L.conv));
+      TRY(upload_f32(c, st, a + "A_log", s.hv, &L.neg_a, 0.0f, true));
+      TRY(upload_f32(c, st, a + "dt_bias", s.hv, &L.dt_bias));
+      TRY(upload_f32(c, st, a + "norm.weight", s.dv, &L.norm));  // gated norm gain used as is (model.rs:173)
+    } else {
+      const std::string a = l + "self_attn.";
+      TRY(upload_rows(c, st,
+                      {{a + "q_proj.weight", 2 * s.nh * s.hd}, {a + "k_proj.weight", s.nkv * s.hd},
+                       {a + "v_proj.weight", s.nkv * s.hd}},
+                      s.d, &L.w_in));
+      TRY(upload_rows(c, st, {{a + "o_proj.weight", s.d}}, s.nh * s.hd, &L.w_out));
+      TRY(upload_f32(c, st, a + "q_norm.weight", s.hd, &L.q_norm, 1.0f));
+      TRY(upload_f32(c, st, a + "k_norm.weight", s.hd, &L.k_norm, 1.0f));
+    }
+    TRY(upload_rows(c, st, {{l + "mlp.gate_proj.weight", s.n}, {l + "mlp.up_proj.weight", s.n}}, s.d, &L.w_gu));
+    TRY(upload_rows(c, st, {{l + "mlp.down_proj.weight", s.d}}, s.n, &L.w_down));
+  }
+  TRY(upload_f32(c, st, p + "norm.weight", s.d, &c->final_norm, 1.0f));
+  return EVIE_OK;
+}
+
+evie_status allocate_state(evie_ctx* c) {
+  auto& s = c->s;
+  const size_t S = c->slots, R = c->max_rows;
+  c->pages_per_slot = (c->max_ctx + kPage - 1) / kPage;
+  const size_t kv_elems = (size_t)std::max(c->n_full, 1) * S * c->pages_per_slot * s.nkv * kPage * s.hd;
+  TRY(c->alloc(&c->conv_state, S * std::max(c->n_lin, 1) * (s.K - 1) * s.conv_dim + 1));
+  TRY(c->alloc(&c->rec_state, S * std::max(c->n_lin, 1) * (size_t)s.hv * s.dk * s.dv));
+  if (c->kv_f32) {
+    float *k, *v;
+    TRY(c->alloc(&k, kv_elems, false));
+    TRY(c->alloc(&v, kv_elems, false));
+    c->k_cache = k;
+    c->v_cache = v;
+  } else {
+    __nv_bfloat16 *k, *v;
+    TRY(c->alloc(&k, kv_elems, false));
+    TRY(c->alloc(&v, kv_elems, false));
+    c->k_cache = k;
+    c->v_cache = v;
+  }
+  c->cache_bytes = (S * std::max(c->n_lin, 1) * ((s.K - 1) * (size_t)s.conv_dim + (size_t)s.hv * s.dk * s.dv)) * 4 +
+                   2 * kv_elems * (c->kv_f32 ? 4 : 2);
+  std::vector<int> pt(S * c->pages_per_slot);
+  for (size_t i = 0; i < pt.size(); i++) pt[i] = (int)i;
+  TRY(c->alloc(&c->page_table, pt.size()));
+  EVIE_CUDA_TRY(cudaMemcpy(c->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
+  TRY(c->alloc(&c->ops, S * kMaxOps));
+  TRY(c->alloc(&c->op_range, S * s.L * 2));
+  TRY(c->alloc(&c->scale, (size_t)s.L * s.n, false));
+  {
+    std::vector<float> one((size_t)s.L * s.n, 1.0f);  // gpu/mod.rs:367: scales start at 1
+    EVIE_CUDA_TRY(cudaMemcpy(c->scale, one.data(), one.size() * 4, cudaMemcpyHostToDevice));
+  }
+  TRY(c->alloc(&c->maxbuf, (size_t)s.L * s.n));
+  const size_t kmax = std::max({(size_t)s.d, (size_t)s.vd, (size_t)s.nh * s.hd, (size_t)s.n});
+  const size_t mmax = std::max({(size_t)s.in_dn, (size_t)s.in_at, (size_t)2 * s.n, (size_t)s.d});
+  TRY(c->alloc(&c->x, R * s.d));
+  TRY(c->alloc(&c->X2, 2 * R * kmax));
+  TRY(c->alloc(&c->Y2, 2 * R * mmax));
+  TRY(c->alloc(&c->act, R * s.conv_dim));
+  TRY(c->alloc(&c->q_rot, R * s.nh * s.hd));
+  TRY(c->alloc(&c->frames, R * s.L * (size_t)s.n, false));
+  TRY(c->alloc(&c->resid, R * s.L * (size_t)s.d, false));
+  TRY(c->alloc(&c->L2, 2 * S * (size_t)s.V, false));
+  TRY(c->alloc(&c->logits, S * (size_t)s.V, false));
+  TRY(c->alloc(&c->best, S));
+  TRY(c->alloc(&c->next, S));
+  {
+    char* p = nullptr;
+    TRY(c->alloc(&p, evie::gqa_scratch_bytes((int)R, s.nkv, s.nh / s.nkv, c->pages_per_slot * kPage)));
+    c->attn_scratch = p;
+  }
+  TRY(c->alloc(&c->d_rows, R));
+  TRY(c->alloc(&c->d_segs, S));
+  EVIE_CUDA_TRY(cudaMallocHost(&c->h_rows, R * sizeof(RowInfo)));
+  EVIE_CUDA_TRY(cudaMallocHost(&c->h_segs, S * sizeof(SegInfo)));
+  return EVIE_OK;
+}
+
+// Y2 [2R][M] f32 = X2 [2R][K] bf16 . W[M][K]^T (one GEMM over both operand planes; fp32 accumulation).
+evie_status gemm(evie_ctx* c, const __nv_bfloat16* W, int M, int K, const __nv_bfloat16* X2, int R, float* Y2) {
+  const float one = 1.0f, zero = 0.0f;
+  cublasStatus_t st = cublasGemmEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, M, 2 * R, K, &one, W, CUDA_R_16BF, K, X2,
+                                   CUDA_R_16BF, K, &zero, Y2, CUDA_R_32F, M, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  if (st != CUBLAS_STATUS_SUCCESS) return evie::fail(EVIE_ERR_CUDA, "cublasGemmEx (%d x %d x %d): status %d", M, 2 * R, K, (int)st);
+  return EVIE_OK;
+}
+
+evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_logits, int capture, float* logits,
+                         int8_t* frames, uint16_t* resid, uint32_t* next_tokens) {
+  auto& s = c->s;
+  // gpu/mod.rs:616-630: limits and row/segment tables
+  EVIE_ARG(nseq >= 1 && nseq <= c->slots, "forward: 1..=%d sequences per call, got %d", c->slots, nseq);
+  int R = 0, max_ctx_rows = 0;
+  std::vector<char> used(c->slots, 0);
+  for (int i = 0; i < nseq; i++) {
+    const evie_seq& q = seqs[i];
+    EVIE_ARG(q.slot >= 0 && q.slot < c->slots, "forward: bad slot %d", q.slot);
+    EVIE_ARG(!used[q.slot], "forward: slot %d appears twice", q.slot);
+    used[q.slot] = 1;
+    EVIE_ARG(q.n_tokens >= 1 && q.tokens, "forward: sequence %d has no tokens", i);
+    EVIE_ARG(q.pos0 >= 0 && (long)q.pos0 + q.n_tokens <= c->max_ctx, "forward: context longer than %d tokens", c->max_ctx);
+    R += q.n_tokens;
+    EVIE_ARG(R <= c->max_rows, "forward: needs 1..=%d rows, got more", c->max_rows);
+    max_ctx_rows = std::max(max_ctx_rows, q.pos0 + q.n_tokens);
+  }
+  int r = 0;
+  for (int i = 0; i < nseq; i++) {
+    const evie_seq& q = seqs[i];
+    c->h_segs[i] = SegInfo{q.slot, r, q.n_tokens, q.pos0};
+    for (int t = 0; t < q.n_tokens; t++) {
+      EVIE_ARG(q.tokens[t] < (uint32_t)s.V, "forward: token id %u out of range", q.tokens[t]);
+      c->h_rows[r++] = RowInfo{q.slot, q.pos0 + t, (int)q.tokens[t], i};
+    }
+  }
+  cudaStream_t st = c->stream;
+  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_rows, c->h_rows, R * sizeof(RowInfo), cudaMemcpyHostToDevice, st));
+  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_segs, c->h_segs, nseq * sizeof(SegInfo), cudaMemcpyHostToDevice, st));
+
+  int8_t* fr = capture ? c->frames : nullptr;
+  uint16_t* rs = capture ? c->resid : nullptr;
+  const size_t cs_slot = (size_t)std::max(c->n_lin, 1) * (s.K - 1) * s.conv_dim;
+  const size_t rs_slot = (size_t)std::max(c->n_lin, 1) * s.hv * s.dk * s.dv;
+  const size_t kv_layer = (size_t)c->slots * c->pages_per_slot * s.nkv * kPage * s.hd;
+  evie::SteerTables steer{c->ops, c->op_range, kMaxOps};
+
+  TRY(evie::k_embed_norm(c->d_rows, R, c->embed, c->x, c->layers[0].ln1, s.eps, s.d, c->X2, st));
+  for (int li = 0; li < s.L; li++) {
+    Layer& L = c->layers[li];
+    if (L.kind == 0) {
+      TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2));
+      float* cs = c->conv_state + (size_t)L.idx * (s.K - 1) * s.conv_dim;
+      TRY(evie::k_conv_silu_norm(c->Y2, s.in_dn, R, c->d_rows, c->d_segs, cs, cs_slot, L.conv, s, c->act, st));
+      TRY(evie::k_conv_state_update(c->Y2, s.in_dn, R, c->d_segs, nseq, cs, cs_slot, s, st));
+      float* rsb = c->rec_state + (size_t)L.idx * s.hv * s.dk * s.dv;
+      TRY(evie::k_gdn_mixer(c->act, c->Y2, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm, s,
+                            c->X2, st));
+      TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2));
+    } else {
+      TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2));
+      const float scale = 1.0f / sqrtf((float)s.hd);
+      if (c->kv_f32) {
+        float* kc = (float*)c->k_cache + (size_t)L.idx * kv_layer;
+        float* vc = (float*)c->v_cache + (size_t)L.idx * kv_layer;
+        TRY(evie::k_attn_prep<float>(c->Y2, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s, c->q_rot, kc,
+                                     vc, c->page_table, c->pages_per_slot, kPage, st));
+        TRY(evie::launch_gqa_model<float>(c->q_rot, c->Y2, (size_t)R * s.in_at, s.in_at, c->X2,
+                                          (size_t)R * s.nh * s.hd, c->d_rows, R, c->page_table, c->pages_per_slot,
+                                          kc, vc, s.nh, s.nkv, kPage, max_ctx_rows, scale, c->attn_scratch, c->max_rows,
+                                          st));
+      } else {
+        auto* kc = (__nv_bfloat16*)c->k_cache + (size_t)L.idx * kv_layer;
+        auto* vc = (__nv_bfloat16*)c->v_cache + (size_t)L.idx * kv_layer;
+        TRY(evie::k_attn_prep<__nv_bfloat16>(c->Y2, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s,
+                                             c->q_rot, kc, vc, c->page_table, c->pages_per_slot, kPage, st));
+        TRY(evie::launch_gqa_model<__nv_bfloat16>(c->q_rot, c->Y2, (size_t)R * s.in_at, s.in_at, c->X2,
+                                                  (size_t)R * s.nh * s.hd, c->d_rows, R, c->page_table,
+                                                  c->pages_per_slot, kc, vc, s.nh, s.nkv, kPage, max_ctx_rows, scale,
+                                                  c->attn_scratch, c->max_rows, st));
+      }
+      TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2));
+    }
+    // model.rs:246-248: residual add after the mixer, then the pre-MLP norm
+    TRY(evie::k_add_norm(c->x, c->Y2, s.d, R, L.ln2, s.eps, s.d, c->X2, nullptr, 0, s.L, st));
+    TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2));
+    TRY(evie::k_swiglu(c->Y2, 2 * s.n, R, c->d_rows, li, s, steer, c->scale, fr, c->track ? c->maxbuf : nullptr,
+                       c->X2, st));
+    TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2));
+    if (li + 1 < s.L) {
+      TRY(evie::k_add_norm(c->x, c->Y2, s.d, R, c->layers[li + 1].ln1, s.eps, s.d, c->X2, rs, li, s.L, st));
+    } else {
+      TRY(evie::k_add_final(c->x, c->Y2, s.d, R, c->d_rows, c->d_segs, nseq, c->final_norm, s.eps, s.d, c->X2, rs,
+                            li, s.L, st));
+    }
+  }
+  // model.rs:271-283: LM head on the last row of every sequence, greedy id on device
+  TRY(gemm(c, c->lm_head, s.V, s.d, c->X2, nseq, c->L2));
+  TRY(evie::k_logits_argmax(c->L2, nseq, s.V, want_logits ? c->logits : nullptr, c->best, c->next, st));
+  if (want_logits && logits)
+    EVIE_CUDA_TRY(cudaMemcpyAsync(logits, c->logits, (size_t)nseq * s.V * 4, cudaMemcpyDeviceToHost, st));
+  if (next_tokens) EVIE_CUDA_TRY(cudaMemcpyAsync(next_tokens, c->next, nseq * 4, cudaMemcpyDeviceToHost, st));
+  if (capture && frames)
+    EVIE_CUDA_TRY(cudaMemcpyAsync(frames, c->frames, (size_t)R * s.L * s.n, cudaMemcpyDeviceToHost, st));
+  if (capture && resid)
+    EVIE_CUDA_TRY(cudaMemcpyAsync(resid, c->resid, (size_t)R * s.L * s.d * 2, cudaMemcpyDeviceToHost, st));
+  EVIE_CUDA_TRY(cudaStreamSynchronize(st));
+  return EVIE_OK;
+}
+
+void destroy(evie_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  for (void* p : c->allocs) cudaFree(p);
+  if (c->h_rows) cudaFreeHost(c->h_rows);
+  if (c->h_segs) cudaFreeHost(c->h_segs);
+  if (c->blas) cublasDestroy(c->blas);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+// Records the thread-local message of a failed call into the context.
+evie_status remember(evie_ctx* c, evie_status rc) {
+  if (rc != EVIE_OK && c) c->err = evie::thread_error();
+  return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+evie_status evie_create(const char* ckpt_dir, int device, int slots, int max_ctx, int max_rows, evie_ctx** out) {
+  if (!out) return evie::fail(EVIE_ERR_ARG, "evie_create: out is null");
+  *out = nullptr;
+  EVIE_ARG(ckpt_dir != nullptr, "evie_create: null checkpoint directory");
+  EVIE_ARG(slots >= 1 && slots <= 4096, "evie_create: slots must be in 1..4096");
+  EVIE_ARG(max_ctx >= 1 && max_ctx <= (int)evie::kGqaMaxContext, "evie_create: max_ctx must be in 1..%ld",
+           (long)evie::kGqaMaxContext);
+  EVIE_ARG(max_rows >= 1 && max_rows <= 65535, "evie_create: max_rows must be in 1..65535");
+  int ndev = 0;
+  EVIE_CUDA_TRY(cudaGetDeviceCount(&ndev));
+  EVIE_ARG(device >= 0 && device < ndev, "evie_create: device %d not present (%d devices)", device, ndev);
+  evie_ctx* c = new evie_ctx();
+  c->device = device;
+  c->slots = slots;
+  c->max_ctx = max_ctx;
+  c->max_rows = max_rows;
+  const char* kvf = getenv("EVIE_KV_F32");
+  c->kv_f32 = kvf && kvf[0] == '1';
+  evie_status rc = EVIE_OK;
+  do {
+    if (cudaSetDevice(device) != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "cudaSetDevice(%d) failed", device); break; }
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "stream creation failed"); break; }
+    if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) { rc = evie::fail(EVIE_ERR_CUDA, "cublasCreate failed"); break; }
+    cublasSetStream(c->blas, c->stream);
+    cublasSetMathMode(c->blas, CUBLAS_DEFAULT_MATH);
+    if ((rc = read_config(c, ckpt_dir)) != EVIE_OK) break;
+    if ((rc = load_weights(c, ckpt_dir)) != EVIE_OK) break;
+    if ((rc = allocate_state(c)) != EVIE_OK) break;
+    void* ws = nullptr;
+    if ((rc = c->alloc((char**)&ws, 64u << 20)) != EVIE_OK) break;
+    cublasSetWorkspace(c->blas, ws, 64u << 20);
+    if (cudaDeviceSynchronize() != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "initialisation failed"); break; }
+  } while (0);
+  if (rc != EVIE_OK) {
+    destroy(c);
+    return rc;
+  }
+  *out = c;
+  return EVIE_OK;
+}
+
+void evie_destroy(evie_ctx* c) { destroy(c); }
+
+const char* evie_last_error(const evie_ctx* c) { return c ? c->err.c_str() : evie::thread_error().c_str(); }
+
+evie_status evie_info(const evie_ctx* c, evie_model_info* out) {
+  EVIE_ARG(c && out, "evie_info: null argument");
+  auto& s = c->s;
+  *out = evie_model_info{s.d, s.n, s.L, s.V, c->n_lin, c->n_full, c->slots, c->max_ctx, c->max_rows, kMaxOps,
+                         (int64_t)c->weight_bytes, (int64_t)c->cache_bytes};
+  return EVIE_OK;
+}
+
+evie_status evie_forward(evie_ctx* c, const evie_seq* seqs, int n_seqs, int want_logits, int capture, float* logits,
+                         int8_t* frames, uint16_t* resid, uint32_t* next_tokens) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_forward: null context");
+  if (!seqs) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_forward: null sequences"));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  return remember(c, forward_impl(c, seqs, n_seqs, want_logits, capture, logits, frames, resid, next_tokens));
+}
+
+// gpu/mod.rs:555-565; ops are kept in the caller's order within each layer (Plan::apply order).
+evie_status evie_set_ops(evie_ctx* c, int slot, const evie_op* ops, int n_ops) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_set_ops: null context");
+  auto& s = c->s;
+  if (slot < 0 || slot >= c->slots) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_ops: bad slot %d", slot));
+  std::vector<evie_op> kept;
+  for (int i = 0; i < n_ops; i++) {
+    const evie_op& o = ops[i];
+    if (o.layer < 0 || o.layer >= s.L || o.neuron < 0 || o.neuron >= s.n) continue;  // as gpu/mod.rs:559
+    if (o.mode < 1 || o.mode > 3)
+      return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_ops: mode %d (1 add, 2 mul, 3 set)", o.mode));
+    kept.push_back(o);
+  }
+  std::stable_sort(kept.begin(), kept.end(), [](const evie_op& a, const evie_op& b) { return a.layer < b.layer; });
+  std::vector<int> range((size_t)s.L * 2, 0);
+  for (size_t i = 0; i < kept.size(); i++) {
+    int l = kept[i].layer;
+    if (range[l * 2 + 1] == 0) range[l * 2] = (int)i;
+    range[l * 2 + 1]++;
+    if (range[l * 2 + 1] > kMaxOps)
+      return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_ops: more than %d ops in layer %d", kMaxOps, l));
+  }
+  if ((int)kept.size() > kMaxOps)
+    return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_ops: at most %d ops per slot (got %zu)", kMaxOps, kept.size()));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess && !kept.empty())
+    e = cudaMemcpy(c->ops + (size_t)slot * kMaxOps, kept.data(), kept.size() * sizeof(evie_op), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(c->op_range + (size_t)slot * s.L * 2, range.data(), range.size() * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_set_ops: %s", cudaGetErrorString(e)));
+  return EVIE_OK;
+}
+
+// gpu/mod.rs:567-575: zero the slot's recurrent and conv state; KV entries are overwritten by position.
+evie_status evie_reset_slot(evie_ctx* c, int slot) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_reset_slot: null context");
+  auto& s = c->s;
+  if (slot < 0 || slot >= c->slots) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_reset_slot: bad slot %d", slot));
+  const size_t cs = (size_t)std::max(c->n_lin, 1) * (s.K - 1) * s.conv_dim;
+  const size_t rs = (size_t)std::max(c->n_lin, 1) * s.hv * s.dk * s.dv;
+  cudaSetDevice(c->device);
+  cudaError_t e = cudaMemsetAsync(c->conv_state + (size_t)slot * cs, 0, cs * 4, c->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(c->rec_state + (size_t)slot * rs, 0, rs * 4, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_reset_slot: %s", cudaGetErrorString(e)));
+  return EVIE_OK;
+}
+
+evie_status evie_set_scale(evie_ctx* c, const float* scale, size_t n) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_set_scale: null context");
+  const size_t want = (size_t)c->s.L * c->s.n;
+  if (!scale || n != want)  // gpu/mod.rs:550 ignores a wrong length; here it is an error the caller sees
+    return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_scale: expected %zu scales, got %zu", want, n));
+  cudaSetDevice(c->device);
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(c->scale, scale, n * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_set_scale: %s", cudaGetErrorString(e)));
+  return EVIE_OK;
+}
+
+evie_status evie_track_max(evie_ctx* c, int on) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_track_max: null context");
+  c->track = on != 0;
+  if (on) {  // gpu/mod.rs:583-587: turning tracking on clears the maxima
+    cudaSetDevice(c->device);
+    cudaError_t e = cudaMemsetAsync(c->maxbuf, 0, (size_t)c->s.L * c->s.n * 4, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_track_max: %s", cudaGetErrorString(e)));
+  }
+  return EVIE_OK;
+}
+
+evie_status evie_read_max(evie_ctx* c, float* out, size_t n) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_read_max: null context");
+  const size_t want = (size_t)c->s.L * c->s.n;
+  if (!out || n < want) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_read_max: need room for %zu values", want));
+  cudaSetDevice(c->device);
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(out, c->maxbuf, want * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_read_max: %s", cudaGetErrorString(e)));
+  return EVIE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,476 @@
+// Kernels of the full-model forward pass between the projections (see model_kernels.h for the operand format).
+// Each follows the corresponding step of evie-core's CPU engine, crates/evie-core/src/model.rs (line numbers
+// below), in f32 with the same formulas; only summation orders differ.
+#include "model_kernels.h"
+
+namespace evie {
+
+namespace {
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();  // red may still be read from a previous call
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < NT / 32; w++) t += red[w];
+  return t;
+}
+
+__device__ __forceinline__ float softplus_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// worker.rs:97-112: q = round(127 sqrt(min(|v|, 1))) with the sign of v.
+__device__ __forceinline__ int8_t compand(float v) {
+  const float q = roundf(sqrtf(fminf(fabsf(v), 1.0f)) * 127.0f);
+  return v < 0.0f ? (int8_t)(-(int)q) : (int8_t)(int)q;
+}
+
+constexpr int kNormThreads = 256;
+
+// model.rs:230-241 (embedding rows, then the first pre-mixer RMSNorm)
+__global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowInfo* __restrict__ rows,
+                                                                  const __nv_bfloat16* __restrict__ embed,
+                                                                  float* __restrict__ x, const float* __restrict__ gain,
+                                                                  float eps, int d, __nv_bfloat16* __restrict__ X2,
+                                                                  size_t xplane) {
+  __shared__ float red[kNormThreads / 32];
+  const int r = blockIdx.x;
+  const __nv_bfloat16* e = embed + (size_t)rows[r].token * d;
+  float* xr = x + (size_t)r * d;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < d; i += kNormThreads) {
+    const float v = __bfloat162float(e[i]);
+    xr[i] = v;
+    ss += v * v;
+  }
+  ss = block_sum<kNormThreads>(ss, red);
+  const float inv = 1.0f / sqrtf(ss / (float)d + eps);
+  for (int i = threadIdx.x; i < d; i += kNormThreads) store_split(X2, xplane, (size_t)r * d + i, xr[i] * inv * gain[i]);
+}
+
+// model.rs:246-248, 260-263 (residual add, residual hook, next RMSNorm)
+__global__ void __launch_bounds__(kNormThreads) add_norm_kernel(float* __restrict__ x, const float* __restrict__ Y2,
+                                                                size_t yplane, int ldy, const float* __restrict__ gain,
+                                                                float eps, int d, __nv_bfloat16* __restrict__ X2,
+                                                                size_t xplane, uint16_t* __restrict__ resid,
+                                                                int cap_layer, int L) {
+  __shared__ float red[kNormThreads / 32];
+  const int r = blockIdx.x;
+  float* xr = x + (size_t)r * d;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < d; i += kNormThreads) {
+    const float v = xr[i] + load_y(Y2, yplane, (size_t)r * ldy + i);
+    xr[i] = v;
+    ss += v * v;
+    if (resid) resid[((size_t)r * L + cap_layer) * d + i] = __half_as_ushort(__float2half_rn(v));
+  }
+  ss = block_sum<kNormThreads>(ss, red);
+  const float inv = 1.0f / sqrtf(ss / (float)d + eps);
+  for (int i = threadIdx.x; i < d; i += kNormThreads) store_split(X2, xplane, (size_t)r * d + i, xr[i] * inv * gain[i]);
+}
+
+// model.rs:260-263 for the last layer, then model.rs:271-290 (last row of each sequence, final norm)
+__global__ void __launch_bounds__(kNormThreads) add_final_kernel(float* __restrict__ x, const float* __restrict__ Y2,
+                                                                 size_t yplane, int ldy,
+                                                                 const RowInfo* __restrict__ rows,
+                                                                 const SegInfo* __restrict__ segs, int nseg,
+                                                                 const float* __restrict__ gain, float eps, int d,
+                                                                 __nv_bfloat16* __restrict__ X2,
+                                                                 uint16_t* __restrict__ resid, int cap_layer, int L) {
+  __shared__ float red[kNormThreads / 32];
+  const int r = blockIdx.x;
+  float* xr = x + (size_t)r * d;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < d; i += kNormThreads) {
+    const float v = xr[i] + load_y(Y2, yplane, (size_t)r * ldy + i);
+    xr[i] = v;
+    ss += v * v;
+    if (resid) resid[((size_t)r * L + cap_layer) * d + i] = __half_as_ushort(__float2half_rn(v));
+  }
+  ss = block_sum<kNormThreads>(ss, red);
+  const int s = rows[r].seg;
+  if (r != segs[s].start + segs[s].count - 1) return;
+  const float inv = 1.0f / sqrtf(ss / (float)d + eps);
+  const size_t plane = (size_t)nseg * d;
+  for (int i = threadIdx.x; i < d; i += kNormThreads) store_split(X2, plane, (size_t)s * d + i, xr[i] * inv * gain[i]);
+}
+
+// model.rs:324-353: causal depthwise conv over [conv state ; rows] + SiLU; L2 norm of q and k heads, q * 1/sqrt(dk).
+// One CTA = one row x one 128-channel head block.
+__global__ void __launch_bounds__(128) conv_silu_norm_kernel(const float* __restrict__ Y2, size_t yplane, int ldy,
+                                                             const RowInfo* __restrict__ rows,
+                                                             const SegInfo* __restrict__ segs,
+                                                             const float* __restrict__ conv_state, size_t cs_slot,
+                                                             const float* __restrict__ conv_w, int K, int conv_dim,
+                                                             int hk, float qscale, float* __restrict__ act) {
+  __shared__ float red[4];
+  const int c = blockIdx.x * 128 + threadIdx.x;
+  const int r = blockIdx.y;
+  const SegInfo sg = segs[rows[r].seg];
+  const int t = r - sg.start;
+  const float* cs = conv_state + (size_t)sg.slot * cs_slot;
+  float acc = 0.f;
+  for (int j = 0; j < K; j++) {
+    const int tt = t - (K - 1) + j;
+    const float u = tt >= 0 ? load_y(Y2, yplane, (size_t)(sg.start + tt) * ldy + c) : cs[(size_t)(K - 1 + tt) * conv_dim + c];
+    acc += conv_w[(size_t)c * K + j] * u;
+  }
+  float out = siluf_(acc);
+  if ((int)blockIdx.x < 2 * hk) {  // q or k head: L2 normalise (kernels.rs dot + 1e-6), q also by 1/sqrt(dk)
+    const float ss = block_sum<128>(out * out, red);
+    const float inv = 1.0f / sqrtf(ss + 1e-6f);
+    out *= inv * ((int)blockIdx.x < hk ? qscale : 1.0f);
+  }
+  act[(size_t)r * conv_dim + c] = out;
+}
+
+// model.rs:339: the conv window keeps the last K-1 raw inputs of [state ; rows].
+__global__ void conv_state_update_kernel(const float* __restrict__ Y2, size_t yplane, int ldy,
+                                         const SegInfo* __restrict__ segs, float* __restrict__ conv_state,
+                                         size_t cs_slot, int K, int conv_dim) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= conv_dim) return;
+  const SegInfo sg = segs[blockIdx.y];
+  if (sg.count == 0) return;
+  float* cs = conv_state + (size_t)sg.slot * cs_slot;
+  for (int i = 0; i < K - 1; i++) {
+    const int src = sg.count + i;  // index into [state (K-1) ; rows (count)]
+    const float v = src < K - 1 ? cs[(size_t)src * conv_dim + c]
+                                : load_y(Y2, yplane, (size_t)(sg.start + src - (K - 1)) * ldy + c);
+    cs[(size_t)i * conv_dim + c] = v;
+  }
+}
+
+// model.rs:362-387 (+ recur_body model.rs:503-524): one CTA per (segment, value head), 256 threads, the head's
+// [128][128] state resident in registers across the segment's rows (16 rows x 4 columns per thread).
+constexpr int kMixThreads = 256;
+__global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
+    const float* __restrict__ act, const float* __restrict__ Y2, size_t yplane, int ldy,
+    const SegInfo* __restrict__ segs, float* __restrict__ rec_state, size_t rs_slot, const float* __restrict__ neg_a,
+    const float* __restrict__ dt_bias, const float* __restrict__ norm_w, int conv_dim, int key_dim, int vd, int hv,
+    int ratio, float eps, __nv_bfloat16* __restrict__ X2, size_t xplane) {
+  constexpr int DK = 128, DV = 128;
+  const int head = blockIdx.x;
+  const SegInfo sg = segs[blockIdx.y];
+  if (sg.count == 0) return;
+  const int kh = head / ratio;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;  // lane: 4 columns; warp: rows warp + 8 r
+  __shared__ float sq[DK], sk[DK];
+  __shared__ float4 red[8][32];
+  __shared__ float sred[4];
+  __shared__ float s_o[DV];
+
+  float* Sh = rec_state + (size_t)sg.slot * rs_slot + (size_t)head * DK * DV + lane * 4;
+  float4 s[16];
+#pragma unroll
+  for (int r = 0; r < 16; r++) s[r] = *reinterpret_cast<const float4*>(Sh + (size_t)(warp + 8 * r) * DV);
+
+  for (int t = 0; t < sg.count; t++) {
+    const int row = sg.start + t;
+    const float* ar = act + (size_t)row * conv_dim;
+    if (tid < DK) sq[tid] = ar[kh * DK + tid];
+    else sk[tid - DK] = ar[key_dim + kh * DK + (tid - DK)];
+    const float4 v4 = *reinterpret_cast<const float4*>(ar + 2 * key_dim + head * DV + lane * 4);
+    const float bb = load_y(Y2, yplane, (size_t)row * ldy + conv_dim + vd + head);
+    const float aa = load_y(Y2, yplane, (size_t)row * ldy + conv_dim + vd + hv + head);
+    const float decay = expf(neg_a[head] * softplus_(aa + dt_bias[head]));
+    const float beta = sigmoidf_(bb);
+    __syncthreads();
+    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+      const float kr = sk[warp + 8 * r];
+      kv.x += s[r].x * kr; kv.y += s[r].y * kr; kv.z += s[r].z * kr; kv.w += s[r].w * kr;
+    }
+    red[warp][lane] = kv;
+    __syncthreads();
+    kv = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; w++) {
+      const float4 u = red[w][lane];
+      kv.x += u.x; kv.y += u.y; kv.z += u.z; kv.w += u.w;
+    }
+    const float d0 = (v4.x - decay * kv.x) * beta, d1 = (v4.y - decay * kv.y) * beta;
+    const float d2 = (v4.z - decay * kv.z) * beta, d3 = (v4.w - decay * kv.w) * beta;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+      const int i = warp + 8 * r;
+      const float kr = sk[i], qr = sq[i];
+      s[r].x = s[r].x * decay + kr * d0; s[r].y = s[r].y * decay + kr * d1;
+      s[r].z = s[r].z * decay + kr * d2; s[r].w = s[r].w * decay + kr * d3;
+      o.x += s[r].x * qr; o.y += s[r].y * qr; o.z += s[r].z * qr; o.w += s[r].w * qr;
+    }
+    __syncthreads();  // everyone has read red (kv) before it is reused
+    red[warp][lane] = o;
+    __syncthreads();
+    if (tid < DV) {  // thread j finishes output column j
+      const float* rf = reinterpret_cast<const float*>(&red[0][0]);
+      float oj = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; w++) oj += rf[w * DV + tid];
+      s_o[tid] = oj;
+      float ss = oj * oj;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) sred[warp] = ss;
+    }
+    __syncthreads();
+    if (tid < DV) {  // gated RMSNorm, model.rs:377-383: o * rsqrt(mean o^2 + eps) * w * silu(z)
+      const float ms = (sred[0] + sred[1] + sred[2] + sred[3]) / (float)DV;
+      const float inv = 1.0f / sqrtf(ms + eps);
+      const float z = load_y(Y2, yplane, (size_t)row * ldy + conv_dim + head * DV + tid);
+      store_split(X2, xplane, (size_t)row * vd + head * DV + tid, s_o[tid] * inv * norm_w[tid] * siluf_(z));
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 16; r++) *reinterpret_cast<float4*>(Sh + (size_t)(warp + 8 * r) * DV) = s[r];
+}
+
+// model.rs:419-442, rope model.rs:470-479: q_norm / k_norm (gains 1+w) + rotate-half RoPE on the first `rot` dims;
+// K and V appended to the paged cache. One CTA per (row, head) with one thread per head dim (hd = 256).
+template <typename KV>
+__global__ void __launch_bounds__(256) attn_prep_kernel(const float* __restrict__ Y2, size_t yplane, int ldy,
+                                                        const RowInfo* __restrict__ rows,
+                                                        const float* __restrict__ q_norm,
+                                                        const float* __restrict__ k_norm,
+                                                        const float* __restrict__ inv_freq, int nh, int nkv, int hd,
+                                                        int rot, float eps, float* __restrict__ q_rot, KV* __restrict__ kc,
+                                                        KV* __restrict__ vc, const int* __restrict__ page_table,
+                                                        int pages_per_slot, int page_size) {
+  __shared__ float red[8];
+  __shared__ float y[256];
+  const int idx = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
+  const RowInfo ri = rows[r];
+  const bool is_q = idx < nh;
+  const int kh = idx - nh;
+  const size_t base = (size_t)r * ldy;
+  const float raw = is_q ? load_y(Y2, yplane, base + (size_t)idx * 2 * hd + d)
+                         : load_y(Y2, yplane, base + (size_t)2 * nh * hd + (size_t)kh * hd + d);
+  const float ss = block_sum<256>(raw * raw, red);
+  const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+  const float yn = raw * inv * (is_q ? q_norm[d] : k_norm[d]);
+  y[d] = yn;
+  __syncthreads();
+  float out = yn;
+  const int half = rot / 2;
+  if (d < rot) {
+    const int i = d < half ? d : d - half;
+    float sn, cs;
+    sincosf((float)ri.pos * inv_freq[i], &sn, &cs);
+    out = d < half ? y[d] * cs - y[d + half] * sn : y[d] * cs + y[d - half] * sn;
+  }
+  if (is_q) {
+    q_rot[((size_t)r * nh + idx) * hd + d] = out;
+  } else {
+    const int page = page_table[(size_t)ri.slot * pages_per_slot + ri.pos / page_size];
+    const size_t off = (((size_t)page * nkv + kh) * page_size + ri.pos % page_size) * hd + d;
+    const float v = load_y(Y2, yplane, base + (size_t)2 * nh * hd + (size_t)nkv * hd + (size_t)kh * hd + d);
+    if constexpr (sizeof(KV) == 2) {
+      kc[off] = __float2bfloat16_rn(out);
+      vc[off] = __float2bfloat16_rn(v);
+    } else {
+      kc[off] = out;
+      vc[off] = v;
+    }
+  }
+}
+
+// model.rs:249-258 with the Probe hook (worker.rs:136-141): silu(gate) * up, the slot's steering ops of this layer
+// in order (steering.rs:189-208), companded capture (worker.rs:97-112) and max |a| over positions > 0
+// (gpu/mod.rs:577-593). One CTA = one row x 1024 neurons.
+__global__ void __launch_bounds__(256) swiglu_kernel(const float* __restrict__ Y2, size_t yplane, int ldy,
+                                                     const RowInfo* __restrict__ rows, int layer, int n, int L,
+                                                     SteerTables steer, const float* __restrict__ scale,
+                                                     int8_t* __restrict__ frames, uint32_t* __restrict__ maxbuf,
+                                                     __nv_bfloat16* __restrict__ X2, size_t xplane) {
+  __shared__ evie_op s_ops[64];
+  __shared__ int s_cnt;
+  const int r = blockIdx.y;
+  const RowInfo ri = rows[r];
+  if (threadIdx.x == 0) {
+    const int* rg = steer.range + ((size_t)ri.slot * L + layer) * 2;
+    s_cnt = min(rg[1], 64);
+  }
+  __syncthreads();
+  const int cnt = s_cnt;
+  if (threadIdx.x < cnt) {
+    const int first = steer.range[((size_t)ri.slot * L + layer) * 2];
+    s_ops[threadIdx.x] = steer.ops[(size_t)ri.slot * steer.max_ops + first + threadIdx.x];
+  }
+  __syncthreads();
+  const int j0 = blockIdx.x * 1024 + threadIdx.x * 4;
+  const size_t yr = (size_t)r * ldy;
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const int j = j0 + e;
+    if (j >= n) break;
+    const float g = load_y(Y2, yplane, yr + j);
+    const float u = load_y(Y2, yplane, yr + n + j);
+    float a = siluf_(g) * u;
+    for (int i = 0; i < cnt; i++) {
+      const evie_op op = s_ops[i];
+      if (op.neuron != j) continue;
+      if (op.mode == 1) a += op.value;
+      else if (op.mode == 2) a *= op.value;
+      else if (op.mode == 3) a = op.value;
+    }
+    store_split(X2, xplane, (size_t)r * n + j, a);
+    if (frames) frames[((size_t)r * L + layer) * n + j] = compand(a / scale[(size_t)layer * n + j]);
+    if (maxbuf && ri.pos > 0) atomicMax(maxbuf + (size_t)layer * n + j, __float_as_uint(fabsf(a)));
+  }
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (0xFFFFFFFFu - i);  // larger value first, then lower index
+}
+
+// kernels.rs:642-662 with k = 1 (sampling.rs:60-62): the first index of the maximum logit.
+__global__ void __launch_bounds__(256) logits_argmax_kernel(const float* __restrict__ L2, int nseg, int V,
+                                                            float* __restrict__ logits,
+                                                            unsigned long long* __restrict__ best) {
+  __shared__ unsigned long long red[8];
+  const int s = blockIdx.y;
+  const size_t plane = (size_t)nseg * V;
+  unsigned long long key = 0;
+  const int i0 = blockIdx.x * 1024 + threadIdx.x;
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const int i = i0 + e * 256;
+    if (i < V) {
+      const float v = L2[(size_t)s * V + i] + L2[plane + (size_t)s * V + i];
+      if (logits) logits[(size_t)s * V + i] = v;
+      const unsigned long long k = argmax_key(v, (uint32_t)i);
+      key = k > key ? k : key;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
+    key = o > key ? o : key;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = key;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long k = red[0];
+    for (int w = 1; w < 8; w++) k = red[w] > k ? red[w] : k;
+    atomicMax(best + s, k);
+  }
+}
+
+__global__ void argmax_finish_kernel(unsigned long long* best, uint32_t* next_tokens, int nseg) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= nseg) return;
+  next_tokens[s] = 0xFFFFFFFFu - (uint32_t)(best[s] & 0xFFFFFFFFull);
+  best[s] = 0;
+}
+
+}  // namespace
+
+evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed, float* x, const float* gain,
+                         float eps, int d, __nv_bfloat16* X2, cudaStream_t st) {
+  if (R == 0) return EVIE_OK;
+  embed_norm_kernel<<<R, kNormThreads, 0, st>>>(rows, embed, x, gain, eps, d, X2, (size_t)R * d);
+  EVIE_CHECK_LAUNCH("embed_norm_kernel");
+  return EVIE_OK;
+}
+
+evie_status k_add_norm(float* x, const float* Y2, int ldy, int R, const float* gain, float eps, int d,
+                       __nv_bfloat16* X2, uint16_t* resid, int cap_layer, int L, cudaStream_t st) {
+  if (R == 0) return EVIE_OK;
+  add_norm_kernel<<<R, kNormThreads, 0, st>>>(x, Y2, (size_t)R * ldy, ldy, gain, eps, d, X2, (size_t)R * d, resid,
+                                              cap_layer, L);
+  EVIE_CHECK_LAUNCH("add_norm_kernel");
+  return EVIE_OK;
+}
+
+evie_status k_add_final(float* x, const float* Y2, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
+                        int nseg, const float* gain, float eps, int d, __nv_bfloat16* X2, uint16_t* resid,
+                        int cap_layer, int L, cudaStream_t st) {
+  if (R == 0) return EVIE_OK;
+  add_final_kernel<<<R, kNormThreads, 0, st>>>(x, Y2, (size_t)R * ldy, ldy, rows, segs, nseg, gain, eps, d, X2, resid,
+                                               cap_layer, L);
+  EVIE_CHECK_LAUNCH("add_final_kernel");
+  return EVIE_OK;
+}
+
+evie_status k_conv_silu_norm(const float* Y2, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
+                             const float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
+                             float* act, cudaStream_t st) {
+  if (R == 0) return EVIE_OK;
+  dim3 grid(s.conv_dim / 128, R);
+  conv_silu_norm_kernel<<<grid, 128, 0, st>>>(Y2, (size_t)R * ldy, ldy, rows, segs, conv_state, cs_slot, conv_w, s.K,
+                                              s.conv_dim, s.hk, 1.0f / sqrtf((float)s.dk), act);
+  EVIE_CHECK_LAUNCH("conv_silu_norm_kernel");
+  return EVIE_OK;
+}
+
+evie_status k_conv_state_update(const float* Y2, int ldy, int R, const SegInfo* segs, int nseg, float* conv_state,
+                                size_t cs_slot, const ModelShape& s, cudaStream_t st) {
+  if (nseg == 0) return EVIE_OK;
+  dim3 grid((s.conv_dim + 255) / 256, nseg);
+  conv_state_update_kernel<<<grid, 256, 0, st>>>(Y2, (size_t)R * ldy, ldy, segs, conv_state, cs_slot, s.K,
+                                                 s.conv_dim);
+  EVIE_CHECK_LAUNCH("conv_state_update_kernel");
+  return EVIE_OK;
+}
+
+evie_status k_gdn_mixer(const float* act, const float* Y2, int ldy, int R, const SegInfo* segs, int nseg,
+                        float* rec_state, size_t rs_slot, const float* neg_a, const float* dt_bias,
+                        const float* norm_w, const ModelShape& s, __nv_bfloat16* X2, cudaStream_t st) {
+  if (nseg == 0) return EVIE_OK;
+  dim3 grid(s.hv, nseg);
+  gdn_mixer_kernel<<<grid, kMixThreads, 0, st>>>(act, Y2, (size_t)R * ldy, ldy, segs, rec_state, rs_slot, neg_a,
+                                                 dt_bias, norm_w, s.conv_dim, s.key_dim, s.vd, s.hv, s.hv / s.hk, s.eps,
+                                                 X2, (size_t)R * s.vd);
+  EVIE_CHECK_LAUNCH("gdn_mixer_kernel");
+  return EVIE_OK;
+}
+
+template <typename KV>
+evie_status k_attn_prep(const float* Y2, int ldy, int R, const RowInfo* rows, const float* q_norm,
+                        const float* k_norm, const float* inv_freq, const ModelShape& s, float* q_rot, KV* kc,
+                        KV* vc, const int* page_table, int pages_per_slot, int page_size, cudaStream_t st) {
+  if (R == 0) return EVIE_OK;
+  dim3 grid(s.nh + s.nkv, R);
+  attn_prep_kernel<KV><<<grid, 256, 0, st>>>(Y2, (size_t)R * ldy, ldy, rows, q_norm, k_norm, inv_freq, s.nh, s.nkv,
+                                             s.hd, s.rot, s.eps, q_rot, kc, vc, page_table, pages_per_slot, page_size);
+  EVIE_CHECK_LAUNCH("attn_prep_kernel");
+  return EVIE_OK;
+}
+template evie_status k_attn_prep<__nv_bfloat16>(const float*, int, int, const RowInfo*, const float*, const float*,
+                                                const float*, const ModelShape&, float*, __nv_bfloat16*,
+                                                __nv_bfloat16*, const int*, int, int, cudaStream_t);
+template evie_status k_attn_prep<float>(const float*, int, int, const RowInfo*, const float*, const float*,
+                                        const float*, const ModelShape&, float*, float*, float*, const int*, int, int,
+                                        cudaStream_t);
+
+evie_status k_swiglu(const float* Y2, int ldy, int R, const RowInfo* rows, int layer, const ModelShape& s,
+                     SteerTables steer, const float* scale, int8_t* frames, uint32_t* maxbuf, __nv_bfloat16* X2,
+                     cudaStream_t st) {
+  if (R == 0) return EVIE_OK;
+  dim3 grid((s.n + 1023) / 1024, R);
+  swiglu_kernel<<<grid, 256, 0, st>>>(Y2, (size_t)R * ldy, ldy, rows, layer, s.n, s.L, steer, scale, frames, maxbuf,
+                                      X2, (size_t)R * s.n);
+  EVIE_CHECK_LAUNCH("swiglu_kernel");
+  return EVIE_OK;
+}
+
+evie_status k_logits_argmax(const float* L2, int nseg, int V, float* logits, unsigned long long* best,
+                            uint32_t* next_tokens, cudaStream_t st) {
+  if (nseg == 0) return EVIE_OK;
+  dim3 grid((V + 1023) / 1024, nseg);
+  logits_argmax_kernel<<<grid, 256, 0, st>>>(L2, nseg, V, logits, best);
+  EVIE_CHECK_LAUNCH("logits_argmax_kernel");
+  argmax_finish_kernel<<<(nseg + 127) / 128, 128, 0, st>>>(best, next_tokens, nseg);
+  EVIE_CHECK_LAUNCH("argmax_finish_kernel");
+  return EVIE_OK;
+}
+
+}  // namespace evie

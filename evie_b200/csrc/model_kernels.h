@@ -1,0 +1,76 @@
+// Kernels of the full-model forward pass (model_kernels.cu) and the shapes they share with the host runtime.
+//
+// Projection operands: the reference multiplies bf16 weights by f32 activations (crates/evie-core/src/kernels.rs
+// :1-4). On tensor cores both operands must be bf16, so every activation matrix X that feeds a projection is
+// written as two stacked bf16 planes, X = hi + lo with hi = bf16(X) and lo = bf16(X - hi) (16 significant bits).
+// One bf16 GEMM over the 2R stacked rows gives Y2 = [X_hi W^T ; X_lo W^T] in f32, and every consumer reads
+// Y = Y2[r] + Y2[R + r]. The weights are read once; the result matches the f32 product to ~2^-16 relative.
+#pragma once
+#include "common.h"
+
+namespace evie {
+
+struct RowInfo {
+  int slot, pos, token, seg;
+};
+struct SegInfo {
+  int slot, start, count, pos0;
+};
+
+// Split-plane helpers: plane 0 = hi, plane 1 = lo, plane stride R*ld elements.
+__device__ __forceinline__ void store_split(__nv_bfloat16* X2, size_t plane, size_t idx, float v) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+  X2[idx] = hi;
+  X2[plane + idx] = __float2bfloat16_rn(v - __bfloat162float(hi));
+}
+__device__ __forceinline__ float load_y(const float* Y2, size_t plane, size_t idx) { return Y2[idx] + Y2[plane + idx]; }
+
+struct ModelShape {
+  int d, n, L, V;
+  float eps;
+  int nh, nkv, hd, rot;
+  int K, hk, hv, dk, dv, conv_dim, vd, key_dim;
+  int in_dn;   // rows of the fused DeltaNet input projection: conv_dim + vd + 2 hv
+  int in_at;   // rows of the fused attention input projection: (2 nh + 2 nkv) hd
+};
+
+evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed, float* x, const float* gain,
+                         float eps, int d, __nv_bfloat16* X2, cudaStream_t st);
+// x += Y (two planes); optional f16 capture of x as the residual leaving `cap_layer`; then X2 = split(rmsnorm(x)).
+evie_status k_add_norm(float* x, const float* Y2, int ldy, int R, const float* gain, float eps, int d,
+                       __nv_bfloat16* X2, uint16_t* resid, int cap_layer, int L, cudaStream_t st);
+// Final residual add (+ capture of the last layer) and final norm of each segment's last row into X2 [2][nseg][d].
+evie_status k_add_final(float* x, const float* Y2, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
+                        int nseg, const float* gain, float eps, int d, __nv_bfloat16* X2, uint16_t* resid,
+                        int cap_layer, int L, cudaStream_t st);
+// Causal depthwise conv over [conv state ; new rows] + SiLU, then L2 norm of the q and k heads (q also 1/sqrt(dk)).
+// conv_state points at this layer's window of slot 0; cs_slot is the element stride between slots.
+evie_status k_conv_silu_norm(const float* Y2, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
+                             const float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
+                             float* act, cudaStream_t st);
+evie_status k_conv_state_update(const float* Y2, int ldy, int R, const SegInfo* segs, int nseg, float* conv_state,
+                                size_t cs_slot, const ModelShape& s, cudaStream_t st);
+// Gated delta rule over each segment's rows (state resident in registers) + gated RMSNorm -> X2 [R][vd].
+// rec_state points at this layer's [hv][dk][dv] state of slot 0; rs_slot is the element stride between slots.
+evie_status k_gdn_mixer(const float* act, const float* Y2, int ldy, int R, const SegInfo* segs, int nseg,
+                        float* rec_state, size_t rs_slot, const float* neg_a, const float* dt_bias,
+                        const float* norm_w, const ModelShape& s, __nv_bfloat16* X2, cudaStream_t st);
+// q/k RMSNorm (1+w gains) + partial RoPE; q -> q_rot f32 [R][nh][hd]; k, v -> paged cache (bf16 or f32).
+template <typename KV>
+evie_status k_attn_prep(const float* Y2, int ldy, int R, const RowInfo* rows, const float* q_norm,
+                        const float* k_norm, const float* inv_freq, const ModelShape& s, float* q_rot, KV* kc,
+                        KV* vc, const int* page_table, int pages_per_slot, int page_size, cudaStream_t st);
+// silu(gate) * up, per-slot steering ops, capture, max tracking -> X2 [R][n].
+struct SteerTables {
+  const evie_op* ops;      // [slots][max_ops], each slot's ops sorted by layer (stable)
+  const int* range;        // [slots][L][2] (first, count) into the slot's ops
+  int max_ops;
+};
+evie_status k_swiglu(const float* Y2, int ldy, int R, const RowInfo* rows, int layer, const ModelShape& s,
+                     SteerTables steer, const float* scale, int8_t* frames, uint32_t* maxbuf, __nv_bfloat16* X2,
+                     cudaStream_t st);
+// logits = two planes summed (optional copy out), greedy argmax (first index of the maximum).
+evie_status k_logits_argmax(const float* L2, int nseg, int V, float* logits, unsigned long long* best,
+                            uint32_t* next_tokens, cudaStream_t st);
+
+}  // namespace evie

@@ -1,0 +1,108 @@
+"""GpuModel: Python view of the full-model C ABI, with the method set of evie-core's GPU backend
+(crates/evie-core/src/gpu/mod.rs: new, forward, set_ops, reset_slot, set_scale, track_max, read_max)."""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import EvieError, capi, lib
+
+MODES = {"add": 1, "mul": 2, "set": 3}
+
+
+@dataclass
+class GpuSeq:
+    """One sequence in a forward call (gpu/mod.rs:147-154)."""
+    slot: int
+    pos0: int
+    tokens: np.ndarray
+
+
+@dataclass
+class GpuOut:
+    """gpu/mod.rs:156-163, plus the greedy token of each sequence."""
+    logits: np.ndarray | None = None                  # [n_seqs, vocab] f32
+    frames: np.ndarray | None = None                  # [rows, layers*neurons] i8
+    resid: np.ndarray | None = None                   # [rows, layers*hidden] f16
+    next_tokens: np.ndarray = field(default_factory=lambda: np.zeros(0, np.uint32))
+
+
+class GpuModel:
+    def __init__(self, ckpt_dir: str, max_ctx: int, slots: int = 2, max_rows: int = 128, device: int = 0):
+        L = lib()
+        h = C.c_void_p()
+        rc = L.evie_create(ckpt_dir.encode(), device, slots, max_ctx, max_rows, C.byref(h))
+        if rc != 0:
+            raise EvieError(rc, (L.evie_last_global_error() or b"").decode())
+        self._h = h
+        info = capi.ModelInfo()
+        self._check(L.evie_info(self._h, C.byref(info)))
+        self.info = info
+        self.layers, self.neurons, self.hidden, self.vocab = info.n_layers, info.intermediate, info.hidden, info.vocab
+        self.slots, self.max_ctx, self.max_rows = info.slots, info.max_ctx, info.max_rows
+
+    def _check(self, rc: int):
+        if rc != 0:
+            raise EvieError(rc, (lib().evie_last_error(self._h) or b"").decode())
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().evie_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, seqs, want_logits: bool = True, capture: bool = False, out: GpuOut | None = None) -> GpuOut:
+        n = len(seqs)
+        arr = (capi.Seq * max(n, 1))()
+        keep = []
+        rows = 0
+        for i, s in enumerate(seqs):
+            t = np.ascontiguousarray(s.tokens, dtype=np.uint32)
+            keep.append(t)
+            arr[i] = capi.Seq(s.slot, s.pos0, t.ctypes.data if t.size else None, t.size)
+            rows += t.size
+        o = out or GpuOut()
+        if want_logits and (o.logits is None or o.logits.shape != (n, self.vocab)):
+            o.logits = np.empty((n, self.vocab), np.float32)
+        if capture:
+            if o.frames is None or o.frames.shape != (rows, self.layers * self.neurons):
+                o.frames = np.empty((rows, self.layers * self.neurons), np.int8)
+            if o.resid is None or o.resid.shape != (rows, self.layers * self.hidden):
+                o.resid = np.empty((rows, self.layers * self.hidden), np.float16)
+        if o.next_tokens.shape != (n,):
+            o.next_tokens = np.empty(n, np.uint32)
+        p = lambda a: a.ctypes.data if a is not None else None  # noqa: E731
+        self._check(lib().evie_forward(self._h, arr, n, int(want_logits), int(capture),
+                                       p(o.logits) if want_logits else None, p(o.frames) if capture else None,
+                                       p(o.resid) if capture else None, p(o.next_tokens)))
+        return o
+
+    def set_ops(self, slot: int, ops):
+        """ops: iterable of (layer, neuron, mode 1/2/3 or 'add'/'mul'/'set', value)."""
+        ops = list(ops)
+        arr = (capi.Op * max(len(ops), 1))()
+        for i, (l, nn, m, v) in enumerate(ops):
+            arr[i] = capi.Op(l, nn, MODES.get(m, m) if isinstance(m, str) else m, v)
+        self._check(lib().evie_set_ops(self._h, slot, arr, len(ops)))
+
+    def reset_slot(self, slot: int):
+        self._check(lib().evie_reset_slot(self._h, slot))
+
+    def set_scale(self, scale: np.ndarray):
+        s = np.ascontiguousarray(scale, dtype=np.float32)
+        self._check(lib().evie_set_scale(self._h, s.ctypes.data, s.size))
+
+    def track_max(self, on: bool):
+        self._check(lib().evie_track_max(self._h, int(on)))
+
+    def read_max(self) -> np.ndarray:
+        out = np.empty(self.layers * self.neurons, np.float32)
+        self._check(lib().evie_read_max(self._h, out.ctypes.data, out.size))
+        return out
