@@ -143,6 +143,55 @@ class Workload:
     def cpu_sample(self, threads: int) -> dict:
         raise NotImplementedError
 
+    # default timing: one CUDA-event pair per step on the current stream, L2 flushed between steps if asked
+    def warmup(self, w):
+        for _ in range(w):
+            self.step()
+
+    def _flush(self):
+        import torch
+
+        if self.flush_l2 and not hasattr(self, "_flushbuf"):
+            self._flushbuf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        return getattr(self, "_flushbuf", None)
+
+    def timed(self, k):
+        import torch
+
+        stream = torch.cuda.current_stream()
+        flush = self._flush()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
+        launches = 0
+        for i in range(k):
+            if flush is not None:
+                flush.fill_(i & 0xFF)
+            ev[i][0].record(stream)
+            launches += self.step()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in ev), launches
+
+    def e2e(self, k):
+        import torch
+
+        stream = torch.cuda.current_stream()
+        flush = self._flush()
+        for _ in range(2):
+            self.e2e_step()
+        torch.cuda.synchronize()
+        ms = 0.0
+        h2d = d2h = 0
+        for i in range(k):
+            if flush is not None:
+                flush.fill_(i & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            h2d, d2h = self.e2e_step()
+            b.record(stream)
+            torch.cuda.synchronize()
+            ms += a.elapsed_time(b)
+        return ms, h2d, d2h
+
 
 class GdnDecode(Workload):
     name = "gdn_decode"
@@ -285,13 +334,216 @@ class GqaDecode(Workload):
                           f"scaled to the batch by context length"}
 
 
-WORKLOADS = {"gdn_decode": GdnDecode, "gqa_decode": GqaDecode}
+class ModelDecode(Workload):
+    """Config 4 per GPU: Qwen3.5-4B shapes, random bf16 weights (seed 5), B sequences = B/2 steered/unsteered pairs,
+    P-token uniform-random prompts, +0.6 dose Add steering on 32 seeded (layer, neuron) pairs on the steered half,
+    every SwiGLU activation captured. A step is one greedy decode step of all B sequences."""
+    name = "model_decode"
+    kernel = "decode step (all kernels)"
+    dtype = "f32 activations x bf16 weights (split-bf16 operands), fp32 DeltaNet state, bf16 KV"
+
+    def __init__(self, B=64, prompt=4096, rank=0):
+        assert B % 2 == 0
+        self.B, self.P, self.rank = B, prompt, rank
+        self.tokens_per_step = B
+        self.n_pairs_total = None
+
+    def config(self):
+        return {"workload": f"Qwen3.5-4B-shaped decode, {self.B} sequences ({self.B // 2} steered/unsteered pairs) per "
+                            f"GPU, {self.P}-token prompts, greedy, steering +0.6 dose on 32 (layer, neuron) pairs, "
+                            f"full SwiGLU capture (config 4)",
+                "model": "qwen3.5-4b-shaped (random init, seed 5)", "global_batch": self.B, "seq_len": self.P,
+                "l2": "inputs larger than L2 (8.4 GB weights + caches per step)",
+                "prefill_tok_s": getattr(self, "prefill_tok_s", None),
+                "prefill_ms": getattr(self, "prefill_ms", None)}
+
+    def setup(self, dev):
+        import torch
+
+        from evie_b200 import checkpoint as ck
+        from evie_b200.gpu import GpuModel, GpuSeq
+
+        base = os.environ.get("EVIE_CKPT_DIR", tempfile.gettempdir())
+        self.ckpt = ck.ensure_checkpoint(os.path.join(base, "evie_qwen35_4b_seed5"), ck.text_config(ck.QWEN35_4B),
+                                         seed=5, device="cuda")
+        self.cfg = json.load(open(os.path.join(self.ckpt, "config.json")))
+        L, n, V = self.cfg["num_hidden_layers"], self.cfg["intermediate_size"], self.cfg["vocab_size"]
+        self.max_ctx = self.P + 1024
+        self.m = GpuModel(self.ckpt, max_ctx=self.max_ctx, slots=self.B, max_rows=min(16384, self.B * self.P),
+                          device=dev.index or 0)
+        g = torch.Generator().manual_seed(5)
+        self.layers = torch.randint(0, L, (32,), generator=g).tolist()
+        self.neurons = torch.randint(0, n, (32,), generator=g).tolist()
+        npairs = self.B // 2
+        g = torch.Generator().manual_seed(5)
+        first = self.rank * npairs
+        all_prompts = [torch.randint(0, V, (self.P,), generator=g) for _ in range(first + npairs)]
+        self.prompts = [p.numpy().astype(np.uint32) for p in all_prompts[first:]]
+        # dose unit: median ||residual leaving layer l|| over tokens 1.. of pair 0's prompt (calib.rs:94-100),
+        # divided by ||W_down[:, n]|| (engine.rs:102-104); measured on the unsteered lane of pair 0.
+        out = self.m.forward([GpuSeq(1, 0, self.prompts[0])], want_logits=False, capture=True)
+        resid = out.resid.reshape(self.P, L, -1).astype(np.float32)
+        norms = np.linalg.norm(resid[1:], axis=-1)
+        self.units = np.median(norms, axis=0)
+        ops = []
+        for l, nn in zip(self.layers, self.neurons):
+            w = ck.read_tensor(self.ckpt, f"model.language_model.layers.{l}.mlp.down_proj.weight")
+            col = float(np.sqrt((w[:, nn].astype(np.float64) ** 2).sum()))
+            ops.append((l, nn, "add", float(0.6 * self.units[l] / max(col, 1e-12))))
+        self.ops = ops
+        for sl in range(self.B):
+            self.m.set_ops(sl, ops if sl % 2 == 0 else [])
+        self.m.reset_slot(1)
+        # prefill every sequence (pair p: slots 2p steered, 2p+1 unsteered), timed on the context's stream
+        stream = torch.cuda.ExternalStream(self.m.stream_ptr())
+        per_call = max(1, min(self.B, 16384 // self.P))
+        self.first_tokens = np.zeros(self.B, np.uint32)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for c0 in range(0, self.B, per_call):
+            seqs = [GpuSeq(sl, 0, self.prompts[sl // 2]) for sl in range(c0, min(self.B, c0 + per_call))]
+            o = self.m.forward(seqs, want_logits=False)
+            self.first_tokens[c0:c0 + len(seqs)] = o.next_tokens
+        e1.record(stream)
+        torch.cuda.synchronize()
+        self.prefill_ms = e0.elapsed_time(e1)
+        self.prefill_tok_s = self.B * self.P / (self.prefill_ms / 1000.0)
+        self.pos = self.P
+        self.next = self.first_tokens.copy()
+        self.stream = stream
+        self.frames_host = torch.empty((self.B, L * n), dtype=torch.int8).pin_memory()
+        self.resid_host = torch.empty((self.B, L * self.cfg["hidden_size"]), dtype=torch.float16).pin_memory()
+
+    def algorithmic(self):
+        """Bytes one decode step must move: every weight once (incl. the tied LM head), each sequence's DeltaNet
+        state and conv window read and written, its KV cache read and the new token's K/V written, the captured
+        frame and residual rows written."""
+        c = self.cfg
+        d, n, L, V = c["hidden_size"], c["intermediate_size"], c["num_hidden_layers"], c["vocab_size"]
+        hk, hv, dk, dv = (c["linear_num_key_heads"], c["linear_num_value_heads"], c["linear_key_head_dim"],
+                          c["linear_value_head_dim"])
+        nh, nkv, hd = c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"]
+        n_lin = sum(1 for t in c["layer_types"] if t == "linear_attention")
+        n_full = L - n_lin
+        conv_dim = 2 * hk * dk + hv * dv
+        w = V * d + n_lin * ((conv_dim + hv * dv + 2 * hv) * d + d * hv * dv) + n_full * ((2 * nh + 2 * nkv) * hd * d
+                                                                                          + d * nh * hd)
+        w += L * 3 * n * d
+        weights = 2 * w
+        state = self.B * n_lin * (hv * dk * dv + (c["linear_conv_kernel_dim"] - 1) * conv_dim) * 4 * 2
+        ctx = getattr(self, "pos_timed", self.pos) + 1 + self.mid_steps() // 2
+        kv = self.B * n_full * nkv * hd * 2 * 2 * (ctx + 1)
+        capture = self.B * L * (n + 2 * d)
+        return weights + state + kv + capture
+
+    def mid_steps(self):
+        return getattr(self, "_steps", 0)
+
+    def seqs(self):
+        from evie_b200.gpu import GpuSeq
+
+        return [GpuSeq(sl, self.pos, self.next[sl:sl + 1]) for sl in range(self.B)]
+
+    def run_device_steps(self, k):
+        """k greedy decode steps kept on the device (evie_decode_greedy), captures written on the device."""
+        toks = self.m.decode_greedy(self.seqs(), k, capture=True)
+        self.next = toks[-1].copy()
+        self.pos += k
+        return k
+
+    def step(self):
+        return self.run_device_steps(1)
+
+    def warmup(self, w):
+        self.run_device_steps(w)
+
+    def timed(self, k):
+        """k device-resident decode steps in one evie_decode_greedy call, timed on the context's stream."""
+        import torch
+
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self.pos_timed = self.pos
+        a.record(self.stream)
+        self.run_device_steps(k)
+        b.record(self.stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b), k * self.launches_per_step()
+
+    def launches_per_step(self):
+        """Our kernels per decode step: embed+norm; per DeltaNet layer conv, conv state, mixer, add-norm x2, SwiGLU;
+        per attention layer prep, attention, add-norm x2, SwiGLU; logits/argmax + finish, row advance."""
+        c = self.cfg
+        L = c["num_hidden_layers"]
+        n_lin = sum(1 for t in c["layer_types"] if t == "linear_attention")
+        return 1 + n_lin * 6 + (L - n_lin) * 5 + 3
+
+    def e2e(self, k):
+        import torch
+
+        for _ in range(2):
+            self.e2e_step()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(self.stream)
+        h2d = d2h = 0
+        for _ in range(k):
+            h2d, d2h = self.e2e_step()
+        b.record(self.stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b), h2d, d2h
+
+    def e2e_step(self):
+        """One decode step through evie_forward with host buffers: the step's tokens go up, the greedy tokens and
+        the captured frames and residual rows come back."""
+        from evie_b200.gpu import GpuOut
+
+        if not hasattr(self, "_out"):
+            self._out = GpuOut(frames=self.frames_host.numpy(), resid=self.resid_host.numpy())
+        o = self.m.forward(self.seqs(), want_logits=False, capture=True, out=self._out)
+        self.next = o.next_tokens.copy()
+        self.pos += 1
+        c = self.cfg
+        return self.B * 4, self.B * 4 + self.B * c["num_hidden_layers"] * (c["intermediate_size"] + 2 * c["hidden_size"])
+
+    def cpu_sample(self, threads):
+        import oracle
+
+        oracle.set_threads(threads)
+        m = oracle.Model(self.ckpt)
+        prompt = self.prompts[0][:64]
+        plan = oracle.compile_plan([dict(layer=l, neuron=nn, mode="add", value=v) for l, nn, _, v in self.ops],
+                                   m.cfg.n_layers, m.cfg.intermediate, lambda l, n: 1.0)
+        gate = oracle.GateState()
+        ca, cb = m.new_cache(), m.new_cache()
+        lg, _, _ = m.forward([dict(cache=ca, tokens=prompt, plan=plan, gate=gate), dict(cache=cb, tokens=prompt)])
+        nxt = [oracle.greedy(lg[0]), oracle.greedy(lg[1])]
+        steps = 0
+        t0 = time.perf_counter()
+        while steps < 8 and time.perf_counter() - t0 < 30.0:
+            lg, _, _ = m.forward([dict(cache=ca, tokens=np.array([nxt[0]], np.uint32), plan=plan, gate=gate,
+                                       frames=True),
+                                  dict(cache=cb, tokens=np.array([nxt[1]], np.uint32))])
+            nxt = [oracle.greedy(lg[0]), oracle.greedy(lg[1])]
+            steps += 1
+        dt = time.perf_counter() - t0
+        return {"value": 2 * steps / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": f"1 steered/unsteered pair, 64-token prompt, {steps} greedy decode steps with capture on the "
+                          f"steered lane, 4B-shaped model (the full 4096-token prefill is ~65 TFLOP per sequence on "
+                          f"the CPU)"}
+
+
+WORKLOADS = {"gdn_decode": GdnDecode, "gqa_decode": GqaDecode, "model_decode": ModelDecode}
 
 
 def make_workload(args):
     cls = WORKLOADS[args.workload]
-    return cls(B=args.batch) if args.batch else cls()
-DEFAULT_WORKLOAD = "gdn_decode"
+    kw = {"B": args.batch} if args.batch else {}
+    if cls is ModelDecode:
+        kw["rank"] = dist_env()[0]
+        if args.prompt:
+            kw["prompt"] = args.prompt
+    return cls(**kw)
+DEFAULT_WORKLOAD = "model_decode"
 
 
 # ------------------------------------------------------------------------------------------------------------
@@ -345,59 +597,24 @@ def run_ours(args):
     evie_b200.lib()
     w = make_workload(args)
     w.setup(dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if w.flush_l2 else None
-    stream = torch.cuda.current_stream()
-
-    for _ in range(max(args.warmup, 3)):
-        w.step()
-    torch.cuda.synchronize()
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    launches = 0
+    w.warmup(max(args.warmup, 3))
+    torch.cuda.synchronize()
+    w._steps = args.steps
     with Clocks(local) as clk:
         barrier()
         t_wall = time.perf_counter()
-        for i in range(args.steps):
-            if flush is not None:
-                flush.fill_(i & 0xFF)
-            ev[i][0].record(stream)
-            launches += w.step()
-            ev[i][1].record(stream)
+        total_ms, launches = w.timed(args.steps)
         barrier()
         t_wall = time.perf_counter() - t_wall
-    step_ms = [a.elapsed_time(b) for a, b in ev]
-    total_ms = sum(step_ms)
     clocks = clk.summary()
-
-    # e2e through the C ABI with host buffers
-    for _ in range(2):
-        w.e2e_step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
-    e0.record(stream)
-    h2d = d2h = 0
-    for i in range(args.steps):
-        if flush is not None:
-            flush.fill_(i & 0xFF)
-        h2d, d2h = w.e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if flush is not None:  # take the flushes out of the e2e time
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        for i in range(args.steps):
-            flush.fill_(i & 0xFF)
-        f1.record(stream)
-        torch.cuda.synchronize()
-        e2e_ms -= f0.elapsed_time(f1)
-
+    e2e_ms, h2d, d2h = w.e2e(args.steps)
     if world > 1:
         t = torch.tensor([total_ms, e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -456,6 +673,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--batch", type=int, default=0, help="override the batch size (small profiling cases)")
+    ap.add_argument("--prompt", type=int, default=0, help="override the prompt length of model_decode")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -32,6 +32,8 @@ SIGNATURES = {
     "evie_last_global_error": (C.c_char_p, []),
     "evie_info": (I, [P, C.POINTER(ModelInfo)]),
     "evie_forward": (I, [P, P, I, I, I, P, P, P, P]),
+    "evie_decode_greedy": (I, [P, P, I, I, P, I, P, P]),
+    "evie_stream": (P, [P]),
     "evie_set_ops": (I, [P, I, P, I]),
     "evie_reset_slot": (I, [P, I]),
     "evie_set_scale": (I, [P, P, SZ]),

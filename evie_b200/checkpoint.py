@@ -138,3 +138,27 @@ def ensure_checkpoint(path: str, cfg: dict, seed: int, device: str = "cpu") -> s
     with open(stamp, "w") as f:
         f.write(want)
     return path
+
+
+def read_tensor(path: str, name: str):
+    """One tensor of a checkpoint directory as a numpy array (bf16 widened to f32)."""
+    import numpy as np
+
+    for fn in sorted(os.listdir(path)):
+        if not fn.endswith(".safetensors"):
+            continue
+        with open(os.path.join(path, fn), "rb") as f:
+            n = struct.unpack("<Q", f.read(8))[0]
+            header = json.loads(f.read(n))
+            if name not in header:
+                continue
+            h = header[name]
+            s, e = h["data_offsets"]
+            f.seek(8 + n + s)
+            raw = f.read(e - s)
+        if h["dtype"] == "BF16":
+            return (np.frombuffer(raw, np.uint16).astype(np.uint32) << 16).view(np.float32).reshape(h["shape"])
+        if h["dtype"] == "F32":
+            return np.frombuffer(raw, np.float32).reshape(h["shape"])
+        raise ValueError(f"{name}: dtype {h['dtype']}")
+    raise KeyError(name)

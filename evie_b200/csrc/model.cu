@@ -190,6 +190,8 @@ struct evie_ctx {
   SegInfo* d_segs = nullptr;
   RowInfo* h_rows = nullptr;  // pinned
   SegInfo* h_segs = nullptr;  // pinned
+  uint32_t* hist = nullptr;   // device token history of evie_decode_greedy
+  size_t hist_cap = 0;
   std::string err;
 
   template <typename T>
@@ -459,10 +461,9 @@ evie_status gemm(evie_ctx* c, const __nv_bfloat16* W, int M, int K, const __nv_b
   return EVIE_OK;
 }
 
-evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_logits, int capture, float* logits,
-                         int8_t* frames, uint16_t* resid, uint32_t* next_tokens) {
+// gpu/mod.rs:616-634: limits, then the row and segment tables uploaded for the kernels.
+evie_status prepare_rows(evie_ctx* c, const evie_seq* seqs, int nseq, int* R_out, int* max_ctx_out) {
   auto& s = c->s;
-  // gpu/mod.rs:616-630: limits and row/segment tables
   EVIE_ARG(nseq >= 1 && nseq <= c->slots, "forward: 1..=%d sequences per call, got %d", c->slots, nseq);
   int R = 0, max_ctx_rows = 0;
   std::vector<char> used(c->slots, 0);
@@ -486,10 +487,17 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
       c->h_rows[r++] = RowInfo{q.slot, q.pos0 + t, (int)q.tokens[t], i};
     }
   }
-  cudaStream_t st = c->stream;
-  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_rows, c->h_rows, R * sizeof(RowInfo), cudaMemcpyHostToDevice, st));
-  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_segs, c->h_segs, nseq * sizeof(SegInfo), cudaMemcpyHostToDevice, st));
+  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_rows, c->h_rows, R * sizeof(RowInfo), cudaMemcpyHostToDevice, c->stream));
+  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_segs, c->h_segs, nseq * sizeof(SegInfo), cudaMemcpyHostToDevice, c->stream));
+  *R_out = R;
+  *max_ctx_out = max_ctx_rows;
+  return EVIE_OK;
+}
 
+// model.rs:230-267: embedding, every layer, and the final norm of each sequence's last row (into X2).
+evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int capture) {
+  auto& s = c->s;
+  cudaStream_t st = c->stream;
   int8_t* fr = capture ? c->frames : nullptr;
   uint16_t* rs = capture ? c->resid : nullptr;
   const size_t cs_slot = (size_t)std::max(c->n_lin, 1) * (s.K - 1) * s.conv_dim;
@@ -546,9 +554,23 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
                             li, s.L, st));
     }
   }
-  // model.rs:271-283: LM head on the last row of every sequence, greedy id on device
-  TRY(gemm(c, c->lm_head, s.V, s.d, c->X2, nseq, c->L2));
-  TRY(evie::k_logits_argmax(c->L2, nseq, s.V, want_logits ? c->logits : nullptr, c->best, c->next, st));
+  return EVIE_OK;
+}
+
+// model.rs:271-283: LM head on the last row of every sequence; greedy id (sampling.rs:60-62) on device.
+evie_status enqueue_head(evie_ctx* c, int nseq, bool want_logits) {
+  TRY(gemm(c, c->lm_head, c->s.V, c->s.d, c->X2, nseq, c->L2));
+  return evie::k_logits_argmax(c->L2, nseq, c->s.V, want_logits ? c->logits : nullptr, c->best, c->next, c->stream);
+}
+
+evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_logits, int capture, float* logits,
+                         int8_t* frames, uint16_t* resid, uint32_t* next_tokens) {
+  auto& s = c->s;
+  int R = 0, max_ctx_rows = 0;
+  TRY(prepare_rows(c, seqs, nseq, &R, &max_ctx_rows));
+  cudaStream_t st = c->stream;
+  TRY(enqueue_layers(c, R, nseq, max_ctx_rows, capture));
+  if (want_logits || next_tokens) TRY(enqueue_head(c, nseq, want_logits != 0));
   if (want_logits && logits)
     EVIE_CUDA_TRY(cudaMemcpyAsync(logits, c->logits, (size_t)nseq * s.V * 4, cudaMemcpyDeviceToHost, st));
   if (next_tokens) EVIE_CUDA_TRY(cudaMemcpyAsync(next_tokens, c->next, nseq * 4, cudaMemcpyDeviceToHost, st));
@@ -560,11 +582,56 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
   return EVIE_OK;
 }
 
+// The decode loop of worker.rs:442-526 with greedy sampling, kept on the device: each step feeds every sequence the
+// greedy token of the previous step at the next position, with no host round trip between steps.
+evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int steps, uint32_t* out_tokens,
+                               int capture, int8_t* frames, uint16_t* resid) {
+  auto& s = c->s;
+  EVIE_ARG(steps >= 1, "decode: steps must be >= 1");
+  for (int i = 0; i < nseq; i++) {
+    EVIE_ARG(seqs[i].n_tokens == 1, "decode: every sequence carries exactly one (first) token");
+    EVIE_ARG((long)seqs[i].pos0 + steps <= c->max_ctx, "decode: %d steps from position %d exceed max_ctx %d", steps,
+             seqs[i].pos0, c->max_ctx);
+  }
+  int R = 0, max_ctx_rows = 0;
+  TRY(prepare_rows(c, seqs, nseq, &R, &max_ctx_rows));
+  const size_t need = (size_t)steps * nseq;
+  if (c->hist_cap < need) {
+    if (c->hist) {
+      EVIE_CUDA_TRY(cudaStreamSynchronize(c->stream));
+      cudaFree(c->hist);
+      c->hist = nullptr;
+    }
+    if (cudaMalloc(&c->hist, need * 4) != cudaSuccess) {
+      cudaGetLastError();
+      return evie::fail(EVIE_ERR_OOM, "decode: cannot allocate the token history");
+    }
+    c->hist_cap = need;
+  }
+  cudaStream_t st = c->stream;
+  for (int i = 0; i < steps; i++) {
+    if (i > 0) TRY(evie::k_advance_rows(c->d_rows, nseq, c->next, st));
+    TRY(enqueue_layers(c, R, nseq, max_ctx_rows + i, capture));
+    TRY(enqueue_head(c, nseq, false));
+    EVIE_CUDA_TRY(cudaMemcpyAsync(c->hist + (size_t)i * nseq, c->next, nseq * 4, cudaMemcpyDeviceToDevice, st));
+    if (capture && frames)
+      EVIE_CUDA_TRY(cudaMemcpyAsync(frames + (size_t)i * nseq * s.L * s.n, c->frames, (size_t)nseq * s.L * s.n,
+                                    cudaMemcpyDeviceToHost, st));
+    if (capture && resid)
+      EVIE_CUDA_TRY(cudaMemcpyAsync(resid + (size_t)i * nseq * s.L * s.d, c->resid, (size_t)nseq * s.L * s.d * 2,
+                                    cudaMemcpyDeviceToHost, st));
+  }
+  if (out_tokens) EVIE_CUDA_TRY(cudaMemcpyAsync(out_tokens, c->hist, need * 4, cudaMemcpyDeviceToHost, st));
+  EVIE_CUDA_TRY(cudaStreamSynchronize(st));
+  return EVIE_OK;
+}
+
 void destroy(evie_ctx* c) {
   if (!c) return;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   for (void* p : c->allocs) cudaFree(p);
+  if (c->hist) cudaFree(c->hist);
   if (c->h_rows) cudaFreeHost(c->h_rows);
   if (c->h_segs) cudaFreeHost(c->h_segs);
   if (c->blas) cublasDestroy(c->blas);
@@ -642,6 +709,16 @@ evie_status evie_forward(evie_ctx* c, const evie_seq* seqs, int n_seqs, int want
   if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
   return remember(c, forward_impl(c, seqs, n_seqs, want_logits, capture, logits, frames, resid, next_tokens));
 }
+
+evie_status evie_decode_greedy(evie_ctx* c, const evie_seq* seqs, int n_seqs, int steps, uint32_t* out_tokens,
+                               int capture, int8_t* frames, uint16_t* resid) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_decode_greedy: null context");
+  if (!seqs) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_decode_greedy: null sequences"));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  return remember(c, decode_greedy_impl(c, seqs, n_seqs, steps, out_tokens, capture, frames, resid));
+}
+
+void* evie_stream(const evie_ctx* c) { return c ? (void*)c->stream : nullptr; }
 
 // gpu/mod.rs:555-565; ops are kept in the caller's order within each layer (Plan::apply order).
 evie_status evie_set_ops(evie_ctx* c, int slot, const evie_op* ops, int n_ops) {

@@ -371,7 +371,20 @@ __global__ void argmax_finish_kernel(unsigned long long* best, uint32_t* next_to
   best[s] = 0;
 }
 
+__global__ void advance_rows_kernel(RowInfo* rows, int nseq, const uint32_t* next) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= nseq) return;
+  rows[s].pos += 1;
+  rows[s].token = (int)next[s];
+}
+
 }  // namespace
+
+evie_status k_advance_rows(RowInfo* rows, int nseq, const uint32_t* next, cudaStream_t st) {
+  advance_rows_kernel<<<(nseq + 127) / 128, 128, 0, st>>>(rows, nseq, next);
+  EVIE_CHECK_LAUNCH("advance_rows_kernel");
+  return EVIE_OK;
+}
 
 evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed, float* x, const float* gain,
                          float eps, int d, __nv_bfloat16* X2, cudaStream_t st) {

@@ -73,4 +73,7 @@ evie_status k_swiglu(const float* Y2, int ldy, int R, const RowInfo* rows, int l
 evie_status k_logits_argmax(const float* L2, int nseg, int V, float* logits, unsigned long long* best,
                             uint32_t* next_tokens, cudaStream_t st);
 
+// Decode loop step: row s (one per sequence) moves to the next position and takes the greedy token next[s].
+evie_status k_advance_rows(RowInfo* rows, int nseq, const uint32_t* next, cudaStream_t st);
+
 }  // namespace evie

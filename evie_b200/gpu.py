@@ -84,6 +84,25 @@ class GpuModel:
                                        p(o.resid) if capture else None, p(o.next_tokens)))
         return o
 
+    def decode_greedy(self, seqs, steps: int, capture: bool = False, frames=None, resid=None) -> np.ndarray:
+        """evie_decode_greedy: `steps` greedy steps on the device. Returns the tokens [steps, n_seqs]."""
+        n = len(seqs)
+        arr = (capi.Seq * n)()
+        keep = []
+        for i, s in enumerate(seqs):
+            t = np.ascontiguousarray(s.tokens, dtype=np.uint32)
+            keep.append(t)
+            arr[i] = capi.Seq(s.slot, s.pos0, t.ctypes.data, t.size)
+        out = np.empty((steps, n), np.uint32)
+        p = lambda a: a.ctypes.data if a is not None else None  # noqa: E731
+        self._check(lib().evie_decode_greedy(self._h, arr, n, steps, out.ctypes.data, int(capture), p(frames),
+                                             p(resid)))
+        return out
+
+    def stream_ptr(self) -> int:
+        """The cudaStream_t the context enqueues its work on (for CUDA-event timing)."""
+        return lib().evie_stream(self._h) or 0
+
     def set_ops(self, slot: int, ops):
         """ops: iterable of (layer, neuron, mode 1/2/3 or 'add'/'mul'/'set', value)."""
         ops = list(ops)

@@ -81,6 +81,17 @@ EVIE_API evie_status evie_info(const evie_ctx* ctx, evie_model_info* out);
 EVIE_API evie_status evie_forward(evie_ctx* ctx, const evie_seq* seqs, int n_seqs, int want_logits, int capture, float* logits,
                          int8_t* frames, uint16_t* resid, uint32_t* next_tokens);
 
+/* The greedy decode loop of evie's worker (crates/evie/src/worker.rs:442-526 with temperature 0) kept on the
+ * device: every sequence carries its first token (n_tokens = 1) at pos0; step i runs the model on each sequence's
+ * greedy token of step i-1 at position pos0 + i, with no host round trip between steps.
+ *   out_tokens  [steps][n_seqs] host, the greedy token produced by each step (may be NULL);
+ *   frames      [steps][n_seqs][layers*intermediate] i8 host, captured activations per step (if capture);
+ *   resid       [steps][n_seqs][layers*hidden] f16 bits host (if capture). */
+EVIE_API evie_status evie_decode_greedy(evie_ctx* ctx, const evie_seq* seqs, int n_seqs, int steps,
+                                        uint32_t* out_tokens, int capture, int8_t* frames, uint16_t* resid);
+/* The CUDA stream (cudaStream_t) all of the context's work is enqueued on, for timing with CUDA events. */
+EVIE_API void* evie_stream(const evie_ctx* ctx);
+
 /* Replaces a slot's steering ops (GpuModel::set_ops, gpu/mod.rs:556). Ops apply in the given order. */
 EVIE_API evie_status evie_set_ops(evie_ctx* ctx, int slot, const evie_op* ops, int n_ops);
 /* Zeroes a slot's recurrent and conv state (GpuModel::reset_slot, gpu/mod.rs:568). */

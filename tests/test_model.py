@@ -160,3 +160,37 @@ def test_limits_are_reported(tiny_ckpt, cuda):
     with pytest.raises(EvieError, match="out of range"):
         m.forward([GpuSeq(0, 0, np.array([5000], np.uint32))])
     m.close()
+
+
+@pytest.mark.gpu
+def test_device_decode_loop_matches_step_calls(tiny_ckpt, cuda):
+    """evie_decode_greedy (steps fed back on the device) gives the tokens and captures of per-step evie_forward."""
+    from evie_b200.gpu import GpuSeq
+
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, 2048, n).astype(np.uint32) for n in (17, 30, 5)]
+    results = []
+    for mode in ("loop", "calls"):
+        m = _gpu_model(tiny_ckpt, False, max_ctx=128, slots=3, max_rows=64)
+        m.set_ops(0, [(2, 9, "add", 1.25)])
+        out = m.forward([GpuSeq(i, 0, p) for i, p in enumerate(prompts)], want_logits=False)
+        first = out.next_tokens.copy()
+        seqs = [GpuSeq(i, len(p), first[i:i + 1]) for i, p in enumerate(prompts)]
+        L, n = m.layers, m.neurons
+        if mode == "loop":
+            frames = np.zeros((6, 3, L * n), np.int8)
+            toks = m.decode_greedy(seqs, 6, capture=True, frames=frames)
+        else:
+            toks, fr = [], []
+            cur = first.copy()
+            for step in range(6):
+                o = m.forward([GpuSeq(i, len(p) + step, cur[i:i + 1]) for i, p in enumerate(prompts)],
+                              want_logits=False, capture=True)
+                cur = o.next_tokens.copy()
+                toks.append(cur)
+                fr.append(o.frames.copy())
+            toks, frames = np.stack(toks), np.stack(fr)
+        results.append((toks, frames))
+        m.close()
+    assert np.array_equal(results[0][0], results[1][0])
+    assert np.array_equal(results[0][1], results[1][1])
