@@ -34,6 +34,8 @@ SIGNATURES = {
     "evie_forward": (I, [P, P, I, I, I, P, P, P, P]),
     "evie_decode_greedy": (I, [P, P, I, I, P, I, P, P]),
     "evie_stream": (P, [P]),
+    "evie_profile": (I, [P, I]),
+    "evie_profile_read": (I, [P, I, C.POINTER(C.c_char_p), C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
     "evie_set_ops": (I, [P, I, P, I]),
     "evie_reset_slot": (I, [P, I]),
     "evie_set_scale": (I, [P, P, SZ]),

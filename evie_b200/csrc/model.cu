@@ -143,6 +143,11 @@ struct Layer {
 
 }  // namespace
 
+// Kernel groups timed by the optional profiling mode (evie_profile).
+enum ProfCat { P_GEMM = 0, P_LMHEAD, P_CONV, P_MIXER, P_ATTN_PREP, P_ATTN, P_NORM, P_SWIGLU, P_OTHER, P_COUNT };
+const char* const kProfNames[P_COUNT] = {"projection_gemm", "lm_head_gemm", "conv", "gdn_mixer", "attn_prep",
+                                         "gqa_attention", "add_norm", "swiglu", "other"};
+
 struct evie_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -192,6 +197,22 @@ struct evie_ctx {
   SegInfo* h_segs = nullptr;  // pinned
   uint32_t* hist = nullptr;   // device token history of evie_decode_greedy
   size_t hist_cap = 0;
+  // profiling: event pairs per kernel group, resolved after each synchronising call
+  bool prof = false;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_pending;
+  std::vector<cudaEvent_t> prof_free;
+  double prof_ms[P_COUNT] = {0};
+  int64_t prof_n[P_COUNT] = {0};
+  cudaEvent_t prof_event() {
+    if (!prof_free.empty()) {
+      cudaEvent_t e = prof_free.back();
+      prof_free.pop_back();
+      return e;
+    }
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    return e;
+  }
   std::string err;
 
   template <typename T>
@@ -209,6 +230,40 @@ struct evie_ctx {
 };
 
 namespace {
+
+// Brackets one kernel group with CUDA events on the context's stream when profiling is on.
+struct ProfScope {
+  evie_ctx* c;
+  int cat;
+  cudaEvent_t a = nullptr;
+  ProfScope(evie_ctx* c_, int cat_) : c(c_), cat(cat_) {
+    if (c->prof) {
+      a = c->prof_event();
+      cudaEventRecord(a, c->stream);
+    }
+  }
+  ~ProfScope() {
+    if (c->prof) {
+      cudaEvent_t b = c->prof_event();
+      cudaEventRecord(b, c->stream);
+      c->prof_pending.push_back({cat, {a, b}});
+    }
+  }
+};
+
+void prof_resolve(evie_ctx* c) {
+  for (auto& p : c->prof_pending) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, p.second.first, p.second.second);
+    c->prof_ms[p.first] += ms;
+    c->prof_n[p.first] += 1;
+    c->prof_free.push_back(p.second.first);
+    c->prof_free.push_back(p.second.second);
+  }
+  c->prof_pending.clear();
+}
+
+#define PROF(cat) ProfScope prof_scope_##__LINE__(c, cat)
 
 #define TRY(expr)                        \
   do {                                   \
@@ -505,26 +560,36 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
   const size_t kv_layer = (size_t)c->slots * c->pages_per_slot * s.nkv * kPage * s.hd;
   evie::SteerTables steer{c->ops, c->op_range, kMaxOps};
 
-  TRY(evie::k_embed_norm(c->d_rows, R, c->embed, c->x, c->layers[0].ln1, s.eps, s.d, c->X2, st));
+  { PROF(P_NORM); TRY(evie::k_embed_norm(c->d_rows, R, c->embed, c->x, c->layers[0].ln1, s.eps, s.d, c->X2, st)); }
   for (int li = 0; li < s.L; li++) {
     Layer& L = c->layers[li];
     if (L.kind == 0) {
-      TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2));
+      { PROF(P_GEMM); TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2)); }
       float* cs = c->conv_state + (size_t)L.idx * (s.K - 1) * s.conv_dim;
-      TRY(evie::k_conv_silu_norm(c->Y2, s.in_dn, R, c->d_rows, c->d_segs, cs, cs_slot, L.conv, s, c->act, st));
-      TRY(evie::k_conv_state_update(c->Y2, s.in_dn, R, c->d_segs, nseq, cs, cs_slot, s, st));
+      {
+        PROF(P_CONV);
+        TRY(evie::k_conv_silu_norm(c->Y2, s.in_dn, R, c->d_rows, c->d_segs, cs, cs_slot, L.conv, s, c->act, st));
+        TRY(evie::k_conv_state_update(c->Y2, s.in_dn, R, c->d_segs, nseq, cs, cs_slot, s, st));
+      }
       float* rsb = c->rec_state + (size_t)L.idx * s.hv * s.dk * s.dv;
-      TRY(evie::k_gdn_mixer(c->act, c->Y2, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm, s,
-                            c->X2, st));
-      TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2));
+      {
+        PROF(P_MIXER);
+        TRY(evie::k_gdn_mixer(c->act, c->Y2, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm,
+                              s, c->X2, st));
+      }
+      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2)); }
     } else {
-      TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2));
+      { PROF(P_GEMM); TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2)); }
       const float scale = 1.0f / sqrtf((float)s.hd);
       if (c->kv_f32) {
         float* kc = (float*)c->k_cache + (size_t)L.idx * kv_layer;
         float* vc = (float*)c->v_cache + (size_t)L.idx * kv_layer;
-        TRY(evie::k_attn_prep<float>(c->Y2, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s, c->q_rot, kc,
-                                     vc, c->page_table, c->pages_per_slot, kPage, st));
+        {
+          PROF(P_ATTN_PREP);
+          TRY(evie::k_attn_prep<float>(c->Y2, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s, c->q_rot,
+                                       kc, vc, c->page_table, c->pages_per_slot, kPage, st));
+        }
+        PROF(P_ATTN);
         TRY(evie::launch_gqa_model<float>(c->q_rot, c->Y2, (size_t)R * s.in_at, s.in_at, c->X2,
                                           (size_t)R * s.nh * s.hd, c->d_rows, R, c->page_table, c->pages_per_slot,
                                           kc, vc, s.nh, s.nkv, kPage, max_ctx_rows, scale, c->attn_scratch, c->max_rows,
@@ -532,21 +597,29 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
       } else {
         auto* kc = (__nv_bfloat16*)c->k_cache + (size_t)L.idx * kv_layer;
         auto* vc = (__nv_bfloat16*)c->v_cache + (size_t)L.idx * kv_layer;
-        TRY(evie::k_attn_prep<__nv_bfloat16>(c->Y2, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s,
-                                             c->q_rot, kc, vc, c->page_table, c->pages_per_slot, kPage, st));
+        {
+          PROF(P_ATTN_PREP);
+          TRY(evie::k_attn_prep<__nv_bfloat16>(c->Y2, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s,
+                                               c->q_rot, kc, vc, c->page_table, c->pages_per_slot, kPage, st));
+        }
+        PROF(P_ATTN);
         TRY(evie::launch_gqa_model<__nv_bfloat16>(c->q_rot, c->Y2, (size_t)R * s.in_at, s.in_at, c->X2,
                                                   (size_t)R * s.nh * s.hd, c->d_rows, R, c->page_table,
                                                   c->pages_per_slot, kc, vc, s.nh, s.nkv, kPage, max_ctx_rows, scale,
                                                   c->attn_scratch, c->max_rows, st));
       }
-      TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2));
+      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2)); }
     }
     // model.rs:246-248: residual add after the mixer, then the pre-MLP norm
-    TRY(evie::k_add_norm(c->x, c->Y2, s.d, R, L.ln2, s.eps, s.d, c->X2, nullptr, 0, s.L, st));
-    TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2));
-    TRY(evie::k_swiglu(c->Y2, 2 * s.n, R, c->d_rows, li, s, steer, c->scale, fr, c->track ? c->maxbuf : nullptr,
-                       c->X2, st));
-    TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2));
+    { PROF(P_NORM); TRY(evie::k_add_norm(c->x, c->Y2, s.d, R, L.ln2, s.eps, s.d, c->X2, nullptr, 0, s.L, st)); }
+    { PROF(P_GEMM); TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2)); }
+    {
+      PROF(P_SWIGLU);
+      TRY(evie::k_swiglu(c->Y2, 2 * s.n, R, c->d_rows, li, s, steer, c->scale, fr, c->track ? c->maxbuf : nullptr,
+                         c->X2, st));
+    }
+    { PROF(P_GEMM); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2)); }
+    PROF(P_NORM);
     if (li + 1 < s.L) {
       TRY(evie::k_add_norm(c->x, c->Y2, s.d, R, c->layers[li + 1].ln1, s.eps, s.d, c->X2, rs, li, s.L, st));
     } else {
@@ -559,7 +632,8 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
 
 // model.rs:271-283: LM head on the last row of every sequence; greedy id (sampling.rs:60-62) on device.
 evie_status enqueue_head(evie_ctx* c, int nseq, bool want_logits) {
-  TRY(gemm(c, c->lm_head, c->s.V, c->s.d, c->X2, nseq, c->L2));
+  { PROF(P_LMHEAD); TRY(gemm(c, c->lm_head, c->s.V, c->s.d, c->X2, nseq, c->L2)); }
+  PROF(P_OTHER);
   return evie::k_logits_argmax(c->L2, nseq, c->s.V, want_logits ? c->logits : nullptr, c->best, c->next, c->stream);
 }
 
@@ -579,6 +653,7 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
   if (capture && resid)
     EVIE_CUDA_TRY(cudaMemcpyAsync(resid, c->resid, (size_t)R * s.L * s.d * 2, cudaMemcpyDeviceToHost, st));
   EVIE_CUDA_TRY(cudaStreamSynchronize(st));
+  prof_resolve(c);
   return EVIE_OK;
 }
 
@@ -610,7 +685,10 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
   }
   cudaStream_t st = c->stream;
   for (int i = 0; i < steps; i++) {
-    if (i > 0) TRY(evie::k_advance_rows(c->d_rows, nseq, c->next, st));
+    if (i > 0) {
+      PROF(P_OTHER);
+      TRY(evie::k_advance_rows(c->d_rows, nseq, c->next, st));
+    }
     TRY(enqueue_layers(c, R, nseq, max_ctx_rows + i, capture));
     TRY(enqueue_head(c, nseq, false));
     EVIE_CUDA_TRY(cudaMemcpyAsync(c->hist + (size_t)i * nseq, c->next, nseq * 4, cudaMemcpyDeviceToDevice, st));
@@ -623,6 +701,7 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
   }
   if (out_tokens) EVIE_CUDA_TRY(cudaMemcpyAsync(out_tokens, c->hist, need * 4, cudaMemcpyDeviceToHost, st));
   EVIE_CUDA_TRY(cudaStreamSynchronize(st));
+  prof_resolve(c);
   return EVIE_OK;
 }
 
@@ -632,6 +711,11 @@ void destroy(evie_ctx* c) {
   if (c->stream) cudaStreamSynchronize(c->stream);
   for (void* p : c->allocs) cudaFree(p);
   if (c->hist) cudaFree(c->hist);
+  for (auto& p : c->prof_pending) {
+    cudaEventDestroy(p.second.first);
+    cudaEventDestroy(p.second.second);
+  }
+  for (auto e : c->prof_free) cudaEventDestroy(e);
   if (c->h_rows) cudaFreeHost(c->h_rows);
   if (c->h_segs) cudaFreeHost(c->h_segs);
   if (c->blas) cublasDestroy(c->blas);
@@ -719,6 +803,21 @@ evie_status evie_decode_greedy(evie_ctx* c, const evie_seq* seqs, int n_seqs, in
 }
 
 void* evie_stream(const evie_ctx* c) { return c ? (void*)c->stream : nullptr; }
+
+evie_status evie_profile(evie_ctx* c, int on) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_profile: null context");
+  c->prof = on != 0;
+  for (int i = 0; i < P_COUNT; i++) c->prof_ms[i] = 0.0, c->prof_n[i] = 0;
+  return EVIE_OK;
+}
+
+int evie_profile_read(const evie_ctx* c, int i, const char** name, double* ms, int64_t* launches) {
+  if (!c || i < 0 || i >= P_COUNT) return 0;
+  if (name) *name = kProfNames[i];
+  if (ms) *ms = c->prof_ms[i];
+  if (launches) *launches = c->prof_n[i];
+  return P_COUNT;
+}
 
 // gpu/mod.rs:555-565; ops are kept in the caller's order within each layer (Plan::apply order).
 evie_status evie_set_ops(evie_ctx* c, int slot, const evie_op* ops, int n_ops) {

@@ -99,6 +99,22 @@ class GpuModel:
                                              p(resid)))
         return out
 
+    def profile(self, on: bool):
+        self._check(lib().evie_profile(self._h, int(on)))
+
+    def profile_read(self) -> dict:
+        """{group: (ms, launches)} accumulated since profiling was switched on."""
+        out = {}
+        i = 0
+        while True:
+            name, ms, n = C.c_char_p(), C.c_double(), C.c_int64()
+            cnt = lib().evie_profile_read(self._h, i, C.byref(name), C.byref(ms), C.byref(n))
+            if i >= cnt:
+                break
+            out[name.value.decode()] = (ms.value, n.value)
+            i += 1
+        return out
+
     def stream_ptr(self) -> int:
         """The cudaStream_t the context enqueues its work on (for CUDA-event timing)."""
         return lib().evie_stream(self._h) or 0

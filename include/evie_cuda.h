@@ -92,6 +92,14 @@ EVIE_API evie_status evie_decode_greedy(evie_ctx* ctx, const evie_seq* seqs, int
 /* The CUDA stream (cudaStream_t) all of the context's work is enqueued on, for timing with CUDA events. */
 EVIE_API void* evie_stream(const evie_ctx* ctx);
 
+/* Profiling mode: when on, every kernel group of later calls is bracketed by CUDA events on the context's stream
+ * and its device time accumulated per group (projection GEMMs, LM head, conv, DeltaNet mixer, attention prep,
+ * attention, add+norm, SwiGLU, other). Turning it on or off clears the totals. */
+EVIE_API evie_status evie_profile(evie_ctx* ctx, int on);
+/* Group i's name, accumulated milliseconds and number of bracketed launches; returns the number of groups
+ * (0 when i is out of range). */
+EVIE_API int evie_profile_read(const evie_ctx* ctx, int i, const char** name, double* ms, int64_t* launches);
+
 /* Replaces a slot's steering ops (GpuModel::set_ops, gpu/mod.rs:556). Ops apply in the given order. */
 EVIE_API evie_status evie_set_ops(evie_ctx* ctx, int slot, const evie_op* ops, int n_ops);
 /* Zeroes a slot's recurrent and conv state (GpuModel::reset_slot, gpu/mod.rs:568). */
