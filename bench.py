@@ -460,7 +460,8 @@ class ModelDecode(Workload):
             "conv": B * n_lin * (K - 1) * conv_dim * 4 * 2,
             "gqa_attention": B * n_full * nkv * hd * 2 * 2 * ctx,
             "attn_prep": B * n_full * nkv * hd * 2 * 2,
-            "swiglu": B * L * (n + n // 1 * 0),
+            # gate and up planes read, the split down_proj operand and the i8 frame written
+            "swiglu": B * L * n * (2 * 2 * 4 + 2 * 2 + 1),
         }
 
     def profile_pass(self, k):
@@ -478,7 +479,7 @@ class ModelDecode(Workload):
                 continue
             per = ms / k
             e = {"ms_per_step": per, "share": ms / total, "launch_groups_per_step": n / k}
-            if name in gb and gb[name] > 0 and name != "swiglu":
+            if name in gb and gb[name] > 0:
                 e["algorithmic_bytes"] = gb[name]
                 e["gbs"] = gb[name] / (per / 1000.0) / 1e9
             out[name] = e

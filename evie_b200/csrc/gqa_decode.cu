@@ -16,6 +16,7 @@
 //   * splits are merged in-kernel: every CTA publishes (m, l, O) for its split, takes a ticket with atomicAdd,
 //     and the CTA that takes the last ticket combines them (no spin-wait, no second launch). A sequence that fits
 //     one split writes its output directly.
+#include <cstdlib>
 #include <map>
 #include <mutex>
 
@@ -73,8 +74,9 @@ struct IsoIO {
   int Hq, max_pages;
   __device__ __forceinline__ int ctx_of(int b) const { return ctx_lens[b]; }
   __device__ __forceinline__ const int32_t* page_row(int b) const { return page_table + (size_t)b * max_pages; }
-  __device__ __forceinline__ void load_q(int b, int h, int lane, float* f) const {
-    bf16x8_to_f32(*reinterpret_cast<const uint4*>(q + ((size_t)b * Hq + h) * kHD + lane * 8), f);
+  __device__ __forceinline__ void load_q(int b, int h, int lane, float* f) const { load_q8(b, h, lane * 8, f); }
+  __device__ __forceinline__ void load_q8(int b, int h, int d0, float* f) const {
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(q + ((size_t)b * Hq + h) * kHD + d0), f);
   }
   __device__ __forceinline__ float gate(int b, int h, int d) const {
     return __bfloat162float(gate_logits[((size_t)b * Hq + h) * kHD + d]);
@@ -98,8 +100,9 @@ struct ModelIO {
   __device__ __forceinline__ const int32_t* page_row(int b) const {
     return page_table + (size_t)rows[b].slot * pages_per_slot;
   }
-  __device__ __forceinline__ void load_q(int b, int h, int lane, float* f) const {
-    const float4* p = reinterpret_cast<const float4*>(q_rot + ((size_t)b * Hq + h) * kHD + lane * 8);
+  __device__ __forceinline__ void load_q(int b, int h, int lane, float* f) const { load_q8(b, h, lane * 8, f); }
+  __device__ __forceinline__ void load_q8(int b, int h, int d0, float* f) const {
+    const float4* p = reinterpret_cast<const float4*>(q_rot + ((size_t)b * Hq + h) * kHD + d0);
     const float4 a = p[0], c = p[1];
     f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = c.x; f[5] = c.y; f[6] = c.z; f[7] = c.w;
   }
@@ -348,6 +351,300 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (tid == 0) scr.tickets[bh] = 0;  // ready for the next call
 }
 
+
+// ---------------------------------------------------------------------------------------------------------------
+// Tensor-core variant for bf16 KV and GQA group 4 (every Qwen3.5 size): scores and P.V on mma.sync m16n8k16, with
+// K and V loaded straight from HBM into the MMA operand registers by 16-byte loads. The 8 columns of each MMA are the
+// 4 query heads x {hi, lo}: q (and later p) is split into two bf16 halves (x = hi + lo, 16 significant bits), so the
+// products match an fp32 computation on the bf16 K/V to ~2^-16 while no MMA column is padding.
+//   QK:  S^T[16 tokens][8] += K[16 tokens][16 dims] . Q^T[16 dims][8]     (16 MMAs per 16 tokens)
+//   PV:  O^T[16 dims][8]   += V^T[16 dims][16 tokens] . P^T[16 tokens][8] (16 MMAs per 16 tokens)
+// Head dims are permuted inside each MMA so that a lane's operand registers come from contiguous 16-byte runs:
+//   QK k-block 2p+e, slots {2c,2c+1 | 2c+8,2c+9} <-> dims 32p + 8c + 4e + {0,1 | 2,3} (c = lane % 4);
+//   PV m-tile i, rows {g | g+8} <-> dims {16g + i | 128 + 16g + i}                      (g = lane / 4).
+// One CTA = 8 warps x 64 tokens = one 512-token split of one (sequence, KV head); the softmax is exact per warp
+// (two passes over its 64 scores held in registers), warps are merged in shared memory, splits as before.
+__device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ uint4 ldg_stream128(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t word_of(const uint4& u, int i) {
+  return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w;
+}
+
+constexpr int kMmaTiles = kTokPerWarp / 16;  // 4 tiles of 16 tokens per warp
+
+template <class IO>
+__global__ void __launch_bounds__(kThreads, 2)
+    gqa_decode_mma_kernel(IO io, const __nv_bfloat16* __restrict__ kp, const __nv_bfloat16* __restrict__ vp, int Hkv,
+                          int page_size, int max_pages, float scale, Scratch scr) {
+  constexpr int GROUP = 4;
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int ctx = min(io.ctx_of(b), max_pages * page_size);
+  const int n_splits = (ctx + kSplit - 1) / kSplit;
+  const int h0 = kvh * GROUP;
+  if (ctx <= 0) {
+    if (split == 0)
+      for (int i = tid; i < GROUP * kHD; i += kThreads) io.store(b, h0 + i / kHD, i % kHD, 0.0f);
+    return;
+  }
+  if (split >= n_splits) return;
+
+  __shared__ __align__(16) __nv_bfloat16 sP[kWarps][8][16];
+  __shared__ float sO[kWarps][GROUP][kHD];
+  __shared__ float sM[kWarps][GROUP], sL[kWarps][GROUP];
+  __shared__ float s_w[kWarps][GROUP];
+  __shared__ float s_fin[GROUP][2];
+  __shared__ int s_last;
+
+  // Q^T fragments: column n = g is head g % 4, half g / 4 (0 = hi, 1 = lo), pre-scaled into the log2 domain.
+  uint32_t qb0[16], qb1[16];
+  {
+    const int head = h0 + (g & 3);
+    const bool lo = g >= 4;
+    const float f = scale * kLog2e;
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+      float v[8];
+      io.load_q8(b, head, 32 * p + 8 * c, v);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float x = v[j] * f;
+        v[j] = lo ? x - bf16_round(x) : x;
+      }
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        qb0[2 * p + e] = pack_bf16x2(v[4 * e + 0], v[4 * e + 1]);
+        qb1[2 * p + e] = pack_bf16x2(v[4 * e + 2], v[4 * e + 3]);
+      }
+    }
+  }
+  const int32_t* pt = io.page_row(b);
+  auto row = [&](const __nv_bfloat16* pages, int j) {
+    const int page = pt[j / page_size];
+    return pages + (((size_t)page * Hkv + kvh) * page_size + (j % page_size)) * kHD;
+  };
+  const int wt0 = split * kSplit + warp * kTokPerWarp;
+
+  // ---- scores: lane holds heads hh, hh+1 (hh = 2 (c & 1)) for tokens g and g+8 of each tile
+  float sc[kMmaTiles][4];
+#pragma unroll
+  for (int t = 0; t < kMmaTiles; t++) {
+    const int jA = wt0 + 16 * t + g, jB = jA + 8;
+    const __nv_bfloat16* pa = jA < ctx ? row(kp, jA) : nullptr;
+    const __nv_bfloat16* pb = jB < ctx ? row(kp, jB) : nullptr;
+    uint4 ka[8], kb[8];
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+      ka[p] = pa ? ldg_stream128(pa + 32 * p + 8 * c) : make_uint4(0, 0, 0, 0);
+      kb[p] = pb ? ldg_stream128(pb + 32 * p + 8 * c) : make_uint4(0, 0, 0, 0);
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int p = 0; p < 8; p++)
+#pragma unroll
+      for (int e = 0; e < 2; e++)
+        mma_bf16_16816(acc, word_of(ka[p], 2 * e), word_of(kb[p], 2 * e), word_of(ka[p], 2 * e + 1),
+                       word_of(kb[p], 2 * e + 1), qb0[2 * p + e], qb1[2 * p + e]);
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 2);  // hi + lo columns
+    sc[t][0] = jA < ctx ? acc[0] : -INFINITY;
+    sc[t][1] = jA < ctx ? acc[1] : -INFINITY;
+    sc[t][2] = jB < ctx ? acc[2] : -INFINITY;
+    sc[t][3] = jB < ctx ? acc[3] : -INFINITY;
+  }
+  // ---- warp softmax statistics per head (lanes with equal c hold the same heads)
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+  for (int t = 0; t < kMmaTiles; t++) {
+    m0 = fmaxf(m0, fmaxf(sc[t][0], sc[t][2]));
+    m1 = fmaxf(m1, fmaxf(sc[t][1], sc[t][3]));
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+  }
+  const float b0m = m0 == -INFINITY ? 0.f : m0, b1m = m1 == -INFINITY ? 0.f : m1;
+  float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+  for (int t = 0; t < kMmaTiles; t++) {
+    sc[t][0] = exp2f(sc[t][0] - b0m);
+    sc[t][1] = exp2f(sc[t][1] - b1m);
+    sc[t][2] = exp2f(sc[t][2] - b0m);
+    sc[t][3] = exp2f(sc[t][3] - b1m);
+    l0 += sc[t][0] + sc[t][2];
+    l1 += sc[t][1] + sc[t][3];
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  const int hh = 2 * (c & 1);
+  if (g == 0 && c < 2) {
+    sM[warp][hh] = m0;
+    sM[warp][hh + 1] = m1;
+    sL[warp][hh] = l0;
+    sL[warp][hh + 1] = l1;
+  }
+
+  // ---- P.V in two halves of the head dims (32 accumulators per lane each)
+#pragma unroll 1
+  for (int half = 0; half < 2; half++) {
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+#pragma unroll
+    for (int t = 0; t < kMmaTiles; t++) {
+      const int base = wt0 + 16 * t;
+      __syncwarp();
+      {  // P^T into shared memory as [h'][token]: lanes c < 2 write the hi halves, c >= 2 the lo halves
+        const int r0 = hh + (c >= 2 ? 4 : 0);
+        float pv[4] = {sc[t][0], sc[t][1], sc[t][2], sc[t][3]};
+        if (c >= 2)
+#pragma unroll
+          for (int i = 0; i < 4; i++) pv[i] -= bf16_round(pv[i]);
+        sP[warp][r0][g] = __float2bfloat16_rn(pv[0]);
+        sP[warp][r0 + 1][g] = __float2bfloat16_rn(pv[1]);
+        sP[warp][r0][g + 8] = __float2bfloat16_rn(pv[2]);
+        sP[warp][r0 + 1][g + 8] = __float2bfloat16_rn(pv[3]);
+      }
+      __syncwarp();
+      const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(&sP[warp][g][2 * c]);
+      const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(&sP[warp][g][2 * c + 8]);
+      uint4 v[4][2];
+#pragma unroll
+      for (int tk = 0; tk < 4; tk++) {
+        const int j = base + 2 * c + (tk & 1) + 8 * (tk >> 1);
+        const __nv_bfloat16* pv = j < ctx ? row(vp, j) : nullptr;
+#pragma unroll
+        for (int r = 0; r < 2; r++)
+          v[tk][r] = pv ? ldg_stream128(pv + 16 * g + 128 * r + 8 * half) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int wi = i >> 1;
+        const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
+        const uint32_t a0 = __byte_perm(word_of(v[0][0], wi), word_of(v[1][0], wi), sel);
+        const uint32_t a1 = __byte_perm(word_of(v[0][1], wi), word_of(v[1][1], wi), sel);
+        const uint32_t a2 = __byte_perm(word_of(v[2][0], wi), word_of(v[3][0], wi), sel);
+        const uint32_t a3 = __byte_perm(word_of(v[2][1], wi), word_of(v[3][1], wi), sel);
+        mma_bf16_16816(o[i], a0, a1, a2, a3, pb0, pb1);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+      for (int k = 0; k < 4; k++) o[i][k] += __shfl_xor_sync(0xffffffffu, o[i][k], 2);  // hi + lo columns
+    if (c < 2) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int d0 = 16 * g + 8 * half + i, d1 = 128 + d0;
+        sO[warp][hh][d0] = o[i][0];
+        sO[warp][hh + 1][d0] = o[i][1];
+        sO[warp][hh][d1] = o[i][2];
+        sO[warp][hh + 1][d1] = o[i][3];
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- merge the 8 warps of this split
+  if (tid < GROUP) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) M = fmaxf(M, sM[w][tid]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) {
+      const float wt = sM[w][tid] == -INFINITY ? 0.f : exp2f(sM[w][tid] - M);
+      s_w[w][tid] = wt;
+      L += wt * sL[w][tid];
+    }
+    s_fin[tid][0] = M;
+    s_fin[tid][1] = L;
+  }
+  __syncthreads();
+  constexpr int kOutPerThread = GROUP * kHD / kThreads;
+  float osum[kOutPerThread];
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) {
+    const int e = tid + i * kThreads;
+    const int h = e / kHD, d = e % kHD;
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) a += s_w[w][h] * sO[w][h][d];
+    osum[i] = a;
+  }
+  if (n_splits == 1) {
+#pragma unroll
+    for (int i = 0; i < kOutPerThread; i++) {
+      const int e = tid + i * kThreads;
+      const int h = e / kHD, d = e % kHD;
+      io.store(b, h0 + h, d, osum[i] / s_fin[h][1] * sigmoidf_(io.gate(b, h0 + h, d)));
+    }
+    return;
+  }
+  const size_t bh = (size_t)b * Hkv + kvh;
+  float* po = scr.o + (bh * scr.max_splits + split) * GROUP * kHD;
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) __stcg(po + tid + i * kThreads, osum[i]);
+  if (tid < GROUP) {
+    float* pml = scr.ml + ((bh * scr.max_splits + split) * GROUP + tid) * 2;
+    __stcg(pml, s_fin[tid][0]);
+    __stcg(pml + 1, s_fin[tid][1]);
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(scr.tickets + bh, 1) == n_splits - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float* s_sw = &sO[0][0][0];  // [GROUP][n_splits] merge weights (n_splits <= 512 fits in sO)
+  if (tid < GROUP) {
+    const float* ml = scr.ml + (bh * scr.max_splits) * GROUP * 2;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < n_splits; s2++) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * GROUP + tid) * 2));
+    float L = 0.f;
+    for (int s2 = 0; s2 < n_splits; s2++) {
+      const float w = exp2f(__ldcg(ml + ((size_t)s2 * GROUP + tid) * 2) - M);
+      s_sw[tid * n_splits + s2] = w;
+      L += w * __ldcg(ml + ((size_t)s2 * GROUP + tid) * 2 + 1);
+    }
+    for (int s2 = 0; s2 < n_splits; s2++) s_sw[tid * n_splits + s2] /= L;
+  }
+  __syncthreads();
+  const float* pob = scr.o + bh * scr.max_splits * GROUP * kHD;
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) {
+    const int e = tid + i * kThreads;
+    const int h = e / kHD, d = e % kHD;
+    float a = 0.f;
+    for (int s2 = 0; s2 < n_splits; s2++) a += s_sw[h * n_splits + s2] * __ldcg(pob + (size_t)s2 * GROUP * kHD + e);
+    io.store(b, h0 + h, d, a * sigmoidf_(io.gate(b, h0 + h, d)));
+  }
+  if (tid == 0) scr.tickets[bh] = 0;
+}
+
 // Split scratch per (device, stream), grown on demand and kept for the process lifetime, so that calls on
 // different streams never share tickets or partials.
 struct DeviceScratch {
@@ -391,12 +688,28 @@ evie_status get_scratch(int B, int Hkv, int group, int max_splits, Scratch* s, c
 }
 
 
+// EVIE_GQA_CUDA_CORES=1 selects the CUDA-core kernel for bf16 KV too (kept as the cross-check of the MMA path).
+bool mma_disabled() {
+  static const bool off = [] {
+    const char* e = getenv("EVIE_GQA_CUDA_CORES");
+    return e && e[0] == '1';
+  }();
+  return off;
+}
+
 template <typename KV, class IO>
 evie_status launch_gqa(const IO& io, const KV* kp, const KV* vp, int B, int Hq, int Hkv, int page_size, int max_pages,
                        int max_ctx, float scale, const Scratch& scr, cudaStream_t st) {
   const int group = Hq / Hkv;
   const int max_splits = (max_ctx + kSplit - 1) / kSplit;
   dim3 grid(max_splits > 0 ? max_splits : 1, Hkv, B);
+  if constexpr (sizeof(KV) == 2) {
+    if (group == 4 && !mma_disabled()) {
+      gqa_decode_mma_kernel<IO><<<grid, kThreads, 0, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale, scr);
+      EVIE_CHECK_LAUNCH("gqa_decode_mma_kernel");
+      return EVIE_OK;
+    }
+  }
   switch (group) {
     case 2: gqa_decode_kernel<2, KV, IO><<<grid, kThreads, 0, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale, scr); break;
     case 4: gqa_decode_kernel<4, KV, IO><<<grid, kThreads, 0, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale, scr); break;
