@@ -44,6 +44,7 @@ SIGNATURES = {
     "evie_gdn_decode_step": (I, [P, P, P, P, P, P, P, I, I, I, I, P]),
     "evie_gdn_chunk_prefill": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, P]),
     "evie_gqa_decode_paged": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, F, P]),
+    "evie_gqa_decode_paged_noalloc": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, F, P]),
 }
 
 

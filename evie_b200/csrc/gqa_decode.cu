@@ -749,6 +749,80 @@ evie_status launch_gqa_decode_bf16(const void* q, const void* gate, const void* 
                                    max_pages, (int)max_tokens, scale, scr, st);
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Allocation-free variant of the isolated op (evie_gqa_decode_paged_noalloc).
+//
+// Some callers cannot let a library allocate device memory for them: serving engines that reserve nearly all of the
+// GPU's memory for their own caching allocator at start-up (a later cudaMalloc then fails, or carves memory out of
+// a pool they manage), and callers on a latency-critical path where cudaMalloc / cudaFree would synchronise the
+// device. For them the split scratch comes from this fixed array, compiled into the library: every GPU that loads
+// the library holds these bytes until the process exits.
+constexpr size_t kNoAllocScratchBytes = 32u << 20;
+static __device__ __align__(256) unsigned char g_gqa_noalloc_scratch[kNoAllocScratchBytes];
+
+// In host code `g_gqa_noalloc_scratch` only names the symbol; it is not a device address, and a kernel given it would
+// fault (or silently use the wrong memory where the GPU can reach host memory). The device address is looked up once
+// per device, with that device current, on the first call there.
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[128] = {};
+
+evie_status noalloc_scratch(void** out) {
+  int dev = 0;
+  EVIE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 128) return fail(EVIE_ERR_ARG, "evie_gqa_decode_paged_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_gqa_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(EVIE_ERR_CUDA, "evie_gqa_decode_paged_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return EVIE_OK;
+}
+
+evie_status launch_gqa_decode_bf16_noalloc(const void* q, const void* gate, const void* kp, const void* vp,
+                                           const int32_t* page_table, const int32_t* ctx_lens, float* out, int B,
+                                           int Hq, int Hkv, int page_size, int max_pages, float scale,
+                                           cudaStream_t st) {
+  const int group = Hq / Hkv;
+  const long max_tokens = (long)max_pages * page_size;
+  const int max_splits = (int)((max_tokens + kSplit - 1) / kSplit);
+  if (B == 0 || max_splits == 0) {
+    if (B > 0) EVIE_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(float) * (size_t)B * Hq * kHD, st));
+    return EVIE_OK;
+  }
+  // Same partition as the allocating path: tickets, then per-split (max, sum), then per-split outputs.
+  const size_t n_t = (size_t)B * Hkv;
+  const size_t t_bytes = (n_t * sizeof(int) + 255) / 256 * 256;
+  const size_t n_ml = (size_t)B * Hkv * max_splits * group * 2;
+  const size_t n_o = (size_t)B * Hkv * max_splits * group * kHD;
+  const size_t need = t_bytes + (n_ml + n_o) * sizeof(float);
+  if (need > kNoAllocScratchBytes)
+    return fail(EVIE_ERR_ARG,
+                "evie_gqa_decode_paged_noalloc: these sizes need %zu bytes of split scratch, more than its fixed %zu "
+                "(B x Hkv x ceil(max_pages x page_size / 512) must stay at most %zu); use evie_gqa_decode_paged",
+                need, kNoAllocScratchBytes,
+                (kNoAllocScratchBytes - 256) / ((size_t)group * (kHD + 2) * sizeof(float)));
+  void* base = nullptr;
+  evie_status rc = noalloc_scratch(&base);
+  if (rc != EVIE_OK) return rc;
+  // The array keeps the previous call's contents; the tickets must start at zero.
+  EVIE_CUDA_TRY(cudaMemsetAsync(base, 0, t_bytes, st));
+  Scratch scr;
+  char* p = (char*)base;
+  scr.tickets = (int*)p;
+  p += t_bytes;
+  scr.ml = (float*)p;
+  p += n_ml * sizeof(float);
+  scr.o = (float*)p;
+  scr.max_splits = max_splits;
+  IsoIO io{(const __nv_bfloat16*)q, (const __nv_bfloat16*)gate, out, page_table, ctx_lens, Hq, max_pages};
+  return launch_gqa<__nv_bfloat16>(io, (const __nv_bfloat16*)kp, (const __nv_bfloat16*)vp, B, Hq, Hkv, page_size,
+                                   max_pages, (int)max_tokens, scale, scr, st);
+}
+
 template <typename KV>
 evie_status launch_gqa_model(const float* q_rot, const float* Y2, size_t yplane, int ldy, __nv_bfloat16* X2,
                              size_t xplane, const RowInfo* rows, int R, const int* page_table, int pages_per_slot,
@@ -796,4 +870,26 @@ extern "C" evie_status evie_gqa_decode_paged(const void* q, const void* gate, co
            "evie_gqa_decode_paged: q and the KV pages must be 16-byte aligned");
   return evie::launch_gqa_decode_bf16(q, gate, k_pages, v_pages, page_table, ctx_lens, out, B, Hq, Hkv, page_size,
                                       max_pages, scale, (cudaStream_t)stream);
+}
+
+// No counterpart in the reference: the allocation-free form of evie_gqa_decode_paged (see the header).
+extern "C" evie_status evie_gqa_decode_paged_noalloc(const void* q, const void* gate, const void* k_pages,
+                                                     const void* v_pages, const int32_t* page_table,
+                                                     const int32_t* ctx_lens, float* out, int B, int Hq, int Hkv,
+                                                     int hd, int page_size, int max_pages, float scale, void* stream) {
+  EVIE_ARG(hd == 256, "evie_gqa_decode_paged_noalloc: head_dim 256 required (got %d)", hd);
+  EVIE_ARG(B >= 0 && Hkv > 0 && Hq > 0 && Hq % Hkv == 0, "evie_gqa_decode_paged_noalloc: bad head counts %d/%d", Hq,
+           Hkv);
+  const int group = Hq / Hkv;
+  EVIE_ARG(group == 2 || group == 4, "evie_gqa_decode_paged_noalloc: GQA group %d unsupported (2 or 4)", group);
+  EVIE_ARG(page_size > 0 && page_size % 64 == 0, "evie_gqa_decode_paged_noalloc: page_size must be a multiple of 64");
+  EVIE_ARG(max_pages >= 0 && (long)max_pages * page_size <= evie::kGqaMaxContext,
+           "evie_gqa_decode_paged_noalloc: max_pages * page_size exceeds %ld tokens", (long)evie::kGqaMaxContext);
+  EVIE_ARG(B <= 65535 && Hkv <= 65535, "evie_gqa_decode_paged_noalloc: grid too large");
+  EVIE_ARG(B == 0 || (q && gate && k_pages && v_pages && page_table && ctx_lens && out),
+           "evie_gqa_decode_paged_noalloc: null pointer");
+  EVIE_ARG((((uintptr_t)q | (uintptr_t)k_pages | (uintptr_t)v_pages) & 15) == 0,
+           "evie_gqa_decode_paged_noalloc: q and the KV pages must be 16-byte aligned");
+  return evie::launch_gqa_decode_bf16_noalloc(q, gate, k_pages, v_pages, page_table, ctx_lens, out, B, Hq, Hkv,
+                                              page_size, max_pages, scale, (cudaStream_t)stream);
 }

@@ -139,6 +139,23 @@ EVIE_API evie_status evie_gqa_decode_paged(const void* q, const void* gate, cons
                                   const int32_t* page_table, const int32_t* ctx_lens, float* out, int B, int Hq,
                                   int Hkv, int hd, int page_size, int max_pages, float scale, void* stream);
 
+/* The same attention as evie_gqa_decode_paged, for callers that cannot let the library allocate device memory:
+ * serving engines that reserve nearly all GPU memory for their own allocator at start-up, and latency-critical
+ * callers that cannot afford cudaMalloc's device synchronisation. It calls no cudaMalloc, cudaFree or allocating
+ * library routine; its split scratch is a fixed 32 MiB array compiled into the library, held on every GPU that
+ * loads the library until the process exits. No counterpart in the reference (evie allocates its buffers itself).
+ *   - Sizes whose scratch exceeds 32 MiB are rejected with EVIE_ERR_ARG (about B x Hkv x ceil(max_pages x
+ *     page_size / 512) <= 8100 for GQA group 4); the allocating entry point has no such limit.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that device
+ *     current; make that first call before any stream capture.
+ *   - Every call on a device shares the one array and it keeps the last call's contents (each call clears the part
+ *     that must start at zero); calls that may overlap on the GPU (other streams, other host threads) race on it,
+ *     so serialise them. */
+EVIE_API evie_status evie_gqa_decode_paged_noalloc(const void* q, const void* gate, const void* k_pages,
+                                                   const void* v_pages, const int32_t* page_table,
+                                                   const int32_t* ctx_lens, float* out, int B, int Hq, int Hkv, int hd,
+                                                   int page_size, int max_pages, float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
