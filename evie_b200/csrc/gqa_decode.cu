@@ -88,8 +88,7 @@ struct IsoIO {
 // from the q projection planes (per head [q | gate]), output written as the split operand of o_proj.
 struct ModelIO {
   const float* q_rot;
-  const float* Y2;
-  size_t yplane;
+  YView y;
   int ldy;
   __nv_bfloat16* X2;
   size_t xplane;
@@ -107,7 +106,7 @@ struct ModelIO {
     f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = c.x; f[5] = c.y; f[6] = c.z; f[7] = c.w;
   }
   __device__ __forceinline__ float gate(int b, int h, int d) const {
-    return load_y(Y2, yplane, (size_t)b * ldy + (size_t)h * 2 * kHD + kHD + d);
+    return y.at((size_t)b * ldy + (size_t)h * 2 * kHD + kHD + d);
   }
   __device__ __forceinline__ void store(int b, int h, int d, float v) const {
     store_split(X2, xplane, (size_t)b * Hq * kHD + (size_t)h * kHD + d, v);
@@ -824,7 +823,7 @@ evie_status launch_gqa_decode_bf16_noalloc(const void* q, const void* gate, cons
 }
 
 template <typename KV>
-evie_status launch_gqa_model(const float* q_rot, const float* Y2, size_t yplane, int ldy, __nv_bfloat16* X2,
+evie_status launch_gqa_model(const float* q_rot, YView y, int ldy, __nv_bfloat16* X2,
                              size_t xplane, const RowInfo* rows, int R, const int* page_table, int pages_per_slot,
                              const KV* kc, const KV* vc, int Hq, int Hkv, int page_size, int max_ctx, float scale,
                              void* scratch, int ticket_rows, cudaStream_t st) {
@@ -839,14 +838,14 @@ evie_status launch_gqa_model(const float* q_rot, const float* Y2, size_t yplane,
   p += (size_t)R * Hkv * max_splits * group * 2 * sizeof(float);
   scr.o = (float*)p;
   scr.max_splits = max_splits;
-  ModelIO io{q_rot, Y2, yplane, ldy, X2, xplane, rows, page_table, pages_per_slot, Hq};
+  ModelIO io{q_rot, y, ldy, X2, xplane, rows, page_table, pages_per_slot, Hq};
   return launch_gqa<KV>(io, kc, vc, R, Hq, Hkv, page_size, pages_per_slot, max_ctx, scale, scr, st);
 }
-template evie_status launch_gqa_model<__nv_bfloat16>(const float*, const float*, size_t, int, __nv_bfloat16*, size_t,
+template evie_status launch_gqa_model<__nv_bfloat16>(const float*, YView, int, __nv_bfloat16*, size_t,
                                                      const RowInfo*, int, const int*, int, const __nv_bfloat16*,
                                                      const __nv_bfloat16*, int, int, int, int, float, void*, int,
                                                      cudaStream_t);
-template evie_status launch_gqa_model<float>(const float*, const float*, size_t, int, __nv_bfloat16*, size_t,
+template evie_status launch_gqa_model<float>(const float*, YView, int, __nv_bfloat16*, size_t,
                                              const RowInfo*, int, const int*, int, const float*, const float*, int, int,
                                              int, int, float, void*, int, cudaStream_t);
 

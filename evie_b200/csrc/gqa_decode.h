@@ -10,11 +10,12 @@ evie_status launch_gqa_decode_bf16(const void* q, const void* gate, const void* 
                                    const int32_t* page_table, const int32_t* ctx_lens, float* out, int B, int Hq,
                                    int Hkv, int page_size, int max_pages, float scale, cudaStream_t st);
 struct RowInfo;
+struct YView;
 // Scratch bytes the model's attention needs for `rows` query rows (tickets must start zeroed).
 size_t gqa_scratch_bytes(int rows, int Hkv, int group, int max_ctx);
 // Model variant: one query per row (ctx = pos + 1), KV in bf16 or f32 pages, output into the o_proj planes.
 template <typename KV>
-evie_status launch_gqa_model(const float* q_rot, const float* Y2, size_t yplane, int ldy, __nv_bfloat16* X2,
+evie_status launch_gqa_model(const float* q_rot, YView y, int ldy, __nv_bfloat16* X2,
                              size_t xplane, const RowInfo* rows, int R, const int* page_table, int pages_per_slot,
                              const KV* kc, const KV* vc, int Hq, int Hkv, int page_size, int max_ctx, float scale,
                              void* scratch, int ticket_rows, cudaStream_t st);

@@ -382,6 +382,8 @@ evie_status read_config(evie_ctx* c, const std::string& dir) {
   if (s.nh % s.nkv || (s.nh / s.nkv != 2 && s.nh / s.nkv != 4)) return evie::fail(EVIE_ERR_ARG, "GQA group must be 2 or 4");
   if (s.hv % s.hk) return evie::fail(EVIE_ERR_ARG, "value heads must be a multiple of key heads");
   if (s.K < 1 || s.K > 16) return evie::fail(EVIE_ERR_ARG, "conv kernel %d out of range", s.K);
+  if (s.d % 4 || s.d > 8192 || s.n % 4)
+    return evie::fail(EVIE_ERR_ARG, "hidden and MLP sizes must be multiples of 4 (hidden <= 8192)");
   return EVIE_OK;
 }
 
@@ -507,12 +509,15 @@ evie_status allocate_state(evie_ctx* c) {
   return EVIE_OK;
 }
 
-// Y2 [2R][M] f32 = X2 [2R][K] bf16 . W[M][K]^T (one GEMM over both operand planes; fp32 accumulation).
-evie_status gemm(evie_ctx* c, const __nv_bfloat16* W, int M, int K, const __nv_bfloat16* X2, int R, float* Y2) {
+// Y = X . W^T for the R rows of the split operand X2 ([2][R][K] bf16): one cuBLAS GEMM over both planes (fp32
+// accumulation); the result is the two planes of *out, which consumers add.
+evie_status gemm(evie_ctx* c, const __nv_bfloat16* W, int M, int K, const __nv_bfloat16* X2, int R, float* Y2,
+                 evie::YView* out) {
   const float one = 1.0f, zero = 0.0f;
   cublasStatus_t st = cublasGemmEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, M, 2 * R, K, &one, W, CUDA_R_16BF, K, X2,
                                    CUDA_R_16BF, K, &zero, Y2, CUDA_R_32F, M, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
   if (st != CUBLAS_STATUS_SUCCESS) return evie::fail(EVIE_ERR_CUDA, "cublasGemmEx (%d x %d x %d): status %d", M, 2 * R, K, (int)st);
+  *out = evie::YView{Y2, (size_t)R * M, 2};
   return EVIE_OK;
 }
 
@@ -563,34 +568,37 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
   { PROF(P_NORM); TRY(evie::k_embed_norm(c->d_rows, R, c->embed, c->x, c->layers[0].ln1, s.eps, s.d, c->X2, st)); }
   for (int li = 0; li < s.L; li++) {
     Layer& L = c->layers[li];
+    evie::YView yo;  // output projection of the mixer
     if (L.kind == 0) {
-      { PROF(P_GEMM); TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2)); }
+      evie::YView y;
+      { PROF(P_GEMM); TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2, &y)); }
       float* cs = c->conv_state + (size_t)L.idx * (s.K - 1) * s.conv_dim;
       {
         PROF(P_CONV);
-        TRY(evie::k_conv_silu_norm(c->Y2, s.in_dn, R, c->d_rows, c->d_segs, cs, cs_slot, L.conv, s, c->act, st));
-        TRY(evie::k_conv_state_update(c->Y2, s.in_dn, R, c->d_segs, nseq, cs, cs_slot, s, st));
+        TRY(evie::k_conv_silu_norm(y, s.in_dn, R, c->d_rows, c->d_segs, cs, cs_slot, L.conv, s, c->act, st));
+        TRY(evie::k_conv_state_update(y, s.in_dn, R, c->d_segs, nseq, cs, cs_slot, s, st));
       }
       float* rsb = c->rec_state + (size_t)L.idx * s.hv * s.dk * s.dv;
       {
         PROF(P_MIXER);
-        TRY(evie::k_gdn_mixer(c->act, c->Y2, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm,
+        TRY(evie::k_gdn_mixer(c->act, y, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm,
                               s, c->X2, st));
       }
-      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2)); }
+      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2, &yo)); }
     } else {
-      { PROF(P_GEMM); TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2)); }
+      evie::YView y;
+      { PROF(P_GEMM); TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2, &y)); }
       const float scale = 1.0f / sqrtf((float)s.hd);
       if (c->kv_f32) {
         float* kc = (float*)c->k_cache + (size_t)L.idx * kv_layer;
         float* vc = (float*)c->v_cache + (size_t)L.idx * kv_layer;
         {
           PROF(P_ATTN_PREP);
-          TRY(evie::k_attn_prep<float>(c->Y2, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s, c->q_rot,
+          TRY(evie::k_attn_prep<float>(y, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s, c->q_rot,
                                        kc, vc, c->page_table, c->pages_per_slot, kPage, st));
         }
         PROF(P_ATTN);
-        TRY(evie::launch_gqa_model<float>(c->q_rot, c->Y2, (size_t)R * s.in_at, s.in_at, c->X2,
+        TRY(evie::launch_gqa_model<float>(c->q_rot, y, s.in_at, c->X2,
                                           (size_t)R * s.nh * s.hd, c->d_rows, R, c->page_table, c->pages_per_slot,
                                           kc, vc, s.nh, s.nkv, kPage, max_ctx_rows, scale, c->attn_scratch, c->max_rows,
                                           st));
@@ -599,31 +607,32 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
         auto* vc = (__nv_bfloat16*)c->v_cache + (size_t)L.idx * kv_layer;
         {
           PROF(P_ATTN_PREP);
-          TRY(evie::k_attn_prep<__nv_bfloat16>(c->Y2, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s,
+          TRY(evie::k_attn_prep<__nv_bfloat16>(y, s.in_at, R, c->d_rows, L.q_norm, L.k_norm, c->inv_freq, s,
                                                c->q_rot, kc, vc, c->page_table, c->pages_per_slot, kPage, st));
         }
         PROF(P_ATTN);
-        TRY(evie::launch_gqa_model<__nv_bfloat16>(c->q_rot, c->Y2, (size_t)R * s.in_at, s.in_at, c->X2,
+        TRY(evie::launch_gqa_model<__nv_bfloat16>(c->q_rot, y, s.in_at, c->X2,
                                                   (size_t)R * s.nh * s.hd, c->d_rows, R, c->page_table,
                                                   c->pages_per_slot, kc, vc, s.nh, s.nkv, kPage, max_ctx_rows, scale,
                                                   c->attn_scratch, c->max_rows, st));
       }
-      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2)); }
+      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2, &yo)); }
     }
     // model.rs:246-248: residual add after the mixer, then the pre-MLP norm
-    { PROF(P_NORM); TRY(evie::k_add_norm(c->x, c->Y2, s.d, R, L.ln2, s.eps, s.d, c->X2, nullptr, 0, s.L, st)); }
-    { PROF(P_GEMM); TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2)); }
+    { PROF(P_NORM); TRY(evie::k_add_norm(c->x, yo, s.d, R, L.ln2, s.eps, s.d, c->X2, nullptr, 0, s.L, st)); }
+    evie::YView yg, yd;
+    { PROF(P_GEMM); TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2, &yg)); }
     {
       PROF(P_SWIGLU);
-      TRY(evie::k_swiglu(c->Y2, 2 * s.n, R, c->d_rows, li, s, steer, c->scale, fr, c->track ? c->maxbuf : nullptr,
+      TRY(evie::k_swiglu(yg, 2 * s.n, R, c->d_rows, li, s, steer, c->scale, fr, c->track ? c->maxbuf : nullptr,
                          c->X2, st));
     }
-    { PROF(P_GEMM); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2)); }
+    { PROF(P_GEMM); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2, &yd)); }
     PROF(P_NORM);
     if (li + 1 < s.L) {
-      TRY(evie::k_add_norm(c->x, c->Y2, s.d, R, c->layers[li + 1].ln1, s.eps, s.d, c->X2, rs, li, s.L, st));
+      TRY(evie::k_add_norm(c->x, yd, s.d, R, c->layers[li + 1].ln1, s.eps, s.d, c->X2, rs, li, s.L, st));
     } else {
-      TRY(evie::k_add_final(c->x, c->Y2, s.d, R, c->d_rows, c->d_segs, nseq, c->final_norm, s.eps, s.d, c->X2, rs,
+      TRY(evie::k_add_final(c->x, yd, s.d, R, c->d_rows, c->d_segs, nseq, c->final_norm, s.eps, s.d, c->X2, rs,
                             li, s.L, st));
     }
   }
@@ -632,9 +641,10 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
 
 // model.rs:271-283: LM head on the last row of every sequence; greedy id (sampling.rs:60-62) on device.
 evie_status enqueue_head(evie_ctx* c, int nseq, bool want_logits) {
-  { PROF(P_LMHEAD); TRY(gemm(c, c->lm_head, c->s.V, c->s.d, c->X2, nseq, c->L2)); }
+  evie::YView yl;
+  { PROF(P_LMHEAD); TRY(gemm(c, c->lm_head, c->s.V, c->s.d, c->X2, nseq, c->L2, &yl)); }
   PROF(P_OTHER);
-  return evie::k_logits_argmax(c->L2, nseq, c->s.V, want_logits ? c->logits : nullptr, c->best, c->next, c->stream);
+  return evie::k_logits_argmax(yl, nseq, c->s.V, want_logits ? c->logits : nullptr, c->best, c->next, c->stream);
 }
 
 evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_logits, int capture, float* logits,

@@ -52,56 +52,105 @@ __global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowInfo*
   for (int i = threadIdx.x; i < d; i += kNormThreads) store_split(X2, xplane, (size_t)r * d + i, xr[i] * inv * gain[i]);
 }
 
-// model.rs:246-248, 260-263 (residual add, residual hook, next RMSNorm)
-__global__ void __launch_bounds__(kNormThreads) add_norm_kernel(float* __restrict__ x, const float* __restrict__ Y2,
-                                                                size_t yplane, int ldy, const float* __restrict__ gain,
-                                                                float eps, int d, __nv_bfloat16* __restrict__ X2,
-                                                                size_t xplane, uint16_t* __restrict__ resid,
-                                                                int cap_layer, int L) {
-  __shared__ float red[kNormThreads / 32];
-  const int r = blockIdx.x;
-  float* xr = x + (size_t)r * d;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < d; i += kNormThreads) {
-    const float v = xr[i] + load_y(Y2, yplane, (size_t)r * ldy + i);
-    xr[i] = v;
-    ss += v * v;
-    if (resid) resid[((size_t)r * L + cap_layer) * d + i] = __half_as_ushort(__float2half_rn(v));
-  }
-  ss = block_sum<kNormThreads>(ss, red);
-  const float inv = 1.0f / sqrtf(ss / (float)d + eps);
-  for (int i = threadIdx.x; i < d; i += kNormThreads) store_split(X2, xplane, (size_t)r * d + i, xr[i] * inv * gain[i]);
+// model.rs:246-248, 260-263 (residual add, residual hook, next RMSNorm). One CTA per row, one float4 of the row
+// per thread (two beyond 4096 columns), every plane of the projection output loaded before any is added.
+__device__ __forceinline__ void store_split4(__nv_bfloat16* X2, size_t plane, size_t idx, float4 v) {
+  const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
+  const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+  const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
+  const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - f1.x, v.w - f1.y);
+  uint2 hi, lo;
+  hi.x = *reinterpret_cast<const uint32_t*>(&h0);
+  hi.y = *reinterpret_cast<const uint32_t*>(&h1);
+  lo.x = *reinterpret_cast<const uint32_t*>(&l0);
+  lo.y = *reinterpret_cast<const uint32_t*>(&l1);
+  *reinterpret_cast<uint2*>(X2 + idx) = hi;
+  *reinterpret_cast<uint2*>(X2 + plane + idx) = lo;
 }
 
-// model.rs:260-263 for the last layer, then model.rs:271-290 (last row of each sequence, final norm)
-__global__ void __launch_bounds__(kNormThreads) add_final_kernel(float* __restrict__ x, const float* __restrict__ Y2,
-                                                                 size_t yplane, int ldy,
-                                                                 const RowInfo* __restrict__ rows,
-                                                                 const SegInfo* __restrict__ segs, int nseg,
-                                                                 const float* __restrict__ gain, float eps, int d,
-                                                                 __nv_bfloat16* __restrict__ X2,
-                                                                 uint16_t* __restrict__ resid, int cap_layer, int L) {
-  __shared__ float red[kNormThreads / 32];
-  const int r = blockIdx.x;
+__device__ __forceinline__ void store_f16x4(uint16_t* dst, float4 v) {
+  const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&a);
+  u.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+
+__device__ __forceinline__ float block_sum_any(float v, float* red) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < nw; w++) t += red[w];
+  return t;
+}
+
+// x[r] += y[r] (all planes), optional f16 capture, then (if do_norm) X2 row out_row = split(rmsnorm(x[r]) * gain).
+__device__ __forceinline__ void add_norm_row(float* __restrict__ x, const YView& y, int ldy, int r, int d,
+                                             const float* __restrict__ gain, float eps, __nv_bfloat16* X2,
+                                             size_t xplane, int out_row, bool do_norm, uint16_t* resid, int cap_layer,
+                                             int L, float* red) {
+  const int n4 = d >> 2;
   float* xr = x + (size_t)r * d;
+  float4 v[2];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < d; i += kNormThreads) {
-    const float v = xr[i] + load_y(Y2, yplane, (size_t)r * ldy + i);
-    xr[i] = v;
-    ss += v * v;
-    if (resid) resid[((size_t)r * L + cap_layer) * d + i] = __half_as_ushort(__float2half_rn(v));
+#pragma unroll
+  for (int k = 0; k < 2; k++) {
+    const int i4 = threadIdx.x + k * blockDim.x;
+    if (i4 < n4) {
+      float4 a = *reinterpret_cast<const float4*>(xr + 4 * i4);
+      const float4 b = y.at4((size_t)r * ldy + 4 * i4);
+      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+      v[k] = a;
+      *reinterpret_cast<float4*>(xr + 4 * i4) = a;
+      if (resid) store_f16x4(resid + ((size_t)r * L + cap_layer) * d + 4 * i4, a);
+      ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+    }
   }
-  ss = block_sum<kNormThreads>(ss, red);
-  const int s = rows[r].seg;
-  if (r != segs[s].start + segs[s].count - 1) return;
+  ss = block_sum_any(ss, red);
+  if (!do_norm) return;
   const float inv = 1.0f / sqrtf(ss / (float)d + eps);
-  const size_t plane = (size_t)nseg * d;
-  for (int i = threadIdx.x; i < d; i += kNormThreads) store_split(X2, plane, (size_t)s * d + i, xr[i] * inv * gain[i]);
+#pragma unroll
+  for (int k = 0; k < 2; k++) {
+    const int i4 = threadIdx.x + k * blockDim.x;
+    if (i4 < n4) {
+      const float4 g = *reinterpret_cast<const float4*>(gain + 4 * i4);
+      const float4 a = v[k];
+      store_split4(X2, xplane, (size_t)out_row * d + 4 * i4,
+                   make_float4(a.x * inv * g.x, a.y * inv * g.y, a.z * inv * g.z, a.w * inv * g.w));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(1024) add_norm_kernel(float* __restrict__ x, YView y, int ldy,
+                                                        const float* __restrict__ gain, float eps, int d,
+                                                        __nv_bfloat16* __restrict__ X2, size_t xplane,
+                                                        uint16_t* __restrict__ resid, int cap_layer, int L) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  add_norm_row(x, y, ldy, r, d, gain, eps, X2, xplane, r, true, resid, cap_layer, L, red);
+}
+
+// model.rs:260-263 for the last layer, then model.rs:271-290 (last row of each sequence, final norm into X2 row s)
+__global__ void __launch_bounds__(1024) add_final_kernel(float* __restrict__ x, YView y, int ldy,
+                                                         const RowInfo* __restrict__ rows,
+                                                         const SegInfo* __restrict__ segs, int nseg,
+                                                         const float* __restrict__ gain, float eps, int d,
+                                                         __nv_bfloat16* __restrict__ X2,
+                                                         uint16_t* __restrict__ resid, int cap_layer, int L) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const int s = rows[r].seg;
+  const bool last = r == segs[s].start + segs[s].count - 1;
+  add_norm_row(x, y, ldy, r, d, gain, eps, X2, (size_t)nseg * d, s, last, resid, cap_layer, L, red);
 }
 
 // model.rs:324-353: causal depthwise conv over [conv state ; rows] + SiLU; L2 norm of q and k heads, q * 1/sqrt(dk).
 // One CTA = one row x one 128-channel head block.
-__global__ void __launch_bounds__(128) conv_silu_norm_kernel(const float* __restrict__ Y2, size_t yplane, int ldy,
+__global__ void __launch_bounds__(128) conv_silu_norm_kernel(YView y, int ldy,
                                                              const RowInfo* __restrict__ rows,
                                                              const SegInfo* __restrict__ segs,
                                                              const float* __restrict__ conv_state, size_t cs_slot,
@@ -116,7 +165,7 @@ __global__ void __launch_bounds__(128) conv_silu_norm_kernel(const float* __rest
   float acc = 0.f;
   for (int j = 0; j < K; j++) {
     const int tt = t - (K - 1) + j;
-    const float u = tt >= 0 ? load_y(Y2, yplane, (size_t)(sg.start + tt) * ldy + c) : cs[(size_t)(K - 1 + tt) * conv_dim + c];
+    const float u = tt >= 0 ? y.at((size_t)(sg.start + tt) * ldy + c) : cs[(size_t)(K - 1 + tt) * conv_dim + c];
     acc += conv_w[(size_t)c * K + j] * u;
   }
   float out = siluf_(acc);
@@ -129,7 +178,7 @@ __global__ void __launch_bounds__(128) conv_silu_norm_kernel(const float* __rest
 }
 
 // model.rs:339: the conv window keeps the last K-1 raw inputs of [state ; rows].
-__global__ void conv_state_update_kernel(const float* __restrict__ Y2, size_t yplane, int ldy,
+__global__ void conv_state_update_kernel(YView y, int ldy,
                                          const SegInfo* __restrict__ segs, float* __restrict__ conv_state,
                                          size_t cs_slot, int K, int conv_dim) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -140,7 +189,7 @@ __global__ void conv_state_update_kernel(const float* __restrict__ Y2, size_t yp
   for (int i = 0; i < K - 1; i++) {
     const int src = sg.count + i;  // index into [state (K-1) ; rows (count)]
     const float v = src < K - 1 ? cs[(size_t)src * conv_dim + c]
-                                : load_y(Y2, yplane, (size_t)(sg.start + src - (K - 1)) * ldy + c);
+                                : y.at((size_t)(sg.start + src - (K - 1)) * ldy + c);
     cs[(size_t)i * conv_dim + c] = v;
   }
 }
@@ -149,7 +198,7 @@ __global__ void conv_state_update_kernel(const float* __restrict__ Y2, size_t yp
 // [128][128] state resident in registers across the segment's rows (16 rows x 4 columns per thread).
 constexpr int kMixThreads = 256;
 __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
-    const float* __restrict__ act, const float* __restrict__ Y2, size_t yplane, int ldy,
+    const float* __restrict__ act, YView y, int ldy,
     const SegInfo* __restrict__ segs, float* __restrict__ rec_state, size_t rs_slot, const float* __restrict__ neg_a,
     const float* __restrict__ dt_bias, const float* __restrict__ norm_w, int conv_dim, int key_dim, int vd, int hv,
     int ratio, float eps, __nv_bfloat16* __restrict__ X2, size_t xplane) {
@@ -175,8 +224,8 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
     if (tid < DK) sq[tid] = ar[kh * DK + tid];
     else sk[tid - DK] = ar[key_dim + kh * DK + (tid - DK)];
     const float4 v4 = *reinterpret_cast<const float4*>(ar + 2 * key_dim + head * DV + lane * 4);
-    const float bb = load_y(Y2, yplane, (size_t)row * ldy + conv_dim + vd + head);
-    const float aa = load_y(Y2, yplane, (size_t)row * ldy + conv_dim + vd + hv + head);
+    const float bb = y.at((size_t)row * ldy + conv_dim + vd + head);
+    const float aa = y.at((size_t)row * ldy + conv_dim + vd + hv + head);
     const float decay = expf(neg_a[head] * softplus_(aa + dt_bias[head]));
     const float beta = sigmoidf_(bb);
     __syncthreads();
@@ -223,7 +272,7 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
     if (tid < DV) {  // gated RMSNorm, model.rs:377-383: o * rsqrt(mean o^2 + eps) * w * silu(z)
       const float ms = (sred[0] + sred[1] + sred[2] + sred[3]) / (float)DV;
       const float inv = 1.0f / sqrtf(ms + eps);
-      const float z = load_y(Y2, yplane, (size_t)row * ldy + conv_dim + head * DV + tid);
+      const float z = y.at((size_t)row * ldy + conv_dim + head * DV + tid);
       store_split(X2, xplane, (size_t)row * vd + head * DV + tid, s_o[tid] * inv * norm_w[tid] * siluf_(z));
     }
   }
@@ -234,7 +283,7 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
 // model.rs:419-442, rope model.rs:470-479: q_norm / k_norm (gains 1+w) + rotate-half RoPE on the first `rot` dims;
 // K and V appended to the paged cache. One CTA per (row, head) with one thread per head dim (hd = 256).
 template <typename KV>
-__global__ void __launch_bounds__(256) attn_prep_kernel(const float* __restrict__ Y2, size_t yplane, int ldy,
+__global__ void __launch_bounds__(256) attn_prep_kernel(YView y, int ldy,
                                                         const RowInfo* __restrict__ rows,
                                                         const float* __restrict__ q_norm,
                                                         const float* __restrict__ k_norm,
@@ -243,18 +292,18 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const float* __restrict_
                                                         KV* __restrict__ vc, const int* __restrict__ page_table,
                                                         int pages_per_slot, int page_size) {
   __shared__ float red[8];
-  __shared__ float y[256];
+  __shared__ float yn_s[256];
   const int idx = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
   const RowInfo ri = rows[r];
   const bool is_q = idx < nh;
   const int kh = idx - nh;
   const size_t base = (size_t)r * ldy;
-  const float raw = is_q ? load_y(Y2, yplane, base + (size_t)idx * 2 * hd + d)
-                         : load_y(Y2, yplane, base + (size_t)2 * nh * hd + (size_t)kh * hd + d);
+  const float raw = is_q ? y.at(base + (size_t)idx * 2 * hd + d)
+                         : y.at(base + (size_t)2 * nh * hd + (size_t)kh * hd + d);
   const float ss = block_sum<256>(raw * raw, red);
   const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
   const float yn = raw * inv * (is_q ? q_norm[d] : k_norm[d]);
-  y[d] = yn;
+  yn_s[d] = yn;
   __syncthreads();
   float out = yn;
   const int half = rot / 2;
@@ -262,14 +311,14 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const float* __restrict_
     const int i = d < half ? d : d - half;
     float sn, cs;
     sincosf((float)ri.pos * inv_freq[i], &sn, &cs);
-    out = d < half ? y[d] * cs - y[d + half] * sn : y[d] * cs + y[d - half] * sn;
+    out = d < half ? yn_s[d] * cs - yn_s[d + half] * sn : yn_s[d] * cs + yn_s[d - half] * sn;
   }
   if (is_q) {
     q_rot[((size_t)r * nh + idx) * hd + d] = out;
   } else {
     const int page = page_table[(size_t)ri.slot * pages_per_slot + ri.pos / page_size];
     const size_t off = (((size_t)page * nkv + kh) * page_size + ri.pos % page_size) * hd + d;
-    const float v = load_y(Y2, yplane, base + (size_t)2 * nh * hd + (size_t)nkv * hd + (size_t)kh * hd + d);
+    const float v = y.at(base + (size_t)2 * nh * hd + (size_t)nkv * hd + (size_t)kh * hd + d);
     if constexpr (sizeof(KV) == 2) {
       kc[off] = __float2bfloat16_rn(out);
       vc[off] = __float2bfloat16_rn(v);
@@ -283,7 +332,7 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const float* __restrict_
 // model.rs:249-258 with the Probe hook (worker.rs:136-141): silu(gate) * up, the slot's steering ops of this layer
 // in order (steering.rs:189-208), companded capture (worker.rs:97-112) and max |a| over positions > 0
 // (gpu/mod.rs:577-593). One CTA = one row x 1024 neurons.
-__global__ void __launch_bounds__(256) swiglu_kernel(const float* __restrict__ Y2, size_t yplane, int ldy,
+__global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
                                                      const RowInfo* __restrict__ rows, int layer, int n, int L,
                                                      SteerTables steer, const float* __restrict__ scale,
                                                      int8_t* __restrict__ frames, uint32_t* __restrict__ maxbuf,
@@ -303,26 +352,30 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const float* __restrict__ Y
     s_ops[threadIdx.x] = steer.ops[(size_t)ri.slot * steer.max_ops + first + threadIdx.x];
   }
   __syncthreads();
-  const int j0 = blockIdx.x * 1024 + threadIdx.x * 4;
+  const int j0 = blockIdx.x * 1024 + threadIdx.x * 4;  // n is a multiple of 4
+  if (j0 >= n) return;
   const size_t yr = (size_t)r * ldy;
-#pragma unroll
-  for (int e = 0; e < 4; e++) {
-    const int j = j0 + e;
-    if (j >= n) break;
-    const float g = load_y(Y2, yplane, yr + j);
-    const float u = load_y(Y2, yplane, yr + n + j);
-    float a = siluf_(g) * u;
-    for (int i = 0; i < cnt; i++) {
-      const evie_op op = s_ops[i];
-      if (op.neuron != j) continue;
-      if (op.mode == 1) a += op.value;
-      else if (op.mode == 2) a *= op.value;
-      else if (op.mode == 3) a = op.value;
-    }
-    store_split(X2, xplane, (size_t)r * n + j, a);
-    if (frames) frames[((size_t)r * L + layer) * n + j] = compand(a / scale[(size_t)layer * n + j]);
-    if (maxbuf && ri.pos > 0) atomicMax(maxbuf + (size_t)layer * n + j, __float_as_uint(fabsf(a)));
+  const float4 g4 = y.at4(yr + j0), u4 = y.at4(yr + n + j0);
+  float a[4] = {siluf_(g4.x) * u4.x, siluf_(g4.y) * u4.y, siluf_(g4.z) * u4.z, siluf_(g4.w) * u4.w};
+  for (int i = 0; i < cnt; i++) {  // steering.rs:189-208, in the slot's order
+    const evie_op op = s_ops[i];
+    const int e = op.neuron - j0;
+    if (e < 0 || e > 3) continue;
+    if (op.mode == 1) a[e] += op.value;
+    else if (op.mode == 2) a[e] *= op.value;
+    else if (op.mode == 3) a[e] = op.value;
   }
+  store_split4(X2, xplane, (size_t)r * n + j0, make_float4(a[0], a[1], a[2], a[3]));
+  if (frames) {
+    const float4 sc = *reinterpret_cast<const float4*>(scale + (size_t)layer * n + j0);
+    const uint32_t packed = (uint32_t)(uint8_t)compand(a[0] / sc.x) | ((uint32_t)(uint8_t)compand(a[1] / sc.y) << 8) |
+                            ((uint32_t)(uint8_t)compand(a[2] / sc.z) << 16) |
+                            ((uint32_t)(uint8_t)compand(a[3] / sc.w) << 24);
+    *reinterpret_cast<uint32_t*>(frames + ((size_t)r * L + layer) * n + j0) = packed;
+  }
+  if (maxbuf && ri.pos > 0)
+#pragma unroll
+    for (int e = 0; e < 4; e++) atomicMax(maxbuf + (size_t)layer * n + j0 + e, __float_as_uint(fabsf(a[e])));
 }
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
@@ -332,19 +385,18 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
 }
 
 // kernels.rs:642-662 with k = 1 (sampling.rs:60-62): the first index of the maximum logit.
-__global__ void __launch_bounds__(256) logits_argmax_kernel(const float* __restrict__ L2, int nseg, int V,
+__global__ void __launch_bounds__(256) logits_argmax_kernel(YView L2, int nseg, int V,
                                                             float* __restrict__ logits,
                                                             unsigned long long* __restrict__ best) {
   __shared__ unsigned long long red[8];
   const int s = blockIdx.y;
-  const size_t plane = (size_t)nseg * V;
   unsigned long long key = 0;
   const int i0 = blockIdx.x * 1024 + threadIdx.x;
 #pragma unroll
   for (int e = 0; e < 4; e++) {
     const int i = i0 + e * 256;
     if (i < V) {
-      const float v = L2[(size_t)s * V + i] + L2[plane + (size_t)s * V + i];
+      const float v = L2.at((size_t)s * V + i);
       if (logits) logits[(size_t)s * V + i] = v;
       const unsigned long long k = argmax_key(v, (uint32_t)i);
       key = k > key ? k : key;
@@ -380,6 +432,13 @@ __global__ void advance_rows_kernel(RowInfo* rows, int nseq, const uint32_t* nex
 
 }  // namespace
 
+// Threads for the row-norm kernels: one float4 per thread up to 1024 threads, two beyond.
+static int norm_threads(int d) {
+  const int n4 = d / 4;
+  const int t = n4 <= 1024 ? n4 : (n4 + 1) / 2;
+  return (t + 31) / 32 * 32;
+}
+
 evie_status k_advance_rows(RowInfo* rows, int nseq, const uint32_t* next, cudaStream_t st) {
   advance_rows_kernel<<<(nseq + 127) / 128, 128, 0, st>>>(rows, nseq, next);
   EVIE_CHECK_LAUNCH("advance_rows_kernel");
@@ -394,52 +453,51 @@ evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed,
   return EVIE_OK;
 }
 
-evie_status k_add_norm(float* x, const float* Y2, int ldy, int R, const float* gain, float eps, int d,
+evie_status k_add_norm(float* x, YView y, int ldy, int R, const float* gain, float eps, int d,
                        __nv_bfloat16* X2, uint16_t* resid, int cap_layer, int L, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
-  add_norm_kernel<<<R, kNormThreads, 0, st>>>(x, Y2, (size_t)R * ldy, ldy, gain, eps, d, X2, (size_t)R * d, resid,
-                                              cap_layer, L);
+  add_norm_kernel<<<R, norm_threads(d), 0, st>>>(x, y, ldy, gain, eps, d, X2, (size_t)R * d, resid, cap_layer, L);
   EVIE_CHECK_LAUNCH("add_norm_kernel");
   return EVIE_OK;
 }
 
-evie_status k_add_final(float* x, const float* Y2, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
+evie_status k_add_final(float* x, YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
                         int nseg, const float* gain, float eps, int d, __nv_bfloat16* X2, uint16_t* resid,
                         int cap_layer, int L, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
-  add_final_kernel<<<R, kNormThreads, 0, st>>>(x, Y2, (size_t)R * ldy, ldy, rows, segs, nseg, gain, eps, d, X2, resid,
-                                               cap_layer, L);
+  add_final_kernel<<<R, norm_threads(d), 0, st>>>(x, y, ldy, rows, segs, nseg, gain, eps, d, X2, resid, cap_layer,
+                                                  L);
   EVIE_CHECK_LAUNCH("add_final_kernel");
   return EVIE_OK;
 }
 
-evie_status k_conv_silu_norm(const float* Y2, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
+evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
                              const float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
                              float* act, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
   dim3 grid(s.conv_dim / 128, R);
-  conv_silu_norm_kernel<<<grid, 128, 0, st>>>(Y2, (size_t)R * ldy, ldy, rows, segs, conv_state, cs_slot, conv_w, s.K,
+  conv_silu_norm_kernel<<<grid, 128, 0, st>>>(y, ldy, rows, segs, conv_state, cs_slot, conv_w, s.K,
                                               s.conv_dim, s.hk, 1.0f / sqrtf((float)s.dk), act);
   EVIE_CHECK_LAUNCH("conv_silu_norm_kernel");
   return EVIE_OK;
 }
 
-evie_status k_conv_state_update(const float* Y2, int ldy, int R, const SegInfo* segs, int nseg, float* conv_state,
+evie_status k_conv_state_update(YView y, int ldy, int R, const SegInfo* segs, int nseg, float* conv_state,
                                 size_t cs_slot, const ModelShape& s, cudaStream_t st) {
   if (nseg == 0) return EVIE_OK;
   dim3 grid((s.conv_dim + 255) / 256, nseg);
-  conv_state_update_kernel<<<grid, 256, 0, st>>>(Y2, (size_t)R * ldy, ldy, segs, conv_state, cs_slot, s.K,
+  conv_state_update_kernel<<<grid, 256, 0, st>>>(y, ldy, segs, conv_state, cs_slot, s.K,
                                                  s.conv_dim);
   EVIE_CHECK_LAUNCH("conv_state_update_kernel");
   return EVIE_OK;
 }
 
-evie_status k_gdn_mixer(const float* act, const float* Y2, int ldy, int R, const SegInfo* segs, int nseg,
+evie_status k_gdn_mixer(const float* act, YView y, int ldy, int R, const SegInfo* segs, int nseg,
                         float* rec_state, size_t rs_slot, const float* neg_a, const float* dt_bias,
                         const float* norm_w, const ModelShape& s, __nv_bfloat16* X2, cudaStream_t st) {
   if (nseg == 0) return EVIE_OK;
   dim3 grid(s.hv, nseg);
-  gdn_mixer_kernel<<<grid, kMixThreads, 0, st>>>(act, Y2, (size_t)R * ldy, ldy, segs, rec_state, rs_slot, neg_a,
+  gdn_mixer_kernel<<<grid, kMixThreads, 0, st>>>(act, y, ldy, segs, rec_state, rs_slot, neg_a,
                                                  dt_bias, norm_w, s.conv_dim, s.key_dim, s.vd, s.hv, s.hv / s.hk, s.eps,
                                                  X2, (size_t)R * s.vd);
   EVIE_CHECK_LAUNCH("gdn_mixer_kernel");
@@ -447,35 +505,35 @@ evie_status k_gdn_mixer(const float* act, const float* Y2, int ldy, int R, const
 }
 
 template <typename KV>
-evie_status k_attn_prep(const float* Y2, int ldy, int R, const RowInfo* rows, const float* q_norm,
+evie_status k_attn_prep(YView y, int ldy, int R, const RowInfo* rows, const float* q_norm,
                         const float* k_norm, const float* inv_freq, const ModelShape& s, float* q_rot, KV* kc,
                         KV* vc, const int* page_table, int pages_per_slot, int page_size, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
   dim3 grid(s.nh + s.nkv, R);
-  attn_prep_kernel<KV><<<grid, 256, 0, st>>>(Y2, (size_t)R * ldy, ldy, rows, q_norm, k_norm, inv_freq, s.nh, s.nkv,
+  attn_prep_kernel<KV><<<grid, 256, 0, st>>>(y, ldy, rows, q_norm, k_norm, inv_freq, s.nh, s.nkv,
                                              s.hd, s.rot, s.eps, q_rot, kc, vc, page_table, pages_per_slot, page_size);
   EVIE_CHECK_LAUNCH("attn_prep_kernel");
   return EVIE_OK;
 }
-template evie_status k_attn_prep<__nv_bfloat16>(const float*, int, int, const RowInfo*, const float*, const float*,
+template evie_status k_attn_prep<__nv_bfloat16>(YView, int, int, const RowInfo*, const float*, const float*,
                                                 const float*, const ModelShape&, float*, __nv_bfloat16*,
                                                 __nv_bfloat16*, const int*, int, int, cudaStream_t);
-template evie_status k_attn_prep<float>(const float*, int, int, const RowInfo*, const float*, const float*,
+template evie_status k_attn_prep<float>(YView, int, int, const RowInfo*, const float*, const float*,
                                         const float*, const ModelShape&, float*, float*, float*, const int*, int, int,
                                         cudaStream_t);
 
-evie_status k_swiglu(const float* Y2, int ldy, int R, const RowInfo* rows, int layer, const ModelShape& s,
+evie_status k_swiglu(YView y, int ldy, int R, const RowInfo* rows, int layer, const ModelShape& s,
                      SteerTables steer, const float* scale, int8_t* frames, uint32_t* maxbuf, __nv_bfloat16* X2,
                      cudaStream_t st) {
   if (R == 0) return EVIE_OK;
   dim3 grid((s.n + 1023) / 1024, R);
-  swiglu_kernel<<<grid, 256, 0, st>>>(Y2, (size_t)R * ldy, ldy, rows, layer, s.n, s.L, steer, scale, frames, maxbuf,
+  swiglu_kernel<<<grid, 256, 0, st>>>(y, ldy, rows, layer, s.n, s.L, steer, scale, frames, maxbuf,
                                       X2, (size_t)R * s.n);
   EVIE_CHECK_LAUNCH("swiglu_kernel");
   return EVIE_OK;
 }
 
-evie_status k_logits_argmax(const float* L2, int nseg, int V, float* logits, unsigned long long* best,
+evie_status k_logits_argmax(YView L2, int nseg, int V, float* logits, unsigned long long* best,
                             uint32_t* next_tokens, cudaStream_t st) {
   if (nseg == 0) return EVIE_OK;
   dim3 grid((V + 1023) / 1024, nseg);

@@ -25,6 +25,32 @@ __device__ __forceinline__ void store_split(__nv_bfloat16* X2, size_t plane, siz
 }
 __device__ __forceinline__ float load_y(const float* Y2, size_t plane, size_t idx) { return Y2[idx] + Y2[plane + idx]; }
 
+// A projection output as `n` partial planes of `plane` floats each, added in a fixed order when read: 2 planes
+// (hi and lo operand products) from the cuBLAS path, or K-split partials from a tensor-core decode GEMM.
+struct YView {
+  const float* p;
+  size_t plane;
+  int n;
+  __device__ __forceinline__ float at(size_t i) const {
+    float s = p[i];
+    for (int k = 1; k < n; k++) s += p[(size_t)k * plane + i];
+    return s;
+  }
+  // Four consecutive elements (i a multiple of 4; rows and planes 16-byte aligned); up to 8 planes are loaded
+  // before any is added, then added in plane order.
+  __device__ __forceinline__ float4 at4(size_t i) const {
+    float4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      if (k < n) v[k] = *reinterpret_cast<const float4*>(p + (size_t)k * plane + i);
+    float4 s = v[0];
+#pragma unroll
+    for (int k = 1; k < 8; k++)
+      if (k < n) s.x += v[k].x, s.y += v[k].y, s.z += v[k].z, s.w += v[k].w;
+    return s;
+  }
+};
+
 struct ModelShape {
   int d, n, L, V;
   float eps;
@@ -37,27 +63,27 @@ struct ModelShape {
 evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed, float* x, const float* gain,
                          float eps, int d, __nv_bfloat16* X2, cudaStream_t st);
 // x += Y (two planes); optional f16 capture of x as the residual leaving `cap_layer`; then X2 = split(rmsnorm(x)).
-evie_status k_add_norm(float* x, const float* Y2, int ldy, int R, const float* gain, float eps, int d,
+evie_status k_add_norm(float* x, YView y, int ldy, int R, const float* gain, float eps, int d,
                        __nv_bfloat16* X2, uint16_t* resid, int cap_layer, int L, cudaStream_t st);
 // Final residual add (+ capture of the last layer) and final norm of each segment's last row into X2 [2][nseg][d].
-evie_status k_add_final(float* x, const float* Y2, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
+evie_status k_add_final(float* x, YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
                         int nseg, const float* gain, float eps, int d, __nv_bfloat16* X2, uint16_t* resid,
                         int cap_layer, int L, cudaStream_t st);
 // Causal depthwise conv over [conv state ; new rows] + SiLU, then L2 norm of the q and k heads (q also 1/sqrt(dk)).
 // conv_state points at this layer's window of slot 0; cs_slot is the element stride between slots.
-evie_status k_conv_silu_norm(const float* Y2, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
+evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
                              const float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
                              float* act, cudaStream_t st);
-evie_status k_conv_state_update(const float* Y2, int ldy, int R, const SegInfo* segs, int nseg, float* conv_state,
+evie_status k_conv_state_update(YView y, int ldy, int R, const SegInfo* segs, int nseg, float* conv_state,
                                 size_t cs_slot, const ModelShape& s, cudaStream_t st);
 // Gated delta rule over each segment's rows (state resident in registers) + gated RMSNorm -> X2 [R][vd].
 // rec_state points at this layer's [hv][dk][dv] state of slot 0; rs_slot is the element stride between slots.
-evie_status k_gdn_mixer(const float* act, const float* Y2, int ldy, int R, const SegInfo* segs, int nseg,
+evie_status k_gdn_mixer(const float* act, YView y, int ldy, int R, const SegInfo* segs, int nseg,
                         float* rec_state, size_t rs_slot, const float* neg_a, const float* dt_bias,
                         const float* norm_w, const ModelShape& s, __nv_bfloat16* X2, cudaStream_t st);
 // q/k RMSNorm (1+w gains) + partial RoPE; q -> q_rot f32 [R][nh][hd]; k, v -> paged cache (bf16 or f32).
 template <typename KV>
-evie_status k_attn_prep(const float* Y2, int ldy, int R, const RowInfo* rows, const float* q_norm,
+evie_status k_attn_prep(YView y, int ldy, int R, const RowInfo* rows, const float* q_norm,
                         const float* k_norm, const float* inv_freq, const ModelShape& s, float* q_rot, KV* kc,
                         KV* vc, const int* page_table, int pages_per_slot, int page_size, cudaStream_t st);
 // silu(gate) * up, per-slot steering ops, capture, max tracking -> X2 [R][n].
@@ -66,11 +92,11 @@ struct SteerTables {
   const int* range;        // [slots][L][2] (first, count) into the slot's ops
   int max_ops;
 };
-evie_status k_swiglu(const float* Y2, int ldy, int R, const RowInfo* rows, int layer, const ModelShape& s,
+evie_status k_swiglu(YView y, int ldy, int R, const RowInfo* rows, int layer, const ModelShape& s,
                      SteerTables steer, const float* scale, int8_t* frames, uint32_t* maxbuf, __nv_bfloat16* X2,
                      cudaStream_t st);
 // logits = two planes summed (optional copy out), greedy argmax (first index of the maximum).
-evie_status k_logits_argmax(const float* L2, int nseg, int V, float* logits, unsigned long long* best,
+evie_status k_logits_argmax(YView L2, int nseg, int V, float* logits, unsigned long long* best,
                             uint32_t* next_tokens, cudaStream_t st);
 
 // Decode loop step: row s (one per sequence) moves to the next position and takes the greedy token next[s].
