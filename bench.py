@@ -258,6 +258,86 @@ class GdnDecode(Workload):
                 "sample": f"{n} full decode steps (B={self.B}, H={self.H}) of the oracle's recur_body restatement"}
 
 
+class GdnPrefill(Workload):
+    """Config 2: chunked Gated DeltaNet prefill, B sequences x T tokens x H heads, dk = dv = 128, S0 = 0."""
+    name = "gdn_prefill"
+    kernel = "gdn_chunk_prefill_kernel"
+    bound = "tensor"
+
+    def __init__(self, B=8, T=8192, H=16, d=128):
+        self.B, self.T, self.H, self.d = B, T, H, d
+        self.tokens_per_step = B * T
+
+    def hbm_bytes(self):
+        B, T, H, d = self.B, self.T, self.H, self.d
+        return B * T * H * d * 2 * 3 + B * T * H * 8 + B * T * H * d * 2 + B * H * d * d * 4
+
+    def config(self):
+        return {"workload": f"gdn_chunk_prefill B={self.B} T={self.T} H={self.H} dk=dv={self.d} chunk=64, "
+                            f"S0=0, o bf16 (config 2)",
+                "global_batch": self.B, "seq_len": self.T, "heads": self.H,
+                "hbm_bytes_per_step": self.hbm_bytes(),
+                "l2": f"inputs larger than L2 ({self.hbm_bytes() / 1e9:.2f} GB)"}
+
+    def algorithmic(self):
+        """6 C d^2 + 10 C^2 d FLOP per (chunk, head), the triangular solve excluded."""
+        C, d = 64, self.d
+        chunks = self.B * self.H * ((self.T + C - 1) // C)
+        return (6 * C * d * d + 10 * C * C * d) * chunks
+
+    def setup(self, dev):
+        import torch
+        from tests._inputs import gdn_prefill_inputs
+
+        x = gdn_prefill_inputs(self.B, self.T, self.H, 3)
+        self.S0 = x["S"].to(dev)
+        self.x = {k: v.to(dev) for k, v in x.items()}
+        self.o = torch.empty(self.B, self.T, self.H, self.d, device=dev, dtype=torch.bfloat16)
+        self.host = {k: x[k].pin_memory() for k in ("q", "k", "v", "g", "beta")}
+        self.dev_in = {k: torch.empty_like(v, device=dev) for k, v in self.host.items()}
+        self.o_host = torch.empty(self.B, self.T, self.H, self.d, dtype=torch.bfloat16).pin_memory()
+
+    def step(self):
+        from evie_b200 import ops
+
+        x = self.x
+        x["S"].copy_(self.S0)
+        ops.gdn_chunk_prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], x["S"], self.o)
+        return 1
+
+    def e2e_step(self):
+        from evie_b200 import ops
+
+        h2d = 0
+        for k, v in self.host.items():
+            self.dev_in[k].copy_(v, non_blocking=True)
+            h2d += v.numel() * v.element_size()
+        d = self.dev_in
+        self.x["S"].copy_(self.S0)
+        ops.gdn_chunk_prefill(d["q"], d["k"], d["v"], d["g"], d["beta"], self.x["S"], self.o)
+        self.o_host.copy_(self.o, non_blocking=True)
+        return h2d, self.o.numel() * 2
+
+    def cpu_sample(self, threads):
+        import oracle
+        from tests._inputs import bf16_bits, gdn_prefill_inputs
+
+        oracle.set_threads(threads)
+        heads = min(threads, self.B * self.H)
+        Ts = min(self.T, 2048)
+        x = gdn_prefill_inputs(1, Ts, heads, 3)
+        args = (bf16_bits(x["q"]), bf16_bits(x["k"]), bf16_bits(x["v"]), x["g"].numpy(), x["beta"].numpy())
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 and n < 50:
+            oracle.gdn_prefill(x["S"].numpy().copy(), *args)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        per_head_token = dt / (heads * Ts)
+        return {"value": 1.0 / (per_head_token * self.H), "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": f"{n} calls of the oracle's token-sequential prefill on {heads} heads x {Ts} tokens, "
+                          f"scaled to {self.H} heads per token"}
+
+
 class GqaDecode(Workload):
     name = "gqa_decode"
     kernel = "gqa_decode_kernel"
@@ -578,12 +658,15 @@ class ModelDecode(Workload):
                           f"the CPU)"}
 
 
-WORKLOADS = {"gdn_decode": GdnDecode, "gqa_decode": GqaDecode, "model_decode": ModelDecode}
+WORKLOADS = {"gdn_decode": GdnDecode, "gdn_prefill": GdnPrefill, "gqa_decode": GqaDecode,
+             "model_decode": ModelDecode}
 
 
 def make_workload(args):
     cls = WORKLOADS[args.workload]
     kw = {"B": args.batch} if args.batch else {}
+    if cls is GdnPrefill and args.seq:
+        kw["T"] = args.seq
     if cls is ModelDecode:
         kw["rank"] = dist_env()[0]
         if args.prompt:
@@ -730,6 +813,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--batch", type=int, default=0, help="override the batch size (small profiling cases)")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length of model_decode")
+    ap.add_argument("--seq", type=int, default=0, help="override the sequence length of gdn_prefill")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

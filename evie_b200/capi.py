@@ -43,6 +43,8 @@ SIGNATURES = {
     "evie_read_max": (I, [P, P, SZ]),
     "evie_gdn_decode_step": (I, [P, P, P, P, P, P, P, I, I, I, I, P]),
     "evie_gdn_chunk_prefill": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, P]),
+    "evie_gdn_prefill_tokenwise": (I, [P, P, P, P, P, P, P, I, I, I, I, I, P]),
+    "evie_poll_device_errors": (I, []),
     "evie_gqa_decode_paged": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, F, P]),
     "evie_gqa_decode_paged_noalloc": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, F, P]),
 }

@@ -12,6 +12,7 @@
 //   * the two reductions over the key index (S^T k and S^T q) use warp shuffles across the 4 row groups
 //     of a warp, then a 4-warp shared-memory stage.
 #include "common.h"
+#include "gdn_chunk.h"
 #include "gdn_decode.h"
 
 namespace evie {
@@ -261,7 +262,21 @@ extern "C" evie_status evie_gdn_chunk_prefill(const void* q, const void* k, cons
   EVIE_ARG(chunk == 64, "evie_gdn_chunk_prefill: chunk must be 64 (got %d)", chunk);
   EVIE_ARG(B >= 0 && T >= 0 && H >= 0, "evie_gdn_chunk_prefill: negative size");
   EVIE_ARG((long)B * H * T == 0 || (q && k && v && g && beta && state && o), "evie_gdn_chunk_prefill: null pointer");
+  EVIE_ARG((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)state) & 15) == 0 && ((uintptr_t)o & 1) == 0,
+           "evie_gdn_chunk_prefill: q, k, v and state must be 16-byte aligned, o 2-byte aligned");
+  EVIE_ARG((long)B * H <= (1L << 31) - 1 && (long)B * T * H <= (1L << 40),
+           "evie_gdn_chunk_prefill: too many heads or tokens");
+  return evie::launch_gdn_chunk_prefill_bf16(q, k, v, g, beta, state, o, B, T, H, (cudaStream_t)stream);
+}
+
+extern "C" evie_status evie_gdn_prefill_tokenwise(const void* q, const void* k, const void* v, const float* g,
+                                                  const float* beta, float* state, void* o, int B, int T, int H,
+                                                  int dk, int dv, void* stream) {
+  EVIE_ARG(dk == 128 && dv == 128, "evie_gdn_prefill_tokenwise: dk = dv = 128 required (got %d, %d)", dk, dv);
+  EVIE_ARG(B >= 0 && T >= 0 && H >= 0, "evie_gdn_prefill_tokenwise: negative size");
+  EVIE_ARG((long)B * H * T == 0 || (q && k && v && g && beta && state && o),
+           "evie_gdn_prefill_tokenwise: null pointer");
   EVIE_ARG(((uintptr_t)state & 15) == 0 && ((uintptr_t)o & 7) == 0,
-           "evie_gdn_chunk_prefill: state must be 16-byte and o 8-byte aligned");
+           "evie_gdn_prefill_tokenwise: state must be 16-byte and o 8-byte aligned");
   return evie::launch_gdn_prefill_seq_bf16(q, k, v, g, beta, state, o, B, T, H, (cudaStream_t)stream);
 }

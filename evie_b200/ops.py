@@ -43,6 +43,22 @@ def gdn_chunk_prefill(q, k, v, g, beta, state, o=None, chunk: int = 64):
     return o
 
 
+def gdn_prefill_tokenwise(q, k, v, g, beta, state, o=None):
+    """Token-by-token Gated DeltaNet prefill (evie_gdn_prefill_tokenwise); same layouts as gdn_chunk_prefill."""
+    B, T, H, dk = q.shape
+    dv = v.shape[-1]
+    if o is None:
+        o = torch.empty(B, T, H, dv, device=q.device, dtype=torch.bfloat16)
+    check(lib().evie_gdn_prefill_tokenwise(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state), _ptr(o), B,
+                                           T, H, dk, dv, _stream()))
+    return o
+
+
+def poll_device_errors() -> None:
+    """Raises EvieError if a kernel gave up a bounded device-side wait since the last poll (synchronises)."""
+    check(lib().evie_poll_device_errors())
+
+
 def gqa_decode_paged(q, gate, k_pages, v_pages, page_table, ctx_lens, scale, out=None):
     """Gated GQA decode attention over a paged bf16 KV cache (evie_gqa_decode_paged).
 

@@ -121,12 +121,28 @@ EVIE_API evie_status evie_read_max(evie_ctx* ctx, float* out, size_t n);
 EVIE_API evie_status evie_gdn_decode_step(const void* q, const void* k, const void* v, const float* g, const float* beta,
                                  float* state, float* o, int B, int H, int dk, int dv, void* stream);
 
-/* Gated DeltaNet prefill over T tokens, chunked (chunk = 64) on tcgen05 tensor cores. Same recurrence as
- * evie-core's token-sequential loop (model.rs:362-387). q,k: [B][T][H][dk] bf16; v: [B][T][H][dv] bf16;
- * g, beta: [B][T][H] f32; state: [B][H][dk][dv] f32, initial state in, final state out; o: [B][T][H][dv] bf16. */
+/* Gated DeltaNet prefill over T tokens, chunked (chunk = 64) on tcgen05 tensor cores: the recurrence of evie-core's
+ * token-sequential loop (model.rs:362-387, recur_body model.rs:501-541) regrouped per chunk with a triangular solve,
+ * every f32 operand split into bf16 hi + lo planes so that the result follows the f32 recurrence (~1e-5 relative).
+ * q,k: [B][T][H][dk] bf16; v: [B][T][H][dv] bf16 (all three 16-byte aligned); g (log decay, <= 0), beta: [B][T][H]
+ * f32; state: [B][H][dk][dv] f32 (16-byte aligned), initial state in, final state out; o: [B][T][H][dv] bf16.
+ * dk = dv = 128, chunk = 64. One CTA per (sequence, head). */
 EVIE_API evie_status evie_gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* g, const float* beta,
                                    float* state, void* o, int B, int T, int H, int dk, int dv, int chunk,
                                    void* stream);
+
+/* The same prefill, token by token (the order of evie-core's loop, model.rs:362-387) with the state slice held in
+ * registers: for short prompts, where chunking has nothing to amortise. Same layouts as evie_gdn_chunk_prefill
+ * (o 8-byte aligned). */
+EVIE_API evie_status evie_gdn_prefill_tokenwise(const void* q, const void* k, const void* v, const float* g,
+                                                const float* beta, float* state, void* o, int B, int T, int H, int dk,
+                                                int dv, void* stream);
+
+/* Synchronises the current device and reports whether any kernel gave up a bounded device-side wait (an mbarrier
+ * that did not complete within 2 s) since the last poll: EVIE_ERR_TIMEOUT with the count in the message, then the
+ * count restarts at zero. Such a kernel drained its copies, freed its tensor memory and left its outputs
+ * incomplete. */
+EVIE_API evie_status evie_poll_device_errors(void);
 
 /* Gated GQA softmax attention decode over a paged bf16 KV cache (the attention core of Model::attention,
  * model.rs:445-464; WGSL attn_scores/attn_out, gpu/kernels.wgsl:508-589), split-KV with an in-kernel combine:
