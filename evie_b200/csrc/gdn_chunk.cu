@@ -5,42 +5,45 @@
 // Grouped into chunks of C = 64 tokens it reads, for one head with S the [dk][dv] state entering the chunk,
 // G_t = g_0 + ... + g_t (in-chunk cumulative log decay) and Gam_t = exp(G_t):
 //   N[t][s] = beta_t (k_t . k_s) exp(G_t - G_s)          for s < t (strictly lower triangular)
-//   T       = (I + N)^-1 diag(beta)                       (forward substitution)
+//   T       = (I + N)^-1 diag(beta)                       (blocked forward substitution)
 //   U       = T (V - diag(Gam) K S)                       (the chunk's delta rows, [C][dv])
 //   O       = diag(Gam) Q S + P U,   P[t][s] = (q_t . k_s) exp(G_t - G_s) for s <= t, else 0
 //   S'      = Gam_C S + K^T diag(exp(G_C - G_t)) U
 // Only exponentials of differences G_t - G_s with s <= t appear (never exp(-G)), so nothing overflows for any
-// chunk length or decay.
+// chunk length or decay. Exponentials are taken as exp2 of log2-scaled sums.
 //
 // Precision. q, k, v are bf16 and enter the tensor core exactly (kind::f16, f32 accumulation). Every f32-valued
 // operand (S, V - Gam K S, U, exp-weighted U, T, P) is split into bf16 planes hi + lo (x - hi - lo ~ 2^-17 |x|);
 // a product with an exact bf16 partner takes two MMAs (hi, lo), a product of two split operands three
 // (hi.hi + hi.lo + lo.hi). The result follows the f32 recurrence to ~1e-5 relative.
 //
-// Work layout. One CTA per (sequence, head), 128 threads, one CTA per SM (it takes 226 KB of shared memory and all
-// 512 TMEM columns). Every S-dependent product is computed transposed, so that M = 128 runs along dv and thread j
-// (TMEM lane j) owns row dv = j of each accumulator:
-//   TMEM [0,128)   S^T           [dv][dk]   persistent across chunks, rescaled by Gam_C in place
-//        [128,192) [K;Q] K^T     lanes 0-63 / 64-127 = the two stacked 64-row operands, columns = s
-//        [192,256) (K S)^T       [dv][t]
-//        [256,320) (Q S)^T       [dv][t]
-//        [320,384) U^T           [dv][t]
-//        [384,448) (P U)^T       [dv][t]
+// Work layout. One CTA per (sequence, head), 256 threads in two warp groups, one CTA per SM (226 KB of shared
+// memory, all 512 TMEM columns).
+//   * Chain warps 0-3 carry the state from chunk to chunk. Every S-dependent product is computed transposed, so
+//     that M = 128 runs along dv and thread j (TMEM lane j) owns row dv = j of each accumulator. Thread 0 issues
+//     their MMAs and all TMA loads.
+//   * Prep warps 4-7 work one chunk ahead on what does not depend on S: the decay sums, [K;Q] K^T (thread 128
+//     issues it), N, P and T. They hand a chunk over through an mbarrier (tp_ready) and wait for the chain to
+//     release the buffers two chunks later (chunk_done).
+// TMEM columns:
+//   [0,128)   S^T f32 [dv][dk], holding Gam_C S entering each chunk's update
+//   [128,192) S^T bf16 hi, [192,256) S^T bf16 lo (A operand of the S products, two values per column)
+//   [256,320) [K;Q] K^T (prep)            [320,448) (S^T [K;Q]^T): (K S)^T and (Q S)^T halves; (P U)^T reuses the
+//   (K S)^T half                          [448,512) U^T
 // Shared memory (1024-aligned offsets):
-//   [0, 48K)        q/k tiles, two dk halves of 24 KB: [K slot 0 | Q | K slot 1], 8 KB each, 128-byte swizzled
-//                   K-major (TMA SW128). K is double-buffered so the next chunk's K loads during this one; the
-//                   stacked [K;Q] (even chunks) or [Q;K] (odd chunks) is one 128-row MMA operand.
-//   [48K, 64K)      v tile [64 t][128 dv] bf16, unswizzled (read by the epilogue threads only)
-//   [64K, 128K)     S^T hi / lo planes (MMA A operand, [dv][dk] K-major, two 64-wide dk atoms)
-//   [128K, 160K)    R^T = (V - Gam K S)^T hi/lo, then U^T hi/lo ([dv][t] K-major)
-//   [160K, 192K)    (exp(G_C - G_t) U)^T hi/lo; earlier in the chunk the f32 N^T for the forward substitution
-//   [192K, 208K)    T hi/lo ([t][s] K-major, the B operand of U^T = R^T T^T)
-//   [208K, 224K)    P hi/lo ([t][s] K-major, the B operand of (P U)^T = U^T P^T)
-//   [224K, +1152)   G, Gam, exp(G_C - G), beta (64 f32 each), mbarriers, TMEM base
+//   [0, 64K)       q/k tiles, two dk halves of 32 KB: [K0 | Q0 | Q1 | K1], 8 KB each, 128-byte swizzled K-major
+//                  (TMA SW128). Chunk c uses K(c&1), Q(c&1); the stacks [K0;Q0] and [Q1;K1] are 128-row operands.
+//   [64K, 80K)     v tile [64 t][128 dv] bf16, unswizzled
+//   [80K, 112K)    R^T = (V - Gam K S)^T hi/lo, then U^T hi/lo ([dv][t] K-major)
+//   [112K, 144K)   (exp(G_C - G_t) U)^T hi/lo
+//   [144K, 176K)   T hi/lo, two buffers ([t][s] K-major, the B operand of U^T = R^T T^T)
+//   [176K, 208K)   P hi/lo, two buffers ([t][s] K-major, the B operand of (P U)^T = U^T P^T)
+//   [208K, 224K)   f32 [64][64]: N^T above the diagonal; the solve's T11 and N21 T11 below it
+//   [224K, +1792)  Gam, exp(G_C - G) (two buffers), G (log2 units), beta, mbarriers, TMEM base
 //
-// Every mbarrier wait is bounded (2 s of %globaltimer). A wait that gives up bumps a device counter (read by
-// evie_poll_device_errors), makes the CTA drain its outstanding copies and MMAs (bounded again), free its TMEM and
-// return.
+// Every mbarrier wait is bounded (2 s of %globaltimer) and every group barrier ORs a failure flag, so both warp
+// groups leave together. A wait that gives up bumps a device counter (read by evie_poll_device_errors); the CTA
+// then drains its outstanding copies and MMAs (bounded again), frees its TMEM and returns.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -57,68 +60,72 @@ namespace {
 
 constexpr int kC = 64;
 constexpr int kD = 128;
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 
-constexpr uint32_t kKQHalf = 24576;  // one dk half of the q/k area
-constexpr uint32_t kSlotQ = 8192;
-__device__ __forceinline__ constexpr uint32_t kslot(int parity) { return parity ? 16384u : 0u; }  // K slots
-constexpr uint32_t kOffV = 49152;
-constexpr uint32_t kOffST = 65536;   // planes 32 KB apart, dk halves 16 KB apart
-constexpr uint32_t kOffRU = 131072;  // planes 16 KB apart
-constexpr uint32_t kOffEU = 163840;  // planes 16 KB apart
-constexpr uint32_t kOffTM = 196608;  // planes 8 KB apart
-constexpr uint32_t kOffPM = 212992;  // planes 8 KB apart
+constexpr uint32_t kKQHalf = 32768;
+__device__ __forceinline__ uint32_t kslot(int p) { return p ? 24576u : 0u; }
+__device__ __forceinline__ uint32_t qslot(int p) { return p ? 16384u : 8192u; }
+__device__ __forceinline__ uint32_t stack_off(int p) { return p ? 16384u : 0u; }  // [K0;Q0] or [Q1;K1]
+constexpr uint32_t kOffV = 65536;
+constexpr uint32_t kOffRU = 81920;   // planes 16 KB apart
+constexpr uint32_t kOffEU = 114688;  // planes 16 KB apart
+constexpr uint32_t kOffTM = 147456;  // buffers 16 KB apart, planes 8 KB apart
+constexpr uint32_t kOffPM = 180224;  // buffers 16 KB apart, planes 8 KB apart
+constexpr uint32_t kOffNT = 212992;
 constexpr uint32_t kOffSmall = 229376;
-constexpr uint32_t kSmallBytes = 1152;
+constexpr uint32_t kSmallBytes = 1792;
 constexpr uint32_t kSmemBytes = kOffSmall + kSmallBytes + 1024;  // + slack to align the base to 1024
 static_assert(kSmemBytes <= 232448, "shared memory map exceeds 227 KB");
 
-constexpr uint32_t kColS = 0, kColA = 128, kColKS = 192, kColQS = 256, kColU = 320, kColO = 384;
+constexpr uint32_t kColS = 0, kColSH = 128, kColSL = 192, kColA = 256, kColKQS = 320, kColU = 448;
+
+// mbarriers
+enum { BK0 = 0, BK1, BQ0, BQ1, BV, BMC, BMP, BTR0, BTR1, BCD0, BCD1, kNumBars };
+constexpr uint32_t kChainBar = 1, kPrepBar = 2;  // named barriers of the two warp groups (128 threads each)
+constexpr float kLog2e = 1.4426950408889634f;
 
 // Byte offset of 16-byte chunk `c` of row `r` in a K-major tile with 128-byte rows and the 128-byte swizzle.
 __device__ __forceinline__ uint32_t swz(int r, int c) {
   return (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
 }
+// Byte offset of 16-bit element `e` of row `r` in the same tile.
+__device__ __forceinline__ uint32_t swz_elem(int r, int e) { return swz(r, e >> 3) + (uint32_t)(e & 7) * 2u; }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo_addr, float hi_addr) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo_addr, hi_addr);
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// 8 floats -> bf16 hi = round(x) and lo = round(x - hi), 8 each packed in a uint4.
-__device__ __forceinline__ void split8(const float* x, uint4& hi, uint4& lo) {
-  float h[8], l[8];
+// 2n floats -> n words of bf16 hi = round(x) and n words of lo = round(x - hi), pairs packed low-half-first.
+template <int N>
+__device__ __forceinline__ void split_pairs(const float* x, uint32_t* hi, uint32_t* lo) {
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
-    h[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
-    l[i] = x[i] - h[i];
+  for (int i = 0; i < N; i++) {
+    const float h0 = __bfloat162float(__float2bfloat16_rn(x[2 * i]));
+    const float h1 = __bfloat162float(__float2bfloat16_rn(x[2 * i + 1]));
+    hi[i] = pack_bf16x2(h0, h1);
+    lo[i] = pack_bf16x2(x[2 * i] - h0, x[2 * i + 1] - h1);
   }
-  hi = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]), pack_bf16x2(h[6], h[7]));
-  lo = make_uint4(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]), pack_bf16x2(l[4], l[5]), pack_bf16x2(l[6], l[7]));
 }
 
 // Row r (64 f32) of a split K-major SW128 tile: hi plane at `tile`, lo plane `plane` bytes further.
 __device__ __forceinline__ void store_row64(uint8_t* tile, uint32_t plane, int r, const float* x) {
 #pragma unroll
   for (int c = 0; c < 8; c++) {
-    uint4 hi, lo;
-    split8(x + 8 * c, hi, lo);
-    *reinterpret_cast<uint4*>(tile + swz(r, c)) = hi;
-    *reinterpret_cast<uint4*>(tile + plane + swz(r, c)) = lo;
+    uint32_t hi[4], lo[4];
+    split_pairs<4>(x + 8 * c, hi, lo);
+    *reinterpret_cast<uint4*>(tile + swz(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(tile + plane + swz(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
 }
 
-// 16 consecutive dk (dk0 a multiple of 16) of row dv of the split S^T operand.
-__device__ __forceinline__ void store_st16(uint8_t* sm, int dv, int dk0, const float* x) {
-  uint8_t* base = sm + kOffST + (dk0 >> 6) * 16384;
-#pragma unroll
-  for (int cc = 0; cc < 2; cc++) {
-    uint4 hi, lo;
-    split8(x + 8 * cc, hi, lo);
-    const uint32_t off = swz(dv, ((dk0 & 63) >> 3) + cc);
-    *reinterpret_cast<uint4*>(base + off) = hi;
-    *reinterpret_cast<uint4*>(base + 32768 + off) = lo;
-  }
+// One split element: T[row][col] into the hi/lo planes of a 64x64 K-major tile.
+__device__ __forceinline__ void store_elem(uint8_t* tile, int row, int col, float x) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+  const uint32_t off = swz_elem(row, col);
+  *reinterpret_cast<__nv_bfloat16*>(tile + off) = hi;
+  *reinterpret_cast<__nv_bfloat16*>(tile + 8192 + off) = lo;
 }
 
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
@@ -126,44 +133,22 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
   for (int i = 0; i < 4; i++) tc::tmem_ld16(taddr + 16 * i, v + 16 * i);
 }
 
-// T = (I + N)^-1 diag(beta), column j, by forward substitution (right-looking: once T[s][j] is known it is pushed
-// into the partial sums of every later row). N^T[s][t] = N[t][s] is read as broadcast float4s.
-__device__ __forceinline__ void solve_T_column(uint8_t* sm, const float* Bs, int j) {
-  const float* NT = reinterpret_cast<const float*>(sm + kOffEU);
-  float x[kC];
+// Forward substitution on a 32x32 diagonal block of (I + N): x holds the right-hand side on entry and the solution
+// on exit. NT[s][t] = N[base+t][base+s] is read as broadcast float4s (row base+s of the f32 N^T array).
+__device__ __forceinline__ void forward32(const float* NT, int base, float* x) {
 #pragma unroll
-  for (int t = 0; t < kC; t++) x[t] = 0.f;
+  for (int s = 0; s < 32; s++) {
+    const float xs = x[s];
+    const float* row = NT + (base + s) * kC + base;
 #pragma unroll
-  for (int s = 0; s < kC; s++) {
-    x[s] = (s == j ? Bs[s] : 0.f) - x[s];
-#pragma unroll
-    for (int t4 = ((s + 1) >> 2) << 2; t4 < kC; t4 += 4) {
-      const float4 n = *reinterpret_cast<const float4*>(NT + s * kC + t4);
-      if (t4 + 0 > s) x[t4 + 0] = fmaf(n.x, x[s], x[t4 + 0]);
-      if (t4 + 1 > s) x[t4 + 1] = fmaf(n.y, x[s], x[t4 + 1]);
-      if (t4 + 2 > s) x[t4 + 2] = fmaf(n.z, x[s], x[t4 + 2]);
-      if (t4 + 3 > s) x[t4 + 3] = fmaf(n.w, x[s], x[t4 + 3]);
+    for (int t4 = ((s + 1) >> 2) << 2; t4 < 32; t4 += 4) {
+      const float4 n = *reinterpret_cast<const float4*>(row + t4);
+      if (t4 + 0 > s) x[t4 + 0] = fmaf(-n.x, xs, x[t4 + 0]);
+      if (t4 + 1 > s) x[t4 + 1] = fmaf(-n.y, xs, x[t4 + 1]);
+      if (t4 + 2 > s) x[t4 + 2] = fmaf(-n.z, xs, x[t4 + 2]);
+      if (t4 + 3 > s) x[t4 + 3] = fmaf(-n.w, xs, x[t4 + 3]);
     }
   }
-  uint8_t* tm = sm + kOffTM;
-#pragma unroll
-  for (int s = 0; s < kC; s++) {
-    const __nv_bfloat16 hi = __float2bfloat16_rn(x[s]);
-    const __nv_bfloat16 lo = __float2bfloat16_rn(x[s] - __bfloat162float(hi));
-    const uint32_t off = (uint32_t)s * 128u + ((uint32_t)((j >> 3) ^ (s & 7)) << 4) + (uint32_t)(j & 7) * 2u;
-    *reinterpret_cast<__nv_bfloat16*>(tm + off) = hi;
-    *reinterpret_cast<__nv_bfloat16*>(tm + 8192 + off) = lo;
-  }
-}
-
-// R^T row dv = V[:, dv] - Gam (K S)^T[dv, :], split into the R^T operand.
-__device__ __forceinline__ void compute_R_row(uint8_t* sm, uint32_t tl, const float* Gam, int dv) {
-  float r[kC];
-  tmem_ld64(tl + kColKS, r);
-  const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + kOffV);
-#pragma unroll
-  for (int t = 0; t < kC; t++) r[t] = fmaf(-Gam[t], r[t], __bfloat162float(V[t * kD + dv]));
-  store_row64(sm + kOffRU, 16384, dv, r);
 }
 
 struct ChunkArgs {
@@ -186,16 +171,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int T = a.T, H = a.H;
   const int nch = (T + kC - 1) / kC;
 
-  float* Gs = reinterpret_cast<float*>(sm + kOffSmall);  // cumulative log decay within the chunk
-  float* Gam = Gs + 64;                                  // exp(G_t)
-  float* Ec = Gs + 128;                                  // exp(G_63 - G_t)
-  float* Bs = Gs + 192;                                  // beta_t (0 past the end of the sequence)
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffSmall + 1024);  // K slot 0, K slot 1, Q, V, MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffSmall + 1024 + 64);
+  float* GamB = reinterpret_cast<float*>(sm + kOffSmall);  // [2][64] exp(G_t)
+  float* EcB = GamB + 128;                                  // [2][64] exp(G_63 - G_t)
+  float* G2 = GamB + 256;                                   // [64] G_t * log2(e) (prep only)
+  float* Bs = GamB + 320;                                   // [64] beta_t, 0 past the end of the sequence
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffSmall + 1536);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffSmall + 1536 + 8 * kNumBars);
+  float* NT = reinterpret_cast<float*>(sm + kOffNT);
 
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
   if (tid == 0) {
-    for (int i = 0; i < 5; i++) tc::mbar_init(&bar[i], 1);
+    for (int i = 0; i < kNumBars; i++)
+      tc::mbar_init(&bar[i], (i == BTR0 || i == BTR1 || i == BCD0 || i == BCD1) ? 128 : 1);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&mq);
     tc::prefetch_tmap(&mk);
@@ -205,265 +192,371 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's quarter of the TMEM lanes
-
-  // Completion counts per barrier: issued (thread 0) and observed (every thread); parity = observed & 1.
-  uint32_t issued[5] = {0, 0, 0, 0, 0}, seen[5] = {0, 0, 0, 0, 0};
+  const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's quarter of the TMEM lanes
   bool ok = true;
-  auto wait = [&](int i) {  // after a failure nothing more is waited for; `seen` counts completions observed
-    if (ok && !tc::mbar_wait(&bar[i], seen[i] & 1)) ok = false;
-    if (ok) seen[i]++;
+  // Barriers with an operation in flight that the issuing thread has not seen complete, and that phase's parity.
+  uint32_t pend = 0, ppar = 0;
+  auto mark = [&](int i, uint32_t parity) {
+    pend |= 1u << i;
+    ppar = (ppar & ~(1u << i)) | (parity << i);
   };
-  auto issue_k = [&](int c) {
-    uint64_t* bb = &bar[c & 1];
-    tc::mbar_arrive_expect_tx(bb, 16384);
-    for (int hf = 0; hf < 2; hf++) tc::tma_load_4d(sm + hf * kKQHalf + kslot(c & 1), &mk, bb, hf * 64, h, c * kC, b);
-    issued[c & 1]++;
-  };
-  auto issue_q = [&](int c) {
-    tc::mbar_arrive_expect_tx(&bar[2], 16384);
-    for (int hf = 0; hf < 2; hf++) tc::tma_load_4d(sm + hf * kKQHalf + kSlotQ, &mq, &bar[2], hf * 64, h, c * kC, b);
-    issued[2]++;
-  };
-  auto issue_v = [&](int c) {
-    tc::mbar_arrive_expect_tx(&bar[3], 16384);
-    tc::tma_load_4d(sm + kOffV, &mv, &bar[3], 0, h, c * kC, b);
-    issued[3]++;
+  auto wait = [&](int i, uint32_t parity) {
+    if (ok && !tc::mbar_wait(&bar[i], parity)) ok = false;
+    if (ok && ((pend >> i) & 1u) && ((ppar >> i) & 1u) == parity) pend &= ~(1u << i);
   };
 
-  if (tid == 0 && nch > 0) {
-    issue_k(0);
-    issue_q(0);
-    issue_v(0);
-  }
-
-  // Entering state: thread j takes column j of S ([dk][dv]) = row j of S^T, into TMEM and the split operand.
-  float* Sg = a.state + (size_t)bh * kD * kD;
-#pragma unroll 1
-  for (int c16 = 0; c16 < 8; c16++) {
-    float col[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) col[i] = Sg[(size_t)(c16 * 16 + i) * kD + tid];
-    tc::tmem_st16(tl + kColS + c16 * 16, col);
-    store_st16(sm, tid, c16 * 16, col);
-  }
-  tc::tmem_st_wait();
-  tc::fence_proxy_async();
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-
-  constexpr uint32_t id64 = tc::idesc(1, 1, 128, 64);
-  constexpr uint32_t idS = tc::idesc(1, 1, 128, 128, false, true);
-  bool aborted = false;
-
-#pragma unroll 1
-  for (int c = 0; c < nch; c++) {
-    const int p = c & 1, t0 = c * kC;
-
-    // ---- decay and beta of this chunk; cumulative sums over the 64 tokens
-    if (tid < 64) {
-      const int t = t0 + tid;
-      float gv = 0.f, bv = 0.f;
-      if (t < T) {
-        const size_t r = ((size_t)b * T + t) * H + h;
-        gv = __ldg(a.g + r);
-        bv = __ldg(a.beta + r);
+  if (warp < 4) {
+    // =================================== chain warps ===================================
+    auto issue_kq = [&](int c) {
+      const int p = c & 1;
+      tc::mbar_arrive_expect_tx(&bar[BK0 + p], 16384);
+      tc::mbar_arrive_expect_tx(&bar[BQ0 + p], 16384);
+      for (int hf = 0; hf < 2; hf++) {
+        tc::tma_load_4d(sm + hf * kKQHalf + kslot(p), &mk, &bar[BK0 + p], hf * 64, h, c * kC, b);
+        tc::tma_load_4d(sm + hf * kKQHalf + qslot(p), &mq, &bar[BQ0 + p], hf * 64, h, c * kC, b);
       }
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, gv, off);
-        if (lane >= off) gv += y;
-      }
-      Gs[tid] = gv;
-      Bs[tid] = bv;
+      mark(BK0 + p, (c >> 1) & 1);
+      mark(BQ0 + p, (c >> 1) & 1);
+    };
+    auto issue_v = [&](int c) {
+      tc::mbar_arrive_expect_tx(&bar[BV], 16384);
+      tc::tma_load_4d(sm + kOffV, &mv, &bar[BV], 0, h, c * kC, b);
+      mark(BV, c & 1);
+    };
+    if (tid == 0 && nch > 0) {
+      issue_kq(0);
+      if (nch > 1) issue_kq(1);
+      issue_v(0);
     }
-    __syncthreads();
-    if (tid >= 32 && tid < 64) Gs[tid] += Gs[31];
-    __syncthreads();
-    if (tid < 64) {
-      Gam[tid] = expf(Gs[tid]);
-      Ec[tid] = expf(Gs[63] - Gs[tid]);
-    }
+    float* Sg = a.state + (size_t)bh * kD * kD;
+    uint32_t nmc = 0;  // completions of the chain's MMA barrier seen
+    constexpr uint32_t id64 = tc::idesc(1, 1, 128, 64);
+    constexpr uint32_t id128 = tc::idesc(1, 1, 128, 128);
+    constexpr uint32_t idS = tc::idesc(1, 1, 128, 128, false, true);
 
-    // ---- this chunk's q, k, v tiles
-    wait(p);
-    wait(2);
-    wait(3);
-    if (__syncthreads_or(!ok)) { aborted = true; break; }
-
-    // ---- MMA: [K;Q] K^T, (K S)^T, (Q S)^T
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t stack = p == 0 ? kslot(0) : kSlotQ;  // [K;Q] on even chunks, [Q;K] on odd ones
-#pragma unroll
-      for (int s = 0; s < 8; s++) {
-        const uint32_t kb = (s >> 2) * kKQHalf + (s & 3) * 32;
-        tc::mma_f16(tmem + kColA, tc::sdesc_k_sw128(sm + kb + stack), tc::sdesc_k_sw128(sm + kb + kslot(p)), id64,
-                    s > 0);
-      }
-#pragma unroll
-      for (int pl = 0; pl < 2; pl++)
-#pragma unroll
-        for (int s = 0; s < 8; s++) {
-          const uint64_t ad = tc::sdesc_k_sw128(sm + kOffST + pl * 32768 + (s >> 2) * 16384 + (s & 3) * 32);
-          const uint32_t kb = (s >> 2) * kKQHalf + (s & 3) * 32;
-          tc::mma_f16(tmem + kColKS, ad, tc::sdesc_k_sw128(sm + kb + kslot(p)), id64, (pl | s) > 0);
-          tc::mma_f16(tmem + kColQS, ad, tc::sdesc_k_sw128(sm + kb + kSlotQ), id64, (pl | s) > 0);
-        }
-      tc::mma_commit(&bar[4]);
-      issued[4]++;
-      if (c + 1 < nch) issue_k(c + 1);  // the other K slot was last read by the previous chunk's S update
-    }
-    wait(4);
-    if (__syncthreads_or(!ok)) { aborted = true; break; }
-    tc::fence_after_sync();
-    if (tid == 0 && c + 1 < nch) issue_q(c + 1);  // Q has been consumed
-
-    // ---- N (forward-substitution matrix, transposed, f32) and P (split), one row per thread
-    {
-      const bool k_rows = (p == 0) == (warp < 2);  // which lane half holds K K^T this chunk
-      const int r = tid & 63;
-      float row[kC];
-      tmem_ld64(tl + kColA, row);
-      const float Gr = Gs[r];
-      if (k_rows) {
-        float* NT = reinterpret_cast<float*>(sm + kOffEU);
-        const float br = Bs[r];
-#pragma unroll
-        for (int s = 0; s < kC; s++) NT[s * kC + r] = s < r ? br * row[s] * expf(Gr - Gs[s]) : 0.f;
-      } else {
-#pragma unroll
-        for (int s = 0; s < kC; s++) row[s] = s <= r ? row[s] * expf(Gr - Gs[s]) : 0.f;
-        store_row64(sm + kOffPM, 8192, r, row);
-      }
-    }
-    tc::fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-
-    // ---- T (warps 0-1, one column each) while warps 2-3 form R^T for dv 64..127; then R^T for dv 0..63
-    if (warp < 2) solve_T_column(sm, Bs, tid);
-    compute_R_row(sm, tl, Gam, tid);
-    tc::fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-
-    // ---- MMA: U^T = R^T T^T (three passes)
-    if (tid == 0) {
-      if (c + 1 < nch) issue_v(c + 1);  // V has been consumed
-      int n = 0;
-#pragma unroll
-      for (int pa = 0; pa < 2; pa++)
-#pragma unroll
-        for (int pb = 0; pb < 2; pb++) {
-          if (pa & pb) continue;
-#pragma unroll
-          for (int s = 0; s < 4; s++, n++)
-            tc::mma_f16(tmem + kColU, tc::sdesc_k_sw128(sm + kOffRU + pa * 16384 + s * 32),
-                        tc::sdesc_k_sw128(sm + kOffTM + pb * 8192 + s * 32), id64, n > 0);
-        }
-      tc::mma_commit(&bar[4]);
-      issued[4]++;
-    }
-    wait(4);
-    if (__syncthreads_or(!ok)) { aborted = true; break; }
-    tc::fence_after_sync();
-
-    // ---- U^T and the exp-weighted U^T as split operands; S^T <- Gam_C S^T in TMEM
-    {
-      float u[kC];
-      tmem_ld64(tl + kColU, u);
-      store_row64(sm + kOffRU, 16384, tid, u);
-#pragma unroll
-      for (int t = 0; t < kC; t++) u[t] *= Ec[t];
-      store_row64(sm + kOffEU, 16384, tid, u);
-      const float gc = Gam[63];
+    // Writes S^T row `tid` (16 dk at a time from `src`) as the split bf16 operand and Gam_C * S^T as the f32
+    // accumulator (or, after the last chunk, S out to global memory).
+    auto stage_state = [&](bool from_global, bool last, float gc) {
 #pragma unroll 1
       for (int c16 = 0; c16 < 8; c16++) {
         float sv[16];
-        tc::tmem_ld16(tl + kColS + c16 * 16, sv);
+        if (from_global) {
+#pragma unroll
+          for (int i = 0; i < 16; i++) sv[i] = Sg[(size_t)(c16 * 16 + i) * kD + tid];
+        } else {
+          tc::tmem_ld16(tl + kColS + c16 * 16, sv);
+        }
+        if (last) {
+#pragma unroll
+          for (int i = 0; i < 16; i++) Sg[(size_t)(c16 * 16 + i) * kD + tid] = sv[i];
+          continue;
+        }
+        uint32_t hi[8], lo[8];
+        split_pairs<8>(sv, hi, lo);
+        tc::tmem_st8(tl + kColSH + c16 * 8, hi);
+        tc::tmem_st8(tl + kColSL + c16 * 8, lo);
 #pragma unroll
         for (int i = 0; i < 16; i++) sv[i] *= gc;
         tc::tmem_st16(tl + kColS + c16 * 16, sv);
       }
       tc::tmem_st_wait();
+    };
+
+    if (nch > 0) {
+      wait(BTR0, 0);
+      if (ok) stage_state(true, false, GamB[63]);
     }
-    tc::fence_proxy_async();
     tc::fence_before_sync();
-    __syncthreads();
+    if (tc::group_sync_or(kChainBar, 128, !ok)) ok = false;
     tc::fence_after_sync();
 
-    // ---- MMA: (P U)^T = U^T P^T (three passes); S^T += (E U)^T K (two passes, K as an MN-major operand)
-    if (tid == 0) {
-      int n = 0;
-#pragma unroll
-      for (int pa = 0; pa < 2; pa++)
-#pragma unroll
-        for (int pb = 0; pb < 2; pb++) {
-          if (pa & pb) continue;
-#pragma unroll
-          for (int s = 0; s < 4; s++, n++)
-            tc::mma_f16(tmem + kColO, tc::sdesc_k_sw128(sm + kOffRU + pa * 16384 + s * 32),
-                        tc::sdesc_k_sw128(sm + kOffPM + pb * 8192 + s * 32), id64, n > 0);
-        }
-#pragma unroll
-      for (int pa = 0; pa < 2; pa++)
-#pragma unroll
-        for (int s = 0; s < 4; s++)
-          tc::mma_f16(tmem + kColS, tc::sdesc_k_sw128(sm + kOffEU + pa * 16384 + s * 32),
-                      tc::sdesc_mn_sw128(sm + kslot(p) + s * 2048, kKQHalf, 1024), idS, 1);
-      tc::mma_commit(&bar[4]);
-      issued[4]++;
-    }
-    wait(4);
-    if (__syncthreads_or(!ok)) { aborted = true; break; }
-    tc::fence_after_sync();
-
-    // ---- outputs o_t = Gam_t (Q S)^T + (P U)^T; the new S^T into the split operand (or out, after the last chunk)
-    {
-      __nv_bfloat16* og = a.o + (((size_t)b * T + t0) * H + h) * kD + tid;
-      const int nt = min(kC, T - t0);
 #pragma unroll 1
-      for (int c16 = 0; c16 < 4; c16++) {
-        float ov[16], qs[16];
-        tc::tmem_ld16(tl + kColO + c16 * 16, ov);
-        tc::tmem_ld16(tl + kColQS + c16 * 16, qs);
+    for (int c = 0; c < nch && ok; c++) {
+      const int p = c & 1, t0 = c * kC;
+      const float* Gam = GamB + 64 * p;
+      const float* Ec = EcB + 64 * p;
+      const uint32_t ks_col = kColKQS + (p ? 64u : 0u), qs_col = kColKQS + (p ? 0u : 64u);
+
+      // ---- (K S)^T | (Q S)^T = S^T [stack]^T, A = S^T hi/lo from TMEM
+      if (tid == 0) {
+        wait(BK0 + p, (c >> 1) & 1);
+        wait(BQ0 + p, (c >> 1) & 1);
+        tc::fence_after_sync();
+        if (ok) {
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const int t = c16 * 16 + i;
-          if (t < nt) og[(size_t)t * H * kD] = __float2bfloat16_rn(fmaf(Gam[t], qs[i], ov[i]));
+          for (int pl = 0; pl < 2; pl++)
+#pragma unroll
+            for (int s = 0; s < 8; s++)
+              tc::mma_f16_ts(tmem + kColKQS, tmem + (pl ? kColSL : kColSH) + s * 8,
+                             tc::sdesc_k_sw128(sm + (s >> 2) * kKQHalf + stack_off(p) + (s & 3) * 32), id128,
+                             (pl | s) > 0);
+          tc::mma_commit(&bar[BMC]);
+          mark(BMC, nmc & 1);
         }
       }
+      wait(BMC, nmc & 1);
+      nmc++;
+      wait(BV, c & 1);
+      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      tc::fence_after_sync();
+
+      // ---- R^T row: V[:, dv] - Gam (K S)^T[dv, :]
+      {
+        float r[kC];
+        tmem_ld64(tl + ks_col, r);
+        const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + kOffV);
+#pragma unroll
+        for (int t = 0; t < kC; t++) r[t] = fmaf(-Gam[t], r[t], __bfloat162float(V[t * kD + tid]));
+        store_row64(sm + kOffRU, 16384, tid, r);
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      tc::fence_after_sync();
+
+      // ---- U^T = R^T T^T (three passes)
+      if (tid == 0) {
+        if (c + 1 < nch) issue_v(c + 1);  // V has been consumed
+        const uint32_t tm = kOffTM + p * 16384;
+        int n = 0;
+#pragma unroll
+        for (int pa = 0; pa < 2; pa++)
+#pragma unroll
+          for (int pb = 0; pb < 2; pb++) {
+            if (pa & pb) continue;
+#pragma unroll
+            for (int s = 0; s < 4; s++, n++)
+              tc::mma_f16(tmem + kColU, tc::sdesc_k_sw128(sm + kOffRU + pa * 16384 + s * 32),
+                          tc::sdesc_k_sw128(sm + tm + pb * 8192 + s * 32), id64, n > 0);
+          }
+        tc::mma_commit(&bar[BMC]);
+        mark(BMC, nmc & 1);
+      }
+      wait(BMC, nmc & 1);
+      nmc++;
+      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      tc::fence_after_sync();
+
+      // ---- U^T and (exp(G_C - G_t) U)^T as split operands
+      {
+        float u[kC];
+        tmem_ld64(tl + kColU, u);
+        store_row64(sm + kOffRU, 16384, tid, u);
+#pragma unroll
+        for (int t = 0; t < kC; t++) u[t] *= Ec[t];
+        store_row64(sm + kOffEU, 16384, tid, u);
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      tc::fence_after_sync();
+
+      // ---- (P U)^T = U^T P^T (three passes, into the (K S)^T half); S^T += (E U)^T K (K as MN-major operand)
+      if (tid == 0) {
+        const uint32_t pm = kOffPM + p * 16384;
+        int n = 0;
+#pragma unroll
+        for (int pa = 0; pa < 2; pa++)
+#pragma unroll
+          for (int pb = 0; pb < 2; pb++) {
+            if (pa & pb) continue;
+#pragma unroll
+            for (int s = 0; s < 4; s++, n++)
+              tc::mma_f16(tmem + ks_col, tc::sdesc_k_sw128(sm + kOffRU + pa * 16384 + s * 32),
+                          tc::sdesc_k_sw128(sm + pm + pb * 8192 + s * 32), id64, n > 0);
+          }
+#pragma unroll
+        for (int pa = 0; pa < 2; pa++)
+#pragma unroll
+          for (int s = 0; s < 4; s++)
+            tc::mma_f16(tmem + kColS, tc::sdesc_k_sw128(sm + kOffEU + pa * 16384 + s * 32),
+                        tc::sdesc_mn_sw128(sm + kslot(p) + s * 2048, kKQHalf, 1024), idS, 1);
+        tc::mma_commit(&bar[BMC]);
+        mark(BMC, nmc & 1);
+      }
+      wait(BMC, nmc & 1);
+      nmc++;
       const bool last = c + 1 == nch;
+      if (!last) wait(BTR0 + (p ^ 1), ((c + 1) >> 1) & 1);  // the next chunk's T, P and decays
+      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      tc::fence_after_sync();
+
+      // ---- o_t = Gam_t (Q S)^T + (P U)^T; the new state staged for the next chunk (or written out)
+      if (tid == 0 && c + 2 < nch) issue_kq(c + 2);  // slot p: read by this chunk's MMAs, all complete
+      {
+        __nv_bfloat16* og = a.o + (((size_t)b * T + t0) * H + h) * kD + tid;
+        const int nt = min(kC, T - t0);
 #pragma unroll 1
-      for (int c16 = 0; c16 < 8; c16++) {
-        float sv[16];
-        tc::tmem_ld16(tl + kColS + c16 * 16, sv);
-        if (last) {
+        for (int c16 = 0; c16 < 4; c16++) {
+          float ov[16], qs[16];
+          tc::tmem_ld16(tl + ks_col + c16 * 16, ov);
+          tc::tmem_ld16(tl + qs_col + c16 * 16, qs);
 #pragma unroll
-          for (int i = 0; i < 16; i++) Sg[(size_t)(c16 * 16 + i) * kD + tid] = sv[i];
-        } else {
-          store_st16(sm, tid, c16 * 16, sv);
+          for (int i = 0; i < 16; i++) {
+            const int t = c16 * 16 + i;
+            if (t < nt) og[(size_t)t * H * kD] = __float2bfloat16_rn(fmaf(Gam[t], qs[i], ov[i]));
+          }
+        }
+        stage_state(false, last, last ? 1.f : GamB[64 * (p ^ 1) + 63]);
+      }
+      tc::mbar_arrive(&bar[BCD0 + p]);  // this chunk's T, P and decay buffers are free
+      tc::fence_before_sync();
+      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      tc::fence_after_sync();
+    }
+    if (!ok && tid == 0) {
+      // Drain the copies and MMAs still in flight before shared memory and TMEM are released.
+      for (int i = 0; i < kNumBars; i++)
+        if ((pend >> i) & 1u) tc::mbar_wait(&bar[i], (ppar >> i) & 1u);
+    }
+  } else {
+    // =================================== prep warps ===================================
+    const int pt = tid - 128, pw = warp - 4;
+    float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;  // warp 4: decay and beta of the next chunk, 2 tokens a lane
+    auto fetch = [&](int c) {
+      const int t = c * kC + 2 * lane;
+      const size_t r = ((size_t)b * T + t) * H + h;
+      gn0 = t < T ? __ldg(a.g + r) : 0.f;
+      bn0 = t < T ? __ldg(a.beta + r) : 0.f;
+      gn1 = t + 1 < T ? __ldg(a.g + r + H) : 0.f;
+      bn1 = t + 1 < T ? __ldg(a.beta + r + H) : 0.f;
+    };
+    if (pw == 0 && nch > 0) fetch(0);
+    constexpr uint32_t idA = tc::idesc(1, 1, 128, 64);
+
+#pragma unroll 1
+    for (int c = 0; c < nch && ok; c++) {
+      const int p = c & 1;
+      float* Gam = GamB + 64 * p;
+      float* Ec = EcB + 64 * p;
+      uint8_t* TM = sm + kOffTM + p * 16384;
+      uint8_t* PM = sm + kOffPM + p * 16384;
+      if (c >= 2) wait(BCD0 + p, ((c >> 1) - 1) & 1);  // the chain is done with chunk c-2's buffers
+
+      // ---- decay sums (log2 units) and beta; warp 4, two tokens a lane
+      if (pw == 0) {
+        const float a0 = gn0 * kLog2e, a1 = a0 + gn1 * kLog2e;
+        float inc = a1;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, inc, off);
+          if (lane >= off) inc += y;
+        }
+        const float e0 = inc - a1 + a0, e1 = inc;
+        const float last = __shfl_sync(0xffffffffu, e1, 31);
+        G2[2 * lane] = e0;
+        G2[2 * lane + 1] = e1;
+        Bs[2 * lane] = bn0;
+        Bs[2 * lane + 1] = bn1;
+        Gam[2 * lane] = exp2f(e0);
+        Gam[2 * lane + 1] = exp2f(e1);
+        Ec[2 * lane] = exp2f(last - e0);
+        Ec[2 * lane + 1] = exp2f(last - e1);
+        if (c + 1 < nch) fetch(c + 1);
+      }
+
+      // ---- [stack] K^T
+      if (pt == 0) {
+        wait(BK0 + p, (c >> 1) & 1);
+        wait(BQ0 + p, (c >> 1) & 1);
+        tc::fence_after_sync();
+        if (ok) {
+#pragma unroll
+          for (int s = 0; s < 8; s++) {
+            const uint32_t kb = (s >> 2) * kKQHalf + (s & 3) * 32;
+            tc::mma_f16(tmem + kColA, tc::sdesc_k_sw128(sm + kb + stack_off(p)),
+                        tc::sdesc_k_sw128(sm + kb + kslot(p)), idA, s > 0);
+          }
+          tc::mma_commit(&bar[BMP]);
+          mark(BMP, c & 1);
         }
       }
+      wait(BMP, c & 1);
+      if (tc::group_sync_or(kPrepBar, 128, !ok)) { ok = false; break; }
+      tc::fence_after_sync();
+
+      // ---- N (f32, transposed, above the diagonal of NT) and P (split), one row per thread
+      {
+        const bool k_rows = (p == 0) == (pw < 2);  // which lane half holds K K^T this chunk
+        const int r = pt & 63;
+        float row[kC];
+        tmem_ld64(tl + kColA, row);
+        const float gr = G2[r];
+        if (k_rows) {
+          const float br = Bs[r];
+#pragma unroll
+          for (int s = 0; s < kC; s++)
+            if (s < r) NT[s * kC + r] = br * row[s] * exp2f(gr - G2[s]);
+        } else {
+#pragma unroll
+          for (int s = 0; s < kC; s++) row[s] = s <= r ? row[s] * exp2f(gr - G2[s]) : 0.f;
+          store_row64(PM, 8192, r, row);
+        }
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      if (tc::group_sync_or(kPrepBar, 128, !ok)) { ok = false; break; }
+      tc::fence_after_sync();
+
+      // ---- T = (I + N)^-1 diag(beta) in 32-blocks: T11, T22 (diagonal solves), then T21 from N21 T11
+      if (pt < 64) {
+        const int blk = pt >> 5, j = pt & 31, base = 32 * blk;
+        float x[32];
+#pragma unroll
+        for (int t = 0; t < 32; t++) x[t] = t == j ? Bs[base + t] : 0.f;
+        forward32(NT, base, x);
+        if (blk == 0) {
+#pragma unroll
+          for (int t = 0; t < 32; t++) {
+            if (t >= j) NT[t * kC + j] = x[t];  // T11, below the diagonal of NT
+            store_elem(TM, t, j, x[t]);
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; t++) {
+            store_elem(TM, t, 32 + j, 0.f);
+            store_elem(TM, 32 + t, 32 + j, x[t]);
+          }
+        }
+      }
+      if (tc::group_sync_or(kPrepBar, 128, !ok)) { ok = false; break; }
+      {
+        // Y = N21 T11: warp pw covers columns 8 pw .. 8 pw + 7, lane = row of the second block
+        const int j0 = 8 * pw;
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) y[i] = 0.f;
+#pragma unroll 4
+        for (int s = 0; s < 32; s++) {
+          const float n = NT[s * kC + 32 + lane];
+          const float4 ta = *reinterpret_cast<const float4*>(NT + s * kC + j0);
+          const float4 tb = *reinterpret_cast<const float4*>(NT + s * kC + j0 + 4);
+          const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            if (s >= j0 + i) y[i] = fmaf(n, tv[i], y[i]);
+        }
+        if (tc::group_sync_or(kPrepBar, 128, false)) { ok = false; break; }  // all reads of T11 rows done
+#pragma unroll
+        for (int i = 0; i < 8; i++) NT[(32 + lane) * kC + j0 + i] = y[i];
+      }
+      if (tc::group_sync_or(kPrepBar, 128, !ok)) { ok = false; break; }
+      if (pt < 32) {
+        // (I + N22) T21 = -N21 T11, column j = lane
+        float x[32];
+#pragma unroll
+        for (int t = 0; t < 32; t++) x[t] = -NT[(32 + t) * kC + lane];
+        forward32(NT, 32, x);
+#pragma unroll
+        for (int t = 0; t < 32; t++) store_elem(TM, 32 + t, lane, x[t]);
+      }
+      tc::fence_proxy_async();
+      tc::mbar_arrive(&bar[BTR0 + p]);  // T, P and the decays of chunk c are ready
     }
-    tc::fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
+    if (!ok && pt == 0 && ((pend >> BMP) & 1u)) tc::mbar_wait(&bar[BMP], (ppar >> BMP) & 1u);
   }
 
-  if (aborted && tid == 0) {
-    atomicAdd(a.timeouts, 1u);
-    // Drain what this CTA still has in flight before its shared memory and TMEM are released.
-    for (int i = 0; i < 5; i++) {
-      uint32_t done = seen[i];
-      while (done < issued[i] && tc::mbar_wait(&bar[i], done & 1)) done++;
-    }
-  }
+  if (!ok) atomicAdd(a.timeouts, 1u);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -555,7 +648,7 @@ extern "C" evie_status evie_poll_device_errors(void) {
   if (n) {
     const unsigned int zero = 0;
     EVIE_CUDA_TRY(cudaMemcpy(p, &zero, sizeof zero, cudaMemcpyHostToDevice));
-    return evie::fail(EVIE_ERR_TIMEOUT, "%u CTA(s) gave up a bounded device-side wait since the last poll", n);
+    return evie::fail(EVIE_ERR_TIMEOUT, "%u thread(s) gave up a bounded device-side wait since the last poll", n);
   }
   return EVIE_OK;
 }
