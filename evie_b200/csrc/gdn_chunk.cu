@@ -36,10 +36,10 @@
 //   [64K, 80K)     v tile [64 t][128 dv] bf16, unswizzled
 //   [80K, 112K)    R^T = (V - Gam K S)^T hi/lo, then U^T hi/lo ([dv][t] K-major)
 //   [112K, 144K)   (exp(G_C - G_t) U)^T hi/lo
-//   [144K, 176K)   T hi/lo, two buffers ([t][s] K-major, the B operand of U^T = R^T T^T)
+//   [144K, 176K)   T^T hi/lo, two buffers ([s][t]: the MN-major B operand of U^T = R^T T^T)
 //   [176K, 208K)   P hi/lo, two buffers ([t][s] K-major, the B operand of (P U)^T = U^T P^T)
 //   [208K, 224K)   f32 [64][64]: N^T above the diagonal; the solve's T11 and N21 T11 below it
-//   [224K, +1792)  Gam, exp(G_C - G) (two buffers), G (log2 units), beta, mbarriers, TMEM base
+//   [224K, +2048)  Gam, exp(G_C - G) (two buffers), G (log2 units), beta, the chain's Gam, mbarriers, TMEM base
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer) and every group barrier ORs a failure flag, so both warp
 // groups leave together. A wait that gives up bumps a device counter (read by evie_poll_device_errors); the CTA
@@ -73,7 +73,7 @@ constexpr uint32_t kOffTM = 147456;  // buffers 16 KB apart, planes 8 KB apart
 constexpr uint32_t kOffPM = 180224;  // buffers 16 KB apart, planes 8 KB apart
 constexpr uint32_t kOffNT = 212992;
 constexpr uint32_t kOffSmall = 229376;
-constexpr uint32_t kSmallBytes = 1792;
+constexpr uint32_t kSmallBytes = 2048;
 constexpr uint32_t kSmemBytes = kOffSmall + kSmallBytes + 1024;  // + slack to align the base to 1024
 static_assert(kSmemBytes <= 232448, "shared memory map exceeds 227 KB");
 
@@ -88,49 +88,41 @@ constexpr float kLog2e = 1.4426950408889634f;
 __device__ __forceinline__ uint32_t swz(int r, int c) {
   return (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
 }
-// Byte offset of 16-bit element `e` of row `r` in the same tile.
-__device__ __forceinline__ uint32_t swz_elem(int r, int e) { return swz(r, e >> 3) + (uint32_t)(e & 7) * 2u; }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo_addr, float hi_addr) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo_addr, hi_addr);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
+// bf16 rounding of f32 bits by integer arithmetic: adding half a bf16 unit to the magnitude bits rounds half away
+// from zero; the high 16 bits are then the bf16 value.
+__device__ __forceinline__ uint32_t round_bf16_bits(float x) { return __float_as_uint(x) + 0x8000u; }
 
-// 2n floats -> n words of bf16 hi = round(x) and n words of lo = round(x - hi), pairs packed low-half-first.
+// 2n floats -> n words of bf16 hi = round(x) and n words of lo = round(x - hi), pairs packed low-half-first
+// (x - hi is exact: hi is within half a bf16 unit of x).
 template <int N>
 __device__ __forceinline__ void split_pairs(const float* x, uint32_t* hi, uint32_t* lo) {
 #pragma unroll
   for (int i = 0; i < N; i++) {
-    const float h0 = __bfloat162float(__float2bfloat16_rn(x[2 * i]));
-    const float h1 = __bfloat162float(__float2bfloat16_rn(x[2 * i + 1]));
-    hi[i] = pack_bf16x2(h0, h1);
-    lo[i] = pack_bf16x2(x[2 * i] - h0, x[2 * i + 1] - h1);
+    const uint32_t ua = round_bf16_bits(x[2 * i]), ub = round_bf16_bits(x[2 * i + 1]);
+    const float ra = x[2 * i] - __uint_as_float(ua & 0xFFFF0000u);
+    const float rb = x[2 * i + 1] - __uint_as_float(ub & 0xFFFF0000u);
+    hi[i] = __byte_perm(ua, ub, 0x7632);
+    lo[i] = __byte_perm(round_bf16_bits(ra), round_bf16_bits(rb), 0x7632);
   }
 }
 
-// Row r (64 f32) of a split K-major SW128 tile: hi plane at `tile`, lo plane `plane` bytes further.
-__device__ __forceinline__ void store_row64(uint8_t* tile, uint32_t plane, int r, const float* x) {
+// 16 f32 (columns 16 q .. 16 q + 15) of row r of a split K-major SW128 tile: hi plane at `tile`, lo plane `plane`
+// bytes further.
+__device__ __forceinline__ void store_row16(uint8_t* tile, uint32_t plane, int r, int q, const float* x) {
 #pragma unroll
-  for (int c = 0; c < 8; c++) {
+  for (int c = 0; c < 2; c++) {
     uint32_t hi[4], lo[4];
     split_pairs<4>(x + 8 * c, hi, lo);
-    *reinterpret_cast<uint4*>(tile + swz(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(tile + plane + swz(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(tile + swz(r, 2 * q + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(tile + plane + swz(r, 2 * q + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
 }
 
-// One split element: T[row][col] into the hi/lo planes of a 64x64 K-major tile.
-__device__ __forceinline__ void store_elem(uint8_t* tile, int row, int col, float x) {
-  const __nv_bfloat16 hi = __float2bfloat16_rn(x);
-  const __nv_bfloat16 lo = __float2bfloat16_rn(x - __bfloat162float(hi));
-  const uint32_t off = swz_elem(row, col);
-  *reinterpret_cast<__nv_bfloat16*>(tile + off) = hi;
-  *reinterpret_cast<__nv_bfloat16*>(tile + 8192 + off) = lo;
-}
-
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
-#pragma unroll
-  for (int i = 0; i < 4; i++) tc::tmem_ld16(taddr + 16 * i, v + 16 * i);
+// f32 -> bf16 bits, round to nearest even (finite inputs).
+__device__ __forceinline__ uint16_t bf16_rne(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
 // Forward substitution on a 32x32 diagonal block of (I + N): x holds the right-hand side on entry and the solution
@@ -175,8 +167,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* EcB = GamB + 128;                                  // [2][64] exp(G_63 - G_t)
   float* G2 = GamB + 256;                                   // [64] G_t * log2(e) (prep only)
   float* Bs = GamB + 320;                                   // [64] beta_t, 0 past the end of the sequence
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffSmall + 1536);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffSmall + 1536 + 8 * kNumBars);
+  float* GamC = GamB + 384;                                 // [64] the chain's copy of exp(G_t)
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffSmall + 1792);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffSmall + 1792 + 8 * kNumBars);
   float* NT = reinterpret_cast<float*>(sm + kOffNT);
 
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
@@ -233,31 +226,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t id64 = tc::idesc(1, 1, 128, 64);
     constexpr uint32_t id128 = tc::idesc(1, 1, 128, 128);
     constexpr uint32_t idS = tc::idesc(1, 1, 128, 128, false, true);
+    constexpr uint32_t id64t = tc::idesc(1, 1, 128, 64, false, true);  // B operand MN-major (T^T rows)
 
     // Writes S^T row `tid` (16 dk at a time from `src`) as the split bf16 operand and Gam_C * S^T as the f32
     // accumulator (or, after the last chunk, S out to global memory).
     auto stage_state = [&](bool from_global, bool last, float gc) {
 #pragma unroll 1
-      for (int c16 = 0; c16 < 8; c16++) {
-        float sv[16];
+      for (int c32 = 0; c32 < 4; c32++) {
+        float sv[32];
         if (from_global) {
 #pragma unroll
-          for (int i = 0; i < 16; i++) sv[i] = Sg[(size_t)(c16 * 16 + i) * kD + tid];
+          for (int i = 0; i < 32; i++) sv[i] = Sg[(size_t)(c32 * 32 + i) * kD + tid];
         } else {
-          tc::tmem_ld16(tl + kColS + c16 * 16, sv);
+          tc::tmem_ld32(tl + kColS + c32 * 32, sv);
         }
         if (last) {
 #pragma unroll
-          for (int i = 0; i < 16; i++) Sg[(size_t)(c16 * 16 + i) * kD + tid] = sv[i];
+          for (int i = 0; i < 32; i++) Sg[(size_t)(c32 * 32 + i) * kD + tid] = sv[i];
           continue;
         }
-        uint32_t hi[8], lo[8];
-        split_pairs<8>(sv, hi, lo);
-        tc::tmem_st8(tl + kColSH + c16 * 8, hi);
-        tc::tmem_st8(tl + kColSL + c16 * 8, lo);
 #pragma unroll
-        for (int i = 0; i < 16; i++) sv[i] *= gc;
-        tc::tmem_st16(tl + kColS + c16 * 16, sv);
+        for (int h2 = 0; h2 < 2; h2++) {
+          uint32_t hi[8], lo[8];
+          split_pairs<8>(sv + 16 * h2, hi, lo);
+          tc::tmem_st8(tl + kColSH + c32 * 16 + h2 * 8, hi);
+          tc::tmem_st8(tl + kColSL + c32 * 16 + h2 * 8, lo);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i++) sv[i] *= gc;
+        tc::tmem_st16(tl + kColS + c32 * 32, sv);
+        tc::tmem_st16(tl + kColS + c32 * 32 + 16, sv + 16);
       }
       tc::tmem_st_wait();
     };
@@ -273,8 +271,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
     for (int c = 0; c < nch && ok; c++) {
       const int p = c & 1, t0 = c * kC;
-      const float* Gam = GamB + 64 * p;
       const float* Ec = EcB + 64 * p;
+      if (tid < 64) GamC[tid] = GamB[64 * p + tid];  // the chain's own copy: buffer p is released before the outputs
       const uint32_t ks_col = kColKQS + (p ? 64u : 0u), qs_col = kColKQS + (p ? 0u : 64u);
 
       // ---- (K S)^T | (Q S)^T = S^T [stack]^T, A = S^T hi/lo from TMEM
@@ -302,12 +300,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // ---- R^T row: V[:, dv] - Gam (K S)^T[dv, :]
       {
-        float r[kC];
-        tmem_ld64(tl + ks_col, r);
         const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + kOffV);
+        float r[kC];
+        tc::tmem_ld64(tl + ks_col, r);
 #pragma unroll
-        for (int t = 0; t < kC; t++) r[t] = fmaf(-Gam[t], r[t], __bfloat162float(V[t * kD + tid]));
-        store_row64(sm + kOffRU, 16384, tid, r);
+        for (int t = 0; t < kC; t++) r[t] = fmaf(-GamC[t], r[t], __bfloat162float(V[t * kD + tid]));
+#pragma unroll
+        for (int q = 0; q < 4; q++) store_row16(sm + kOffRU, 16384, tid, q, r + 16 * q);
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
@@ -327,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int s = 0; s < 4; s++, n++)
               tc::mma_f16(tmem + kColU, tc::sdesc_k_sw128(sm + kOffRU + pa * 16384 + s * 32),
-                          tc::sdesc_k_sw128(sm + tm + pb * 8192 + s * 32), id64, n > 0);
+                          tc::sdesc_mn_sw128(sm + tm + pb * 8192 + s * 2048, 8192, 1024), id64t, n > 0);
           }
         tc::mma_commit(&bar[BMC]);
         mark(BMC, nmc & 1);
@@ -340,11 +339,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- U^T and (exp(G_C - G_t) U)^T as split operands
       {
         float u[kC];
-        tmem_ld64(tl + kColU, u);
-        store_row64(sm + kOffRU, 16384, tid, u);
+        tc::tmem_ld64(tl + kColU, u);
 #pragma unroll
-        for (int t = 0; t < kC; t++) u[t] *= Ec[t];
-        store_row64(sm + kOffEU, 16384, tid, u);
+        for (int q = 0; q < 4; q++) {
+          store_row16(sm + kOffRU, 16384, tid, q, u + 16 * q);
+#pragma unroll
+          for (int i = 0; i < 16; i++) u[16 * q + i] *= Ec[16 * q + i];
+          store_row16(sm + kOffEU, 16384, tid, q, u + 16 * q);
+        }
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
@@ -376,6 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       wait(BMC, nmc & 1);
       nmc++;
+      tc::mbar_arrive(&bar[BCD0 + p]);  // T, P, Ec of this chunk are consumed: prep may refill buffer p
       const bool last = c + 1 == nch;
       if (!last) wait(BTR0 + (p ^ 1), ((c + 1) >> 1) & 1);  // the next chunk's T, P and decays
       if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
@@ -387,19 +390,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         __nv_bfloat16* og = a.o + (((size_t)b * T + t0) * H + h) * kD + tid;
         const int nt = min(kC, T - t0);
 #pragma unroll 1
-        for (int c16 = 0; c16 < 4; c16++) {
-          float ov[16], qs[16];
-          tc::tmem_ld16(tl + ks_col + c16 * 16, ov);
-          tc::tmem_ld16(tl + qs_col + c16 * 16, qs);
+        for (int c32 = 0; c32 < 2; c32++) {
+          float ov[32], qs[32];
+          tc::tmem_ld32x2(tl + ks_col + c32 * 32, tl + qs_col + c32 * 32, ov, qs);
 #pragma unroll
-          for (int i = 0; i < 16; i++) {
-            const int t = c16 * 16 + i;
-            if (t < nt) og[(size_t)t * H * kD] = __float2bfloat16_rn(fmaf(Gam[t], qs[i], ov[i]));
+          for (int i = 0; i < 32; i++) {
+            const int t = c32 * 32 + i;
+            if (t < nt) reinterpret_cast<uint16_t*>(og)[(size_t)t * H * kD] = bf16_rne(fmaf(GamC[t], qs[i], ov[i]));
           }
         }
         stage_state(false, last, last ? 1.f : GamB[64 * (p ^ 1) + 63]);
       }
-      tc::mbar_arrive(&bar[BCD0 + p]);  // this chunk's T, P and decay buffers are free
       tc::fence_before_sync();
       if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
       tc::fence_after_sync();
@@ -427,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
     for (int c = 0; c < nch && ok; c++) {
       const int p = c & 1;
-      float* Gam = GamB + 64 * p;
+      float* Gam = GamB + 64 * p;  // chunk c's decays, read by the chain
       float* Ec = EcB + 64 * p;
       uint8_t* TM = sm + kOffTM + p * 16384;
       uint8_t* PM = sm + kOffPM + p * 16384;
@@ -479,18 +480,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         const bool k_rows = (p == 0) == (pw < 2);  // which lane half holds K K^T this chunk
         const int r = pt & 63;
+        const float gr = G2[r], br = Bs[r];
         float row[kC];
-        tmem_ld64(tl + kColA, row);
-        const float gr = G2[r];
+        tc::tmem_ld64(tl + kColA, row);
         if (k_rows) {
-          const float br = Bs[r];
 #pragma unroll
           for (int s = 0; s < kC; s++)
             if (s < r) NT[s * kC + r] = br * row[s] * exp2f(gr - G2[s]);
         } else {
 #pragma unroll
           for (int s = 0; s < kC; s++) row[s] = s <= r ? row[s] * exp2f(gr - G2[s]) : 0.f;
-          store_row64(PM, 8192, r, row);
+#pragma unroll
+          for (int q = 0; q < 4; q++) store_row16(PM, 8192, r, q, row + 16 * q);
         }
       }
       tc::fence_proxy_async();
@@ -499,6 +500,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_after_sync();
 
       // ---- T = (I + N)^-1 diag(beta) in 32-blocks: T11, T22 (diagonal solves), then T21 from N21 T11
+      // TM holds T^T: row s (128 bytes, swizzled) = column s of T, read by the MMA as an MN-major B operand.
+      float t11[32];  // warp 4: column `lane` of T11, kept for the row write after T21
       if (pt < 64) {
         const int blk = pt >> 5, j = pt & 31, base = 32 * blk;
         float x[32];
@@ -509,14 +512,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int t = 0; t < 32; t++) {
             if (t >= j) NT[t * kC + j] = x[t];  // T11, below the diagonal of NT
-            store_elem(TM, t, j, x[t]);
+            t11[t] = x[t];
           }
         } else {
+          float zero[16];
 #pragma unroll
-          for (int t = 0; t < 32; t++) {
-            store_elem(TM, t, 32 + j, 0.f);
-            store_elem(TM, 32 + t, 32 + j, x[t]);
-          }
+          for (int i = 0; i < 16; i++) zero[i] = 0.f;
+          store_row16(TM, 8192, 32 + j, 0, zero);
+          store_row16(TM, 8192, 32 + j, 1, zero);
+          store_row16(TM, 8192, 32 + j, 2, x);
+          store_row16(TM, 8192, 32 + j, 3, x + 16);
         }
       }
       if (tc::group_sync_or(kPrepBar, 128, !ok)) { ok = false; break; }
@@ -547,8 +552,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < 32; t++) x[t] = -NT[(32 + t) * kC + lane];
         forward32(NT, 32, x);
-#pragma unroll
-        for (int t = 0; t < 32; t++) store_elem(TM, 32 + t, lane, x[t]);
+        store_row16(TM, 8192, lane, 0, t11);
+        store_row16(TM, 8192, lane, 1, t11 + 16);
+        store_row16(TM, 8192, lane, 2, x);
+        store_row16(TM, 8192, lane, 3, x + 16);
       }
       tc::fence_proxy_async();
       tc::mbar_arrive(&bar[BTR0 + p]);  // T, P and the decays of chunk c are ready

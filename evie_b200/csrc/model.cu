@@ -182,6 +182,8 @@ struct evie_ctx {
   float* x = nullptr;
   __nv_bfloat16* X2 = nullptr;
   float* Y2 = nullptr;
+  size_t y2_cols = 0;  // Y2 holds 2 * max_rows rows of y2_cols floats
+  int ksplit = 4;      // K slices of the residual-feeding projections (EVIE_GEMM_KSPLIT overrides, 1..8)
   float* act = nullptr;
   float* q_rot = nullptr;
   int8_t* frames = nullptr;
@@ -489,6 +491,8 @@ evie_status allocate_state(evie_ctx* c) {
   TRY(c->alloc(&c->x, R * s.d));
   TRY(c->alloc(&c->X2, 2 * R * kmax));
   TRY(c->alloc(&c->Y2, 2 * R * mmax));
+  c->y2_cols = mmax;
+  if (const char* e = getenv("EVIE_GEMM_KSPLIT")) c->ksplit = std::min(8, std::max(1, atoi(e)));
   TRY(c->alloc(&c->act, R * s.conv_dim));
   TRY(c->alloc(&c->q_rot, R * s.nh * s.hd));
   TRY(c->alloc(&c->frames, R * s.L * (size_t)s.n, false));
@@ -510,15 +514,35 @@ evie_status allocate_state(evie_ctx* c) {
 }
 
 // Y = X . W^T for the R rows of the split operand X2 ([2][R][K] bf16): one cuBLAS GEMM over both planes (fp32
-// accumulation); the result is the two planes of *out, which consumers add.
+// accumulation); the result is the two planes of *out, which consumers add. With ksplit > 1 the K range is cut into
+// ksplit slices, computed as one strided-batched GEMM whose 2 * ksplit output planes are contiguous R x M blocks
+// (slice i, operand plane j at plane 2 i + j): ksplit times as many CTAs stream the weight, and the consumer's plane
+// sum is the split-K reduction. Used for the narrow (M = d) projections that feed the residual add.
 evie_status gemm(evie_ctx* c, const __nv_bfloat16* W, int M, int K, const __nv_bfloat16* X2, int R, float* Y2,
-                 evie::YView* out) {
+                 evie::YView* out, int ksplit = 1) {
   const float one = 1.0f, zero = 0.0f;
-  cublasStatus_t st = cublasGemmEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, M, 2 * R, K, &one, W, CUDA_R_16BF, K, X2,
-                                   CUDA_R_16BF, K, &zero, Y2, CUDA_R_32F, M, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-  if (st != CUBLAS_STATUS_SUCCESS) return evie::fail(EVIE_ERR_CUDA, "cublasGemmEx (%d x %d x %d): status %d", M, 2 * R, K, (int)st);
-  *out = evie::YView{Y2, (size_t)R * M, 2};
+  cublasStatus_t st;
+  if (ksplit > 1) {
+    const int ks = K / ksplit;
+    st = cublasGemmStridedBatchedEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, M, 2 * R, ks, &one, W, CUDA_R_16BF, K, ks,
+                                    X2, CUDA_R_16BF, K, ks, &zero, Y2, CUDA_R_32F, M, (long long)2 * R * M, ksplit,
+                                    CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  } else {
+    st = cublasGemmEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, M, 2 * R, K, &one, W, CUDA_R_16BF, K, X2, CUDA_R_16BF, K,
+                      &zero, Y2, CUDA_R_32F, M, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  }
+  if (st != CUBLAS_STATUS_SUCCESS)
+    return evie::fail(EVIE_ERR_CUDA, "cuBLAS GEMM (%d x %d x %d, %d slices): status %d", M, 2 * R, K, ksplit, (int)st);
+  *out = evie::YView{Y2, (size_t)R * M, 2 * ksplit};
   return EVIE_OK;
+}
+
+// K slices for a residual-feeding projection of depth K: as many as fit the consumer's plane limit and the Y2
+// buffer, with 16-byte aligned slice starts.
+int residual_ksplit(const evie_ctx* c, int K) {
+  int ks = c->ksplit;
+  while (ks > 1 && (K % ks != 0 || (K / ks) % 8 != 0 || (size_t)ks * c->s.d > c->y2_cols)) ks--;
+  return ks;
 }
 
 // gpu/mod.rs:616-634: limits, then the row and segment tables uploaded for the kernels.
@@ -584,7 +608,7 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
         TRY(evie::k_gdn_mixer(c->act, y, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm,
                               s, c->X2, st));
       }
-      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2, &yo)); }
+      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2, &yo, residual_ksplit(c, s.vd))); }
     } else {
       evie::YView y;
       { PROF(P_GEMM); TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2, &y)); }
@@ -616,7 +640,7 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
                                                   c->pages_per_slot, kc, vc, s.nh, s.nkv, kPage, max_ctx_rows, scale,
                                                   c->attn_scratch, c->max_rows, st));
       }
-      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2, &yo)); }
+      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2, &yo, residual_ksplit(c, s.nh * s.hd))); }
     }
     // model.rs:246-248: residual add after the mixer, then the pre-MLP norm
     { PROF(P_NORM); TRY(evie::k_add_norm(c->x, yo, s.d, R, L.ln2, s.eps, s.d, c->X2, nullptr, 0, s.L, st)); }
@@ -627,7 +651,7 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
       TRY(evie::k_swiglu(yg, 2 * s.n, R, c->d_rows, li, s, steer, c->scale, fr, c->track ? c->maxbuf : nullptr,
                          c->X2, st));
     }
-    { PROF(P_GEMM); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2, &yd)); }
+    { PROF(P_GEMM); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2, &yd, residual_ksplit(c, s.n))); }
     PROF(P_NORM);
     if (li + 1 < s.L) {
       TRY(evie::k_add_norm(c->x, yd, s.d, R, c->layers[li + 1].ln1, s.eps, s.d, c->X2, rs, li, s.L, st));

@@ -36,16 +36,17 @@ struct YView {
     for (int k = 1; k < n; k++) s += p[(size_t)k * plane + i];
     return s;
   }
-  // Four consecutive elements (i a multiple of 4; rows and planes 16-byte aligned); up to 8 planes are loaded
-  // before any is added, then added in plane order.
+  // Four consecutive elements (i a multiple of 4; rows and planes 16-byte aligned); up to kMaxPlanes planes are
+  // loaded before any is added, then added in plane order.
+  static constexpr int kMaxPlanes = 16;
   __device__ __forceinline__ float4 at4(size_t i) const {
-    float4 v[8];
+    float4 v[kMaxPlanes];
 #pragma unroll
-    for (int k = 0; k < 8; k++)
+    for (int k = 0; k < kMaxPlanes; k++)
       if (k < n) v[k] = *reinterpret_cast<const float4*>(p + (size_t)k * plane + i);
     float4 s = v[0];
 #pragma unroll
-    for (int k = 1; k < 8; k++)
+    for (int k = 1; k < kMaxPlanes; k++)
       if (k < n) s.x += v[k].x, s.y += v[k].y, s.z += v[k].z, s.w += v[k].w;
     return s;
   }
