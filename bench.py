@@ -735,12 +735,19 @@ def run_ours(args):
     w.warmup(max(args.warmup, 3))
     torch.cuda.synchronize()
     w._steps = args.steps
+    # EVIE_PROFILE_RANGE=1 brackets the timed region with cudaProfilerStart/Stop, so that
+    # `ncu --profile-from-start off` lists exactly the timed launches
+    prange = os.environ.get("EVIE_PROFILE_RANGE") == "1"
     with Clocks(local) as clk:
         barrier()
+        if prange:
+            torch.cuda.profiler.start()
         t_wall = time.perf_counter()
         total_ms, launches = w.timed(args.steps)
         barrier()
         t_wall = time.perf_counter() - t_wall
+        if prange:
+            torch.cuda.profiler.stop()
     clocks = clk.summary()
     barrier()
     e2e_ms, h2d, d2h = w.e2e(args.steps)

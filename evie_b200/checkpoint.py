@@ -127,16 +127,27 @@ def write_checkpoint(path: str, cfg: dict, seed: int, std: float = 0.02, device:
 
 
 def ensure_checkpoint(path: str, cfg: dict, seed: int, device: str = "cpu") -> str:
-    """Writes the checkpoint unless an identical one (same config and seed) is already there."""
+    """Writes the checkpoint unless an identical one (same config and seed) is already there. Processes sharing the
+    path (one per GPU) serialise on an exclusive lock next to it: the first writes, the others find it complete."""
+    import fcntl
+
     stamp = os.path.join(path, "SYNTHETIC")
     want = json.dumps({"cfg": cfg, "seed": seed, "device": device}, sort_keys=True)
-    if os.path.exists(stamp) and os.path.exists(os.path.join(path, "model.safetensors")):
-        with open(stamp) as f:
-            if f.read() == want:
-                return path
-    write_checkpoint(path, cfg, seed, device=device)
-    with open(stamp, "w") as f:
-        f.write(want)
+    os.makedirs(os.path.dirname(os.path.abspath(path)) or ".", exist_ok=True)
+    with open(os.path.abspath(path) + ".lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if os.path.exists(stamp) and os.path.exists(os.path.join(path, "model.safetensors")):
+                with open(stamp) as f:
+                    if f.read() == want:
+                        return path
+            if os.path.exists(stamp):
+                os.unlink(stamp)
+            write_checkpoint(path, cfg, seed, device=device)
+            with open(stamp, "w") as f:
+                f.write(want)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
     return path
 
 

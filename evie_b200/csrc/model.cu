@@ -599,8 +599,10 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
       float* cs = c->conv_state + (size_t)L.idx * (s.K - 1) * s.conv_dim;
       {
         PROF(P_CONV);
-        TRY(evie::k_conv_silu_norm(y, s.in_dn, R, c->d_rows, c->d_segs, cs, cs_slot, L.conv, s, c->act, st));
-        TRY(evie::k_conv_state_update(y, s.in_dn, R, c->d_segs, nseq, cs, cs_slot, s, st));
+        const bool single_rows = R == nseq && s.K <= 8;  // decode: one row per segment, the conv kernel shifts the window
+        TRY(evie::k_conv_silu_norm(y, s.in_dn, R, c->d_rows, c->d_segs, cs, cs_slot, L.conv, s, c->act, st,
+                                   single_rows));
+        if (!single_rows) TRY(evie::k_conv_state_update(y, s.in_dn, R, c->d_segs, nseq, cs, cs_slot, s, st));
       }
       float* rsb = c->rec_state + (size_t)L.idx * s.hv * s.dk * s.dv;
       {
@@ -718,13 +720,46 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
     c->hist_cap = need;
   }
   cudaStream_t st = c->stream;
-  for (int i = 0; i < steps; i++) {
-    if (i > 0) {
-      PROF(P_OTHER);
-      TRY(evie::k_advance_rows(c->d_rows, nseq, c->next, st));
+  // Steps after the first replay one captured CUDA graph of (advance rows, layers, head): every per-step input is
+  // already on the device, and the attention's split count uses a context bound valid for all steps. The profiling
+  // mode (events around kernel groups) runs the steps eagerly. EVIE_NO_GRAPH=1 also forces eager steps.
+  const char* ng = getenv("EVIE_NO_GRAPH");
+  const bool use_graph = !c->prof && steps > 1 && !(ng && ng[0] == '1');
+  const int ctx_bound = max_ctx_rows + steps - 1;
+  cudaGraphExec_t exec = nullptr;
+  struct ExecGuard {
+    cudaGraphExec_t* e;
+    ~ExecGuard() {
+      if (*e) cudaGraphExecDestroy(*e);
     }
-    TRY(enqueue_layers(c, R, nseq, max_ctx_rows + i, capture));
-    TRY(enqueue_head(c, nseq, false));
+  } guard{&exec};
+  for (int i = 0; i < steps; i++) {
+    if (use_graph && i > 0) {
+      if (!exec) {
+        cudaGraph_t g = nullptr;
+        EVIE_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        evie_status rc = evie::k_advance_rows(c->d_rows, nseq, c->next, st);
+        if (rc == EVIE_OK) rc = enqueue_layers(c, R, nseq, ctx_bound, capture);
+        if (rc == EVIE_OK) rc = enqueue_head(c, nseq, false);
+        const cudaError_t ce = cudaStreamEndCapture(st, &g);
+        if (rc != EVIE_OK) {
+          if (g) cudaGraphDestroy(g);
+          return rc;
+        }
+        EVIE_CUDA_TRY(ce);
+        const cudaError_t ie = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        EVIE_CUDA_TRY(ie);
+      }
+      EVIE_CUDA_TRY(cudaGraphLaunch(exec, st));
+    } else {
+      if (i > 0) {
+        PROF(P_OTHER);
+        TRY(evie::k_advance_rows(c->d_rows, nseq, c->next, st));
+      }
+      TRY(enqueue_layers(c, R, nseq, use_graph ? ctx_bound : max_ctx_rows + i, capture));
+      TRY(enqueue_head(c, nseq, false));
+    }
     EVIE_CUDA_TRY(cudaMemcpyAsync(c->hist + (size_t)i * nseq, c->next, nseq * 4, cudaMemcpyDeviceToDevice, st));
     if (capture && frames)
       EVIE_CUDA_TRY(cudaMemcpyAsync(frames + (size_t)i * nseq * s.L * s.n, c->frames, (size_t)nseq * s.L * s.n,

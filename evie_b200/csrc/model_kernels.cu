@@ -110,6 +110,12 @@ __device__ __forceinline__ void add_norm_row(float* __restrict__ x, const YView&
       ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
     }
   }
+  float4 gv[2];
+#pragma unroll
+  for (int k = 0; k < 2; k++) {  // issued before the reduction's barriers
+    const int i4 = threadIdx.x + k * blockDim.x;
+    if (do_norm && i4 < n4) gv[k] = *reinterpret_cast<const float4*>(gain + 4 * i4);
+  }
   ss = block_sum_any(ss, red);
   if (!do_norm) return;
   const float inv = 1.0f / sqrtf(ss / (float)d + eps);
@@ -117,7 +123,7 @@ __device__ __forceinline__ void add_norm_row(float* __restrict__ x, const YView&
   for (int k = 0; k < 2; k++) {
     const int i4 = threadIdx.x + k * blockDim.x;
     if (i4 < n4) {
-      const float4 g = *reinterpret_cast<const float4*>(gain + 4 * i4);
+      const float4 g = gv[k];
       const float4 a = v[k];
       store_split4(X2, xplane, (size_t)out_row * d + 4 * i4,
                    make_float4(a.x * inv * g.x, a.y * inv * g.y, a.z * inv * g.z, a.w * inv * g.w));
@@ -153,20 +159,29 @@ __global__ void __launch_bounds__(1024) add_final_kernel(float* __restrict__ x, 
 __global__ void __launch_bounds__(128) conv_silu_norm_kernel(YView y, int ldy,
                                                              const RowInfo* __restrict__ rows,
                                                              const SegInfo* __restrict__ segs,
-                                                             const float* __restrict__ conv_state, size_t cs_slot,
+                                                             float* __restrict__ conv_state, size_t cs_slot,
                                                              const float* __restrict__ conv_w, int K, int conv_dim,
-                                                             int hk, float qscale, float* __restrict__ act) {
+                                                             int hk, float qscale, float* __restrict__ act,
+                                                             bool update_window) {
   __shared__ float red[4];
   const int c = blockIdx.x * 128 + threadIdx.x;
   const int r = blockIdx.y;
   const SegInfo sg = segs[rows[r].seg];
   const int t = r - sg.start;
-  const float* cs = conv_state + (size_t)sg.slot * cs_slot;
+  float* cs = conv_state + (size_t)sg.slot * cs_slot;
+  constexpr int kMaxK = 8;
+  float win[kMaxK];  // [state ; rows] inputs of this output, oldest first
   float acc = 0.f;
   for (int j = 0; j < K; j++) {
     const int tt = t - (K - 1) + j;
     const float u = tt >= 0 ? y.at((size_t)(sg.start + tt) * ldy + c) : cs[(size_t)(K - 1 + tt) * conv_dim + c];
+    if (j < kMaxK) win[j] = u;
     acc += conv_w[(size_t)c * K + j] * u;
+  }
+  if (update_window) {
+    // Single-row segments (decode): this thread is the only reader of its channel's window, so it can shift the
+    // window in place (model.rs:339: keep the last K-1 raw inputs).
+    for (int j = 1; j < K && j < kMaxK; j++) cs[(size_t)(j - 1) * conv_dim + c] = win[j];
   }
   float out = siluf_(acc);
   if ((int)blockIdx.x < 2 * hk) {  // q or k head: L2 normalise (kernels.rs dot + 1e-6), q also by 1/sqrt(dk)
@@ -340,6 +355,14 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
   __shared__ evie_op s_ops[64];
   __shared__ int s_cnt;
   const int r = blockIdx.y;
+  const int j0 = blockIdx.x * 1024 + threadIdx.x * 4;  // n is a multiple of 4
+  const bool active = j0 < n;
+  const size_t yr = (size_t)r * ldy;
+  float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), u4 = g4;
+  if (active) {  // issued before the row and steering lookups, which then overlap these loads
+    g4 = y.at4(yr + j0);
+    u4 = y.at4(yr + n + j0);
+  }
   const RowInfo ri = rows[r];
   if (threadIdx.x == 0) {
     const int* rg = steer.range + ((size_t)ri.slot * L + layer) * 2;
@@ -352,10 +375,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
     s_ops[threadIdx.x] = steer.ops[(size_t)ri.slot * steer.max_ops + first + threadIdx.x];
   }
   __syncthreads();
-  const int j0 = blockIdx.x * 1024 + threadIdx.x * 4;  // n is a multiple of 4
-  if (j0 >= n) return;
-  const size_t yr = (size_t)r * ldy;
-  const float4 g4 = y.at4(yr + j0), u4 = y.at4(yr + n + j0);
+  if (!active) return;
   float a[4] = {siluf_(g4.x) * u4.x, siluf_(g4.y) * u4.y, siluf_(g4.z) * u4.z, siluf_(g4.w) * u4.w};
   for (int i = 0; i < cnt; i++) {  // steering.rs:189-208, in the slot's order
     const evie_op op = s_ops[i];
@@ -472,12 +492,12 @@ evie_status k_add_final(float* x, YView y, int ldy, int R, const RowInfo* rows, 
 }
 
 evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
-                             const float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
-                             float* act, cudaStream_t st) {
+                             float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
+                             float* act, cudaStream_t st, bool update_window) {
   if (R == 0) return EVIE_OK;
   dim3 grid(s.conv_dim / 128, R);
   conv_silu_norm_kernel<<<grid, 128, 0, st>>>(y, ldy, rows, segs, conv_state, cs_slot, conv_w, s.K,
-                                              s.conv_dim, s.hk, 1.0f / sqrtf((float)s.dk), act);
+                                              s.conv_dim, s.hk, 1.0f / sqrtf((float)s.dk), act, update_window);
   EVIE_CHECK_LAUNCH("conv_silu_norm_kernel");
   return EVIE_OK;
 }
