@@ -631,9 +631,47 @@ class ModelDecode(Workload):
         c = self.cfg
         return self.B * 4, self.B * 4 + self.B * c["num_hidden_layers"] * (c["intermediate_size"] + 2 * c["hidden_size"])
 
+    def prepare_cpu(self, threads):
+        """Inputs of the CPU sample when setup() (the GPU arm) has not run, e.g. for `--impl reference`: the same
+        checkpoint (generated the same way, so the GPU arm finds it), pair 0's prompt and the 32 steered
+        (layer, neuron) pairs; the dose unit is measured by the oracle on the 64-token sample prompt (median residual
+        norm over its tokens 1..), since an oracle pass over the whole 4096-token prompt takes hours on the CPU."""
+        import torch
+
+        import oracle
+        from evie_b200 import checkpoint as ck
+
+        base = os.environ.get("EVIE_CKPT_DIR", tempfile.gettempdir())
+        self.ckpt = ck.ensure_checkpoint(os.path.join(base, "evie_qwen35_4b_seed5"), ck.text_config(ck.QWEN35_4B),
+                                         seed=5, device="cuda" if torch.cuda.is_available() else "cpu")
+        self.cfg = json.load(open(os.path.join(self.ckpt, "config.json")))
+        L, n, V = self.cfg["num_hidden_layers"], self.cfg["intermediate_size"], self.cfg["vocab_size"]
+        g = torch.Generator().manual_seed(5)
+        self.layers = torch.randint(0, L, (32,), generator=g).tolist()
+        self.neurons = torch.randint(0, n, (32,), generator=g).tolist()
+        g = torch.Generator().manual_seed(5)
+        first = self.rank * (self.B // 2)
+        all_prompts = [torch.randint(0, V, (self.P,), generator=g) for _ in range(first + 1)]
+        self.prompts = [all_prompts[first].numpy().astype(np.uint32)]
+        oracle.set_threads(threads)
+        m = oracle.Model(self.ckpt)
+        _, _, rs = m.forward([dict(cache=m.new_cache(), tokens=self.prompts[0][:64], resid=True)])
+        resid = rs[0].view(np.float16).astype(np.float32).reshape(64, L, -1)
+        units = np.median(np.linalg.norm(resid[1:], axis=-1), axis=0)
+        ops = []
+        for l, nn in zip(self.layers, self.neurons):
+            w = ck.read_tensor(self.ckpt, f"model.language_model.layers.{l}.mlp.down_proj.weight")
+            col = float(np.sqrt((w[:, nn].astype(np.float64) ** 2).sum()))
+            ops.append((l, nn, "add", float(0.6 * units[l] / max(col, 1e-12))))
+        self.ops = ops
+
     def cpu_sample(self, threads):
         import oracle
 
+        dose_note = ""
+        if not hasattr(self, "ops"):
+            self.prepare_cpu(threads)
+            dose_note = "; dose unit measured by the oracle on the 64-token sample prompt"
         oracle.set_threads(threads)
         m = oracle.Model(self.ckpt)
         prompt = self.prompts[0][:64]
@@ -655,7 +693,7 @@ class ModelDecode(Workload):
         return {"value": 2 * steps / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
                 "sample": f"1 steered/unsteered pair, 64-token prompt, {steps} greedy decode steps with capture on the "
                           f"steered lane, 4B-shaped model (the full 4096-token prefill is ~65 TFLOP per sequence on "
-                          f"the CPU)"}
+                          f"the CPU){dose_note}"}
 
 
 WORKLOADS = {"gdn_decode": GdnDecode, "gdn_prefill": GdnPrefill, "gqa_decode": GqaDecode,
