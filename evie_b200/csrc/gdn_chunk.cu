@@ -17,29 +17,29 @@
 // a product with an exact bf16 partner takes two MMAs (hi, lo), a product of two split operands three
 // (hi.hi + hi.lo + lo.hi). The result follows the f32 recurrence to ~1e-5 relative.
 //
-// Work layout. One CTA per (sequence, head), 256 threads in two warp groups, one CTA per SM (226 KB of shared
-// memory, all 512 TMEM columns).
-//   * Chain warps 0-3 carry the state from chunk to chunk. Every S-dependent product is computed transposed, so
-//     that M = 128 runs along dv and thread j (TMEM lane j) owns row dv = j of each accumulator. Thread 0 issues
-//     their MMAs and all TMA loads.
-//   * Prep warps 4-7 work one chunk ahead on what does not depend on S: the decay sums, [K;Q] K^T (thread 128
+// Work layout. One CTA per (sequence, head), 512 threads in two groups of 8 warps, one CTA per SM (all 512 TMEM
+// columns). Two warps share each TMEM lane quarter and split the columns between them.
+//   * Chain warps 0-7 carry the state from chunk to chunk. Every S-dependent product is computed transposed, so
+//     that M = 128 runs along dv: TMEM lane j is row dv = j of each accumulator; warp w handles lane quarter w % 4
+//     and column half w / 4. Thread 0 issues their MMAs and all TMA loads.
+//   * Prep warps 8-15 work one chunk ahead on what does not depend on S: the decay sums, [K;Q] K^T (thread 256
 //     issues it), N, P and T. They hand a chunk over through an mbarrier (tp_ready) and wait for the chain to
 //     release the buffers two chunks later (chunk_done).
 // TMEM columns:
 //   [0,128)   S^T f32 [dv][dk], holding Gam_C S entering each chunk's update
-//   [128,192) S^T bf16 hi, [192,256) S^T bf16 lo (A operand of the S products, two values per column)
+//   [128,256) the A operands of the chain's MMAs, bf16 pairs: S^T hi | S^T lo (64 + 64 columns) for S^T [K;Q]^T;
+//             then R^T hi | R^T lo (32 + 32) for R^T T^T; then U^T hi | U^T lo | (E U)^T hi | (E U)^T lo
+//             (32 each) for U^T P^T and (E U)^T K
 //   [256,320) [K;Q] K^T (prep)            [320,448) (S^T [K;Q]^T): (K S)^T and (Q S)^T halves; (P U)^T reuses the
-//   (K S)^T half                          [448,512) U^T
+//   (K S)^T half                          [448,512) U^T f32
 // Shared memory (1024-aligned offsets):
 //   [0, 64K)       q/k tiles, two dk halves of 32 KB: [K0 | Q0 | Q1 | K1], 8 KB each, 128-byte swizzled K-major
 //                  (TMA SW128). Chunk c uses K(c&1), Q(c&1); the stacks [K0;Q0] and [Q1;K1] are 128-row operands.
 //   [64K, 80K)     v tile [64 t][128 dv] bf16, unswizzled
-//   [80K, 112K)    R^T = (V - Gam K S)^T hi/lo, then U^T hi/lo ([dv][t] K-major)
-//   [112K, 144K)   (exp(G_C - G_t) U)^T hi/lo
-//   [144K, 176K)   T^T hi/lo, two buffers ([s][t]: the MN-major B operand of U^T = R^T T^T)
-//   [176K, 208K)   P hi/lo, two buffers ([t][s] K-major, the B operand of (P U)^T = U^T P^T)
-//   [208K, 224K)   f32 [64][64]: N^T above the diagonal; the solve's T11 and N21 T11 below it
-//   [224K, +2048)  Gam, exp(G_C - G) (two buffers), G (log2 units), beta, the chain's Gam, mbarriers, TMEM base
+//   [80K, 112K)    T^T hi/lo, two buffers ([s][t]: the MN-major B operand of U^T = R^T T^T)
+//   [112K, 144K)   P hi/lo, two buffers ([t][s] K-major, the B operand of (P U)^T = U^T P^T)
+//   [144K, 160K)   f32 [64][64]: N^T above the diagonal; the solve's T11 and N21 T11 below it
+//   [160K, +2048)  Gam, exp(G_C - G) (two buffers), G (log2 units), beta, the chain's Gam, mbarriers, TMEM base
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer) and every group barrier ORs a failure flag, so both warp
 // groups leave together. A wait that gives up bumps a device counter (read by evie_poll_device_errors); the CTA
@@ -60,28 +60,29 @@ namespace {
 
 constexpr int kC = 64;
 constexpr int kD = 128;
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
+constexpr int kGroup = 256;  // threads per warp group
 
 constexpr uint32_t kKQHalf = 32768;
 __device__ __forceinline__ uint32_t kslot(int p) { return p ? 24576u : 0u; }
 __device__ __forceinline__ uint32_t qslot(int p) { return p ? 16384u : 8192u; }
 __device__ __forceinline__ uint32_t stack_off(int p) { return p ? 16384u : 0u; }  // [K0;Q0] or [Q1;K1]
 constexpr uint32_t kOffV = 65536;
-constexpr uint32_t kOffRU = 81920;   // planes 16 KB apart
-constexpr uint32_t kOffEU = 114688;  // planes 16 KB apart
-constexpr uint32_t kOffTM = 147456;  // buffers 16 KB apart, planes 8 KB apart
-constexpr uint32_t kOffPM = 180224;  // buffers 16 KB apart, planes 8 KB apart
-constexpr uint32_t kOffNT = 212992;
-constexpr uint32_t kOffSmall = 229376;
+constexpr uint32_t kOffTM = 81920;   // buffers 16 KB apart, planes 8 KB apart
+constexpr uint32_t kOffPM = 114688;  // buffers 16 KB apart, planes 8 KB apart
+constexpr uint32_t kOffNT = 147456;
+constexpr uint32_t kOffSmall = 163840;
 constexpr uint32_t kSmallBytes = 2048;
 constexpr uint32_t kSmemBytes = kOffSmall + kSmallBytes + 1024;  // + slack to align the base to 1024
 static_assert(kSmemBytes <= 232448, "shared memory map exceeds 227 KB");
 
 constexpr uint32_t kColS = 0, kColSH = 128, kColSL = 192, kColA = 256, kColKQS = 320, kColU = 448;
+constexpr uint32_t kColRH = 128, kColRL = 160;                              // R^T, then U^T planes
+constexpr uint32_t kColEH = 192, kColEL = 224;                              // (E U)^T planes
 
 // mbarriers
 enum { BK0 = 0, BK1, BQ0, BQ1, BV, BMC, BMP, BTR0, BTR1, BCD0, BCD1, kNumBars };
-constexpr uint32_t kChainBar = 1, kPrepBar = 2;  // named barriers of the two warp groups (128 threads each)
+constexpr uint32_t kChainBar = 1, kPrepBar = 2;  // named barriers of the two warp groups (256 threads each)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Byte offset of 16-byte chunk `c` of row `r` in a K-major tile with 128-byte rows and the 128-byte swizzle.
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q4 = warp & 3, hf = (warp >> 2) & 1;  // TMEM lane quarter, column half
   const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
   const int T = a.T, H = a.H;
   const int nch = (T + kC - 1) / kC;
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
   if (tid == 0) {
     for (int i = 0; i < kNumBars; i++)
-      tc::mbar_init(&bar[i], (i == BTR0 || i == BTR1 || i == BCD0 || i == BCD1) ? 128 : 1);
+      tc::mbar_init(&bar[i], (i == BTR0 || i == BTR1 || i == BCD0 || i == BCD1) ? kGroup : 1);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&mq);
     tc::prefetch_tmap(&mk);
@@ -185,7 +187,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's quarter of the TMEM lanes
+  const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);  // this warp's quarter of the TMEM lanes
+  // Shared-memory descriptors relative to `sm`: the start address is the low 14-bit field, so adding (offset >> 4)
+  // to a base descriptor moves it (addresses stay below 256 KB).
+  const uint64_t dK = tc::sdesc_k_sw128(sm);                     // K-major, 128-byte swizzle
+  const uint64_t dMnK = tc::sdesc_mn_sw128(sm, kKQHalf, 1024);   // K^T operand (two 64-wide dk blocks)
+  const uint64_t dMnT = tc::sdesc_mn_sw128(sm, 8192, 1024);      // T^T operand (one 64-wide block)
   bool ok = true;
   // Barriers with an operation in flight that the issuing thread has not seen complete, and that phase's parity.
   uint32_t pend = 0, ppar = 0;
@@ -198,15 +205,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && ((pend >> i) & 1u) && ((ppar >> i) & 1u) == parity) pend &= ~(1u << i);
   };
 
-  if (warp < 4) {
+  if (warp < 8) {
     // =================================== chain warps ===================================
+    const int dv = q4 * 32 + lane;
     auto issue_kq = [&](int c) {
       const int p = c & 1;
       tc::mbar_arrive_expect_tx(&bar[BK0 + p], 16384);
       tc::mbar_arrive_expect_tx(&bar[BQ0 + p], 16384);
-      for (int hf = 0; hf < 2; hf++) {
-        tc::tma_load_4d(sm + hf * kKQHalf + kslot(p), &mk, &bar[BK0 + p], hf * 64, h, c * kC, b);
-        tc::tma_load_4d(sm + hf * kKQHalf + qslot(p), &mq, &bar[BQ0 + p], hf * 64, h, c * kC, b);
+      for (int hh = 0; hh < 2; hh++) {
+        tc::tma_load_4d(sm + hh * kKQHalf + kslot(p), &mk, &bar[BK0 + p], hh * 64, h, c * kC, b);
+        tc::tma_load_4d(sm + hh * kKQHalf + qslot(p), &mq, &bar[BQ0 + p], hh * 64, h, c * kC, b);
       }
       mark(BK0 + p, (c >> 1) & 1);
       mark(BQ0 + p, (c >> 1) & 1);
@@ -228,34 +236,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t idS = tc::idesc(1, 1, 128, 128, false, true);
     constexpr uint32_t id64t = tc::idesc(1, 1, 128, 64, false, true);  // B operand MN-major (T^T rows)
 
-    // Writes S^T row `tid` (16 dk at a time from `src`) as the split bf16 operand and Gam_C * S^T as the f32
-    // accumulator (or, after the last chunk, S out to global memory).
+    // S^T row dv, dk in [64 hf, 64 hf + 64): the split bf16 operand and Gam_C * S^T as the f32 accumulator (or,
+    // after the last chunk, S out to global memory).
     auto stage_state = [&](bool from_global, bool last, float gc) {
 #pragma unroll 1
-      for (int c32 = 0; c32 < 4; c32++) {
+      for (int k = 0; k < 2; k++) {
+        const int dk0 = 64 * hf + 32 * k;
         float sv[32];
         if (from_global) {
 #pragma unroll
-          for (int i = 0; i < 32; i++) sv[i] = Sg[(size_t)(c32 * 32 + i) * kD + tid];
+          for (int i = 0; i < 32; i++) sv[i] = Sg[(size_t)(dk0 + i) * kD + dv];
         } else {
-          tc::tmem_ld32(tl + kColS + c32 * 32, sv);
+          tc::tmem_ld32(tl + kColS + dk0, sv);
         }
         if (last) {
 #pragma unroll
-          for (int i = 0; i < 32; i++) Sg[(size_t)(c32 * 32 + i) * kD + tid] = sv[i];
+          for (int i = 0; i < 32; i++) Sg[(size_t)(dk0 + i) * kD + dv] = sv[i];
           continue;
         }
-#pragma unroll
-        for (int h2 = 0; h2 < 2; h2++) {
-          uint32_t hi[8], lo[8];
-          split_pairs<8>(sv + 16 * h2, hi, lo);
-          tc::tmem_st8(tl + kColSH + c32 * 16 + h2 * 8, hi);
-          tc::tmem_st8(tl + kColSL + c32 * 16 + h2 * 8, lo);
-        }
+        uint32_t hi[16], lo[16];
+        split_pairs<16>(sv, hi, lo);
+        tc::tmem_st16u(tl + kColSH + dk0 / 2, hi);
+        tc::tmem_st16u(tl + kColSL + dk0 / 2, lo);
 #pragma unroll
         for (int i = 0; i < 32; i++) sv[i] *= gc;
-        tc::tmem_st16(tl + kColS + c32 * 32, sv);
-        tc::tmem_st16(tl + kColS + c32 * 32 + 16, sv + 16);
+        tc::tmem_st32(tl + kColS + dk0, sv);
       }
       tc::tmem_st_wait();
     };
@@ -265,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) stage_state(true, false, GamB[63]);
     }
     tc::fence_before_sync();
-    if (tc::group_sync_or(kChainBar, 128, !ok)) ok = false;
+    if (tc::group_sync_or(kChainBar, kGroup, !ok)) ok = false;
     tc::fence_after_sync();
 
 #pragma unroll 1
@@ -286,8 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int s = 0; s < 8; s++)
               tc::mma_f16_ts(tmem + kColKQS, tmem + (pl ? kColSL : kColSH) + s * 8,
-                             tc::sdesc_k_sw128(sm + (s >> 2) * kKQHalf + stack_off(p) + (s & 3) * 32), id128,
-                             (pl | s) > 0);
+                             dK + (((s >> 2) * kKQHalf + stack_off(p) + (s & 3) * 32) >> 4), id128, (pl | s) > 0);
           tc::mma_commit(&bar[BMC]);
           mark(BMC, nmc & 1);
         }
@@ -295,25 +299,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait(BMC, nmc & 1);
       nmc++;
       wait(BV, c & 1);
-      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
-      // ---- R^T row: V[:, dv] - Gam (K S)^T[dv, :]
+      // ---- R^T row dv, t in [32 hf, 32 hf + 32): V[t][dv] - Gam_t (K S)^T[dv][t], split into TMEM
       {
         const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + kOffV);
-        float r[kC];
-        tc::tmem_ld64(tl + ks_col, r);
+        float r[32];
+        tc::tmem_ld32(tl + ks_col + 32 * hf, r);
 #pragma unroll
-        for (int t = 0; t < kC; t++) r[t] = fmaf(-GamC[t], r[t], __bfloat162float(V[t * kD + tid]));
-#pragma unroll
-        for (int q = 0; q < 4; q++) store_row16(sm + kOffRU, 16384, tid, q, r + 16 * q);
+        for (int i = 0; i < 32; i++) {
+          const int t = 32 * hf + i;
+          r[i] = fmaf(-GamC[t], r[i], __bfloat162float(V[t * kD + dv]));
+        }
+        uint32_t hi[16], lo[16];
+        split_pairs<16>(r, hi, lo);
+        tc::tmem_st16u(tl + kColRH + 16 * hf, hi);
+        tc::tmem_st16u(tl + kColRL + 16 * hf, lo);
+        tc::tmem_st_wait();
       }
-      tc::fence_proxy_async();
       tc::fence_before_sync();
-      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
-      // ---- U^T = R^T T^T (three passes)
+      // ---- U^T = R^T T^T (three passes; A from TMEM, B = T^T rows MN-major)
       if (tid == 0) {
         if (c + 1 < nch) issue_v(c + 1);  // V has been consumed
         const uint32_t tm = kOffTM + p * 16384;
@@ -325,32 +334,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (pa & pb) continue;
 #pragma unroll
             for (int s = 0; s < 4; s++, n++)
-              tc::mma_f16(tmem + kColU, tc::sdesc_k_sw128(sm + kOffRU + pa * 16384 + s * 32),
-                          tc::sdesc_mn_sw128(sm + tm + pb * 8192 + s * 2048, 8192, 1024), id64t, n > 0);
+              tc::mma_f16_ts(tmem + kColU, tmem + (pa ? kColRL : kColRH) + s * 8,
+                             dMnT + ((tm + pb * 8192 + s * 2048) >> 4), id64t, n > 0);
           }
         tc::mma_commit(&bar[BMC]);
         mark(BMC, nmc & 1);
       }
       wait(BMC, nmc & 1);
       nmc++;
-      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
-      // ---- U^T and (exp(G_C - G_t) U)^T as split operands
+      // ---- U^T and (exp(G_C - G_t) U)^T as split TMEM operands
       {
-        float u[kC];
-        tc::tmem_ld64(tl + kColU, u);
+        float u[32];
+        tc::tmem_ld32(tl + kColU + 32 * hf, u);
+        uint32_t hi[16], lo[16];
+        split_pairs<16>(u, hi, lo);
+        tc::tmem_st16u(tl + kColRH + 16 * hf, hi);
+        tc::tmem_st16u(tl + kColRL + 16 * hf, lo);
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-          store_row16(sm + kOffRU, 16384, tid, q, u + 16 * q);
-#pragma unroll
-          for (int i = 0; i < 16; i++) u[16 * q + i] *= Ec[16 * q + i];
-          store_row16(sm + kOffEU, 16384, tid, q, u + 16 * q);
-        }
+        for (int i = 0; i < 32; i++) u[i] *= Ec[32 * hf + i];
+        split_pairs<16>(u, hi, lo);
+        tc::tmem_st16u(tl + kColEH + 16 * hf, hi);
+        tc::tmem_st16u(tl + kColEL + 16 * hf, lo);
+        tc::tmem_st_wait();
       }
-      tc::fence_proxy_async();
       tc::fence_before_sync();
-      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
       // ---- (P U)^T = U^T P^T (three passes, into the (K S)^T half); S^T += (E U)^T K (K as MN-major operand)
@@ -364,15 +375,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (pa & pb) continue;
 #pragma unroll
             for (int s = 0; s < 4; s++, n++)
-              tc::mma_f16(tmem + ks_col, tc::sdesc_k_sw128(sm + kOffRU + pa * 16384 + s * 32),
-                          tc::sdesc_k_sw128(sm + pm + pb * 8192 + s * 32), id64, n > 0);
+              tc::mma_f16_ts(tmem + ks_col, tmem + (pa ? kColRL : kColRH) + s * 8,
+                             dK + ((pm + pb * 8192 + s * 32) >> 4), id64, n > 0);
           }
 #pragma unroll
         for (int pa = 0; pa < 2; pa++)
 #pragma unroll
           for (int s = 0; s < 4; s++)
-            tc::mma_f16(tmem + kColS, tc::sdesc_k_sw128(sm + kOffEU + pa * 16384 + s * 32),
-                        tc::sdesc_mn_sw128(sm + kslot(p) + s * 2048, kKQHalf, 1024), idS, 1);
+            tc::mma_f16_ts(tmem + kColS, tmem + (pa ? kColEL : kColEH) + s * 8,
+                           dMnK + ((kslot(p) + s * 2048) >> 4), idS, 1);
         tc::mma_commit(&bar[BMC]);
         mark(BMC, nmc & 1);
       }
@@ -381,28 +392,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_arrive(&bar[BCD0 + p]);  // T, P, Ec of this chunk are consumed: prep may refill buffer p
       const bool last = c + 1 == nch;
       if (!last) wait(BTR0 + (p ^ 1), ((c + 1) >> 1) & 1);  // the next chunk's T, P and decays
-      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
-      // ---- o_t = Gam_t (Q S)^T + (P U)^T; the new state staged for the next chunk (or written out)
+      // ---- o_t = Gam_t (Q S)^T + (P U)^T for t in [32 hf, 32 hf + 32); the new state staged for the next chunk
       if (tid == 0 && c + 2 < nch) issue_kq(c + 2);  // slot p: read by this chunk's MMAs, all complete
       {
-        __nv_bfloat16* og = a.o + (((size_t)b * T + t0) * H + h) * kD + tid;
+        __nv_bfloat16* og = a.o + (((size_t)b * T + t0) * H + h) * kD + dv;
         const int nt = min(kC, T - t0);
-#pragma unroll 1
-        for (int c32 = 0; c32 < 2; c32++) {
-          float ov[32], qs[32];
-          tc::tmem_ld32x2(tl + ks_col + c32 * 32, tl + qs_col + c32 * 32, ov, qs);
+        float ov[32], qs[32];
+        tc::tmem_ld32x2(tl + ks_col + 32 * hf, tl + qs_col + 32 * hf, ov, qs);
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            const int t = c32 * 32 + i;
-            if (t < nt) reinterpret_cast<uint16_t*>(og)[(size_t)t * H * kD] = bf16_rne(fmaf(GamC[t], qs[i], ov[i]));
-          }
+        for (int i = 0; i < 32; i++) {
+          const int t = 32 * hf + i;
+          if (t < nt) reinterpret_cast<uint16_t*>(og)[(size_t)t * H * kD] = bf16_rne(fmaf(GamC[t], qs[i], ov[i]));
         }
         stage_state(false, last, last ? 1.f : GamB[64 * (p ^ 1) + 63]);
       }
       tc::fence_before_sync();
-      if (tc::group_sync_or(kChainBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
     }
     if (!ok && tid == 0) {
@@ -412,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // =================================== prep warps ===================================
-    const int pt = tid - 128, pw = warp - 4;
-    float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;  // warp 4: decay and beta of the next chunk, 2 tokens a lane
+    const int pt = tid - kGroup, pw = warp - 8;
+    float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;  // warp 8: decay and beta of the next chunk, 2 tokens a lane
     auto fetch = [&](int c) {
       const int t = c * kC + 2 * lane;
       const size_t r = ((size_t)b * T + t) * H + h;
@@ -434,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* PM = sm + kOffPM + p * 16384;
       if (c >= 2) wait(BCD0 + p, ((c >> 1) - 1) & 1);  // the chain is done with chunk c-2's buffers
 
-      // ---- decay sums (log2 units) and beta; warp 4, two tokens a lane
+      // ---- decay sums (log2 units) and beta; warp 8, two tokens a lane
       if (pw == 0) {
         const float a0 = gn0 * kLog2e, a1 = a0 + gn1 * kLog2e;
         float inc = a1;
@@ -444,15 +452,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane >= off) inc += y;
         }
         const float e0 = inc - a1 + a0, e1 = inc;
-        const float last = __shfl_sync(0xffffffffu, e1, 31);
+        const float lst = __shfl_sync(0xffffffffu, e1, 31);
         G2[2 * lane] = e0;
         G2[2 * lane + 1] = e1;
         Bs[2 * lane] = bn0;
         Bs[2 * lane + 1] = bn1;
         Gam[2 * lane] = exp2f(e0);
         Gam[2 * lane + 1] = exp2f(e1);
-        Ec[2 * lane] = exp2f(last - e0);
-        Ec[2 * lane + 1] = exp2f(last - e1);
+        Ec[2 * lane] = exp2f(lst - e0);
+        Ec[2 * lane + 1] = exp2f(lst - e1);
         if (c + 1 < nch) fetch(c + 1);
       }
 
@@ -465,43 +473,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int s = 0; s < 8; s++) {
             const uint32_t kb = (s >> 2) * kKQHalf + (s & 3) * 32;
-            tc::mma_f16(tmem + kColA, tc::sdesc_k_sw128(sm + kb + stack_off(p)),
-                        tc::sdesc_k_sw128(sm + kb + kslot(p)), idA, s > 0);
+            tc::mma_f16(tmem + kColA, dK + ((kb + stack_off(p)) >> 4), dK + ((kb + kslot(p)) >> 4), idA, s > 0);
           }
           tc::mma_commit(&bar[BMP]);
           mark(BMP, c & 1);
         }
       }
       wait(BMP, c & 1);
-      if (tc::group_sync_or(kPrepBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kPrepBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
-      // ---- N (f32, transposed, above the diagonal of NT) and P (split), one row per thread
+      // ---- N (f32, transposed, above the diagonal of NT) and P (split): row r, s in [32 hf, 32 hf + 32)
       {
-        const bool k_rows = (p == 0) == (pw < 2);  // which lane half holds K K^T this chunk
-        const int r = pt & 63;
+        const bool k_rows = (p == 0) == (q4 < 2);  // which lane half holds K K^T this chunk
+        const int r = (q4 & 1) * 32 + lane;
         const float gr = G2[r], br = Bs[r];
-        float row[kC];
-        tc::tmem_ld64(tl + kColA, row);
+        float row[32];
+        tc::tmem_ld32(tl + kColA + 32 * hf, row);
         if (k_rows) {
 #pragma unroll
-          for (int s = 0; s < kC; s++)
-            if (s < r) NT[s * kC + r] = br * row[s] * exp2f(gr - G2[s]);
+          for (int i = 0; i < 32; i++) {
+            const int s = 32 * hf + i;
+            if (s < r) NT[s * kC + r] = br * row[i] * exp2f(gr - G2[s]);
+          }
         } else {
 #pragma unroll
-          for (int s = 0; s < kC; s++) row[s] = s <= r ? row[s] * exp2f(gr - G2[s]) : 0.f;
-#pragma unroll
-          for (int q = 0; q < 4; q++) store_row16(PM, 8192, r, q, row + 16 * q);
+          for (int i = 0; i < 32; i++) {
+            const int s = 32 * hf + i;
+            row[i] = s <= r ? row[i] * exp2f(gr - G2[s]) : 0.f;
+          }
+          store_row16(PM, 8192, r, 2 * hf, row);
+          store_row16(PM, 8192, r, 2 * hf + 1, row + 16);
         }
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
-      if (tc::group_sync_or(kPrepBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kPrepBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
-      // ---- T = (I + N)^-1 diag(beta) in 32-blocks: T11, T22 (diagonal solves), then T21 from N21 T11
+      // ---- T = (I + N)^-1 diag(beta) in 32-blocks: T11, T22 (diagonal solves), then T21 from N21 T11.
       // TM holds T^T: row s (128 bytes, swizzled) = column s of T, read by the MMA as an MN-major B operand.
-      float t11[32];  // warp 4: column `lane` of T11, kept for the row write after T21
+      float t11[32];  // warp 8: column `lane` of T11, kept for the row write after T21
       if (pt < 64) {
         const int blk = pt >> 5, j = pt & 31, base = 32 * blk;
         float x[32];
@@ -524,28 +536,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_row16(TM, 8192, 32 + j, 3, x + 16);
         }
       }
-      if (tc::group_sync_or(kPrepBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kPrepBar, kGroup, !ok)) { ok = false; break; }
       {
-        // Y = N21 T11: warp pw covers columns 8 pw .. 8 pw + 7, lane = row of the second block
-        const int j0 = 8 * pw;
-        float y[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) y[i] = 0.f;
-#pragma unroll 4
+        // Y = N21 T11: warp pw covers columns 4 pw .. 4 pw + 3, lane = row of the second block
+        const int j0 = 4 * pw;
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
         for (int s = 0; s < 32; s++) {
           const float n = NT[s * kC + 32 + lane];
-          const float4 ta = *reinterpret_cast<const float4*>(NT + s * kC + j0);
-          const float4 tb = *reinterpret_cast<const float4*>(NT + s * kC + j0 + 4);
-          const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
-#pragma unroll
-          for (int i = 0; i < 8; i++)
-            if (s >= j0 + i) y[i] = fmaf(n, tv[i], y[i]);
+          const float4 tv = *reinterpret_cast<const float4*>(NT + s * kC + j0);
+          if (s >= j0 + 0) y[0] = fmaf(n, tv.x, y[0]);
+          if (s >= j0 + 1) y[1] = fmaf(n, tv.y, y[1]);
+          if (s >= j0 + 2) y[2] = fmaf(n, tv.z, y[2]);
+          if (s >= j0 + 3) y[3] = fmaf(n, tv.w, y[3]);
         }
-        if (tc::group_sync_or(kPrepBar, 128, false)) { ok = false; break; }  // all reads of T11 rows done
-#pragma unroll
-        for (int i = 0; i < 8; i++) NT[(32 + lane) * kC + j0 + i] = y[i];
+        if (tc::group_sync_or(kPrepBar, kGroup, false)) { ok = false; break; }  // all reads of T11 rows done
+        *reinterpret_cast<float4*>(NT + (32 + lane) * kC + j0) = make_float4(y[0], y[1], y[2], y[3]);
       }
-      if (tc::group_sync_or(kPrepBar, 128, !ok)) { ok = false; break; }
+      if (tc::group_sync_or(kPrepBar, kGroup, !ok)) { ok = false; break; }
       if (pt < 32) {
         // (I + N22) T21 = -N21 T11, column j = lane
         float x[32];
@@ -563,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok && pt == 0 && ((pend >> BMP) & 1u)) tc::mbar_wait(&bar[BMP], (ppar >> BMP) & 1u);
   }
 
-  if (!ok) atomicAdd(a.timeouts, 1u);
+  if (!ok && (tid == 0 || tid == kGroup)) atomicAdd(a.timeouts, 1u);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();

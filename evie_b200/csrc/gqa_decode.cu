@@ -360,7 +360,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 //   PV:  O^T[16 dims][8]   += V^T[16 dims][16 tokens] . P^T[16 tokens][8] (16 MMAs per 16 tokens)
 // Head dims are permuted inside each MMA so that a lane's operand registers come from contiguous 16-byte runs:
 //   QK k-block 2p+e, slots {2c,2c+1 | 2c+8,2c+9} <-> dims 32p + 8c + 4e + {0,1 | 2,3} (c = lane % 4);
-//   PV m-tile i, rows {g | g+8} <-> dims {16g + i | 128 + 16g + i}                      (g = lane / 4).
+//   PV half h, m-tile i, rows {g | g+8} <-> dims {128h + 16g + i | 128h + 16g + 8 + i}  (g = lane / 4),
+//   so a lane's two 16-byte V loads of a token fill one 32-byte sector and each half reads whole sectors.
 // One CTA = 8 warps x 64 tokens = one 512-token split of one (sequence, KV head); the softmax is exact per warp
 // (two passes over its 64 scores held in registers), warps are merged in shared memory, splits as before.
 __device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -537,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const __nv_bfloat16* pv = j < ctx ? row(vp, j) : nullptr;
 #pragma unroll
         for (int r = 0; r < 2; r++)
-          v[tk][r] = pv ? ldg_stream128(pv + 16 * g + 128 * r + 8 * half) : make_uint4(0, 0, 0, 0);
+          v[tk][r] = pv ? ldg_stream128(pv + 128 * half + 16 * g + 8 * r) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
       for (int i = 0; i < 8; i++) {
@@ -557,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (c < 2) {
 #pragma unroll
       for (int i = 0; i < 8; i++) {
-        const int d0 = 16 * g + 8 * half + i, d1 = 128 + d0;
+        const int d0 = 128 * half + 16 * g + i, d1 = d0 + 8;
         sO[warp][hh][d0] = o[i][0];
         sO[warp][hh + 1][d0] = o[i][1];
         sO[warp][hh][d1] = o[i][2];
