@@ -120,6 +120,14 @@ __device__ __forceinline__ void store_row16(uint8_t* tile, uint32_t plane, int r
   }
 }
 
+// 2^x by the hardware approximation (relative error below 2^-22; results below 2^-126 flush to zero, which only
+// drops decay factors that small).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // f32 -> bf16 bits, round to nearest even (finite inputs).
 __device__ __forceinline__ uint16_t bf16_rne(float x) {
   const uint32_t u = __float_as_uint(x);
@@ -432,6 +440,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     if (pw == 0 && nch > 0) fetch(0);
     constexpr uint32_t idA = tc::idesc(1, 1, 128, 64);
+    auto issue_a = [&](int c) {  // thread 256 issues [stack] K^T of chunk c into the A accumulator
+      if (pt != 0) return;
+      const int p = c & 1;
+      wait(BK0 + p, (c >> 1) & 1);
+      wait(BQ0 + p, (c >> 1) & 1);
+      tc::fence_after_sync();
+      if (!ok) return;
+#pragma unroll
+      for (int s = 0; s < 8; s++) {
+        const uint32_t kb = (s >> 2) * kKQHalf + (s & 3) * 32;
+        tc::mma_f16(tmem + kColA, dK + ((kb + stack_off(p)) >> 4), dK + ((kb + kslot(p)) >> 4), idA, s > 0);
+      }
+      tc::mma_commit(&bar[BMP]);
+      mark(BMP, c & 1);
+    };
+    if (nch > 0) issue_a(0);
 
 #pragma unroll 1
     for (int c = 0; c < nch && ok; c++) {
@@ -457,28 +481,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         G2[2 * lane + 1] = e1;
         Bs[2 * lane] = bn0;
         Bs[2 * lane + 1] = bn1;
-        Gam[2 * lane] = exp2f(e0);
-        Gam[2 * lane + 1] = exp2f(e1);
-        Ec[2 * lane] = exp2f(lst - e0);
-        Ec[2 * lane + 1] = exp2f(lst - e1);
+        Gam[2 * lane] = ex2(e0);
+        Gam[2 * lane + 1] = ex2(e1);
+        Ec[2 * lane] = ex2(lst - e0);
+        Ec[2 * lane + 1] = ex2(lst - e1);
         if (c + 1 < nch) fetch(c + 1);
       }
 
-      // ---- [stack] K^T
-      if (pt == 0) {
-        wait(BK0 + p, (c >> 1) & 1);
-        wait(BQ0 + p, (c >> 1) & 1);
-        tc::fence_after_sync();
-        if (ok) {
-#pragma unroll
-          for (int s = 0; s < 8; s++) {
-            const uint32_t kb = (s >> 2) * kKQHalf + (s & 3) * 32;
-            tc::mma_f16(tmem + kColA, dK + ((kb + stack_off(p)) >> 4), dK + ((kb + kslot(p)) >> 4), idA, s > 0);
-          }
-          tc::mma_commit(&bar[BMP]);
-          mark(BMP, c & 1);
-        }
-      }
+      // ---- [stack] K^T (issued at the end of the previous chunk's prep, or before the loop)
       wait(BMP, c & 1);
       if (tc::group_sync_or(kPrepBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
@@ -494,13 +504,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; i++) {
             const int s = 32 * hf + i;
-            if (s < r) NT[s * kC + r] = br * row[i] * exp2f(gr - G2[s]);
+            if (s < r) NT[s * kC + r] = br * row[i] * ex2(gr - G2[s]);
           }
         } else {
 #pragma unroll
           for (int i = 0; i < 32; i++) {
             const int s = 32 * hf + i;
-            row[i] = s <= r ? row[i] * exp2f(gr - G2[s]) : 0.f;
+            row[i] = s <= r ? row[i] * ex2(gr - G2[s]) : 0.f;
           }
           store_row16(PM, 8192, r, 2 * hf, row);
           store_row16(PM, 8192, r, 2 * hf + 1, row + 16);
@@ -567,6 +577,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::fence_proxy_async();
       tc::mbar_arrive(&bar[BTR0 + p]);  // T, P and the decays of chunk c are ready
+      // The A accumulator was consumed by this chunk's N/P: start the next chunk's [stack] K^T now, so that it runs
+      // while the buffers are awaited and the decays summed. (Its K/Q tiles are loaded by the chain only after it has
+      // taken this chunk's T, hence after the hand-over above.)
+      if (c + 1 < nch) issue_a(c + 1);
     }
     if (!ok && pt == 0 && ((pend >> BMP) & 1u)) tc::mbar_wait(&bar[BMP], (ppar >> BMP) & 1u);
   }
