@@ -449,7 +449,10 @@ class ModelDecode(Workload):
         self.cfg = json.load(open(os.path.join(self.ckpt, "config.json")))
         L, n, V = self.cfg["num_hidden_layers"], self.cfg["intermediate_size"], self.cfg["vocab_size"]
         self.max_ctx = self.P + 1024
-        self.m = GpuModel(self.ckpt, max_ctx=self.max_ctx, slots=self.B, max_rows=min(16384, self.B * self.P),
+        # prefill feeds whole prompts, up to EVIE_PREFILL_ROWS rows per call: more sequences per call give the per-row
+        # mixer and attention kernels more CTAs (rows index a grid dimension, so at most 65535)
+        rows = int(os.environ.get("EVIE_PREFILL_ROWS", "32768"))
+        self.m = GpuModel(self.ckpt, max_ctx=self.max_ctx, slots=self.B, max_rows=min(rows, self.B * self.P),
                           device=dev.index or 0)
         g = torch.Generator().manual_seed(5)
         self.layers = torch.randint(0, L, (32,), generator=g).tolist()
@@ -476,7 +479,7 @@ class ModelDecode(Workload):
         self.m.reset_slot(1)
         # prefill every sequence (pair p: slots 2p steered, 2p+1 unsteered), timed on the context's stream
         stream = torch.cuda.ExternalStream(self.m.stream_ptr())
-        per_call = max(1, min(self.B, 16384 // self.P))
+        per_call = max(1, min(self.B, rows // self.P))
         self.first_tokens = np.zeros(self.B, np.uint32)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
