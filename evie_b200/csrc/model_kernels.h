@@ -36,18 +36,18 @@ struct YView {
     for (int k = 1; k < n; k++) s += p[(size_t)k * plane + i];
     return s;
   }
-  // Four consecutive elements (i a multiple of 4; rows and planes 16-byte aligned); up to kMaxPlanes planes are
-  // loaded before any is added, then added in plane order.
+  // Four consecutive elements (i a multiple of 4; rows and planes 16-byte aligned), planes added in plane order.
+  // Each plane is added as it arrives: the loads are independent, so the compiler still issues them ahead, without
+  // holding every plane in registers at once.
   static constexpr int kMaxPlanes = 16;
   __device__ __forceinline__ float4 at4(size_t i) const {
-    float4 v[kMaxPlanes];
-#pragma unroll
-    for (int k = 0; k < kMaxPlanes; k++)
-      if (k < n) v[k] = *reinterpret_cast<const float4*>(p + (size_t)k * plane + i);
-    float4 s = v[0];
+    float4 s = *reinterpret_cast<const float4*>(p + i);
 #pragma unroll
     for (int k = 1; k < kMaxPlanes; k++)
-      if (k < n) s.x += v[k].x, s.y += v[k].y, s.z += v[k].z, s.w += v[k].w;
+      if (k < n) {
+        const float4 v = *reinterpret_cast<const float4*>(p + (size_t)k * plane + i);
+        s.x += v.x, s.y += v.y, s.z += v.z, s.w += v.w;
+      }
     return s;
   }
 };
