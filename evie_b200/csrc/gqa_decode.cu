@@ -23,6 +23,7 @@
 #include "common.h"
 #include "gqa_decode.h"
 #include "model_kernels.h"
+#include "mma_sync.h"
 
 namespace evie {
 
@@ -364,30 +365,6 @@ __global__ void __launch_bounds__(kThreads, 2)
 //   so a lane's two 16-byte V loads of a token fill one 32-byte sector and each half reads whole sectors.
 // One CTA = 8 warps x 64 tokens = one 512-token split of one (sequence, KV head); the softmax is exact per warp
 // (two passes over its 64 scores held in registers), warps are merged in shared memory, splits as before.
-__device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                               uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-__device__ __forceinline__ uint4 ldg_stream128(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
-__device__ __forceinline__ uint32_t word_of(const uint4& u, int i) {
-  return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w;
-}
-
 constexpr int kMmaTiles = kTokPerWarp / 16;  // 4 tiles of 16 tokens per warp
 
 template <class IO>

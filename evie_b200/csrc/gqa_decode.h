@@ -19,4 +19,12 @@ evie_status launch_gqa_model(const float* q_rot, YView y, int ldy, __nv_bfloat16
                              size_t xplane, const RowInfo* rows, int R, const int* page_table, int pages_per_slot,
                              const KV* kc, const KV* vc, int Hq, int Hkv, int page_size, int max_ctx, float scale,
                              void* scratch, int ticket_rows, cudaStream_t st);
+struct SegInfo;
+// Prefill rows (several rows per segment): flash-style blocks of 16 rows per KV head over bf16 pages, GQA group 4,
+// page size a multiple of 32 (gqa_prefill.cu). max_seg_rows = the largest segment's row count.
+evie_status launch_gqa_prefill_model(const float* q_rot, YView y, int ldy, __nv_bfloat16* X2, size_t xplane,
+                                     const RowInfo* rows, const SegInfo* segs, int nseg, int max_seg_rows,
+                                     const int* page_table, int pages_per_slot, const __nv_bfloat16* kc,
+                                     const __nv_bfloat16* vc, int Hq, int Hkv, int page_size, float scale,
+                                     cudaStream_t st);
 }  // namespace evie

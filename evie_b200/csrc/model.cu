@@ -184,6 +184,7 @@ struct evie_ctx {
   float* Y2 = nullptr;
   size_t y2_cols = 0;  // Y2 holds 2 * max_rows rows of y2_cols floats
   int ksplit = 4;      // K slices of the residual-feeding projections (EVIE_GEMM_KSPLIT overrides, 1..8)
+  bool attn_rowwise = false;  // EVIE_ATTN_ROWWISE=1 at creation: prefill rows use the per-row split-KV kernel too
   float* act = nullptr;
   float* q_rot = nullptr;
   int8_t* frames = nullptr;
@@ -493,6 +494,7 @@ evie_status allocate_state(evie_ctx* c) {
   TRY(c->alloc(&c->Y2, 2 * R * mmax));
   c->y2_cols = mmax;
   if (const char* e = getenv("EVIE_GEMM_KSPLIT")) c->ksplit = std::min(8, std::max(1, atoi(e)));
+  if (const char* e = getenv("EVIE_ATTN_ROWWISE")) c->attn_rowwise = e[0] == '1';
   TRY(c->alloc(&c->act, R * s.conv_dim));
   TRY(c->alloc(&c->q_rot, R * s.nh * s.hd));
   TRY(c->alloc(&c->frames, R * s.L * (size_t)s.n, false));
@@ -637,10 +639,19 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
                                                c->q_rot, kc, vc, c->page_table, c->pages_per_slot, kPage, st));
         }
         PROF(P_ATTN);
-        TRY(evie::launch_gqa_model<__nv_bfloat16>(c->q_rot, y, s.in_at, c->X2,
-                                                  (size_t)R * s.nh * s.hd, c->d_rows, R, c->page_table,
-                                                  c->pages_per_slot, kc, vc, s.nh, s.nkv, kPage, max_ctx_rows, scale,
-                                                  c->attn_scratch, c->max_rows, st));
+        if (R > nseq && !c->attn_rowwise && s.nh == 4 * s.nkv) {
+          // prefill: blocks of 16 rows of a segment share every K/V tile (gqa_prefill.cu)
+          int max_seg_rows = 0;
+          for (int i = 0; i < nseq; i++) max_seg_rows = std::max(max_seg_rows, c->h_segs[i].count);
+          TRY(evie::launch_gqa_prefill_model(c->q_rot, y, s.in_at, c->X2, (size_t)R * s.nh * s.hd, c->d_rows,
+                                             c->d_segs, nseq, max_seg_rows, c->page_table, c->pages_per_slot, kc, vc,
+                                             s.nh, s.nkv, kPage, scale, st));
+        } else {
+          TRY(evie::launch_gqa_model<__nv_bfloat16>(c->q_rot, y, s.in_at, c->X2,
+                                                    (size_t)R * s.nh * s.hd, c->d_rows, R, c->page_table,
+                                                    c->pages_per_slot, kc, vc, s.nh, s.nkv, kPage, max_ctx_rows,
+                                                    scale, c->attn_scratch, c->max_rows, st));
+        }
       }
       { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2, &yo, residual_ksplit(c, s.nh * s.hd))); }
     }

@@ -194,3 +194,40 @@ def test_device_decode_loop_matches_step_calls(tiny_ckpt, cuda):
         m.close()
     assert np.array_equal(results[0][0], results[1][0])
     assert np.array_equal(results[0][1], results[1][1])
+
+
+@pytest.fixture(scope="module")
+def group4_ckpt(tmp_path_factory):
+    """GQA group 4 (the Qwen3.5 sizes' grouping), which selects the flash prefill attention for multi-row calls."""
+    path = str(tmp_path_factory.mktemp("ckpt4") / "tiny4")
+    ck.write_checkpoint(path, ck.tiny_config(vocab_size=2048, num_hidden_layers=8, num_attention_heads=8,
+                                             num_key_value_heads=2), seed=4)
+    return path
+
+
+@pytest.mark.gpu
+def test_flash_prefill_matches_rowwise_attention(group4_ckpt, cuda):
+    """Prefill attention in blocks of 16 rows (gqa_prefill.cu) against the per-row split-KV kernel on the same bf16
+    KV: ragged prompt lengths in one call (partial blocks, segments of different lengths), then one prompt continued
+    in a second multi-row call (rows whose context starts before the call). Both paths compute the same f32-grade
+    scores on the same bf16 keys and values, so logits agree to f32 rounding."""
+    from evie_b200.gpu import GpuSeq
+
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, 2048, n).astype(np.uint32) for n in (40, 17, 70, 1)]
+    more = rng.integers(0, 2048, 35).astype(np.uint32)
+    results = []
+    for rowwise in ("0", "1"):
+        os.environ["EVIE_ATTN_ROWWISE"] = rowwise
+        try:
+            m = _gpu_model(group4_ckpt, False, max_ctx=256, slots=4, max_rows=256)
+        finally:
+            del os.environ["EVIE_ATTN_ROWWISE"]
+        a = m.forward([GpuSeq(i, 0, p) for i, p in enumerate(prompts)])
+        b = m.forward([GpuSeq(2, len(prompts[2]), more)])
+        results.append((a.logits.copy(), a.next_tokens.copy(), b.logits.copy(), b.next_tokens.copy()))
+        m.close()
+    (la, ta, lb, tb), (ra, rta, rb, rtb) = results
+    assert np.abs(la - ra).max() < 1e-3, np.abs(la - ra).max()
+    assert np.abs(lb - rb).max() < 1e-3, np.abs(lb - rb).max()
+    assert np.array_equal(ta, rta) and np.array_equal(tb, rtb)
