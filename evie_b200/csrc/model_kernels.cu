@@ -295,6 +295,133 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
   for (int r = 0; r < 16; r++) *reinterpret_cast<float4*>(Sh + (size_t)(warp + 8 * r) * DV) = s[r];
 }
 
+// Prefill form of the mixer (segments of many rows): one CTA per (segment, value head), the head's state in registers
+// with warp w owning columns 16w .. 16w + 15 and lane (rg, cg) = (lane / 4, lane % 4) rows rg + 8 r, columns
+// 16 w + 4 cg .. + 3, so both reductions over the key index (S^T k and S^T q) stay inside a warp: no CTA barrier per
+// token. q, k, v, z, decay and beta of 32 tokens are staged in shared memory at a time, and the gated RMSNorm of
+// those 32 outputs runs in parallel after them. Same recurrence and order of operations per token as
+// gdn_mixer_kernel (model.rs:501-524; gated RMSNorm model.rs:377-383).
+constexpr int kSeqChunk = 32;
+__global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_seq_kernel(
+    const float* __restrict__ act, YView y, int ldy, const SegInfo* __restrict__ segs, float* __restrict__ rec_state,
+    size_t rs_slot, const float* __restrict__ neg_a, const float* __restrict__ dt_bias, const float* __restrict__ norm_w,
+    int conv_dim, int key_dim, int vd, int hv, int ratio, float eps, __nv_bfloat16* __restrict__ X2, size_t xplane) {
+  constexpr int DK = 128, DV = 128;
+  extern __shared__ __align__(16) float smf[];
+  float* sq = smf;                          // [32][128]
+  float* sk = sq + kSeqChunk * DK;          // [32][128]
+  float* sv = sk + kSeqChunk * DK;          // [32][128]
+  float* sz = sv + kSeqChunk * DV;          // [32][128]
+  float* so = sz + kSeqChunk * DV;          // [32][128] outputs before the norm
+  float* sdec = so + kSeqChunk * DV;        // [32]
+  float* sbeta = sdec + kSeqChunk;          // [32]
+  const int head = blockIdx.x;
+  const SegInfo sg = segs[blockIdx.y];
+  if (sg.count == 0) return;
+  const int kh = head / ratio;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rg = lane >> 2, cg = lane & 3;
+  const int c0 = 16 * warp + 4 * cg;
+  float* Sh = rec_state + (size_t)sg.slot * rs_slot + (size_t)head * DK * DV + c0;
+  float4 s[16];
+#pragma unroll
+  for (int r = 0; r < 16; r++) s[r] = *reinterpret_cast<const float4*>(Sh + (size_t)(rg + 8 * r) * DV);
+
+  for (int t0 = 0; t0 < sg.count; t0 += kSeqChunk) {
+    const int nt = min(kSeqChunk, sg.count - t0);
+    // ---- stage the chunk's inputs (rows of act and y for this head)
+#pragma unroll 1
+    for (int i = tid; i < nt * 128; i += kMixThreads) {
+      const int t = i >> 7, part = (i >> 5) & 3, j = (i & 31) * 4;  // per token: q, k, v, z, 32 float4 each
+      const size_t row = (size_t)sg.start + t0 + t;
+      float4 val;
+      if (part == 3) {
+        val = y.at4(row * ldy + conv_dim + head * DV + j);
+      } else {
+        const int off = part == 0 ? kh * DK : part == 1 ? key_dim + kh * DK : 2 * key_dim + head * DV;
+        val = *reinterpret_cast<const float4*>(act + row * conv_dim + off + j);
+      }
+      *reinterpret_cast<float4*>(smf + (size_t)part * kSeqChunk * DK + t * DK + j) = val;
+    }
+    if (tid < nt) {
+      const int row = sg.start + t0 + tid;
+      const float bb = y.at((size_t)row * ldy + conv_dim + vd + head);
+      const float aa = y.at((size_t)row * ldy + conv_dim + vd + hv + head);
+      sdec[tid] = expf(neg_a[head] * softplus_(aa + dt_bias[head]));
+      sbeta[tid] = sigmoidf_(bb);
+    }
+    __syncthreads();
+    // ---- the recurrence, token by token, warp-local
+    for (int t = 0; t < nt; t++) {
+      const float* kt = sk + t * DK;
+      const float* qt = sq + t * DK;
+      const float decay = sdec[t], beta = sbeta[t];
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < 16; r++) {
+        const float kr = kt[rg + 8 * r];
+        kv.x += s[r].x * kr; kv.y += s[r].y * kr; kv.z += s[r].z * kr; kv.w += s[r].w * kr;
+      }
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        kv.x += __shfl_xor_sync(0xffffffffu, kv.x, off);
+        kv.y += __shfl_xor_sync(0xffffffffu, kv.y, off);
+        kv.z += __shfl_xor_sync(0xffffffffu, kv.z, off);
+        kv.w += __shfl_xor_sync(0xffffffffu, kv.w, off);
+      }
+      const float4 v4 = *reinterpret_cast<const float4*>(sv + t * DV + c0);
+      const float d0 = (v4.x - decay * kv.x) * beta, d1 = (v4.y - decay * kv.y) * beta;
+      const float d2 = (v4.z - decay * kv.z) * beta, d3 = (v4.w - decay * kv.w) * beta;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < 16; r++) {
+        const int i = rg + 8 * r;
+        const float kr = kt[i], qr = qt[i];
+        s[r].x = s[r].x * decay + kr * d0; s[r].y = s[r].y * decay + kr * d1;
+        s[r].z = s[r].z * decay + kr * d2; s[r].w = s[r].w * decay + kr * d3;
+        o.x += s[r].x * qr; o.y += s[r].y * qr; o.z += s[r].z * qr; o.w += s[r].w * qr;
+      }
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        o.x += __shfl_xor_sync(0xffffffffu, o.x, off);
+        o.y += __shfl_xor_sync(0xffffffffu, o.y, off);
+        o.z += __shfl_xor_sync(0xffffffffu, o.z, off);
+        o.w += __shfl_xor_sync(0xffffffffu, o.w, off);
+      }
+      if (rg == 0) *reinterpret_cast<float4*>(so + t * DV + c0) = o;
+    }
+    __syncthreads();
+    // ---- gated RMSNorm of the chunk's outputs: 8 threads per token, 16 columns each
+    {
+      // Every lane takes part in the shuffles (a full-mask shuffle must be reached by the whole warp); only the
+      // loads and stores are limited to the chunk's tokens.
+      const int t = tid >> 3, part = tid & 7;
+      const bool live = t < nt;
+      const float* ot = so + t * DV + 16 * part;
+      float ss = 0.f;
+      if (live) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) ss += ot[j] * ot[j];
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (live) {
+        const float inv = 1.0f / sqrtf(ss / (float)DV + eps);
+        const int row = sg.start + t0 + t;
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int col = 16 * part + j;
+          store_split(X2, xplane, (size_t)row * vd + head * DV + col,
+                      ot[j] * inv * norm_w[col] * siluf_(sz[t * DV + col]));
+        }
+      }
+    }
+    __syncthreads();  // the chunk buffers are refilled next
+  }
+#pragma unroll
+  for (int r = 0; r < 16; r++) *reinterpret_cast<float4*>(Sh + (size_t)(rg + 8 * r) * DV) = s[r];
+}
+
 // model.rs:419-442, rope model.rs:470-479: q_norm / k_norm (gains 1+w) + rotate-half RoPE on the first `rot` dims;
 // K and V appended to the paged cache. One CTA per (row, head) with one thread per head dim (hd = 256).
 template <typename KV>
@@ -517,6 +644,21 @@ evie_status k_gdn_mixer(const float* act, YView y, int ldy, int R, const SegInfo
                         const float* norm_w, const ModelShape& s, __nv_bfloat16* X2, cudaStream_t st) {
   if (nseg == 0) return EVIE_OK;
   dim3 grid(s.hv, nseg);
+  if (R > nseg) {  // some segment has several rows: the warp-local sequential kernel
+    constexpr int kSmemSeq = (5 * kSeqChunk * 128 + 2 * kSeqChunk) * 4;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    EVIE_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 64 && !attr_set[dev]) {
+      EVIE_CUDA_TRY(cudaFuncSetAttribute(gdn_mixer_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemSeq));
+      attr_set[dev] = true;
+    }
+    gdn_mixer_seq_kernel<<<grid, kMixThreads, kSmemSeq, st>>>(act, y, ldy, segs, rec_state, rs_slot, neg_a, dt_bias,
+                                                              norm_w, s.conv_dim, s.key_dim, s.vd, s.hv, s.hv / s.hk,
+                                                              s.eps, X2, (size_t)R * s.vd);
+    EVIE_CHECK_LAUNCH("gdn_mixer_seq_kernel");
+    return EVIE_OK;
+  }
   gdn_mixer_kernel<<<grid, kMixThreads, 0, st>>>(act, y, ldy, segs, rec_state, rs_slot, neg_a,
                                                  dt_bias, norm_w, s.conv_dim, s.key_dim, s.vd, s.hv, s.hv / s.hk, s.eps,
                                                  X2, (size_t)R * s.vd);
