@@ -111,6 +111,34 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------------------------------------
+# multi-GPU host logic (one process per GPU, weak scaling)
+
+def rank_prompts(rank: int, npairs: int, P: int, V: int, count: int | None = None):
+    """The prompts of `rank`'s steered/unsteered pairs: pairs [rank * npairs, (rank + 1) * npairs) of one seeded
+    stream (seed 5), so that every rank draws disjoint pairs of the same global set whatever the world size. `count`
+    limits how many of the rank's pairs are drawn."""
+    import torch
+
+    count = npairs if count is None else count
+    g = torch.Generator().manual_seed(5)
+    first = rank * npairs
+    drawn = [torch.randint(0, V, (P,), generator=g) for _ in range(first + count)]
+    return [p.numpy().astype(np.uint32) for p in drawn[first:]]
+
+
+def max_over_ranks(values, device=None):
+    """Element-wise max of a list of floats over all ranks (every rank gets the result); identity with one rank."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return list(values)
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+# ------------------------------------------------------------------------------------------------------------
 # workloads
 
 class Workload:
@@ -457,11 +485,7 @@ class ModelDecode(Workload):
         g = torch.Generator().manual_seed(5)
         self.layers = torch.randint(0, L, (32,), generator=g).tolist()
         self.neurons = torch.randint(0, n, (32,), generator=g).tolist()
-        npairs = self.B // 2
-        g = torch.Generator().manual_seed(5)
-        first = self.rank * npairs
-        all_prompts = [torch.randint(0, V, (self.P,), generator=g) for _ in range(first + npairs)]
-        self.prompts = [p.numpy().astype(np.uint32) for p in all_prompts[first:]]
+        self.prompts = rank_prompts(self.rank, self.B // 2, self.P, V)
         # dose unit: median ||residual leaving layer l|| over tokens 1.. of pair 0's prompt (calib.rs:94-100),
         # divided by ||W_down[:, n]|| (engine.rs:102-104); measured on the unsteered lane of pair 0.
         out = self.m.forward([GpuSeq(1, 0, self.prompts[0])], want_logits=False, capture=True)
@@ -652,10 +676,7 @@ class ModelDecode(Workload):
         g = torch.Generator().manual_seed(5)
         self.layers = torch.randint(0, L, (32,), generator=g).tolist()
         self.neurons = torch.randint(0, n, (32,), generator=g).tolist()
-        g = torch.Generator().manual_seed(5)
-        first = self.rank * (self.B // 2)
-        all_prompts = [torch.randint(0, V, (self.P,), generator=g) for _ in range(first + 1)]
-        self.prompts = [all_prompts[first].numpy().astype(np.uint32)]
+        self.prompts = rank_prompts(self.rank, self.B // 2, self.P, V, count=1)
         oracle.set_threads(threads)
         m = oracle.Model(self.ckpt)
         _, _, rs = m.forward([dict(cache=m.new_cache(), tokens=self.prompts[0][:64], resid=True)])
@@ -793,10 +814,7 @@ def run_ours(args):
     barrier()
     e2e_ms, h2d, d2h = w.e2e(args.steps)
     kernels = w.profile_pass(args.steps) if hasattr(w, "profile_pass") else None
-    if world > 1:
-        t = torch.tensor([total_ms, e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, e2e_ms = t.tolist()
+    total_ms, e2e_ms = max_over_ranks([total_ms, e2e_ms], device=dev)
 
     pk = peaks()
     avg_s = total_ms / 1000.0 / args.steps
