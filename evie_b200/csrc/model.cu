@@ -602,8 +602,11 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
       {
         PROF(P_CONV);
         const bool single_rows = R == nseq && s.K <= 8;  // decode: one row per segment, the conv kernel shifts the window
+        int max_seg_rows = 1;
+        if (!single_rows)
+          for (int i = 0; i < nseq; i++) max_seg_rows = std::max(max_seg_rows, c->h_segs[i].count);
         TRY(evie::k_conv_silu_norm(y, s.in_dn, R, c->d_rows, c->d_segs, cs, cs_slot, L.conv, s, c->act, st,
-                                   single_rows));
+                                   single_rows, nseq, max_seg_rows));
         if (!single_rows) TRY(evie::k_conv_state_update(y, s.in_dn, R, c->d_segs, nseq, cs, cs_slot, s, st));
       }
       float* rsb = c->rec_state + (size_t)L.idx * s.hv * s.dk * s.dv;

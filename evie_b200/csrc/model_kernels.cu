@@ -192,6 +192,49 @@ __global__ void __launch_bounds__(128) conv_silu_norm_kernel(YView y, int ldy,
   act[(size_t)r * conv_dim + c] = out;
 }
 
+// The same conv for segments of many rows (prefill): one CTA per (128-channel block, segment, 64 consecutive rows),
+// one thread per channel walking the rows with its K-1 previous inputs in registers, so every input is read once.
+// Same products, summation order and head-norm reduction as conv_silu_norm_kernel.
+constexpr int kConvRows = 64;
+template <int K>
+__global__ void __launch_bounds__(128) conv_rows_kernel(YView y, int ldy, const SegInfo* __restrict__ segs,
+                                                        const float* __restrict__ conv_state, size_t cs_slot,
+                                                        const float* __restrict__ conv_w, int conv_dim, int hk,
+                                                        float qscale, float* __restrict__ act) {
+  __shared__ float red[4];
+  const int c = blockIdx.x * 128 + threadIdx.x;
+  const SegInfo sg = segs[blockIdx.y];
+  const int t0 = blockIdx.z * kConvRows;
+  if (t0 >= sg.count) return;
+  const int nt = min(kConvRows, sg.count - t0);
+  const float* cs = conv_state + (size_t)sg.slot * cs_slot;
+  float w[K], win[K];
+#pragma unroll
+  for (int j = 0; j < K; j++) w[j] = conv_w[(size_t)c * K + j];
+#pragma unroll
+  for (int j = 0; j < K - 1; j++) {
+    const int tt = t0 - (K - 1) + j;
+    win[j] = tt >= 0 ? y.at((size_t)(sg.start + tt) * ldy + c) : cs[(size_t)(K - 1 + tt) * conv_dim + c];
+  }
+  const bool head_norm = (int)blockIdx.x < 2 * hk;
+  const float scl = (int)blockIdx.x < hk ? qscale : 1.0f;
+  for (int t = 0; t < nt; t++) {
+    const size_t row = (size_t)sg.start + t0 + t;
+    win[K - 1] = y.at(row * ldy + c);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; j++) acc += w[j] * win[j];
+#pragma unroll
+    for (int j = 0; j < K - 1; j++) win[j] = win[j + 1];
+    float out = siluf_(acc);
+    if (head_norm) {  // q or k head: L2 normalise (kernels.rs dot + 1e-6), q also by 1/sqrt(dk)
+      const float ss = block_sum<128>(out * out, red);
+      out *= (1.0f / sqrtf(ss + 1e-6f)) * scl;
+    }
+    act[row * conv_dim + c] = out;
+  }
+}
+
 // model.rs:339: the conv window keeps the last K-1 raw inputs of [state ; rows].
 __global__ void conv_state_update_kernel(YView y, int ldy,
                                          const SegInfo* __restrict__ segs, float* __restrict__ conv_state,
@@ -620,8 +663,15 @@ evie_status k_add_final(float* x, YView y, int ldy, int R, const RowInfo* rows, 
 
 evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
                              float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
-                             float* act, cudaStream_t st, bool update_window) {
+                             float* act, cudaStream_t st, bool update_window, int nseg, int max_seg_rows) {
   if (R == 0) return EVIE_OK;
+  if (max_seg_rows > 1 && s.K == 4 && !update_window) {
+    dim3 grid(s.conv_dim / 128, nseg, (max_seg_rows + kConvRows - 1) / kConvRows);
+    conv_rows_kernel<4><<<grid, 128, 0, st>>>(y, ldy, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
+                                              1.0f / sqrtf((float)s.dk), act);
+    EVIE_CHECK_LAUNCH("conv_rows_kernel");
+    return EVIE_OK;
+  }
   dim3 grid(s.conv_dim / 128, R);
   conv_silu_norm_kernel<<<grid, 128, 0, st>>>(y, ldy, rows, segs, conv_state, cs_slot, conv_w, s.K,
                                               s.conv_dim, s.hk, 1.0f / sqrtf((float)s.dk), act, update_window);
