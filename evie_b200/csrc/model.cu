@@ -22,6 +22,8 @@
 #include <cstring>
 #include <dirent.h>
 #include <fstream>
+#include <map>
+#include <tuple>
 #include <memory>
 #include <sstream>
 #include <string>
@@ -185,6 +187,9 @@ struct evie_ctx {
   size_t y2_cols = 0;  // Y2 holds 2 * max_rows rows of y2_cols floats
   int ksplit = 4;      // K slices of the residual-feeding projections (EVIE_GEMM_KSPLIT overrides, 1..8)
   bool attn_rowwise = false;  // EVIE_ATTN_ROWWISE=1 at creation: prefill rows use the per-row split-KV kernel too
+  bool no_graph = false;      // EVIE_NO_GRAPH=1 at creation: decode-shaped calls run eagerly
+  // Captured decode-shaped forward calls, keyed by (sequences, want logits, head, capture, tracking, context bound).
+  std::map<std::tuple<int, int, int, int, int, int>, cudaGraphExec_t> fwd_graphs;
   float* act = nullptr;
   float* q_rot = nullptr;
   int8_t* frames = nullptr;
@@ -495,6 +500,7 @@ evie_status allocate_state(evie_ctx* c) {
   c->y2_cols = mmax;
   if (const char* e = getenv("EVIE_GEMM_KSPLIT")) c->ksplit = std::min(8, std::max(1, atoi(e)));
   if (const char* e = getenv("EVIE_ATTN_ROWWISE")) c->attn_rowwise = e[0] == '1';
+  if (const char* e = getenv("EVIE_NO_GRAPH")) c->no_graph = e[0] == '1';
   TRY(c->alloc(&c->act, R * s.conv_dim));
   TRY(c->alloc(&c->q_rot, R * s.nh * s.hd));
   TRY(c->alloc(&c->frames, R * s.L * (size_t)s.n, false));
@@ -548,7 +554,14 @@ int residual_ksplit(const evie_ctx* c, int K) {
 }
 
 // gpu/mod.rs:616-634: limits, then the row and segment tables uploaded for the kernels.
-evie_status prepare_rows(evie_ctx* c, const evie_seq* seqs, int nseq, int* R_out, int* max_ctx_out) {
+evie_status upload_rows(evie_ctx* c, int R, int nseq) {
+  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_rows, c->h_rows, R * sizeof(RowInfo), cudaMemcpyHostToDevice, c->stream));
+  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_segs, c->h_segs, nseq * sizeof(SegInfo), cudaMemcpyHostToDevice, c->stream));
+  return EVIE_OK;
+}
+
+evie_status prepare_rows(evie_ctx* c, const evie_seq* seqs, int nseq, int* R_out, int* max_ctx_out,
+                         bool upload = true) {
   auto& s = c->s;
   EVIE_ARG(nseq >= 1 && nseq <= c->slots, "forward: 1..=%d sequences per call, got %d", c->slots, nseq);
   int R = 0, max_ctx_rows = 0;
@@ -573,8 +586,7 @@ evie_status prepare_rows(evie_ctx* c, const evie_seq* seqs, int nseq, int* R_out
       c->h_rows[r++] = RowInfo{q.slot, q.pos0 + t, (int)q.tokens[t], i};
     }
   }
-  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_rows, c->h_rows, R * sizeof(RowInfo), cudaMemcpyHostToDevice, c->stream));
-  EVIE_CUDA_TRY(cudaMemcpyAsync(c->d_segs, c->h_segs, nseq * sizeof(SegInfo), cudaMemcpyHostToDevice, c->stream));
+  if (upload) TRY(upload_rows(c, R, nseq));
   *R_out = R;
   *max_ctx_out = max_ctx_rows;
   return EVIE_OK;
@@ -691,10 +703,40 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
                          int8_t* frames, uint16_t* resid, uint32_t* next_tokens) {
   auto& s = c->s;
   int R = 0, max_ctx_rows = 0;
-  TRY(prepare_rows(c, seqs, nseq, &R, &max_ctx_rows));
+  TRY(prepare_rows(c, seqs, nseq, &R, &max_ctx_rows, false));
   cudaStream_t st = c->stream;
-  TRY(enqueue_layers(c, R, nseq, max_ctx_rows, capture));
-  if (want_logits || next_tokens) TRY(enqueue_head(c, nseq, want_logits != 0));
+  const bool head = want_logits || next_tokens;
+  if (R == nseq && !c->prof && !c->no_graph) {
+    // Decode-shaped call (one token per sequence): replay a captured graph of (row-table upload, layers, head).
+    // The tables are copied from the same pinned host arrays each replay; the attention's split count uses a
+    // context bound rounded up to a multiple of 2048, so a graph serves every call until the context passes it.
+    const int bound = std::min(c->max_ctx, (max_ctx_rows + 2047) / 2048 * 2048);
+    const auto key = std::make_tuple(nseq, want_logits != 0, (int)head, capture != 0, (int)c->track, bound);
+    auto it = c->fwd_graphs.find(key);
+    if (it == c->fwd_graphs.end()) {
+      cudaGraph_t g = nullptr;
+      EVIE_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      evie_status rc = upload_rows(c, R, nseq);
+      if (rc == EVIE_OK) rc = enqueue_layers(c, R, nseq, bound, capture);
+      if (rc == EVIE_OK && head) rc = enqueue_head(c, nseq, want_logits != 0);
+      const cudaError_t ce = cudaStreamEndCapture(st, &g);
+      if (rc != EVIE_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      EVIE_CUDA_TRY(ce);
+      cudaGraphExec_t exec = nullptr;
+      const cudaError_t ie = cudaGraphInstantiate(&exec, g, 0);
+      cudaGraphDestroy(g);
+      EVIE_CUDA_TRY(ie);
+      it = c->fwd_graphs.emplace(key, exec).first;
+    }
+    EVIE_CUDA_TRY(cudaGraphLaunch(it->second, st));
+  } else {
+    TRY(upload_rows(c, R, nseq));
+    TRY(enqueue_layers(c, R, nseq, max_ctx_rows, capture));
+    if (head) TRY(enqueue_head(c, nseq, want_logits != 0));
+  }
   if (want_logits && logits)
     EVIE_CUDA_TRY(cudaMemcpyAsync(logits, c->logits, (size_t)nseq * s.V * 4, cudaMemcpyDeviceToHost, st));
   if (next_tokens) EVIE_CUDA_TRY(cudaMemcpyAsync(next_tokens, c->next, nseq * 4, cudaMemcpyDeviceToHost, st));
@@ -736,9 +778,8 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
   cudaStream_t st = c->stream;
   // Steps after the first replay one captured CUDA graph of (advance rows, layers, head): every per-step input is
   // already on the device, and the attention's split count uses a context bound valid for all steps. The profiling
-  // mode (events around kernel groups) runs the steps eagerly. EVIE_NO_GRAPH=1 also forces eager steps.
-  const char* ng = getenv("EVIE_NO_GRAPH");
-  const bool use_graph = !c->prof && steps > 1 && !(ng && ng[0] == '1');
+  // mode (events around kernel groups) runs the steps eagerly, as does a context created with EVIE_NO_GRAPH=1.
+  const bool use_graph = !c->prof && steps > 1 && !c->no_graph;
   const int ctx_bound = max_ctx_rows + steps - 1;
   cudaGraphExec_t exec = nullptr;
   struct ExecGuard {
@@ -792,6 +833,7 @@ void destroy(evie_ctx* c) {
   if (!c) return;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
+  for (auto& g : c->fwd_graphs) cudaGraphExecDestroy(g.second);
   for (void* p : c->allocs) cudaFree(p);
   if (c->hist) cudaFree(c->hist);
   for (auto& p : c->prof_pending) {
