@@ -14,6 +14,23 @@ class Op(C.Structure):
     _fields_ = [("layer", C.c_int32), ("neuron", C.c_int32), ("mode", C.c_int32), ("value", C.c_float)]
 
 
+class PlanOp(C.Structure):
+    """evie_plan_op"""
+    _fields_ = [("layer", C.c_int32), ("neuron", C.c_int32), ("mode", C.c_int32), ("value", C.c_float),
+                ("gate", C.c_int32)]
+
+
+class Detector(C.Structure):
+    """evie_detector"""
+    _fields_ = [("gate", C.c_int32), ("layer", C.c_int32), ("neuron", C.c_int32), ("weight", C.c_float)]
+
+
+class SampleParams(C.Structure):
+    """evie_sample_params"""
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("min_p", C.c_float),
+                ("repetition_penalty", C.c_float), ("seed", C.c_uint64)]
+
+
 class ModelInfo(C.Structure):
     """evie_model_info"""
     _fields_ = [
@@ -37,6 +54,12 @@ SIGNATURES = {
     "evie_profile": (I, [P, I]),
     "evie_profile_read": (I, [P, I, C.POINTER(C.c_char_p), C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
     "evie_set_ops": (I, [P, I, P, I]),
+    "evie_set_plan": (I, [P, I, P, I, P, I, P, I]),
+    "evie_gate_state": (I, [P, I, P, P, I]),
+    "evie_reset_gates": (I, [P, I]),
+    "evie_set_sampler": (I, [P, I, P]),
+    "evie_sampler_seed_state": (C.c_uint64, [C.c_uint64]),
+    "evie_sample": (I, [P, I, I, P, P, P, P, P, P]),
     "evie_reset_slot": (I, [P, I]),
     "evie_set_scale": (I, [P, P, SZ]),
     "evie_track_max": (I, [P, I]),

@@ -33,6 +33,7 @@
 #include "gqa_decode.h"
 #include "json.h"
 #include "model_kernels.h"
+#include "sampler.h"
 
 using evie::RowInfo;
 using evie::SegInfo;
@@ -41,6 +42,8 @@ namespace {
 
 constexpr int kPage = 256;
 constexpr int kMaxOps = 64;
+constexpr int kMaxGates = 32;
+constexpr int kMaxDets = 128;
 
 struct Tensor {
   std::string dtype;
@@ -177,6 +180,25 @@ struct evie_ctx {
   // steering / capture
   evie_op* ops = nullptr;      // [slots][kMaxOps]
   int* op_range = nullptr;     // [slots][L][2]
+  int* op_gate = nullptr;      // [slots][kMaxOps]
+  evie::GateSpec* gates = nullptr;  // [slots][kMaxGates]
+  int* n_gates = nullptr;           // [slots]
+  evie::DetSpec* dets = nullptr;    // [slots][kMaxDets]
+  int* det_range = nullptr;         // [slots][L][2]
+  int* gate_open = nullptr;         // [slots][kMaxGates]
+  float* gate_score = nullptr;      // [slots][kMaxGates]
+  int* gate_from = nullptr;         // [slots][kMaxGates]
+  float* gate_partial = nullptr;    // [max_rows][kMaxGates]
+  std::vector<int> h_n_gates;                // [slots]
+  std::vector<std::vector<char>> h_gate_layers;  // per slot: layers that hold a detector or a gate decision
+  std::vector<char> gate_layers;             // [L]: some slot's plan needs the detector kernel at this layer
+  // sampling (sampling.rs:21-93): per-slot parameters and generator state, bitmap of every token fed since reset
+  evie::SamplerParams* samp = nullptr;  // [slots]
+  uint64_t* samp_rng = nullptr;         // [slots]
+  uint32_t* seen = nullptr;             // [slots][seen_words]
+  int seen_words = 0;
+  std::vector<char> h_samp_on;          // [slots]: not plain greedy
+  bool samp_active = false;             // some slot is not plain greedy: the sampler kernel follows the argmax
   float* scale = nullptr;      // [L][n]
   uint32_t* maxbuf = nullptr;  // [L][n]
   bool track = false;
@@ -486,6 +508,29 @@ evie_status allocate_state(evie_ctx* c) {
   EVIE_CUDA_TRY(cudaMemcpy(c->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
   TRY(c->alloc(&c->ops, S * kMaxOps));
   TRY(c->alloc(&c->op_range, S * s.L * 2));
+  TRY(c->alloc(&c->op_gate, S * kMaxOps));
+  TRY(c->alloc(&c->gates, S * kMaxGates));
+  TRY(c->alloc(&c->n_gates, S));
+  TRY(c->alloc(&c->dets, S * kMaxDets));
+  TRY(c->alloc(&c->det_range, S * s.L * 2));
+  TRY(c->alloc(&c->gate_open, S * kMaxGates));
+  TRY(c->alloc(&c->gate_score, S * kMaxGates));
+  TRY(c->alloc(&c->gate_from, S * kMaxGates));
+  TRY(c->alloc(&c->gate_partial, R * kMaxGates));
+  c->h_n_gates.assign(S, 0);
+  c->seen_words = (s.V + 31) / 32;
+  TRY(c->alloc(&c->samp, S));
+  TRY(c->alloc(&c->samp_rng, S));
+  TRY(c->alloc(&c->seen, S * c->seen_words));
+  {
+    std::vector<evie::SamplerParams> dflt(S, evie::SamplerParams{0.0f, 1.0f, 0.0f, 1.0f});  // SampleParams::default
+    EVIE_CUDA_TRY(cudaMemcpy(c->samp, dflt.data(), S * sizeof(evie::SamplerParams), cudaMemcpyHostToDevice));
+    std::vector<uint64_t> rng(S, evie::sampler_seed_state(0));
+    EVIE_CUDA_TRY(cudaMemcpy(c->samp_rng, rng.data(), S * 8, cudaMemcpyHostToDevice));
+  }
+  c->h_samp_on.assign(S, 0);
+  c->h_gate_layers.assign(S, std::vector<char>(s.L, 0));
+  c->gate_layers.assign(s.L, 0);
   TRY(c->alloc(&c->scale, (size_t)s.L * s.n, false));
   {
     std::vector<float> one((size_t)s.L * s.n, 1.0f);  // gpu/mod.rs:367: scales start at 1
@@ -601,9 +646,15 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
   const size_t cs_slot = (size_t)std::max(c->n_lin, 1) * (s.K - 1) * s.conv_dim;
   const size_t rs_slot = (size_t)std::max(c->n_lin, 1) * s.hv * s.dk * s.dv;
   const size_t kv_layer = (size_t)c->slots * c->pages_per_slot * s.nkv * kPage * s.hd;
-  evie::SteerTables steer{c->ops, c->op_range, kMaxOps};
+  evie::SteerTables steer{c->ops, c->op_range, kMaxOps, c->op_gate, c->gates, c->gate_open, c->gate_from, kMaxGates};
+  const evie::GateTables gt{c->gates,    c->n_gates,    c->dets,      c->det_range, kMaxGates,
+                            kMaxDets,    c->gate_open,  c->gate_score, c->gate_from, c->gate_partial};
 
-  { PROF(P_NORM); TRY(evie::k_embed_norm(c->d_rows, R, c->embed, c->x, c->layers[0].ln1, s.eps, s.d, c->X2, st)); }
+  {
+    PROF(P_NORM);
+    TRY(evie::k_embed_norm(c->d_rows, R, c->embed, c->x, c->layers[0].ln1, s.eps, s.d, c->X2, c->seen,
+                           c->seen_words, st));
+  }
   for (int li = 0; li < s.L; li++) {
     Layer& L = c->layers[li];
     evie::YView yo;  // output projection of the mixer
@@ -676,6 +727,7 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
     { PROF(P_GEMM); TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2, &yg)); }
     {
       PROF(P_SWIGLU);
+      if (c->gate_layers[li]) TRY(evie::k_gate_detect(yg, 2 * s.n, c->d_segs, nseq, li, s, gt, st));
       TRY(evie::k_swiglu(yg, 2 * s.n, R, c->d_rows, li, s, steer, c->scale, fr, c->track ? c->maxbuf : nullptr,
                          c->X2, st));
     }
@@ -696,7 +748,12 @@ evie_status enqueue_head(evie_ctx* c, int nseq, bool want_logits) {
   evie::YView yl;
   { PROF(P_LMHEAD); TRY(gemm(c, c->lm_head, c->s.V, c->s.d, c->X2, nseq, c->L2, &yl)); }
   PROF(P_OTHER);
-  return evie::k_logits_argmax(yl, nseq, c->s.V, want_logits ? c->logits : nullptr, c->best, c->next, c->stream);
+  TRY(evie::k_logits_argmax(yl, nseq, c->s.V, want_logits ? c->logits : nullptr, c->best, c->next, c->stream));
+  if (!c->samp_active) return EVIE_OK;
+  // some slot samples (or penalises repeats): every sequence's token comes from its slot's sampler
+  const evie::SampleArgs a{yl, c->s.V, c->d_segs, c->samp, c->samp_rng, c->seen, c->seen_words, nullptr, nullptr,
+                           c->next};
+  return evie::k_sample(a, nseq, c->stream);
 }
 
 evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_logits, int capture, float* logits,
@@ -848,6 +905,96 @@ void destroy(evie_ctx* c) {
   delete c;
 }
 
+// gpu/mod.rs:555-565 extended with the gates of Plan (steering.rs:97-139): ops and detectors are kept in the
+// caller's order within each layer (Plan::apply order); out-of-range ones are dropped as Plan::compile drops them.
+evie_status set_plan_impl(evie_ctx* c, int slot, const evie_plan_op* ops, int n_ops, const float* thresholds,
+                          int n_gates, const evie_detector* dets, int n_dets) {
+  auto& s = c->s;
+  EVIE_ARG(slot >= 0 && slot < c->slots, "set_plan: bad slot %d", slot);
+  EVIE_ARG(n_ops >= 0 && (n_ops == 0 || ops), "set_plan: bad op list");
+  EVIE_ARG(n_gates >= 0 && n_gates <= kMaxGates, "set_plan: at most %d gates per slot (got %d)", kMaxGates, n_gates);
+  EVIE_ARG(n_gates == 0 || thresholds, "set_plan: null thresholds");
+  EVIE_ARG(n_dets >= 0 && (n_dets == 0 || dets), "set_plan: bad detector list");
+  std::vector<evie_op> kept;
+  std::vector<int> kept_gate;
+  std::vector<int> idx;
+  for (int i = 0; i < n_ops; i++) {
+    const evie_plan_op& o = ops[i];
+    if (o.layer < 0 || o.layer >= s.L || o.neuron < 0 || o.neuron >= s.n) continue;  // as gpu/mod.rs:559
+    EVIE_ARG(o.mode >= 1 && o.mode <= 3, "set_plan: mode %d (1 add, 2 mul, 3 set)", o.mode);
+    EVIE_ARG(o.gate >= -1 && o.gate < n_gates, "set_plan: op %d names gate %d of %d", i, o.gate, n_gates);
+    idx.push_back(i);
+  }
+  std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return ops[a].layer < ops[b].layer; });
+  EVIE_ARG((int)idx.size() <= kMaxOps, "set_plan: at most %d ops per slot (got %zu)", kMaxOps, idx.size());
+  std::vector<int> range((size_t)s.L * 2, 0);
+  for (size_t i = 0; i < idx.size(); i++) {
+    const evie_plan_op& o = ops[idx[i]];
+    kept.push_back(evie_op{o.layer, o.neuron, o.mode, o.value});
+    kept_gate.push_back(o.gate);
+    if (range[o.layer * 2 + 1] == 0) range[o.layer * 2] = (int)i;
+    range[o.layer * 2 + 1]++;
+  }
+  // detectors: steering.rs:128-131 (filtered, per-layer lists in push order); gate layers: steering.rs:129-133
+  std::vector<int> didx;
+  std::vector<evie::GateSpec> gspec(n_gates, evie::GateSpec{0.f, 0, 0, 0});
+  std::vector<char> has_det(n_gates, 0);
+  for (int g = 0; g < n_gates; g++) gspec[g].threshold = thresholds[g];
+  for (int i = 0; i < n_dets; i++) {
+    const evie_detector& d = dets[i];
+    EVIE_ARG(d.gate >= 0 && d.gate < n_gates, "set_plan: detector %d names gate %d of %d", i, d.gate, n_gates);
+    if (d.layer < 0 || d.layer >= s.L || d.neuron < 0 || d.neuron >= s.n) continue;
+    didx.push_back(i);
+    evie::GateSpec& gs = gspec[d.gate];
+    gs.first_layer = has_det[d.gate] ? std::min(gs.first_layer, d.layer) : d.layer;
+    gs.last_layer = has_det[d.gate] ? std::max(gs.last_layer, d.layer) : d.layer;
+    has_det[d.gate] = 1;
+  }
+  EVIE_ARG((int)didx.size() <= kMaxDets, "set_plan: at most %d detectors per slot (got %zu)", kMaxDets, didx.size());
+  std::stable_sort(didx.begin(), didx.end(), [&](int a, int b) { return dets[a].layer < dets[b].layer; });
+  std::vector<evie::DetSpec> dk;
+  std::vector<int> drange((size_t)s.L * 2, 0);
+  for (size_t i = 0; i < didx.size(); i++) {
+    const evie_detector& d = dets[didx[i]];
+    dk.push_back(evie::DetSpec{d.gate, d.neuron, d.weight, 0});
+    if (drange[d.layer * 2 + 1] == 0) drange[d.layer * 2] = (int)i;
+    drange[d.layer * 2 + 1]++;
+  }
+  std::vector<char> layers(s.L, 0);
+  for (size_t i = 0; i < didx.size(); i++) layers[dets[didx[i]].layer] = 1;
+  for (int g = 0; g < n_gates; g++) layers[gspec[g].last_layer] = 1;
+
+  EVIE_CUDA_TRY(cudaSetDevice(c->device));
+  EVIE_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  const size_t so = (size_t)slot * kMaxOps, sg = (size_t)slot * kMaxGates, sd = (size_t)slot * kMaxDets;
+  const size_t sr = (size_t)slot * s.L * 2;
+  if (!kept.empty()) {
+    EVIE_CUDA_TRY(cudaMemcpy(c->ops + so, kept.data(), kept.size() * sizeof(evie_op), cudaMemcpyHostToDevice));
+    EVIE_CUDA_TRY(cudaMemcpy(c->op_gate + so, kept_gate.data(), kept_gate.size() * 4, cudaMemcpyHostToDevice));
+  }
+  EVIE_CUDA_TRY(cudaMemcpy(c->op_range + sr, range.data(), range.size() * 4, cudaMemcpyHostToDevice));
+  if (n_gates)
+    EVIE_CUDA_TRY(cudaMemcpy(c->gates + sg, gspec.data(), gspec.size() * sizeof(evie::GateSpec), cudaMemcpyHostToDevice));
+  if (!dk.empty())
+    EVIE_CUDA_TRY(cudaMemcpy(c->dets + sd, dk.data(), dk.size() * sizeof(evie::DetSpec), cudaMemcpyHostToDevice));
+  EVIE_CUDA_TRY(cudaMemcpy(c->det_range + sr, drange.data(), drange.size() * 4, cudaMemcpyHostToDevice));
+  EVIE_CUDA_TRY(cudaMemcpy(c->n_gates + slot, &n_gates, 4, cudaMemcpyHostToDevice));
+  EVIE_CUDA_TRY(cudaMemset(c->gate_open + sg, 0, kMaxGates * 4));  // Plan::new_state, steering.rs:145-148
+  EVIE_CUDA_TRY(cudaMemset(c->gate_score + sg, 0, kMaxGates * 4));
+  EVIE_CUDA_TRY(cudaMemset(c->gate_from + sg, 0, kMaxGates * 4));
+  c->h_n_gates[slot] = n_gates;
+  c->h_gate_layers[slot] = layers;
+  // The set of layers that launch the detector kernel is part of every captured forward graph: a change drops them.
+  std::vector<char> all(s.L, 0);
+  for (int i = 0; i < c->slots; i++)
+    for (int l = 0; l < s.L; l++) all[l] |= c->h_gate_layers[i][l];
+  if (all != c->gate_layers) {
+    for (auto& g : c->fwd_graphs) cudaGraphExecDestroy(g.second);
+    c->fwd_graphs.clear();
+    c->gate_layers = all;
+  }
+  return EVIE_OK;
+}
 // Records the thread-local message of a failed call into the context.
 evie_status remember(evie_ctx* c, evie_status rc) {
   if (rc != EVIE_OK && c) c->err = evie::thread_error();
@@ -944,37 +1091,69 @@ int evie_profile_read(const evie_ctx* c, int i, const char** name, double* ms, i
   return P_COUNT;
 }
 
-// gpu/mod.rs:555-565; ops are kept in the caller's order within each layer (Plan::apply order).
 evie_status evie_set_ops(evie_ctx* c, int slot, const evie_op* ops, int n_ops) {
   if (!c) return evie::fail(EVIE_ERR_ARG, "evie_set_ops: null context");
-  auto& s = c->s;
-  if (slot < 0 || slot >= c->slots) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_ops: bad slot %d", slot));
-  std::vector<evie_op> kept;
-  for (int i = 0; i < n_ops; i++) {
-    const evie_op& o = ops[i];
-    if (o.layer < 0 || o.layer >= s.L || o.neuron < 0 || o.neuron >= s.n) continue;  // as gpu/mod.rs:559
-    if (o.mode < 1 || o.mode > 3)
-      return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_ops: mode %d (1 add, 2 mul, 3 set)", o.mode));
-    kept.push_back(o);
-  }
-  std::stable_sort(kept.begin(), kept.end(), [](const evie_op& a, const evie_op& b) { return a.layer < b.layer; });
-  std::vector<int> range((size_t)s.L * 2, 0);
-  for (size_t i = 0; i < kept.size(); i++) {
-    int l = kept[i].layer;
-    if (range[l * 2 + 1] == 0) range[l * 2] = (int)i;
-    range[l * 2 + 1]++;
-    if (range[l * 2 + 1] > kMaxOps)
-      return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_ops: more than %d ops in layer %d", kMaxOps, l));
-  }
-  if ((int)kept.size() > kMaxOps)
-    return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_ops: at most %d ops per slot (got %zu)", kMaxOps, kept.size()));
+  if (n_ops < 0 || (n_ops > 0 && !ops)) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_ops: bad op list"));
+  std::vector<evie_plan_op> p(n_ops);
+  for (int i = 0; i < n_ops; i++) p[i] = evie_plan_op{ops[i].layer, ops[i].neuron, ops[i].mode, ops[i].value, -1};
+  return remember(c, set_plan_impl(c, slot, p.data(), n_ops, nullptr, 0, nullptr, 0));
+}
+
+evie_status evie_set_plan(evie_ctx* c, int slot, const evie_plan_op* ops, int n_ops, const float* thresholds,
+                          int n_gates, const evie_detector* dets, int n_dets) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_set_plan: null context");
+  return remember(c, set_plan_impl(c, slot, ops, n_ops, thresholds, n_gates, dets, n_dets));
+}
+
+evie_status evie_gate_state(evie_ctx* c, int slot, int32_t* open, float* score, int n_gates) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_gate_state: null context");
+  if (slot < 0 || slot >= c->slots) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_gate_state: bad slot %d", slot));
+  const int ng = c->h_n_gates[slot];
+  if (n_gates < ng)
+    return remember(c, evie::fail(EVIE_ERR_ARG, "evie_gate_state: slot %d has %d gates, room for %d", slot, ng, n_gates));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  const size_t sg = (size_t)slot * kMaxGates;
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess && open && ng) e = cudaMemcpy(open, c->gate_open + sg, ng * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && score && ng) e = cudaMemcpy(score, c->gate_score + sg, ng * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_gate_state: %s", cudaGetErrorString(e)));
+  return EVIE_OK;
+}
+
+evie_status evie_reset_gates(evie_ctx* c, int slot) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_reset_gates: null context");
+  if (slot < 0 || slot >= c->slots) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_reset_gates: bad slot %d", slot));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  const size_t sg = (size_t)slot * kMaxGates;
+  cudaError_t e = cudaMemsetAsync(c->gate_open + sg, 0, kMaxGates * 4, c->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(c->gate_score + sg, 0, kMaxGates * 4, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_reset_gates: %s", cudaGetErrorString(e)));
+  return EVIE_OK;
+}
+
+// sampling.rs:27-29 (Sampler::new) per slot; NULL = SampleParams::default (greedy).
+evie_status evie_set_sampler(evie_ctx* c, int slot, const evie_sample_params* p) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_set_sampler: null context");
+  if (slot < 0 || slot >= c->slots) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_sampler: bad slot %d", slot));
+  const evie_sample_params d{0.0f, 1.0f, 0.0f, 1.0f, 0};
+  const evie_sample_params& q = p ? *p : d;
+  const evie::SamplerParams sp{q.temperature, q.top_p, q.min_p, q.repetition_penalty};
+  const uint64_t rng = evie::sampler_seed_state(q.seed);
   if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
   cudaError_t e = cudaStreamSynchronize(c->stream);
-  if (e == cudaSuccess && !kept.empty())
-    e = cudaMemcpy(c->ops + (size_t)slot * kMaxOps, kept.data(), kept.size() * sizeof(evie_op), cudaMemcpyHostToDevice);
-  if (e == cudaSuccess)
-    e = cudaMemcpy(c->op_range + (size_t)slot * s.L * 2, range.data(), range.size() * 4, cudaMemcpyHostToDevice);
-  if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_set_ops: %s", cudaGetErrorString(e)));
+  if (e == cudaSuccess) e = cudaMemcpy(c->samp + slot, &sp, sizeof(sp), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(c->samp_rng + slot, &rng, 8, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_set_sampler: %s", cudaGetErrorString(e)));
+  // plain greedy (temperature <= 0, no penalty) is the argmax kernel's token; anything else needs the sampler
+  c->h_samp_on[slot] = !(q.temperature <= 0.0f) || q.repetition_penalty != 1.0f;
+  bool any = false;
+  for (char on : c->h_samp_on) any = any || on;
+  if (any != c->samp_active) {  // the sampler launch is part of every captured forward graph
+    for (auto& g : c->fwd_graphs) cudaGraphExecDestroy(g.second);
+    c->fwd_graphs.clear();
+    c->samp_active = any;
+  }
   return EVIE_OK;
 }
 
@@ -988,6 +1167,8 @@ evie_status evie_reset_slot(evie_ctx* c, int slot) {
   cudaSetDevice(c->device);
   cudaError_t e = cudaMemsetAsync(c->conv_state + (size_t)slot * cs, 0, cs * 4, c->stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(c->rec_state + (size_t)slot * rs, 0, rs * 4, c->stream);
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(c->seen + (size_t)slot * c->seen_words, 0, (size_t)c->seen_words * 4, c->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_reset_slot: %s", cudaGetErrorString(e)));
   return EVIE_OK;

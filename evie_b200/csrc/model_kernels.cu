@@ -3,6 +3,8 @@
 // below), in f32 with the same formulas; only summation orders differ.
 #include "model_kernels.h"
 
+#include <climits>
+
 namespace evie {
 
 namespace {
@@ -36,10 +38,14 @@ __global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowInfo*
                                                                   const __nv_bfloat16* __restrict__ embed,
                                                                   float* __restrict__ x, const float* __restrict__ gain,
                                                                   float eps, int d, __nv_bfloat16* __restrict__ X2,
-                                                                  size_t xplane) {
+                                                                  size_t xplane, uint32_t* __restrict__ seen,
+                                                                  int seen_words) {
   __shared__ float red[kNormThreads / 32];
   const int r = blockIdx.x;
-  const __nv_bfloat16* e = embed + (size_t)rows[r].token * d;
+  const RowInfo ri = rows[r];
+  if (threadIdx.x == 0 && seen)
+    atomicOr(seen + (size_t)ri.slot * seen_words + (ri.token >> 5), 1u << (ri.token & 31));
+  const __nv_bfloat16* e = embed + (size_t)ri.token * d;
   float* xr = x + (size_t)r * d;
   float ss = 0.f;
   for (int i = threadIdx.x; i < d; i += kNormThreads) {
@@ -514,6 +520,10 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(YView y, int ldy,
   }
 }
 
+// silu(g) * u with the product rounded on its own, so that the gate detectors (which recompute a few of these
+// activations) see exactly the values the SwiGLU kernel steers and captures.
+__device__ __forceinline__ float swiglu_act(float g, float u) { return __fmul_rn(siluf_(g), u); }
+
 // model.rs:249-258 with the Probe hook (worker.rs:136-141): silu(gate) * up, the slot's steering ops of this layer
 // in order (steering.rs:189-208), companded capture (worker.rs:97-112) and max |a| over positions > 0
 // (gpu/mod.rs:577-593). One CTA = one row x 1024 neurons.
@@ -542,11 +552,19 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
   const int cnt = s_cnt;
   if (threadIdx.x < cnt) {
     const int first = steer.range[((size_t)ri.slot * L + layer) * 2];
-    s_ops[threadIdx.x] = steer.ops[(size_t)ri.slot * steer.max_ops + first + threadIdx.x];
+    const size_t oi = (size_t)ri.slot * steer.max_ops + first + threadIdx.x;
+    evie_op op = steer.ops[oi];
+    const int g = steer.op_gate[oi];
+    if (g >= 0) {  // steering.rs:190-199: closed -> skip; opened in this call -> from the trigger row at/after its layer
+      const size_t gi = (size_t)ri.slot * steer.max_gates + g;
+      const bool on = steer.open[gi] && (layer < steer.gates[gi].last_layer || ri.pos >= steer.from[gi]);
+      if (!on) op.mode = 0;
+    }
+    s_ops[threadIdx.x] = op;
   }
   __syncthreads();
   if (!active) return;
-  float a[4] = {siluf_(g4.x) * u4.x, siluf_(g4.y) * u4.y, siluf_(g4.z) * u4.z, siluf_(g4.w) * u4.w};
+  float a[4] = {swiglu_act(g4.x, u4.x), swiglu_act(g4.y, u4.y), swiglu_act(g4.z, u4.z), swiglu_act(g4.w, u4.w)};
   for (int i = 0; i < cnt; i++) {  // steering.rs:189-208, in the slot's order
     const evie_op op = s_ops[i];
     const int e = op.neuron - j0;
@@ -568,8 +586,65 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
     for (int e = 0; e < 4; e++) atomicMax(maxbuf + (size_t)layer * n + j0 + e, __float_as_uint(fabsf(a[e])));
 }
 
+// steering.rs:164-187 for one segment (= one sequence and its slot's plan). Each thread owns rows: the gates whose
+// first detector layer is this one restart at 0, then the layer's detector terms are added in plan order
+// (p += w * a, each step rounded as the reference's f32 arithmetic). Then, per gate deciding here, the score is the
+// last row's sum and a closed gate latches at the first row whose sum exceeds the threshold.
+__global__ void __launch_bounds__(256) gate_detect_kernel(YView y, int ldy, const SegInfo* __restrict__ segs,
+                                                          int layer, int n, int L, GateTables t) {
+  __shared__ int s_min[8];
+  const SegInfo sg = segs[blockIdx.x];
+  const int sl = sg.slot;
+  const int ng = t.n_gates[sl];
+  if (ng == 0) return;
+  const GateSpec* gs = t.gates + (size_t)sl * t.max_gates;
+  const DetSpec* ds = t.dets + (size_t)sl * t.max_dets;
+  const int d0 = t.det_range[((size_t)sl * L + layer) * 2];
+  const int nd = t.det_range[((size_t)sl * L + layer) * 2 + 1];
+  for (int i = threadIdx.x; i < sg.count; i += blockDim.x) {
+    const int r = sg.start + i;
+    float* p = t.partial + (size_t)r * t.max_gates;
+    for (int g = 0; g < ng; g++)
+      if (gs[g].first_layer == layer) p[g] = 0.0f;
+    const size_t yr = (size_t)r * ldy;
+    for (int k = 0; k < nd; k++) {
+      const DetSpec d = ds[d0 + k];
+      const float a = swiglu_act(y.at(yr + d.neuron), y.at(yr + n + d.neuron));
+      p[d.gate] = __fadd_rn(p[d.gate], __fmul_rn(d.weight, a));
+    }
+  }
+  __syncthreads();
+  for (int g = 0; g < ng; g++) {
+    const GateSpec spec = gs[g];
+    if (spec.last_layer != layer) continue;
+    const size_t gi = (size_t)sl * t.max_gates + g;
+    const bool was_open = t.open[gi] != 0;
+    int first = INT_MAX;  // rows are visited in increasing order, so a thread's first hit is its minimum
+    if (!was_open)
+      for (int i = threadIdx.x; i < sg.count; i += blockDim.x)
+        if (t.partial[(size_t)(sg.start + i) * t.max_gates + g] > spec.threshold) {
+          first = i;
+          break;
+        }
+    first = __reduce_min_sync(0xffffffffu, first);
+    if ((threadIdx.x & 31) == 0) s_min[threadIdx.x >> 5] = first;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < (int)(blockDim.x >> 5); w++) first = min(first, s_min[w]);
+      t.score[gi] = t.partial[(size_t)(sg.start + sg.count - 1) * t.max_gates + g];
+      if (was_open) {
+        t.from[gi] = INT_MIN;
+      } else if (first != INT_MAX) {
+        t.open[gi] = 1;
+        t.from[gi] = sg.pos0 + first;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
-  uint32_t u = __float_as_uint(v);
+  uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);  // -0 and +0 tie, as the reference compares them
   u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   return ((unsigned long long)u << 32) | (0xFFFFFFFFu - i);  // larger value first, then lower index
 }
@@ -636,9 +711,9 @@ evie_status k_advance_rows(RowInfo* rows, int nseq, const uint32_t* next, cudaSt
 }
 
 evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed, float* x, const float* gain,
-                         float eps, int d, __nv_bfloat16* X2, cudaStream_t st) {
+                         float eps, int d, __nv_bfloat16* X2, uint32_t* seen, int seen_words, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
-  embed_norm_kernel<<<R, kNormThreads, 0, st>>>(rows, embed, x, gain, eps, d, X2, (size_t)R * d);
+  embed_norm_kernel<<<R, kNormThreads, 0, st>>>(rows, embed, x, gain, eps, d, X2, (size_t)R * d, seen, seen_words);
   EVIE_CHECK_LAUNCH("embed_norm_kernel");
   return EVIE_OK;
 }
@@ -742,6 +817,14 @@ evie_status k_swiglu(YView y, int ldy, int R, const RowInfo* rows, int layer, co
   swiglu_kernel<<<grid, 256, 0, st>>>(y, ldy, rows, layer, s.n, s.L, steer, scale, frames, maxbuf,
                                       X2, (size_t)R * s.n);
   EVIE_CHECK_LAUNCH("swiglu_kernel");
+  return EVIE_OK;
+}
+
+evie_status k_gate_detect(YView y, int ldy, const SegInfo* segs, int nseg, int layer, const ModelShape& s,
+                          GateTables t, cudaStream_t st) {
+  if (nseg == 0) return EVIE_OK;
+  gate_detect_kernel<<<nseg, 256, 0, st>>>(y, ldy, segs, layer, s.n, s.L, t);
+  EVIE_CHECK_LAUNCH("gate_detect_kernel");
   return EVIE_OK;
 }
 

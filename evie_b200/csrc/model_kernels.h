@@ -61,8 +61,10 @@ struct ModelShape {
   int in_at;   // rows of the fused attention input projection: (2 nh + 2 nkv) hd
 };
 
+// seen: per-slot bitmap (seen_words words per slot) of every token fed since the slot's reset, the sampler's
+// repetition history; the kernel sets each row's token bit.
 evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed, float* x, const float* gain,
-                         float eps, int d, __nv_bfloat16* X2, cudaStream_t st);
+                         float eps, int d, __nv_bfloat16* X2, uint32_t* seen, int seen_words, cudaStream_t st);
 // x += Y (two planes); optional f16 capture of x as the residual leaving `cap_layer`; then X2 = split(rmsnorm(x)).
 evie_status k_add_norm(float* x, YView y, int ldy, int R, const float* gain, float eps, int d,
                        __nv_bfloat16* X2, uint16_t* resid, int cap_layer, int L, cudaStream_t st);
@@ -90,12 +92,46 @@ template <typename KV>
 evie_status k_attn_prep(YView y, int ldy, int R, const RowInfo* rows, const float* q_norm,
                         const float* k_norm, const float* inv_freq, const ModelShape& s, float* q_rot, KV* kc,
                         KV* vc, const int* page_table, int pages_per_slot, int page_size, cudaStream_t st);
+// A latching detector gate of a slot's plan (GateSpec, steering.rs:91-95): its detectors sit in layers
+// first_layer..last_layer, it decides at last_layer (both 0 when it has no detector in range).
+struct GateSpec {
+  float threshold;
+  int first_layer, last_layer, pad;
+};
+struct DetSpec {
+  int gate, neuron;
+  float weight;
+  int pad;
+};
+// Per-slot gate state: open latches across calls; from is the first position a gate covers at or after its
+// deciding layer in the current call (INT_MIN when it was open before the call).
+struct GateTables {
+  const GateSpec* gates;   // [slots][max_gates]
+  const int* n_gates;      // [slots]
+  const DetSpec* dets;     // [slots][max_dets], each slot's detectors sorted by layer (stable)
+  const int* det_range;    // [slots][L][2] (first, count) into the slot's detectors
+  int max_gates, max_dets;
+  int* open;               // [slots][max_gates]
+  float* score;            // [slots][max_gates] detector sum on the last row of the latest call
+  int* from;               // [slots][max_gates]
+  float* partial;          // [max_rows][max_gates] running detector sums of the call's rows
+};
 // silu(gate) * up, per-slot steering ops, capture, max tracking -> X2 [R][n].
 struct SteerTables {
   const evie_op* ops;      // [slots][max_ops], each slot's ops sorted by layer (stable)
   const int* range;        // [slots][L][2] (first, count) into the slot's ops
   int max_ops;
+  const int* op_gate;      // [slots][max_ops] gate of each op, -1 = ungated
+  const GateSpec* gates;   // [slots][max_gates]
+  const int* open;         // [slots][max_gates]
+  const int* from;         // [slots][max_gates]
+  int max_gates;
 };
+// Plan::apply's detector half (steering.rs:164-187) for `layer`, before the layer's SwiGLU kernel applies the ops:
+// adds every detector term of this layer to each row's running sums, then lets the gates that decide here take
+// their score and latch open at the first row over the threshold. One CTA per segment.
+evie_status k_gate_detect(YView y, int ldy, const SegInfo* segs, int nseg, int layer, const ModelShape& s,
+                          GateTables t, cudaStream_t st);
 evie_status k_swiglu(YView y, int ldy, int R, const RowInfo* rows, int layer, const ModelShape& s,
                      SteerTables steer, const float* scale, int8_t* frames, uint32_t* maxbuf, __nv_bfloat16* X2,
                      cudaStream_t st);

@@ -1,5 +1,6 @@
 """GpuModel: Python view of the full-model C ABI, with the method set of evie-core's GPU backend
-(crates/evie-core/src/gpu/mod.rs: new, forward, set_ops, reset_slot, set_scale, track_max, read_max)."""
+(crates/evie-core/src/gpu/mod.rs: new, forward, set_ops, reset_slot, set_scale, track_max, read_max), plus the
+gated steering plans (set_plan, gate_state, reset_gates) and per-slot samplers (set_sampler) of the CPU engine."""
 from __future__ import annotations
 
 import ctypes as C
@@ -42,6 +43,7 @@ class GpuModel:
         self.info = info
         self.layers, self.neurons, self.hidden, self.vocab = info.n_layers, info.intermediate, info.hidden, info.vocab
         self.slots, self.max_ctx, self.max_rows = info.slots, info.max_ctx, info.max_rows
+        self._n_gates: dict[int, int] = {}
 
     def _check(self, rc: int):
         if rc != 0:
@@ -126,6 +128,33 @@ class GpuModel:
         for i, (l, nn, m, v) in enumerate(ops):
             arr[i] = capi.Op(l, nn, MODES.get(m, m) if isinstance(m, str) else m, v)
         self._check(lib().evie_set_ops(self._h, slot, arr, len(ops)))
+        self._n_gates[slot] = 0
+
+    def set_plan(self, slot: int, plan):
+        """A compiled steering.Plan with its detector gates; closes the slot's gates (Plan::new_state)."""
+        ops = (capi.PlanOp * max(len(plan.ops), 1))(*[capi.PlanOp(*o) for o in plan.ops])
+        th = np.ascontiguousarray(plan.thresholds, dtype=np.float32)
+        dets = (capi.Detector * max(len(plan.detectors), 1))(*[capi.Detector(*d) for d in plan.detectors])
+        self._check(lib().evie_set_plan(self._h, slot, ops, len(plan.ops), th.ctypes.data if th.size else None,
+                                        th.size, dets, len(plan.detectors)))
+        self._n_gates[slot] = th.size
+
+    def gate_state(self, slot: int) -> tuple[np.ndarray, np.ndarray]:
+        """(open [n_gates] bool, score [n_gates] f32) of the slot's gates (GateState::open / ::score)."""
+        n = self._n_gates.get(slot, 0)
+        op = np.zeros(max(n, 1), np.int32)
+        sc = np.zeros(max(n, 1), np.float32)
+        self._check(lib().evie_gate_state(self._h, slot, op.ctypes.data, sc.ctypes.data, max(n, 1)))
+        return op[:n].astype(bool), sc[:n]
+
+    def set_sampler(self, slot: int, temperature: float = 0.0, top_p: float = 1.0, min_p: float = 0.0,
+                    repetition_penalty: float = 1.0, seed: int = 0):
+        """Sampler::new(SampleParams) for the slot (sampling.rs:27-29); the defaults are greedy."""
+        sp = capi.SampleParams(temperature, top_p, min_p, repetition_penalty, seed)
+        self._check(lib().evie_set_sampler(self._h, slot, C.byref(sp)))
+
+    def reset_gates(self, slot: int):
+        self._check(lib().evie_reset_gates(self._h, slot))
 
     def reset_slot(self, slot: int):
         self._check(lib().evie_reset_slot(self._h, slot))

@@ -54,6 +54,36 @@ def gdn_prefill_tokenwise(q, k, v, g, beta, state, o=None):
     return o
 
 
+def sampler_seed_state(seed: int) -> int:
+    """Sampler::new's generator state for a seed (sampling.rs:27-29)."""
+    return int(lib().evie_sampler_seed_state(seed))
+
+
+def sample(logits, params, rng, histories):
+    """Sampler::sample (sampling.rs:41-93) for each row of logits [B,V] f32 (CUDA) with params[b] = dict(temperature,
+    top_p, min_p, repetition_penalty) and histories[b] a list of token ids. rng: list of B generator states, advanced
+    in place. Returns the B tokens (synchronous)."""
+    import ctypes as C
+
+    import numpy as np
+
+    from . import capi
+
+    B, V = logits.shape
+    ps = (capi.SampleParams * B)(*[capi.SampleParams(p.get("temperature", 0.0), p.get("top_p", 1.0),
+                                                     p.get("min_p", 0.0), p.get("repetition_penalty", 1.0), 0)
+                                   for p in params])
+    st = (C.c_uint64 * B)(*rng)
+    off = np.zeros(B + 1, np.int64)
+    off[1:] = np.cumsum([len(h) for h in histories])
+    flat = np.concatenate([np.asarray(h, np.uint32) for h in histories] + [np.zeros(1, np.uint32)])
+    hist = torch.from_numpy(flat.astype(np.int32)).to(logits.device)
+    out = np.zeros(B, np.uint32)
+    check(lib().evie_sample(_ptr(logits), B, V, ps, st, _ptr(hist), off.ctypes.data, out.ctypes.data, _stream()))
+    rng[:] = list(st)
+    return out
+
+
 def poll_device_errors() -> None:
     """Raises EvieError if a kernel gave up a bounded device-side wait since the last poll (synchronises)."""
     check(lib().evie_poll_device_errors())

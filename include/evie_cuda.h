@@ -54,6 +54,34 @@ typedef struct {
   float value;
 } evie_op;
 
+/* One op of a compiled steering plan with its gate (the Op of Plan, crates/evie-core/src/steering.rs:85-89).
+ * gate = -1 for an ungated op, else the index of the gate (0..n_gates-1) in the same evie_set_plan call. */
+typedef struct {
+  int32_t layer;
+  int32_t neuron;
+  int32_t mode;  /* 1 add, 2 mul, 3 set, as evie_op */
+  float value;
+  int32_t gate;
+} evie_plan_op;
+
+/* One detector term of a gate (Detector, steering.rs:21-27; Plan::detectors entries, steering.rs:102-103). */
+typedef struct {
+  int32_t gate;
+  int32_t layer;
+  int32_t neuron;
+  float weight;
+} evie_detector;
+
+/* Sampling parameters of one sequence (SampleParams, crates/evie-core/src/sampling.rs:5-13). temperature <= 0 is
+ * greedy; top_p 1, min_p 0 and repetition_penalty 1 switch those steps off. */
+typedef struct {
+  float temperature;
+  float top_p;
+  float min_p;
+  float repetition_penalty;
+  uint64_t seed;
+} evie_sample_params;
+
 /* Model dimensions, for sizing host buffers. */
 typedef struct {
   int32_t hidden, intermediate, n_layers, vocab;
@@ -76,15 +104,18 @@ EVIE_API evie_status evie_info(const evie_ctx* ctx, evie_model_info* out);
  *   logits       [n_seqs][vocab] f32, next-token logits of each sequence's last new token (if want_logits);
  *   frames       [rows][layers*intermediate] i8 sqrt-companded activations after steering (if capture);
  *   resid        [rows][layers*hidden] f16 bits, residual stream leaving each layer (if capture);
- *   next_tokens  [n_seqs] greedy token id = first index of the maximum logit (topk(logits, 1), sampling.rs:60).
+ *   next_tokens  [n_seqs] the token each sequence's slot sampler picks from its last row's logits: greedy = the
+ *                first index of the maximum logit (topk(logits, 1), sampling.rs:60) unless evie_set_sampler
+ *                gave the slot other parameters (Sampler::sample, sampling.rs:41-93).
  * rows are the concatenation of every sequence's new tokens, in call order. */
 EVIE_API evie_status evie_forward(evie_ctx* ctx, const evie_seq* seqs, int n_seqs, int want_logits, int capture, float* logits,
                          int8_t* frames, uint16_t* resid, uint32_t* next_tokens);
 
-/* The greedy decode loop of evie's worker (crates/evie/src/worker.rs:442-526 with temperature 0) kept on the
- * device: every sequence carries its first token (n_tokens = 1) at pos0; step i runs the model on each sequence's
- * greedy token of step i-1 at position pos0 + i, with no host round trip between steps.
- *   out_tokens  [steps][n_seqs] host, the greedy token produced by each step (may be NULL);
+/* The decode loop of evie's worker (crates/evie/src/worker.rs:442-526) kept on the device: every sequence carries
+ * its first token (n_tokens = 1) at pos0; step i runs the model on each sequence's token of step i-1 at position
+ * pos0 + i, with no host round trip between steps. Tokens come from each slot's sampler as in evie_forward: greedy
+ * unless evie_set_sampler says otherwise (the name keeps the greedy default).
+ *   out_tokens  [steps][n_seqs] host, the token produced by each step (may be NULL);
  *   frames      [steps][n_seqs][layers*intermediate] i8 host, captured activations per step (if capture);
  *   resid       [steps][n_seqs][layers*hidden] f16 bits host (if capture). */
 EVIE_API evie_status evie_decode_greedy(evie_ctx* ctx, const evie_seq* seqs, int n_seqs, int steps,
@@ -100,9 +131,37 @@ EVIE_API evie_status evie_profile(evie_ctx* ctx, int on);
  * (0 when i is out of range). */
 EVIE_API int evie_profile_read(const evie_ctx* ctx, int i, const char** name, double* ms, int64_t* launches);
 
-/* Replaces a slot's steering ops (GpuModel::set_ops, gpu/mod.rs:556). Ops apply in the given order. */
+/* Replaces a slot's steering ops (GpuModel::set_ops, gpu/mod.rs:556). Ops apply in the given order. Clears the
+ * slot's gates (as evie_set_plan with no gates). */
 EVIE_API evie_status evie_set_ops(evie_ctx* ctx, int slot, const evie_op* ops, int n_ops);
-/* Zeroes a slot's recurrent and conv state (GpuModel::reset_slot, gpu/mod.rs:568). */
+
+/* Replaces a slot's steering plan with one that may hold latching detector gates (Plan, steering.rs:97-104,
+ * compiled by Plan::compile, steering.rs:118-139; evie-core's wgpu backend has no gates). gate g opens, and stays
+ * open across calls, once on some new row the weighted sum of its detectors' activations exceeds thresholds[g]:
+ *   - detectors read the activations of their layer before that layer's ops (Plan::apply, steering.rs:163-172);
+ *     their terms are summed in f32 layer by layer, within a layer in the given order (a detector's position in
+ *     `dets` among those of its layer is its position in Plan::detectors);
+ *   - a gate decides at its last detector layer (0 when none of its detectors is in range): its score becomes the
+ *     sum on the call's last row of that sequence, and a closed gate opens at the first row over the threshold;
+ *   - a gated op applies to every row while its gate was open before the call; a gate that opened during the call
+ *     applies from the trigger row on at layers at or after its deciding layer, and from the next call on before
+ *     it (steering.rs:189-199).
+ * Ops and detectors whose layer or neuron is out of range are dropped (steering.rs:121, 128). Setting a plan
+ * closes the slot's gates and zeroes their scores (Plan::new_state, steering.rs:145-148). Limits: evie_info's
+ * max_ops ops, 32 gates and 128 detectors per slot. */
+EVIE_API evie_status evie_set_plan(evie_ctx* ctx, int slot, const evie_plan_op* ops, int n_ops, const float* thresholds,
+                                   int n_gates, const evie_detector* dets, int n_dets);
+/* Reads a slot's gate state after the calls so far (GateState::open and ::score, steering.rs:106-114): n_gates
+ * entries each (the slot's plan count; fewer is an error). Either pointer may be NULL. */
+EVIE_API evie_status evie_gate_state(evie_ctx* ctx, int slot, int32_t* open, float* score, int n_gates);
+/* Closes a slot's gates and zeroes their scores, keeping its plan (a fresh GateState for a new conversation). */
+EVIE_API evie_status evie_reset_gates(evie_ctx* ctx, int slot);
+/* Sets a slot's sampler (Sampler::new, sampling.rs:27-29): the parameters and a generator state started from
+ * params->seed; NULL restores the greedy default. The repetition penalty's history is every token fed to the slot
+ * since its last evie_reset_slot (the worker's prompt ids + generated tokens, worker.rs:241, 320). One uniform is
+ * drawn per sampled token at temperature > 0. */
+EVIE_API evie_status evie_set_sampler(evie_ctx* ctx, int slot, const evie_sample_params* params);
+/* Zeroes a slot's recurrent and conv state (GpuModel::reset_slot, gpu/mod.rs:568) and its sampler history. */
 EVIE_API evie_status evie_reset_slot(evie_ctx* ctx, int slot);
 /* Per-neuron activation scales used to normalise captured frames, layer-major (gpu/mod.rs:549). */
 EVIE_API evie_status evie_set_scale(evie_ctx* ctx, const float* scale, size_t n);
@@ -112,6 +171,17 @@ EVIE_API evie_status evie_track_max(evie_ctx* ctx, int on);
 EVIE_API evie_status evie_read_max(evie_ctx* ctx, float* out, size_t n);
 
 /* ---- isolated ops: device pointers, enqueued on `stream` (a cudaStream_t, NULL = legacy default) ---- */
+
+/* Sampler::new's generator state for a seed (sampling.rs:27-29), for evie_sample's rng array. */
+EVIE_API uint64_t evie_sampler_seed_state(uint64_t seed);
+/* Sampler::sample (sampling.rs:41-93) for B sequences; synchronous (returns after the stream has run it).
+ *   logits    [B][V] f32 device;
+ *   params    [B] host; rng [B] host generator states (evie_sampler_seed_state), advanced in place;
+ *   history   device token ids, sequence b's at history[hist_off[b] .. hist_off[b+1]) (hist_off [B+1] host);
+ *   out       [B] host tokens.
+ * V <= 1048576. */
+EVIE_API evie_status evie_sample(const float* logits, int B, int V, const evie_sample_params* params, uint64_t* rng,
+                                 const uint32_t* history, const int64_t* hist_off, uint32_t* out, void* stream);
 
 /* One Gated DeltaNet recurrent decode step over B*H heads (recur_step, crates/evie-core/src/model.rs:501-541;
  * the `deltanet` WGSL kernel, gpu/kernels.wgsl:379-442):

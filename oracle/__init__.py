@@ -86,6 +86,12 @@ def _declare(L):
         "oracle_gate_state_new": (P, []),
         "oracle_gate_state_free": (None, [P]),
         "oracle_gate_state_open": (I, [P, I]),
+        "oracle_sampler_new": (P, [F, F, F, F, C.c_uint64]),
+        "oracle_sampler_free": (None, [P]),
+        "oracle_sampler_rng": (C.c_uint64, [P]),
+        "oracle_sampler_sample": (C.c_uint32, [P, P, LG, P, LG]),
+        "oracle_gate_state_score": (F, [P, I]),
+        "oracle_gate_state_partial": (LG, [P, I, P, LG]),
         "oracle_plan_begin": (None, [P, P, LG]),
         "oracle_plan_apply": (None, [P, I, P, LG, LG, P]),
         "oracle_forward": (None, [P, P, I, P, P, I, P]),
@@ -135,6 +141,27 @@ def topk(v: np.ndarray, k: int):
 def greedy(logits: np.ndarray) -> int:
     """sampling.rs:60-62 with temperature 0: topk(logits, 1)."""
     return int(topk(logits, 1)[0][0])
+
+
+class Sampler:
+    """sampling.rs:21-93: Sampler::new(params) and Sampler::sample(logits, history)."""
+
+    def __init__(self, temperature=0.0, top_p=1.0, min_p=0.0, repetition_penalty=1.0, seed=0):
+        self._h = lib().oracle_sampler_new(temperature, top_p, min_p, repetition_penalty, seed)
+
+    def __del__(self):
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.oracle_sampler_free(self._h)
+            self._h = None
+
+    @property
+    def rng(self) -> int:
+        return int(lib().oracle_sampler_rng(self._h))
+
+    def sample(self, logits: np.ndarray, history) -> int:
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        h = np.ascontiguousarray(history, dtype=np.uint32)
+        return int(lib().oracle_sampler_sample(self._h, _p(lg), lg.size, _p(h) if h.size else None, h.size))
 
 
 def compand(v: float) -> int:
@@ -458,6 +485,17 @@ class GateState:
     def open(self, g: int) -> bool:
         return bool(lib().oracle_gate_state_open(self._h, g))
 
+    def score(self, g: int) -> float:
+        return float(lib().oracle_gate_state_score(self._h, g))
+
+    def partial(self, g: int) -> np.ndarray:
+        """Detector sums of gate g per row of the latest pass."""
+        n = lib().oracle_gate_state_partial(self._h, g, None, 0)
+        out = np.zeros(n, np.float32)
+        if n:
+            lib().oracle_gate_state_partial(self._h, g, _p(out), n)
+        return out
+
 
 MODE = {"add": 1, "mul": 2, "set": 3}
 
@@ -469,7 +507,10 @@ def compile_plan(ivs, n_layers: int, n_neurons: int, unit) -> Plan:
         if not iv.get("enabled", True) or not (iv["layer"] < n_layers and iv["neuron"] < n_neurons):
             continue
         mode = iv.get("mode", "add")
-        value = iv["value"] * unit(iv["layer"], iv["neuron"]) if mode == "add" else iv["value"]
+        if mode == "add":  # f32 value x f32 unit, as steering.rs:123 multiplies them
+            value = np.float32(iv["value"]) * np.float32(unit(iv["layer"], iv["neuron"]))
+        else:
+            value = iv["value"]
         value = float(np.float32(value))
         gi = -1
         g = iv.get("gate")

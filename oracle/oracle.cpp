@@ -14,6 +14,7 @@
 //   crates/evie-core/src/model.rs:398-479     Model::attention + rope
 //   crates/evie-core/src/model.rs:501-524     recur_body (loop order kept)
 //   crates/evie-core/src/steering.rs:150-210  Plan::begin / Plan::apply (add / mul / set, latching gates)
+//   crates/evie-core/src/sampling.rs:21-93    Sampler (splitmix64) and Sampler::sample
 //   crates/evie/src/worker.rs:97-121          Capture (sqrt-companded i8 frames, f16 residual)
 //   crates/evie-core/src/gpu/mod.rs:577-593   track_max semantics (max |a| over positions > 0)
 //
@@ -209,6 +210,84 @@ int topk(const float* v, size_t n, int k, uint32_t* idx, float* val) {
     if (val) val[i] = best[i].second;
   }
   return (int)best.size();
+}
+
+// sampling.rs:21-93: Sampler (splitmix64 uniforms) and Sampler::sample.
+struct Sampler {
+  float temperature, top_p, min_p, repetition_penalty;
+  uint64_t rng;
+};
+
+// sampling.rs:27-29
+Sampler sampler_new(float t, float top_p, float min_p, float rep, uint64_t seed) {
+  return Sampler{t, top_p, min_p, rep, (seed * 0x9E3779B97F4A7C15ull) ^ 0xD1B54A32D192ED03ull};
+}
+
+// sampling.rs:31-39
+float sampler_uniform(Sampler& s) {
+  s.rng += 0x9E3779B97F4A7C15ull;
+  uint64_t z = s.rng;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) / (float)(1ull << 24);
+}
+
+// sampling.rs:41-93
+uint32_t sampler_sample(Sampler& s, const float* logits_in, size_t n, const uint32_t* history, size_t nh) {
+  std::vector<float> adjusted;
+  const float* logits = logits_in;
+  if (s.repetition_penalty != 1.0f && nh > 0) {
+    adjusted.assign(logits_in, logits_in + n);
+    std::vector<uint32_t> seen(history, history + nh);
+    std::sort(seen.begin(), seen.end());
+    seen.erase(std::unique(seen.begin(), seen.end()), seen.end());
+    for (uint32_t t : seen)
+      if (t < n) {
+        float& v = adjusted[t];
+        v = v > 0.0f ? v / s.repetition_penalty : v * s.repetition_penalty;
+      }
+    logits = adjusted.data();
+  }
+  if (s.temperature <= 0.0f) {
+    uint32_t i = 0;
+    topk(logits, n, 1, &i, nullptr);
+    return i;
+  }
+  std::vector<uint32_t> ci(512);
+  std::vector<float> cv(512);
+  const int k = topk(logits, n, 512, ci.data(), cv.data());
+  const float top = cv[0];
+  std::vector<std::pair<uint32_t, float>> probs(k);
+  for (int j = 0; j < k; j++) probs[j] = {ci[j], expf((cv[j] - top) / s.temperature)};
+  float total = 0.0f;
+  for (auto& x : probs) total += x.second;
+  for (auto& x : probs) x.second /= total;
+  if (s.min_p > 0.0f) {
+    const float floor = probs[0].second * s.min_p;
+    std::vector<std::pair<uint32_t, float>> kept;
+    for (auto& x : probs)
+      if (x.second >= floor) kept.push_back(x);
+    probs.swap(kept);
+  }
+  if (s.top_p < 1.0f) {
+    float acc = 0.0f;
+    size_t keep = 0;
+    for (auto& x : probs) {
+      acc += x.second;
+      keep++;
+      if (acc >= s.top_p) break;
+    }
+    if (probs.size() > std::max<size_t>(keep, 1)) probs.resize(std::max<size_t>(keep, 1));
+  }
+  float total2 = 0.0f;
+  for (auto& x : probs) total2 += x.second;
+  float r = sampler_uniform(s) * total2;
+  for (auto& x : probs) {
+    r -= x.second;
+    if (r <= 0.0f) return x.first;
+  }
+  return probs.empty() ? ci[0] : probs.back().first;
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -828,6 +907,14 @@ EXPORT int oracle_threads() { return n_threads(); }
 EXPORT void oracle_matmul(const uint16_t* w, long rows, long cols, const float* x, long n, float* y) {
   matmul(w, rows, cols, x, n, y);
 }
+EXPORT void* oracle_sampler_new(float t, float top_p, float min_p, float rep, uint64_t seed) {
+  return new Sampler(sampler_new(t, top_p, min_p, rep, seed));
+}
+EXPORT void oracle_sampler_free(void* s) { delete (Sampler*)s; }
+EXPORT uint64_t oracle_sampler_rng(void* s) { return ((Sampler*)s)->rng; }
+EXPORT uint32_t oracle_sampler_sample(void* s, const float* logits, long n, const uint32_t* history, long nh) {
+  return sampler_sample(*(Sampler*)s, logits, (size_t)n, history, (size_t)nh);
+}
 EXPORT int oracle_topk(const float* v, long n, int k, uint32_t* idx, float* val) { return topk(v, n, k, idx, val); }
 EXPORT void oracle_softmax(float* x, long n) { softmax_inplace(x, n); }
 EXPORT float oracle_dot(const float* a, const float* b, long n) { return dot(a, b, n); }
@@ -1026,6 +1113,18 @@ EXPORT void oracle_gate_state_free(void* s) { delete (GateState*)s; }
 EXPORT int oracle_gate_state_open(void* s, int g) {
   GateState* st = (GateState*)s;
   return g < (int)st->open.size() ? st->open[g] : 0;
+}
+EXPORT float oracle_gate_state_score(void* s, int g) {
+  GateState* st = (GateState*)s;
+  return g < (int)st->score.size() ? st->score[g] : 0.0f;
+}
+// The running detector sums of gate g over the rows of the latest pass (GateState::partial, steering.rs:112).
+EXPORT long oracle_gate_state_partial(void* s, int g, float* dst, long cap) {
+  GateState* st = (GateState*)s;
+  if (g >= (int)st->partial.size()) return 0;
+  long n = (long)st->partial[g].size();
+  if (dst && cap >= n) memcpy(dst, st->partial[g].data(), sizeof(float) * n);
+  return n;
 }
 // Runs Plan::begin + Plan::apply on a plain activation block (steering.rs unit tests).
 EXPORT void oracle_plan_begin(void* p, void* s, long rows) { plan_begin(*(Plan*)p, *(GateState*)s, rows); }
