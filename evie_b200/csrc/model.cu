@@ -156,6 +156,10 @@ const char* const kProfNames[P_COUNT] = {"projection_gemm", "lm_head_gemm", "con
 struct evie_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
+  // Capture read-back: per-layer copies of frames and residual rows to page-locked host buffers run on cstream,
+  // forked from the compute stream after each layer and joined at the end of the call (cap_ev: one per layer + 1).
+  cudaStream_t cstream = nullptr;
+  std::vector<cudaEvent_t> cap_ev;
   cublasHandle_t blas = nullptr;
   void* blas_ws = nullptr;
   evie::ModelShape s{};
@@ -211,7 +215,10 @@ struct evie_ctx {
   bool attn_rowwise = false;  // EVIE_ATTN_ROWWISE=1 at creation: prefill rows use the per-row split-KV kernel too
   bool no_graph = false;      // EVIE_NO_GRAPH=1 at creation: decode-shaped calls run eagerly
   // Captured decode-shaped forward calls, keyed by (sequences, want logits, head, capture, tracking, context bound).
-  std::map<std::tuple<int, int, int, int, int, int>, cudaGraphExec_t> fwd_graphs;
+  // The host capture destinations are part of the key: their copies are nodes of the graph.
+  std::map<std::tuple<int, int, int, int, int, int, uintptr_t, uintptr_t>, cudaGraphExec_t> fwd_graphs;
+  // Captured decode-loop steps, keyed by (sequences, capture, tracking, context bound).
+  std::map<std::tuple<int, int, int, int>, cudaGraphExec_t> dec_graphs;
   float* act = nullptr;
   float* q_rot = nullptr;
   int8_t* frames = nullptr;
@@ -529,6 +536,8 @@ evie_status allocate_state(evie_ctx* c) {
     EVIE_CUDA_TRY(cudaMemcpy(c->samp_rng, rng.data(), S * 8, cudaMemcpyHostToDevice));
   }
   c->h_samp_on.assign(S, 0);
+  c->cap_ev.assign(s.L + 1, nullptr);
+  for (auto& e : c->cap_ev) EVIE_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   c->h_gate_layers.assign(S, std::vector<char>(s.L, 0));
   c->gate_layers.assign(s.L, 0);
   TRY(c->alloc(&c->scale, (size_t)s.L * s.n, false));
@@ -638,7 +647,28 @@ evie_status prepare_rows(evie_ctx* c, const evie_seq* seqs, int nseq, int* R_out
 }
 
 // model.rs:230-267: embedding, every layer, and the final norm of each sequence's last row (into X2).
-evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int capture) {
+// Page-locked host destinations of a call's captures ([R][L][n] i8 frames, [R][L][d] f16 residual rows).
+struct CapHost {
+  int8_t* frames;
+  uint16_t* resid;
+};
+
+// True when [p, p + bytes) lies in page-locked (pinned or registered) host memory, so copies into it can run
+// asynchronously on a second stream.
+bool page_locked(const void* p, size_t bytes) {
+  if (!p || !bytes) return false;
+  for (const char* q : {(const char*)p, (const char*)p + bytes - 1}) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (a.type != cudaMemoryTypeHost) return false;
+  }
+  return true;
+}
+
+evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int capture, const CapHost* ch = nullptr) {
   auto& s = c->s;
   cudaStream_t st = c->stream;
   int8_t* fr = capture ? c->frames : nullptr;
@@ -732,14 +762,34 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
                          c->X2, st));
     }
     { PROF(P_GEMM); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2, &yd, residual_ksplit(c, s.n))); }
-    PROF(P_NORM);
-    if (li + 1 < s.L) {
-      TRY(evie::k_add_norm(c->x, yd, s.d, R, c->layers[li + 1].ln1, s.eps, s.d, c->X2, rs, li, s.L, st));
-    } else {
-      TRY(evie::k_add_final(c->x, yd, s.d, R, c->d_rows, c->d_segs, nseq, c->final_norm, s.eps, s.d, c->X2, rs,
-                            li, s.L, st));
+    {
+      PROF(P_NORM);
+      if (li + 1 < s.L) {
+        TRY(evie::k_add_norm(c->x, yd, s.d, R, c->layers[li + 1].ln1, s.eps, s.d, c->X2, rs, li, s.L, st));
+      } else {
+        TRY(evie::k_add_final(c->x, yd, s.d, R, c->d_rows, c->d_segs, nseq, c->final_norm, s.eps, s.d, c->X2, rs,
+                              li, s.L, st));
+      }
+    }
+    if (ch) {  // this layer's frames and residual rows are final: copy them out while later layers run
+      EVIE_CUDA_TRY(cudaEventRecord(c->cap_ev[li], st));
+      EVIE_CUDA_TRY(cudaStreamWaitEvent(c->cstream, c->cap_ev[li], 0));
+      if (ch->frames)
+        EVIE_CUDA_TRY(cudaMemcpy2DAsync(ch->frames + (size_t)li * s.n, (size_t)s.L * s.n, c->frames + (size_t)li * s.n,
+                                        (size_t)s.L * s.n, s.n, R, cudaMemcpyDeviceToHost, c->cstream));
+      if (ch->resid)
+        EVIE_CUDA_TRY(cudaMemcpy2DAsync(ch->resid + (size_t)li * s.d, (size_t)s.L * s.d * 2,
+                                        c->resid + (size_t)li * s.d, (size_t)s.L * s.d * 2, (size_t)s.d * 2, R,
+                                        cudaMemcpyDeviceToHost, c->cstream));
     }
   }
+  return EVIE_OK;
+}
+
+// Joins the capture copy stream back into the compute stream (after the head, which overlaps the last copies).
+evie_status join_captures(evie_ctx* c) {
+  EVIE_CUDA_TRY(cudaEventRecord(c->cap_ev[c->s.L], c->cstream));
+  EVIE_CUDA_TRY(cudaStreamWaitEvent(c->stream, c->cap_ev[c->s.L], 0));
   return EVIE_OK;
 }
 
@@ -763,19 +813,34 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
   TRY(prepare_rows(c, seqs, nseq, &R, &max_ctx_rows, false));
   cudaStream_t st = c->stream;
   const bool head = want_logits || next_tokens;
+  // Captures into page-locked host buffers are copied layer by layer on the copy stream while later layers run;
+  // other destinations get one copy at the end.
+  CapHost chv{nullptr, nullptr};
+  if (capture && !c->prof) {
+    if (frames && page_locked(frames, (size_t)R * s.L * s.n)) chv.frames = frames;
+    if (resid && page_locked(resid, (size_t)R * s.L * s.d * 2)) chv.resid = resid;
+  }
+  const CapHost* ch = (chv.frames || chv.resid) ? &chv : nullptr;
   if (R == nseq && !c->prof && !c->no_graph) {
     // Decode-shaped call (one token per sequence): replay a captured graph of (row-table upload, layers, head).
     // The tables are copied from the same pinned host arrays each replay; the attention's split count uses a
     // context bound rounded up to a multiple of 2048, so a graph serves every call until the context passes it.
     const int bound = std::min(c->max_ctx, (max_ctx_rows + 2047) / 2048 * 2048);
-    const auto key = std::make_tuple(nseq, want_logits != 0, (int)head, capture != 0, (int)c->track, bound);
+    const auto key = std::make_tuple(nseq, want_logits != 0, (int)head, capture != 0, (int)c->track, bound,
+                                     (uintptr_t)chv.frames, (uintptr_t)chv.resid);
     auto it = c->fwd_graphs.find(key);
     if (it == c->fwd_graphs.end()) {
+      if (c->fwd_graphs.size() >= 32) {  // callers that rotate capture buffers: start over rather than grow
+        EVIE_CUDA_TRY(cudaStreamSynchronize(st));
+        for (auto& g : c->fwd_graphs) cudaGraphExecDestroy(g.second);
+        c->fwd_graphs.clear();
+      }
       cudaGraph_t g = nullptr;
       EVIE_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
       evie_status rc = upload_rows(c, R, nseq);
-      if (rc == EVIE_OK) rc = enqueue_layers(c, R, nseq, bound, capture);
+      if (rc == EVIE_OK) rc = enqueue_layers(c, R, nseq, bound, capture, ch);
       if (rc == EVIE_OK && head) rc = enqueue_head(c, nseq, want_logits != 0);
+      if (rc == EVIE_OK && ch) rc = join_captures(c);
       const cudaError_t ce = cudaStreamEndCapture(st, &g);
       if (rc != EVIE_OK) {
         if (g) cudaGraphDestroy(g);
@@ -791,15 +856,16 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
     EVIE_CUDA_TRY(cudaGraphLaunch(it->second, st));
   } else {
     TRY(upload_rows(c, R, nseq));
-    TRY(enqueue_layers(c, R, nseq, max_ctx_rows, capture));
+    TRY(enqueue_layers(c, R, nseq, max_ctx_rows, capture, ch));
     if (head) TRY(enqueue_head(c, nseq, want_logits != 0));
+    if (ch) TRY(join_captures(c));
   }
   if (want_logits && logits)
     EVIE_CUDA_TRY(cudaMemcpyAsync(logits, c->logits, (size_t)nseq * s.V * 4, cudaMemcpyDeviceToHost, st));
   if (next_tokens) EVIE_CUDA_TRY(cudaMemcpyAsync(next_tokens, c->next, nseq * 4, cudaMemcpyDeviceToHost, st));
-  if (capture && frames)
+  if (capture && frames && !chv.frames)
     EVIE_CUDA_TRY(cudaMemcpyAsync(frames, c->frames, (size_t)R * s.L * s.n, cudaMemcpyDeviceToHost, st));
-  if (capture && resid)
+  if (capture && resid && !chv.resid)
     EVIE_CUDA_TRY(cudaMemcpyAsync(resid, c->resid, (size_t)R * s.L * s.d * 2, cudaMemcpyDeviceToHost, st));
   EVIE_CUDA_TRY(cudaStreamSynchronize(st));
   prof_resolve(c);
@@ -833,44 +899,51 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
     c->hist_cap = need;
   }
   cudaStream_t st = c->stream;
-  // Steps after the first replay one captured CUDA graph of (advance rows, layers, head): every per-step input is
-  // already on the device, and the attention's split count uses a context bound valid for all steps. The profiling
-  // mode (events around kernel groups) runs the steps eagerly, as does a context created with EVIE_NO_GRAPH=1.
-  const bool use_graph = !c->prof && steps > 1 && !c->no_graph;
-  const int ctx_bound = max_ctx_rows + steps - 1;
+  // Every step is (layers, head, advance rows): the advance moves each sequence to its next position and token, so
+  // all steps, the first included, are the same work on device-resident inputs. They replay one captured CUDA
+  // graph, cached across calls like the forward graphs (key: sequences, capture, tracking, and a context bound
+  // that covers every step, rounded up to a multiple of 2048, from which the attention takes its split count).
+  // The profiling mode (events around kernel groups) runs the steps eagerly, as does a context created with
+  // EVIE_NO_GRAPH=1.
+  const bool use_graph = !c->prof && !c->no_graph;
+  const int bound = std::min(c->max_ctx, (max_ctx_rows + steps - 1 + 2047) / 2048 * 2048);
   cudaGraphExec_t exec = nullptr;
-  struct ExecGuard {
-    cudaGraphExec_t* e;
-    ~ExecGuard() {
-      if (*e) cudaGraphExecDestroy(*e);
-    }
-  } guard{&exec};
-  for (int i = 0; i < steps; i++) {
-    if (use_graph && i > 0) {
-      if (!exec) {
-        cudaGraph_t g = nullptr;
-        EVIE_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-        evie_status rc = evie::k_advance_rows(c->d_rows, nseq, c->next, st);
-        if (rc == EVIE_OK) rc = enqueue_layers(c, R, nseq, ctx_bound, capture);
-        if (rc == EVIE_OK) rc = enqueue_head(c, nseq, false);
-        const cudaError_t ce = cudaStreamEndCapture(st, &g);
-        if (rc != EVIE_OK) {
-          if (g) cudaGraphDestroy(g);
-          return rc;
-        }
-        EVIE_CUDA_TRY(ce);
-        const cudaError_t ie = cudaGraphInstantiate(&exec, g, 0);
-        cudaGraphDestroy(g);
-        EVIE_CUDA_TRY(ie);
+  if (use_graph) {
+    const auto key = std::make_tuple(nseq, capture != 0, (int)c->track, bound);
+    auto it = c->dec_graphs.find(key);
+    if (it == c->dec_graphs.end()) {
+      if (c->dec_graphs.size() >= 32) {
+        EVIE_CUDA_TRY(cudaStreamSynchronize(st));
+        for (auto& g : c->dec_graphs) cudaGraphExecDestroy(g.second);
+        c->dec_graphs.clear();
       }
+      cudaGraph_t g = nullptr;
+      EVIE_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      evie_status rc = enqueue_layers(c, R, nseq, bound, capture);
+      if (rc == EVIE_OK) rc = enqueue_head(c, nseq, false);
+      if (rc == EVIE_OK) rc = evie::k_advance_rows(c->d_rows, nseq, c->next, st);
+      const cudaError_t ce = cudaStreamEndCapture(st, &g);
+      if (rc != EVIE_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      EVIE_CUDA_TRY(ce);
+      cudaGraphExec_t e = nullptr;
+      const cudaError_t ie = cudaGraphInstantiate(&e, g, 0);
+      cudaGraphDestroy(g);
+      EVIE_CUDA_TRY(ie);
+      it = c->dec_graphs.emplace(key, e).first;
+    }
+    exec = it->second;
+  }
+  for (int i = 0; i < steps; i++) {
+    if (exec) {
       EVIE_CUDA_TRY(cudaGraphLaunch(exec, st));
     } else {
-      if (i > 0) {
-        PROF(P_OTHER);
-        TRY(evie::k_advance_rows(c->d_rows, nseq, c->next, st));
-      }
-      TRY(enqueue_layers(c, R, nseq, use_graph ? ctx_bound : max_ctx_rows + i, capture));
+      TRY(enqueue_layers(c, R, nseq, max_ctx_rows + i, capture));
       TRY(enqueue_head(c, nseq, false));
+      PROF(P_OTHER);
+      TRY(evie::k_advance_rows(c->d_rows, nseq, c->next, st));
     }
     EVIE_CUDA_TRY(cudaMemcpyAsync(c->hist + (size_t)i * nseq, c->next, nseq * 4, cudaMemcpyDeviceToDevice, st));
     if (capture && frames)
@@ -891,6 +964,7 @@ void destroy(evie_ctx* c) {
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   for (auto& g : c->fwd_graphs) cudaGraphExecDestroy(g.second);
+  for (auto& g : c->dec_graphs) cudaGraphExecDestroy(g.second);
   for (void* p : c->allocs) cudaFree(p);
   if (c->hist) cudaFree(c->hist);
   for (auto& p : c->prof_pending) {
@@ -901,8 +975,18 @@ void destroy(evie_ctx* c) {
   if (c->h_rows) cudaFreeHost(c->h_rows);
   if (c->h_segs) cudaFreeHost(c->h_segs);
   if (c->blas) cublasDestroy(c->blas);
+  for (auto e : c->cap_ev) cudaEventDestroy(e);
+  if (c->cstream) cudaStreamDestroy(c->cstream);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
+}
+
+// Destroys every cached graph (the caller has synchronised the stream): their launch sets no longer match.
+void drop_graphs(evie_ctx* c) {
+  for (auto& g : c->fwd_graphs) cudaGraphExecDestroy(g.second);
+  for (auto& g : c->dec_graphs) cudaGraphExecDestroy(g.second);
+  c->fwd_graphs.clear();
+  c->dec_graphs.clear();
 }
 
 // gpu/mod.rs:555-565 extended with the gates of Plan (steering.rs:97-139): ops and detectors are kept in the
@@ -989,8 +1073,7 @@ evie_status set_plan_impl(evie_ctx* c, int slot, const evie_plan_op* ops, int n_
   for (int i = 0; i < c->slots; i++)
     for (int l = 0; l < s.L; l++) all[l] |= c->h_gate_layers[i][l];
   if (all != c->gate_layers) {
-    for (auto& g : c->fwd_graphs) cudaGraphExecDestroy(g.second);
-    c->fwd_graphs.clear();
+    drop_graphs(c);
     c->gate_layers = all;
   }
   return EVIE_OK;
@@ -1027,6 +1110,7 @@ evie_status evie_create(const char* ckpt_dir, int device, int slots, int max_ctx
   do {
     if (cudaSetDevice(device) != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "cudaSetDevice(%d) failed", device); break; }
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "stream creation failed"); break; }
+    if (cudaStreamCreateWithFlags(&c->cstream, cudaStreamNonBlocking) != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "stream creation failed"); break; }
     if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) { rc = evie::fail(EVIE_ERR_CUDA, "cublasCreate failed"); break; }
     cublasSetStream(c->blas, c->stream);
     cublasSetMathMode(c->blas, CUBLAS_DEFAULT_MATH);
@@ -1149,9 +1233,8 @@ evie_status evie_set_sampler(evie_ctx* c, int slot, const evie_sample_params* p)
   c->h_samp_on[slot] = !(q.temperature <= 0.0f) || q.repetition_penalty != 1.0f;
   bool any = false;
   for (char on : c->h_samp_on) any = any || on;
-  if (any != c->samp_active) {  // the sampler launch is part of every captured forward graph
-    for (auto& g : c->fwd_graphs) cudaGraphExecDestroy(g.second);
-    c->fwd_graphs.clear();
+  if (any != c->samp_active) {  // the sampler launch is part of every captured graph
+    drop_graphs(c);
     c->samp_active = any;
   }
   return EVIE_OK;

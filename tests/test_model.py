@@ -231,3 +231,41 @@ def test_flash_prefill_matches_rowwise_attention(group4_ckpt, cuda):
     assert np.abs(la - ra).max() < 1e-3, np.abs(la - ra).max()
     assert np.abs(lb - rb).max() < 1e-3, np.abs(lb - rb).max()
     assert np.array_equal(ta, rta) and np.array_equal(tb, rtb)
+
+
+@pytest.mark.gpu
+def test_pinned_capture_matches_pageable(tiny_ckpt, cuda):
+    """Captures into page-locked host buffers are copied layer by layer on a second stream while later layers run
+    (eager multi-row calls and graph-replayed decode calls); they equal the single end-of-call copy into pageable
+    buffers of the same calls."""
+    import torch
+
+    from evie_b200.gpu import GpuOut, GpuSeq
+
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, 2048, n).astype(np.uint32) for n in (9, 14)]
+    got = []
+    for pinned in (True, False):
+        m = _gpu_model(tiny_ckpt, False, max_ctx=128, slots=2, max_rows=64)
+        m.set_ops(0, [(1, 4, "add", 0.5)])
+        L, n, d = m.layers, m.neurons, m.hidden
+        runs = []
+        calls = [[GpuSeq(i, 0, p) for i, p in enumerate(prompts)]]
+        out = None
+        for step in range(4):
+            if step > 0:
+                calls.append([GpuSeq(i, len(p) + step - 1, out.next_tokens[i:i + 1].copy())
+                              for i, p in enumerate(prompts)])
+            rows = sum(len(q.tokens) for q in calls[-1])
+            if pinned:
+                fr = torch.empty((rows, L * n), dtype=torch.int8).pin_memory().numpy()
+                rs = torch.empty((rows, L * d), dtype=torch.float16).pin_memory().numpy()
+            else:
+                fr = np.empty((rows, L * n), np.int8)
+                rs = np.empty((rows, L * d), np.float16)
+            out = m.forward(calls[-1], capture=True, out=GpuOut(frames=fr, resid=rs))
+            runs.append((out.frames.copy(), out.resid.copy(), out.logits.copy()))
+        got.append(runs)
+        m.close()
+    for (fa, ra, la), (fb, rb, lb) in zip(*got):
+        assert np.array_equal(fa, fb) and np.array_equal(ra, rb) and np.array_equal(la, lb)
