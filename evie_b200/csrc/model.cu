@@ -222,6 +222,8 @@ struct evie_ctx {
   float* act = nullptr;
   float* q_rot = nullptr;
   int8_t* frames = nullptr;
+  int cap_rows = 0;             // rows the last capturing call left in `frames`
+  int32_t* topk = nullptr;      // [max_rows][100] scratch of evie_read_top_active
   uint16_t* resid = nullptr;
   float* L2 = nullptr;
   float* logits = nullptr;
@@ -558,6 +560,7 @@ evie_status allocate_state(evie_ctx* c) {
   TRY(c->alloc(&c->act, R * s.conv_dim));
   TRY(c->alloc(&c->q_rot, R * s.nh * s.hd));
   TRY(c->alloc(&c->frames, R * s.L * (size_t)s.n, false));
+  TRY(c->alloc(&c->topk, R * 100, false));
   TRY(c->alloc(&c->resid, R * s.L * (size_t)s.d, false));
   TRY(c->alloc(&c->L2, 2 * S * (size_t)s.V, false));
   TRY(c->alloc(&c->logits, S * (size_t)s.V, false));
@@ -869,6 +872,7 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
     EVIE_CUDA_TRY(cudaMemcpyAsync(resid, c->resid, (size_t)R * s.L * s.d * 2, cudaMemcpyDeviceToHost, st));
   EVIE_CUDA_TRY(cudaStreamSynchronize(st));
   prof_resolve(c);
+  if (capture) c->cap_rows = R;
   return EVIE_OK;
 }
 
@@ -956,6 +960,7 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
   if (out_tokens) EVIE_CUDA_TRY(cudaMemcpyAsync(out_tokens, c->hist, need * 4, cudaMemcpyDeviceToHost, st));
   EVIE_CUDA_TRY(cudaStreamSynchronize(st));
   prof_resolve(c);
+  if (capture) c->cap_rows = nseq;
   return EVIE_OK;
 }
 
@@ -1213,6 +1218,23 @@ evie_status evie_reset_gates(evie_ctx* c, int slot) {
   if (e == cudaSuccess) e = cudaMemsetAsync(c->gate_score + sg, 0, kMaxGates * 4, c->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_reset_gates: %s", cudaGetErrorString(e)));
+  return EVIE_OK;
+}
+
+// mcp.rs:242-256 over the frames the last capturing call left on the device.
+evie_status evie_read_top_active(evie_ctx* c, int k, int32_t* out, int* rows) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_read_top_active: null context");
+  if (k < 1 || k > 100) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_read_top_active: k must be in 1..100"));
+  if (c->cap_rows == 0) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_read_top_active: no captured rows yet"));
+  if (!out) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_read_top_active: null output"));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  const long long width = (long long)c->s.L * c->s.n;
+  evie_status rc = evie::k_top_active(c->frames, c->cap_rows, width, k, c->topk, c->stream);
+  if (rc != EVIE_OK) return remember(c, rc);
+  cudaError_t e = cudaMemcpyAsync(out, c->topk, (size_t)c->cap_rows * k * 4, cudaMemcpyDeviceToHost, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "evie_read_top_active: %s", cudaGetErrorString(e)));
+  if (rows) *rows = c->cap_rows;
   return EVIE_OK;
 }
 

@@ -135,6 +135,8 @@ evie_status k_gate_detect(YView y, int ldy, const SegInfo* segs, int nseg, int l
 evie_status k_swiglu(YView y, int ldy, int R, const RowInfo* rows, int layer, const ModelShape& s,
                      SteerTables steer, const float* scale, int8_t* frames, uint32_t* maxbuf, __nv_bfloat16* X2,
                      cudaStream_t st);
+// top_active (mcp.rs:242-256) per frame row: the k largest |q|, equal |q| by increasing index -> out [rows][k].
+evie_status k_top_active(const int8_t* frames, int rows, long long width, int k, int32_t* out, cudaStream_t st);
 // logits = two planes summed (optional copy out), greedy argmax (first index of the maximum).
 evie_status k_logits_argmax(YView L2, int nseg, int V, float* logits, unsigned long long* best,
                             uint32_t* next_tokens, cudaStream_t st);

@@ -153,6 +153,14 @@ class GpuModel:
         sp = capi.SampleParams(temperature, top_p, min_p, repetition_penalty, seed)
         self._check(lib().evie_set_sampler(self._h, slot, C.byref(sp)))
 
+    def top_active(self, k: int = 20) -> np.ndarray:
+        """[rows, k] flat neuron indices (layer * neurons + neuron) of the k largest |frame| entries of every row the
+        last capturing call left on the device, as evie's top_active tool ranks them (equal |q|: lower index)."""
+        out = np.empty((max(self.max_rows, 1), k), np.int32)
+        rows = C.c_int()
+        self._check(lib().evie_read_top_active(self._h, k, out.ctypes.data, C.byref(rows)))
+        return out[:rows.value].copy()
+
     def reset_gates(self, slot: int):
         self._check(lib().evie_reset_gates(self._h, slot))
 

@@ -84,6 +84,16 @@ def sample(logits, params, rng, histories):
     return out
 
 
+def top_active(frames, k: int, out=None):
+    """evie's top_active (mcp.rs:242-256) for every row of frames [rows, width] int8 (CUDA): [rows, k] int32 flat
+    indices, by |q| descending, equal |q| by increasing index."""
+    rows, width = frames.shape
+    if out is None:
+        out = torch.empty(rows, k, device=frames.device, dtype=torch.int32)
+    check(lib().evie_top_active(_ptr(frames), rows, width, k, _ptr(out), _stream()))
+    return out
+
+
 def poll_device_errors() -> None:
     """Raises EvieError if a kernel gave up a bounded device-side wait since the last poll (synchronises)."""
     check(lib().evie_poll_device_errors())

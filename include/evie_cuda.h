@@ -169,8 +169,18 @@ EVIE_API evie_status evie_set_scale(evie_ctx* ctx, const float* scale, size_t n)
 EVIE_API evie_status evie_track_max(evie_ctx* ctx, int on);
 /* Reads the tracked maxima, layer-major (gpu/mod.rs:590). */
 EVIE_API evie_status evie_read_max(evie_ctx* ctx, float* out, size_t n);
+/* The k (1..100) most active neurons of every row the last capturing call left on the device (the rows of the last
+ * evie_forward with capture, or of the last step of evie_decode_greedy with capture), as evie's top_active tool
+ * ranks one token's frame (crates/evie/src/mcp.rs:242-256): by |q| of the i8 frame, largest first, equal |q| in
+ * increasing flat index (layer * intermediate + neuron). out: [rows][k] host; *rows receives the row count. */
+EVIE_API evie_status evie_read_top_active(evie_ctx* ctx, int k, int32_t* out, int* rows);
 
 /* ---- isolated ops: device pointers, enqueued on `stream` (a cudaStream_t, NULL = legacy default) ---- */
+
+/* top_active (mcp.rs:242-256) over `rows` device frames of `width` i8 entries: out [rows][k] device int32 flat
+ * indices, by |q| descending, equal |q| in increasing index. 1 <= k <= 100 (k > width leaves the tail unwritten). */
+EVIE_API evie_status evie_top_active(const int8_t* frames, int rows, long long width, int k, int32_t* out,
+                                     void* stream);
 
 /* Sampler::new's generator state for a seed (sampling.rs:27-29), for evie_sample's rng array. */
 EVIE_API uint64_t evie_sampler_seed_state(uint64_t seed);

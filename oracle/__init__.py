@@ -86,6 +86,7 @@ def _declare(L):
         "oracle_gate_state_new": (P, []),
         "oracle_gate_state_free": (None, [P]),
         "oracle_gate_state_open": (I, [P, I]),
+        "oracle_top_active": (I, [P, LG, I, P]),
         "oracle_sampler_new": (P, [F, F, F, F, C.c_uint64]),
         "oracle_sampler_free": (None, [P]),
         "oracle_sampler_rng": (C.c_uint64, [P]),
@@ -162,6 +163,14 @@ class Sampler:
         lg = np.ascontiguousarray(logits, dtype=np.float32)
         h = np.ascontiguousarray(history, dtype=np.uint32)
         return int(lib().oracle_sampler_sample(self._h, _p(lg), lg.size, _p(h) if h.size else None, h.size))
+
+
+def top_active(frame: np.ndarray, k: int) -> np.ndarray:
+    """mcp.rs:242-256: flat indices of the k largest |q| of one i8 frame, equal |q| by lower index."""
+    f = np.ascontiguousarray(frame, dtype=np.int8)
+    out = np.zeros(max(k, 1), np.int32)
+    n = lib().oracle_top_active(_p(f), f.size, k, _p(out))
+    return out[:n].copy()
 
 
 def compand(v: float) -> int:

@@ -15,6 +15,7 @@
 //   crates/evie-core/src/model.rs:501-524     recur_body (loop order kept)
 //   crates/evie-core/src/steering.rs:150-210  Plan::begin / Plan::apply (add / mul / set, latching gates)
 //   crates/evie-core/src/sampling.rs:21-93    Sampler (splitmix64) and Sampler::sample
+//   crates/evie/src/mcp.rs:242-256            top_active (ties: lower flat index first)
 //   crates/evie/src/worker.rs:97-121          Capture (sqrt-companded i8 frames, f16 residual)
 //   crates/evie-core/src/gpu/mod.rs:577-593   track_max semantics (max |a| over positions > 0)
 //
@@ -914,6 +915,19 @@ EXPORT void oracle_sampler_free(void* s) { delete (Sampler*)s; }
 EXPORT uint64_t oracle_sampler_rng(void* s) { return ((Sampler*)s)->rng; }
 EXPORT uint32_t oracle_sampler_sample(void* s, const float* logits, long n, const uint32_t* history, long nh) {
   return sampler_sample(*(Sampler*)s, logits, (size_t)n, history, (size_t)nh);
+}
+// crates/evie/src/mcp.rs:242-256 (top_active): the k entries of one frame with the largest |q|, largest first; the
+// reference leaves the order of equal |q| undefined (select_nth_unstable_by), here it is the lower flat index first.
+EXPORT int oracle_top_active(const int8_t* f, long n, int k, int32_t* out) {
+  if (k > n) k = (int)n;
+  std::vector<int32_t> idx(n);
+  for (long i = 0; i < n; i++) idx[i] = (int32_t)i;
+  auto mag = [&](int32_t i) { return f[i] < 0 ? -(int)f[i] : (int)f[i]; };
+  std::partial_sort(idx.begin(), idx.begin() + k, idx.end(), [&](int32_t a, int32_t b) {
+    return mag(a) != mag(b) ? mag(a) > mag(b) : a < b;
+  });
+  for (int i = 0; i < k; i++) out[i] = idx[i];
+  return k;
 }
 EXPORT int oracle_topk(const float* v, long n, int k, uint32_t* idx, float* val) { return topk(v, n, k, idx, val); }
 EXPORT void oracle_softmax(float* x, long n) { softmax_inplace(x, n); }
