@@ -21,9 +21,11 @@
 #include <mutex>
 
 #include "common.h"
+#include "gdn_chunk.h"
 #include "gqa_decode.h"
 #include "model_kernels.h"
 #include "mma_sync.h"
+#include "tc.h"
 
 namespace evie {
 
@@ -622,6 +624,332 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (tid == 0) scr.tickets[bh] = 0;
 }
 
+// The same tensor-core kernel with K and V streamed into shared memory by bulk copies. Each warp owns 64 tokens of
+// the split, i.e. 4 K tiles and 4 V tiles of 16 tokens; a 16-token tile of one KV head is one contiguous 8 KB run of
+// a page, so it arrives by one cp.async.bulk completing on the warp's mbarrier. The warp keeps three tiles in flight
+// in a private 3-stage ring and refills a stage as soon as it has read it, so its next loads overlap the MMAs,
+// the softmax and the P.V of the current tile (the register-fed kernel above has one tile in flight per warp and
+// none while it computes). Tiles past the context are neither copied nor read; rows past the context inside the
+// last tile are masked as before. 192 KB of ring per CTA (which also holds the warps' P.V results at the end): one
+// CTA of 8 warps per SM.
+constexpr int kTileBytes = 16 * kHD * 2;                  // 8 KB
+constexpr int kStages = 3;                                // tiles in flight per warp
+constexpr int kWarpRing = kStages * kTileBytes;           // 24 KB
+constexpr int kRingBytes = kWarps * kWarpRing;            // 192 KB
+
+template <class IO>
+__global__ void __launch_bounds__(kThreads, 1)
+    gqa_decode_bulk_kernel(IO io, const __nv_bfloat16* __restrict__ kp, const __nv_bfloat16* __restrict__ vp,
+                           int Hkv, int page_size, int max_pages, float scale, Scratch scr,
+                           unsigned int* timeouts) {
+  constexpr int GROUP = 4;
+  extern __shared__ __align__(128) uint8_t ring_all[];
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int ctx = min(io.ctx_of(b), max_pages * page_size);
+  const int n_splits = (ctx + kSplit - 1) / kSplit;
+  const int h0 = kvh * GROUP;
+  if (ctx <= 0) {
+    if (split == 0)
+      for (int i = tid; i < GROUP * kHD; i += kThreads) io.store(b, h0 + i / kHD, i % kHD, 0.0f);
+    return;
+  }
+  if (split >= n_splits) return;
+
+  __shared__ __align__(16) __nv_bfloat16 sP[kWarps][8][16];
+  // a warp's [GROUP][kHD] P.V result goes into its own ring once its last tile has been read
+  auto sO = [&](int w, int h) { return reinterpret_cast<float*>(ring_all + w * kWarpRing) + h * kHD; };
+  __shared__ float sM[kWarps][GROUP], sL[kWarps][GROUP];
+  __shared__ float s_w[kWarps][GROUP];
+  __shared__ float s_fin[GROUP][2];
+  __shared__ int s_last;
+  __shared__ __align__(8) uint64_t s_bar[kWarps][kStages];
+
+  const int32_t* pt = io.page_row(b);
+  auto row = [&](const __nv_bfloat16* pages, int j) {
+    const int page = pt[j / page_size];
+    return pages + (((size_t)page * Hkv + kvh) * page_size + (j % page_size)) * kHD;
+  };
+  const int wt0 = split * kSplit + warp * kTokPerWarp;
+  // valid tiles of this warp: the first nt K tiles, then the first nt V tiles (n = 0 .. 2 nt - 1)
+  const int nt = min(kMmaTiles, max(0, (ctx - wt0 + 15) / 16));
+  uint8_t* ring = ring_all + warp * kWarpRing;
+  uint64_t* bar = s_bar[warp];
+  if (lane == 0) {
+    for (int i = 0; i < kStages; i++) tc::mbar_init(&bar[i], 1);
+    tc::fence_barrier_init();
+  }
+  __syncwarp();
+  bool ok = true;
+  int issued = 0, consumed = 0;
+  auto issue = [&](int n) {  // tile n into stage n % kStages (lane 0; the warp has finished reading that stage)
+    if (!ok) return;
+    const bool isv = n >= nt;
+    const int base = wt0 + 16 * (isv ? n - nt : n);
+    const int rows = min(16, ctx - base);
+    if (lane == 0) {
+      tc::fence_proxy_async();
+      tc::mbar_arrive_expect_tx(&bar[n % kStages], (uint32_t)rows * kHD * 2);
+      tc::bulk_load(ring + (n % kStages) * kTileBytes, row(isv ? vp : kp, base), (uint32_t)rows * kHD * 2,
+                    &bar[n % kStages]);
+    }
+    issued = n + 1;
+  };
+  auto take = [&](int n) -> const uint8_t* {  // wait for tile n; its stage
+    if (ok && !tc::mbar_wait(&bar[n % kStages], (n / kStages) & 1)) ok = false;
+    if (ok) consumed = n + 1;
+    return ring + (n % kStages) * kTileBytes;
+  };
+  for (int n = 0; n < kStages && n < 2 * nt; n++) issue(n);
+
+  // Q^T fragments: column n = g is head g % 4, half g / 4 (0 = hi, 1 = lo), pre-scaled into the log2 domain.
+  uint32_t qb0[16], qb1[16];
+  {
+    const int head = h0 + (g & 3);
+    const bool lo = g >= 4;
+    const float f = scale * kLog2e;
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+      float v[8];
+      io.load_q8(b, head, 32 * p + 8 * c, v);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float x = v[j] * f;
+        v[j] = lo ? x - bf16_round(x) : x;
+      }
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        qb0[2 * p + e] = pack_bf16x2(v[4 * e + 0], v[4 * e + 1]);
+        qb1[2 * p + e] = pack_bf16x2(v[4 * e + 2], v[4 * e + 3]);
+      }
+    }
+  }
+
+  // ---- scores: lane holds heads hh, hh+1 (hh = 2 (c & 1)) for tokens g and g+8 of each tile
+  float sc[kMmaTiles][4];
+#pragma unroll
+  for (int t = 0; t < kMmaTiles; t++) {
+    const int jA = wt0 + 16 * t + g, jB = jA + 8;
+    if (t < nt) {
+      const uint8_t* tile = take(t);
+      const bool va = jA < ctx, vb = jB < ctx;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < 8; p++) {
+        const uint4 ka = va ? *reinterpret_cast<const uint4*>(tile + g * 512 + (32 * p + 8 * c) * 2)
+                            : make_uint4(0, 0, 0, 0);
+        const uint4 kb = vb ? *reinterpret_cast<const uint4*>(tile + (g + 8) * 512 + (32 * p + 8 * c) * 2)
+                            : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int e = 0; e < 2; e++)
+          mma_bf16_16816(acc, word_of(ka, 2 * e), word_of(kb, 2 * e), word_of(ka, 2 * e + 1), word_of(kb, 2 * e + 1),
+                         qb0[2 * p + e], qb1[2 * p + e]);
+      }
+      __syncwarp();
+      if (t + kStages < 2 * nt) issue(t + kStages);
+#pragma unroll
+      for (int i = 0; i < 4; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 2);  // hi + lo columns
+      sc[t][0] = va ? acc[0] : -INFINITY;
+      sc[t][1] = va ? acc[1] : -INFINITY;
+      sc[t][2] = vb ? acc[2] : -INFINITY;
+      sc[t][3] = vb ? acc[3] : -INFINITY;
+    } else {
+      sc[t][0] = sc[t][1] = sc[t][2] = sc[t][3] = -INFINITY;
+    }
+  }
+  // ---- warp softmax statistics per head (lanes with equal c hold the same heads)
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+  for (int t = 0; t < kMmaTiles; t++) {
+    m0 = fmaxf(m0, fmaxf(sc[t][0], sc[t][2]));
+    m1 = fmaxf(m1, fmaxf(sc[t][1], sc[t][3]));
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+  }
+  const float b0m = m0 == -INFINITY ? 0.f : m0, b1m = m1 == -INFINITY ? 0.f : m1;
+  float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+  for (int t = 0; t < kMmaTiles; t++) {
+    sc[t][0] = exp2f(sc[t][0] - b0m);
+    sc[t][1] = exp2f(sc[t][1] - b1m);
+    sc[t][2] = exp2f(sc[t][2] - b0m);
+    sc[t][3] = exp2f(sc[t][3] - b1m);
+    l0 += sc[t][0] + sc[t][2];
+    l1 += sc[t][1] + sc[t][3];
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  const int hh = 2 * (c & 1);
+  if (g == 0 && c < 2) {
+    sM[warp][hh] = m0;
+    sM[warp][hh + 1] = m1;
+    sL[warp][hh] = l0;
+    sL[warp][hh + 1] = l1;
+  }
+
+  // ---- P.V: both halves of the head dims per tile (the tile is read from shared memory once per half)
+  float o[2][8][4];
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int i = 0; i < 8; i++) o[h][i][0] = o[h][i][1] = o[h][i][2] = o[h][i][3] = 0.f;
+#pragma unroll 1
+  for (int t = 0; t < nt; t++) {
+    const int base = wt0 + 16 * t;
+    __syncwarp();
+    {  // P^T into shared memory as [h'][token]: lanes c < 2 write the hi halves, c >= 2 the lo halves
+      const int r0 = hh + (c >= 2 ? 4 : 0);
+      float pv[4] = {sc[0][0], sc[0][1], sc[0][2], sc[0][3]};
+#pragma unroll
+      for (int tt = 1; tt < kMmaTiles; tt++)
+        if (tt == t) pv[0] = sc[tt][0], pv[1] = sc[tt][1], pv[2] = sc[tt][2], pv[3] = sc[tt][3];
+      if (c >= 2)
+#pragma unroll
+        for (int i = 0; i < 4; i++) pv[i] -= bf16_round(pv[i]);
+      sP[warp][r0][g] = __float2bfloat16_rn(pv[0]);
+      sP[warp][r0 + 1][g] = __float2bfloat16_rn(pv[1]);
+      sP[warp][r0][g + 8] = __float2bfloat16_rn(pv[2]);
+      sP[warp][r0 + 1][g + 8] = __float2bfloat16_rn(pv[3]);
+    }
+    __syncwarp();
+    const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(&sP[warp][g][2 * c]);
+    const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(&sP[warp][g][2 * c + 8]);
+    const uint8_t* tile = take(nt + t);
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+      uint4 v[4][2];
+#pragma unroll
+      for (int tk = 0; tk < 4; tk++) {
+        const int jl = 2 * c + (tk & 1) + 8 * (tk >> 1);
+#pragma unroll
+        for (int r = 0; r < 2; r++)
+          v[tk][r] = base + jl < ctx
+                         ? *reinterpret_cast<const uint4*>(tile + jl * 512 + (128 * half + 16 * g + 8 * r) * 2)
+                         : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int wi = i >> 1;
+        const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
+        const uint32_t a0 = __byte_perm(word_of(v[0][0], wi), word_of(v[1][0], wi), sel);
+        const uint32_t a1 = __byte_perm(word_of(v[0][1], wi), word_of(v[1][1], wi), sel);
+        const uint32_t a2 = __byte_perm(word_of(v[2][0], wi), word_of(v[3][0], wi), sel);
+        const uint32_t a3 = __byte_perm(word_of(v[2][1], wi), word_of(v[3][1], wi), sel);
+        mma_bf16_16816(o[half][i], a0, a1, a2, a3, pb0, pb1);
+      }
+    }
+    __syncwarp();
+    if (nt + t + kStages < 2 * nt) issue(nt + t + kStages);
+  }
+  // every copy this warp issued has been waited for (consumed == issued); after a give-up, let them land first
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok) {
+    for (int n = consumed; n < issued; n++) tc::mbar_wait(&bar[n % kStages], (n / kStages) & 1);
+    if (lane == 0) atomicAdd(timeouts, 1u);
+  }
+#pragma unroll
+  for (int half = 0; half < 2; half++) {
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+      for (int k = 0; k < 4; k++) o[half][i][k] += __shfl_xor_sync(0xffffffffu, o[half][i][k], 2);  // hi + lo
+    if (c < 2) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int d0 = 128 * half + 16 * g + i, d1 = d0 + 8;
+        sO(warp, hh)[d0] = o[half][i][0];
+        sO(warp, hh + 1)[d0] = o[half][i][1];
+        sO(warp, hh)[d1] = o[half][i][2];
+        sO(warp, hh + 1)[d1] = o[half][i][3];
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- merge the 8 warps of this split
+  if (tid < GROUP) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) M = fmaxf(M, sM[w][tid]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) {
+      const float wt = sM[w][tid] == -INFINITY ? 0.f : exp2f(sM[w][tid] - M);
+      s_w[w][tid] = wt;
+      L += wt * sL[w][tid];
+    }
+    s_fin[tid][0] = M;
+    s_fin[tid][1] = L;
+  }
+  __syncthreads();
+  constexpr int kOutPerThread = GROUP * kHD / kThreads;
+  float osum[kOutPerThread];
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) {
+    const int e = tid + i * kThreads;
+    const int h = e / kHD, d = e % kHD;
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) a += s_w[w][h] * sO(w, h)[d];
+    osum[i] = a;
+  }
+  if (n_splits == 1) {
+#pragma unroll
+    for (int i = 0; i < kOutPerThread; i++) {
+      const int e = tid + i * kThreads;
+      const int h = e / kHD, d = e % kHD;
+      io.store(b, h0 + h, d, osum[i] / s_fin[h][1] * sigmoidf_(io.gate(b, h0 + h, d)));
+    }
+    return;
+  }
+  const size_t bh = (size_t)b * Hkv + kvh;
+  float* po = scr.o + (bh * scr.max_splits + split) * GROUP * kHD;
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) __stcg(po + tid + i * kThreads, osum[i]);
+  if (tid < GROUP) {
+    float* pml = scr.ml + ((bh * scr.max_splits + split) * GROUP + tid) * 2;
+    __stcg(pml, s_fin[tid][0]);
+    __stcg(pml + 1, s_fin[tid][1]);
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(scr.tickets + bh, 1) == n_splits - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float* s_sw = sO(0, 0);  // [GROUP][n_splits] merge weights (n_splits <= 512 fits in warp 0's ring)
+  if (tid < GROUP) {
+    const float* ml = scr.ml + (bh * scr.max_splits) * GROUP * 2;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < n_splits; s2++) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * GROUP + tid) * 2));
+    float L = 0.f;
+    for (int s2 = 0; s2 < n_splits; s2++) {
+      const float w = exp2f(__ldcg(ml + ((size_t)s2 * GROUP + tid) * 2) - M);
+      s_sw[tid * n_splits + s2] = w;
+      L += w * __ldcg(ml + ((size_t)s2 * GROUP + tid) * 2 + 1);
+    }
+    for (int s2 = 0; s2 < n_splits; s2++) s_sw[tid * n_splits + s2] /= L;
+  }
+  __syncthreads();
+  const float* pob = scr.o + bh * scr.max_splits * GROUP * kHD;
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) {
+    const int e = tid + i * kThreads;
+    const int h = e / kHD, d = e % kHD;
+    float a = 0.f;
+    for (int s2 = 0; s2 < n_splits; s2++) a += s_sw[h * n_splits + s2] * __ldcg(pob + (size_t)s2 * GROUP * kHD + e);
+    io.store(b, h0 + h, d, a * sigmoidf_(io.gate(b, h0 + h, d)));
+  }
+  if (tid == 0) scr.tickets[bh] = 0;
+}
+
 // Split scratch per (device, stream), grown on demand and kept for the process lifetime, so that calls on
 // different streams never share tickets or partials.
 struct DeviceScratch {
@@ -674,6 +1002,15 @@ bool mma_disabled() {
   return off;
 }
 
+// EVIE_GQA_BULK=0 keeps the register-fed tensor-core kernel instead of the bulk-copy one (same results).
+bool bulk_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("EVIE_GQA_BULK");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <typename KV, class IO>
 evie_status launch_gqa(const IO& io, const KV* kp, const KV* vp, int B, int Hq, int Hkv, int page_size, int max_pages,
                        int max_ctx, float scale, const Scratch& scr, cudaStream_t st) {
@@ -682,6 +1019,22 @@ evie_status launch_gqa(const IO& io, const KV* kp, const KV* vp, int B, int Hq, 
   dim3 grid(max_splits > 0 ? max_splits : 1, Hkv, B);
   if constexpr (sizeof(KV) == 2) {
     if (group == 4 && !mma_disabled()) {
+      if (bulk_enabled()) {
+        unsigned int* counter = device_timeout_counter();
+        if (!counter) return fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
+        int dev = 0;
+        EVIE_CUDA_TRY(cudaGetDevice(&dev));
+        static bool attr_set[64] = {};
+        if (dev < 64 && !attr_set[dev]) {
+          EVIE_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_bulk_kernel<IO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kRingBytes));
+          attr_set[dev] = true;
+        }
+        gqa_decode_bulk_kernel<IO><<<grid, kThreads, kRingBytes, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale,
+                                                                        scr, counter);
+        EVIE_CHECK_LAUNCH("gqa_decode_bulk_kernel");
+        return EVIE_OK;
+      }
       gqa_decode_mma_kernel<IO><<<grid, kThreads, 0, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale, scr);
       EVIE_CHECK_LAUNCH("gqa_decode_mma_kernel");
       return EVIE_OK;

@@ -32,6 +32,7 @@
 #include "common.h"
 #include "gqa_decode.h"
 #include "json.h"
+#include "gdn_chunk.h"
 #include "model_kernels.h"
 #include "sampler.h"
 
@@ -1119,6 +1120,8 @@ evie_status evie_create(const char* ckpt_dir, int device, int slots, int max_ctx
     if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) { rc = evie::fail(EVIE_ERR_CUDA, "cublasCreate failed"); break; }
     cublasSetStream(c->blas, c->stream);
     cublasSetMathMode(c->blas, CUBLAS_DEFAULT_MATH);
+    // the device's timeout counter of the bounded-wait kernels, looked up now rather than inside a graph capture
+    if (!evie::device_timeout_counter()) { rc = evie::fail(EVIE_ERR_CUDA, "device timeout counter unavailable"); break; }
     if ((rc = read_config(c, ckpt_dir)) != EVIE_OK) break;
     if ((rc = load_weights(c, ckpt_dir)) != EVIE_OK) break;
     if ((rc = allocate_state(c)) != EVIE_OK) break;
