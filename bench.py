@@ -767,7 +767,7 @@ def run_reference(args):
                          "sample": vals[0]["sample"]},
         "e2e": {"value": v, "unit": vals[0]["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -862,14 +862,31 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = w.cpu_sample(int(os.environ.get("EVIE_CPU_THREADS", os.cpu_count() or 1)))
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
 
 
+_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Writes the run's one JSON line to the process's original standard output."""
+    out = _OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _OUT
+    # Standard output carries exactly one JSON line: keep a handle on it and send everything else that writes to
+    # file descriptor 1 (NCCL's version banner under torchrun, library messages, prints) to standard error.
+    sys.stdout.flush()
+    _OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = os.fdopen(os.dup(2), "w", buffering=1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
