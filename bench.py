@@ -3,10 +3,9 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
 Workloads (per GPU; with N GPUs each rank runs its own share: weak scaling, no data-path collective):
-  gdn_decode   Gated DeltaNet decode step, B=64 sequences x 16 heads, dk=dv=128, fp32 state (config 1)
+  gdn_decode   Gated DeltaNet decode step, B=64 sequences x 16 heads, dk=dv=128, fp32 state
   gqa_decode   gated GQA decode attention, B=64, 16 q / 4 kv heads, hd 256, ctx ~ U[1024, 32768], 256-token pages
-               (config 3)
-  gdn_prefill  Gated DeltaNet prefill, B=8, T=8192, 16 heads (config 2)
+  gdn_prefill  Gated DeltaNet prefill, B=8, T=8192, 16 heads
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the launching stream; L2 is
 flushed (a 256 MiB write) between timed steps whenever a step's working set fits in L2. The K-step region is
@@ -231,7 +230,7 @@ class GdnDecode(Workload):
         self.tokens_per_step = B
 
     def config(self):
-        return {"workload": f"gdn_decode_step B={self.B} H={self.H} dk=dv={self.d} fp32 state (config 1)",
+        return {"workload": f"gdn_decode_step B={self.B} H={self.H} dk=dv={self.d} fp32 state",
                 "global_batch": self.B, "heads": self.H, "l2": "flushed between timed steps"}
 
     def algorithmic(self):
@@ -287,7 +286,7 @@ class GdnDecode(Workload):
 
 
 class GdnPrefill(Workload):
-    """Config 2: chunked Gated DeltaNet prefill, B sequences x T tokens x H heads, dk = dv = 128, S0 = 0."""
+    """Chunked Gated DeltaNet prefill, B sequences x T tokens x H heads, dk = dv = 128, S0 = 0."""
     name = "gdn_prefill"
     kernel = "gdn_chunk_prefill_kernel"
     bound = "tensor"
@@ -302,7 +301,7 @@ class GdnPrefill(Workload):
 
     def config(self):
         return {"workload": f"gdn_chunk_prefill B={self.B} T={self.T} H={self.H} dk=dv={self.d} chunk=64, "
-                            f"S0=0, o bf16 (config 2)",
+                            f"S0=0, o bf16",
                 "global_batch": self.B, "seq_len": self.T, "heads": self.H,
                 "hbm_bytes_per_step": self.hbm_bytes(),
                 "l2": f"inputs larger than L2 ({self.hbm_bytes() / 1e9:.2f} GB)"}
@@ -380,7 +379,7 @@ class GqaDecode(Workload):
 
     def config(self):
         return {"workload": f"gqa_decode B={self.B} Hq={self.Hq} Hkv={self.Hkv} hd={self.hd} ctx~U[1024,32768] "
-                            f"(sum {sum(self.ctx)}) page={self.page} bf16 KV (config 3)",
+                            f"(sum {sum(self.ctx)}) page={self.page} bf16 KV",
                 "global_batch": self.B, "l2": f"inputs larger than L2 ({self.algorithmic() / 1e9:.2f} GB)"}
 
     def algorithmic(self):
@@ -443,7 +442,7 @@ class GqaDecode(Workload):
 
 
 class ModelDecode(Workload):
-    """Config 4 per GPU: Qwen3.5-4B shapes, random bf16 weights (seed 5), B sequences = B/2 steered/unsteered pairs,
+    """Per GPU: Qwen3.5-4B shapes, random bf16 weights (seed 5), B sequences = B/2 steered/unsteered pairs,
     P-token uniform-random prompts, +0.6 dose Add steering on 32 seeded (layer, neuron) pairs on the steered half,
     every SwiGLU activation captured. A step is one greedy decode step of all B sequences."""
     name = "model_decode"
@@ -459,7 +458,7 @@ class ModelDecode(Workload):
     def config(self):
         return {"workload": f"Qwen3.5-4B-shaped decode, {self.B} sequences ({self.B // 2} steered/unsteered pairs) per "
                             f"GPU, {self.P}-token prompts, greedy, steering +0.6 dose on 32 (layer, neuron) pairs, "
-                            f"full SwiGLU capture (config 4)",
+                            f"full SwiGLU capture",
                 "model": "qwen3.5-4b-shaped (random init, seed 5)", "global_batch": self.B, "seq_len": self.P,
                 "l2": "inputs larger than L2 (8.4 GB weights + caches per step)",
                 "prefill_tok_s": getattr(self, "prefill_tok_s", None),

@@ -9,7 +9,7 @@ def bf16_bits(t: torch.Tensor) -> np.ndarray:
 
 
 def gdn_decode_inputs(B, H, seed, d=128):
-    """Config 1 distributions: S ~ N(0, 0.1) f32; q, k ~ N(0,1) bf16 L2-normalised per head; v ~ N(0,1) bf16;
+    """Decode-step distributions: S ~ N(0, 0.1) f32; q, k ~ N(0,1) bf16 L2-normalised per head; v ~ N(0,1) bf16;
     beta = sigmoid(N(0,1)); log decay g ~ U(-5, 0)."""
     g = torch.Generator().manual_seed(seed)
     S = torch.randn(B, H, d, d, generator=g) * 0.1
@@ -24,7 +24,7 @@ def gdn_decode_inputs(B, H, seed, d=128):
 
 
 def gdn_prefill_inputs(B, T, H, seed, d=128, s0=False):
-    """Config 2 distributions (token-major [B, T, H, d]); the initial state is zero unless s0."""
+    """Chunked-prefill distributions (token-major [B, T, H, d]); the initial state is zero unless s0."""
     g = torch.Generator().manual_seed(seed)
     q = torch.randn(B, T, H, d, generator=g)
     k = torch.randn(B, T, H, d, generator=g)
@@ -38,7 +38,7 @@ def gdn_prefill_inputs(B, T, H, seed, d=128, s0=False):
 
 
 def gqa_inputs(B, Hq, Hkv, ctx, seed, hd=256, page=256, shuffle_pages=True):
-    """Config 3 distributions: bf16 KV ~ N(0,1) in `page`-token pages (page table a random permutation);
+    """Paged-attention distributions: bf16 KV ~ N(0,1) in `page`-token pages (page table a random permutation);
     q ~ N(0,1) bf16; gate logits ~ N(0,1) bf16."""
     g = torch.Generator().manual_seed(seed)
     ctx = [int(c) for c in ctx]

@@ -49,7 +49,7 @@ def test_prefill_matches_oracle(B, T, H, s0, impl, cuda):
 
 @pytest.mark.gpu
 def test_prefill_config2_size_sampled_heads(cuda):
-    """B=8, T=8192, H=16 (config 2, S0 = 0) through the chunked kernel; four (sequence, head) pairs against the
+    """B=8, T=8192, H=16 (S0 = 0) through the chunked kernel; four (sequence, head) pairs against the
     oracle over the whole 8192-token sequence."""
     from evie_b200 import ops
 

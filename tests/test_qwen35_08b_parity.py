@@ -1,5 +1,5 @@
-"""Config 0: Qwen3.5-0.8B shapes (24 layers, MLP width 3584, 18 DeltaNet + 6 gated-attention layers), every
-weight bf16 N(0, 0.02) from seed 0 with norm gains stored as 1.0, batch 1, a 64-token prompt of uniform random ids
+"""Qwen3.5-0.8B parity run: the public 0.8B shapes (24 layers, MLP width 3584, 18 DeltaNet + 6 gated-attention
+layers), every weight bf16 N(0, 0.02) from seed 0 with norm gains stored as 1.0, batch 1, a 64-token prompt of uniform random ids
 from seed 1, then 64 greedy decode steps. The GPU path must produce the oracle's greedy ids exactly and logits
 within 2e-3 max-abs at every step. The checkpoint (about 2 GB) is written to a temporary directory."""
 import os
@@ -20,7 +20,7 @@ STEPS = 64
 LOGIT_TOL = {True: 2e-3, False: 3e-2}
 
 
-def config0_prompt(vocab: int) -> np.ndarray:
+def parity_prompt(vocab: int) -> np.ndarray:
     g = torch.Generator().manual_seed(1)
     return torch.randint(0, vocab, (64,), generator=g).numpy().astype(np.uint32)
 
@@ -36,7 +36,7 @@ def c0_reference(c0_ckpt):
     """The oracle's greedy run: ids and per-step logits (prefill logits first)."""
     oracle.set_threads(os.cpu_count() or 1)
     m = oracle.Model(c0_ckpt)
-    prompt = config0_prompt(m.cfg.vocab)
+    prompt = parity_prompt(m.cfg.vocab)
     cache = m.new_cache()
     lg, _, _ = m.forward([dict(cache=cache, tokens=prompt)])
     ids, logits = [], [lg[0].copy()]
@@ -55,7 +55,7 @@ def _margin(l):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("kv_f32", [True, False])
-def test_config0_greedy_ids_and_logits(c0_ckpt, c0_reference, kv_f32, cuda):
+def test_08b_greedy_ids_and_logits(c0_ckpt, c0_reference, kv_f32, cuda):
     from evie_b200.gpu import GpuModel, GpuSeq
 
     prompt, ids_ref, logits_ref = c0_reference
