@@ -59,6 +59,7 @@ SIGNATURES = {
     "evie_reset_gates": (I, [P, I]),
     "evie_set_sampler": (I, [P, I, P]),
     "evie_read_top_active": (I, [P, I, P, P]),
+    "evie_neuron_sigma": (I, [P, P, SZ, P, P]),
     "evie_top_active": (I, [P, I, C.c_longlong, I, P, P]),
     "evie_sampler_seed_state": (C.c_uint64, [C.c_uint64]),
     "evie_sample": (I, [P, I, I, P, P, P, P, P, P]),

@@ -1224,6 +1224,20 @@ evie_status evie_reset_gates(evie_ctx* c, int slot) {
   return EVIE_OK;
 }
 
+// analysis.rs:129-201 (no lens) on the context's weights.
+evie_status evie_neuron_sigma(evie_ctx* c, float* sigma, size_t n, float* mean, float* m_scale) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_neuron_sigma: null context");
+  auto& s = c->s;
+  if (!sigma || n != (size_t)s.L * s.n)
+    return remember(c, evie::fail(EVIE_ERR_ARG, "evie_neuron_sigma: expected %zu outputs, got %zu",
+                                  (size_t)s.L * s.n, n));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  std::vector<const __nv_bfloat16*> downs;
+  for (const Layer& L : c->layers) downs.push_back(L.w_down);
+  return remember(c, evie::neuron_sigma_run(c->blas, c->stream, c->lm_head, s.V, s.d, c->final_norm, downs, s.n,
+                                            sigma, mean, m_scale));
+}
+
 // mcp.rs:242-256 over the frames the last capturing call left on the device.
 evie_status evie_read_top_active(evie_ctx* c, int k, int32_t* out, int* rows) {
   if (!c) return evie::fail(EVIE_ERR_ARG, "evie_read_top_active: null context");

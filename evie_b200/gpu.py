@@ -161,6 +161,14 @@ class GpuModel:
         self._check(lib().evie_read_top_active(self._h, k, out.ctypes.data, C.byref(rows)))
         return out[:rows.value].copy()
 
+    def neuron_sigma(self):
+        """analysis.rs:129-201 without a lens: (sigma [layers * neurons], unembedding mean [hidden], m_scale)."""
+        sig = np.empty(self.layers * self.neurons, np.float32)
+        mean = np.empty(self.hidden, np.float32)
+        ms = C.c_float()
+        self._check(lib().evie_neuron_sigma(self._h, sig.ctypes.data, sig.size, mean.ctypes.data, C.byref(ms)))
+        return sig, mean, ms.value
+
     def reset_gates(self, slot: int):
         self._check(lib().evie_reset_gates(self._h, slot))
 

@@ -165,6 +165,14 @@ EVIE_API evie_status evie_set_sampler(evie_ctx* ctx, int slot, const evie_sample
 EVIE_API evie_status evie_reset_slot(evie_ctx* ctx, int slot);
 /* Per-neuron activation scales used to normalise captured frames, layer-major (gpu/mod.rs:549). */
 EVIE_API evie_status evie_set_scale(evie_ctx* ctx, const float* scale, size_t n);
+/* Offline analysis (crates/evie-core/src/analysis.rs:129-201, without a lens): the unembedding statistics
+ * (UnembedStats::compute: mean of the LM-head rows, gain-weighted covariance of a strided subsample stored as f16 with
+ * its scale) and every neuron's logit spread sqrt(u^T M u) over its down_proj column u (neuron_sigma).
+ *   sigma    [layers * intermediate] host, layer-major (n must equal that count);
+ *   mean     [hidden] host or NULL;  m_scale  host or NULL.
+ * Allocates and frees ~(hidden x min(vocab, 16384) x 8 + hidden x intermediate x 8) bytes of device memory per call;
+ * synchronous. */
+EVIE_API evie_status evie_neuron_sigma(evie_ctx* ctx, float* sigma, size_t n, float* mean, float* m_scale);
 /* Track the max |activation| of every neuron over positions > 0 across later calls (gpu/mod.rs:578). */
 EVIE_API evie_status evie_track_max(evie_ctx* ctx, int on);
 /* Reads the tracked maxima, layer-major (gpu/mod.rs:590). */

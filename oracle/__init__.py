@@ -87,6 +87,7 @@ def _declare(L):
         "oracle_gate_state_free": (None, [P]),
         "oracle_gate_state_open": (I, [P, I]),
         "oracle_top_active": (I, [P, LG, I, P]),
+        "oracle_neuron_sigma": (F, [P, P, P]),
         "oracle_sampler_new": (P, [F, F, F, F, C.c_uint64]),
         "oracle_sampler_free": (None, [P]),
         "oracle_sampler_rng": (C.c_uint64, [P]),
@@ -402,6 +403,13 @@ class Model:
         if getattr(self, "_h", None) and _lib is not None:
             _lib.oracle_model_free(self._h)
             self._h = None
+
+    def neuron_sigma(self):
+        """analysis.rs:129-201 without a lens: (sigma [layers * intermediate], unembedding mean [hidden], m_scale)."""
+        sig = np.zeros(self.cfg.n_layers * self.cfg.intermediate, np.float32)
+        mean = np.zeros(self.cfg.hidden, np.float32)
+        ms = lib().oracle_neuron_sigma(self._h, _p(sig), _p(mean))
+        return sig, mean, float(ms)
 
     def new_cache(self) -> "Cache":
         return Cache(lib().oracle_cache_new(self._h))

@@ -386,12 +386,16 @@ __attribute__((target("avx2,fma,f16c"))) void multi_dot(const uint16_t* w, size_
   }
 }
 
-// kernels.rs:427-464 (the packed values are exact f32 widenings; the 8x8 transpose only moves them)
-__attribute__((target("avx2,fma,f16c"))) void pack_panel(const uint16_t* w, size_t cols, size_t rows, size_t r0,
+// kernels.rs:427-464 (the packed values are exact f32 widenings; the 8x8 transpose only moves them). The float
+// form packs a matrix already widened from f16 (Kind16::F16), which the same micro-kernel then multiplies.
+inline float widen(uint16_t x) { return bf16_to_f32(x); }
+inline float widen(float x) { return x; }
+template <typename WT>
+__attribute__((target("avx2,fma,f16c"))) void pack_panel(const WT* w, size_t cols, size_t rows, size_t r0,
                                                            size_t k0, size_t kc, float* pack) {
   size_t nr = std::min(NR, rows - r0);
   for (size_t k = 0; k < kc; k++)
-    for (size_t i = 0; i < NR; i++) pack[k * NR + i] = i < nr ? bf16_to_f32(w[(r0 + i) * cols + k0 + k]) : 0.0f;
+    for (size_t i = 0; i < NR; i++) pack[k * NR + i] = i < nr ? widen(w[(r0 + i) * cols + k0 + k]) : 0.0f;
 }
 
 // kernels.rs:466-521
@@ -439,26 +443,9 @@ void matvec(const uint16_t* w, size_t rows, size_t cols, const float* x, float* 
   });
 }
 
-// kernels.rs:163-268
-void matmul(const uint16_t* w, size_t rows, size_t cols, const float* x, size_t n, float* y) {
-  if (n == 0) return;
-  if (n == 1) return matvec(w, rows, cols, x, y);
-  if (n < 8) {
-    size_t chunk = std::min<size_t>(512, std::max<size_t>(4, rows / (n_threads() * 6)));
-    long nch = (long)((rows + chunk - 1) / chunk);
-    par_for(nch, [&](long ci) {
-      size_t r0 = ci * chunk, nr = std::min(chunk, rows - r0);
-      switch (n) {
-        case 2: multi_dot<2>(w, cols, r0, nr, x, y, rows); break;
-        case 3: multi_dot<3>(w, cols, r0, nr, x, y, rows); break;
-        case 4: multi_dot<4>(w, cols, r0, nr, x, y, rows); break;
-        case 5: multi_dot<5>(w, cols, r0, nr, x, y, rows); break;
-        case 6: multi_dot<6>(w, cols, r0, nr, x, y, rows); break;
-        default: multi_dot<7>(w, cols, r0, nr, x, y, rows); break;
-      }
-    });
-    return;
-  }
+// kernels.rs:221-268: the packed GEMM for n >= 8 rows of x
+template <typename WT>
+void packed_gemm(const WT* w, size_t rows, size_t cols, const float* x, size_t n, float* y) {
   size_t panels = (rows + NR - 1) / NR;
   size_t tb_size = std::min<size_t>((std::max<size_t>((2u << 20) / (cols * 4), 6) / 6) * 6, 480);
   for (size_t tb0 = 0; tb0 < n; tb0 += tb_size) {
@@ -490,6 +477,29 @@ void matmul(const uint16_t* w, size_t rows, size_t cols, const float* x, size_t 
   }
 }
 
+// kernels.rs:163-268
+void matmul(const uint16_t* w, size_t rows, size_t cols, const float* x, size_t n, float* y) {
+  if (n == 0) return;
+  if (n == 1) return matvec(w, rows, cols, x, y);
+  if (n < 8) {
+    size_t chunk = std::min<size_t>(512, std::max<size_t>(4, rows / (n_threads() * 6)));
+    long nch = (long)((rows + chunk - 1) / chunk);
+    par_for(nch, [&](long ci) {
+      size_t r0 = ci * chunk, nr = std::min(chunk, rows - r0);
+      switch (n) {
+        case 2: multi_dot<2>(w, cols, r0, nr, x, y, rows); break;
+        case 3: multi_dot<3>(w, cols, r0, nr, x, y, rows); break;
+        case 4: multi_dot<4>(w, cols, r0, nr, x, y, rows); break;
+        case 5: multi_dot<5>(w, cols, r0, nr, x, y, rows); break;
+        case 6: multi_dot<6>(w, cols, r0, nr, x, y, rows); break;
+        default: multi_dot<7>(w, cols, r0, nr, x, y, rows); break;
+      }
+    });
+    return;
+  }
+  packed_gemm(w, rows, cols, x, n, y);
+}
+
 // ------------------------------------------------------------------------------------------------
 // gated delta rule step (model.rs:501-524), loop order kept
 
@@ -514,6 +524,7 @@ inline void recur_body(float* s, const float* q, const float* k, const float* v,
 }
 
 inline uint16_t f32_to_f16(float v) { return (uint16_t)_cvtss_sh(v, _MM_FROUND_TO_NEAREST_INT); }
+inline float f16_to_f32(uint16_t h) { return _cvtsh_ss(h); }
 
 // worker.rs:97-112 companding: q = round(127 * sqrt(min(|v|, 1))), sign of v.
 inline int8_t compand(float v) {
@@ -928,6 +939,65 @@ EXPORT int oracle_top_active(const int8_t* f, long n, int k, int32_t* out) {
   });
   for (int i = 0; i < k; i++) out[i] = idx[i];
   return k;
+}
+// crates/evie-core/src/analysis.rs:129-175 (UnembedStats::compute) and 183-201 (neuron_sigma without a lens):
+// mean of the unembedding rows (f64 sums), the gain-weighted covariance of a strided subsample of at most 16384
+// rows (the centred rows scaled by 64 and rounded to f16 as the GEMM's weight operand), normalised to its largest
+// magnitude and stored as f16; then sigma = sqrt(max(u . (M u) * m_scale, 1e-30)) for every down_proj column u.
+struct UnembedStats {
+  std::vector<float> mean;
+  std::vector<float> m;  // d x d, the f16 values widened
+  float m_scale = 0.0f;
+};
+UnembedStats unembed_stats(const Model& m) {
+  const Mat& w = m.lm_head;
+  const size_t v = w.rows, d = w.cols;
+  const float* g = m.final_norm.data();
+  std::vector<double> sums(d, 0.0);
+  for (size_t r = 0; r < v; r++)
+    for (size_t i = 0; i < d; i++) sums[i] += (double)bf16_to_f32(w.p[r * d + i]);
+  UnembedStats st;
+  st.mean.resize(d);
+  for (size_t i = 0; i < d; i++) st.mean[i] = (float)(sums[i] / (double)v);
+  const size_t s = std::min<size_t>(16384, v), stride = v / s;
+  std::vector<float> xt(d * s), xw(d * s);  // x^T (d x s) and its f16(64 x) widening, the GEMM weight
+  for (size_t j = 0; j < s; j++)
+    for (size_t i = 0; i < d; i++) {
+      const float x = (bf16_to_f32(w.p[j * stride * d + i]) - st.mean[i]) * g[i];
+      xt[i * s + j] = x;
+      xw[i * s + j] = f16_to_f32(f32_to_f16(x * 64.0f));
+    }
+  std::vector<float> cov(d * d);
+  packed_gemm(xw.data(), d, s, xt.data(), d, cov.data());
+  const float norm = 1.0f / ((float)s * 64.0f);
+  float mx = 0.0f;
+  for (auto& c : cov) {
+    c *= norm;
+    mx = std::max(mx, std::fabs(c));
+  }
+  st.m_scale = std::max(mx, 1e-30f);
+  st.m.resize(d * d);
+  for (size_t i = 0; i < d * d; i++) st.m[i] = f16_to_f32(f32_to_f16(cov[i] / st.m_scale));
+  return st;
+}
+void neuron_sigma(const Model& m, const UnembedStats& st, float* sigma) {
+  const size_t nl = m.layers.size(), n = m.cfg.intermediate, d = m.cfg.hidden;
+  std::vector<float> u(n * d), mu(n * d);
+  for (size_t l = 0; l < nl; l++) {
+    const Mat& dn = m.layers[l].down;  // [d][n]
+    for (size_t k = 0; k < d; k++)
+      for (size_t i = 0; i < n; i++) u[i * d + k] = bf16_to_f32(dn.p[k * n + i]);  // transpose_to_f32
+    packed_gemm(st.m.data(), d, d, u.data(), n, mu.data());
+    for (size_t i = 0; i < n; i++)
+      sigma[l * n + i] = std::sqrt(std::max(dot(u.data() + i * d, mu.data() + i * d, d) * st.m_scale, 1e-30f));
+  }
+}
+EXPORT float oracle_neuron_sigma(void* model, float* sigma, float* mean) {
+  const Model& m = *(const Model*)model;
+  UnembedStats st = unembed_stats(m);
+  if (mean) memcpy(mean, st.mean.data(), st.mean.size() * sizeof(float));
+  neuron_sigma(m, st, sigma);
+  return st.m_scale;
 }
 EXPORT int oracle_topk(const float* v, long n, int k, uint32_t* idx, float* val) { return topk(v, n, k, idx, val); }
 EXPORT void oracle_softmax(float* x, long n) { softmax_inplace(x, n); }
