@@ -150,9 +150,27 @@ struct Layer {
 }  // namespace
 
 // Kernel groups timed by the optional profiling mode (evie_profile).
-enum ProfCat { P_GEMM = 0, P_LMHEAD, P_CONV, P_MIXER, P_ATTN_PREP, P_ATTN, P_NORM, P_SWIGLU, P_OTHER, P_COUNT };
-const char* const kProfNames[P_COUNT] = {"projection_gemm", "lm_head_gemm", "conv", "gdn_mixer", "attn_prep",
-                                         "gqa_attention", "add_norm", "swiglu", "other"};
+// The projections are one group per weight (each is its own cuBLAS kernel shape).
+enum ProfCat {
+  P_GEMM_LIN_IN = 0,
+  P_GEMM_LIN_OUT,
+  P_GEMM_ATT_IN,
+  P_GEMM_ATT_OUT,
+  P_GEMM_GATE_UP,
+  P_GEMM_DOWN,
+  P_LMHEAD,
+  P_CONV,
+  P_MIXER,
+  P_ATTN_PREP,
+  P_ATTN,
+  P_NORM,
+  P_SWIGLU,
+  P_OTHER,
+  P_COUNT
+};
+const char* const kProfNames[P_COUNT] = {"gemm_linear_in", "gemm_linear_out", "gemm_attn_in", "gemm_attn_out",
+                                         "gemm_mlp_gate_up", "gemm_mlp_down", "lm_head_gemm", "conv", "gdn_mixer",
+                                         "attn_prep", "gqa_attention", "add_norm", "swiglu", "other"};
 
 struct evie_ctx {
   int device = 0;
@@ -243,15 +261,32 @@ struct evie_ctx {
   std::vector<cudaEvent_t> prof_free;
   double prof_ms[P_COUNT] = {0};
   int64_t prof_n[P_COUNT] = {0};
+  bool prof_failed = false;  // an event could not be created, recorded or timed
   cudaEvent_t prof_event() {
     if (!prof_free.empty()) {
       cudaEvent_t e = prof_free.back();
       prof_free.pop_back();
       return e;
     }
-    cudaEvent_t e;
-    cudaEventCreate(&e);
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) {
+      cudaGetLastError();
+      prof_failed = true;
+      return nullptr;
+    }
     return e;
+  }
+  // Creates events ahead of a stream capture, so that none is created while capturing.
+  void prof_reserve(size_t n) {
+    while (prof_free.size() < n) {
+      cudaEvent_t e = nullptr;
+      if (cudaEventCreate(&e) != cudaSuccess) {
+        cudaGetLastError();
+        prof_failed = true;
+        return;
+      }
+      prof_free.push_back(e);
+    }
   }
   std::string err;
 
@@ -271,6 +306,21 @@ struct evie_ctx {
 
 namespace {
 
+// Records a profiling event on the context's stream. Inside a stream capture the record becomes an event-record
+// node of the graph (cudaEventRecordExternal), so the replayed graph timestamps the group where it runs.
+void prof_record(evie_ctx* c, cudaEvent_t e) {
+  if (!e) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t rc = cudaStreamIsCapturing(c->stream, &cs);
+  if (rc == cudaSuccess)
+    rc = cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(e, c->stream, cudaEventRecordExternal)
+                                             : cudaEventRecord(e, c->stream);
+  if (rc != cudaSuccess) {
+    cudaGetLastError();
+    c->prof_failed = true;
+  }
+}
+
 // Brackets one kernel group with CUDA events on the context's stream when profiling is on.
 struct ProfScope {
   evie_ctx* c;
@@ -279,14 +329,14 @@ struct ProfScope {
   ProfScope(evie_ctx* c_, int cat_) : c(c_), cat(cat_) {
     if (c->prof) {
       a = c->prof_event();
-      cudaEventRecord(a, c->stream);
+      prof_record(c, a);
     }
   }
   ~ProfScope() {
     if (c->prof) {
       cudaEvent_t b = c->prof_event();
-      cudaEventRecord(b, c->stream);
-      c->prof_pending.push_back({cat, {a, b}});
+      prof_record(c, b);
+      if (a && b) c->prof_pending.push_back({cat, {a, b}});
     }
   }
 };
@@ -294,9 +344,13 @@ struct ProfScope {
 void prof_resolve(evie_ctx* c) {
   for (auto& p : c->prof_pending) {
     float ms = 0.f;
-    cudaEventElapsedTime(&ms, p.second.first, p.second.second);
-    c->prof_ms[p.first] += ms;
-    c->prof_n[p.first] += 1;
+    if (cudaEventElapsedTime(&ms, p.second.first, p.second.second) == cudaSuccess) {
+      c->prof_ms[p.first] += ms;
+      c->prof_n[p.first] += 1;
+    } else {
+      cudaGetLastError();
+      c->prof_failed = true;
+    }
     c->prof_free.push_back(p.second.first);
     c->prof_free.push_back(p.second.second);
   }
@@ -694,7 +748,7 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
     evie::YView yo;  // output projection of the mixer
     if (L.kind == 0) {
       evie::YView y;
-      { PROF(P_GEMM); TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2, &y)); }
+      { PROF(P_GEMM_LIN_IN); TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2, &y)); }
       float* cs = c->conv_state + (size_t)L.idx * (s.K - 1) * s.conv_dim;
       {
         PROF(P_CONV);
@@ -712,10 +766,10 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
         TRY(evie::k_gdn_mixer(c->act, y, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm,
                               s, c->X2, st));
       }
-      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2, &yo, residual_ksplit(c, s.vd))); }
+      { PROF(P_GEMM_LIN_OUT); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2, &yo, residual_ksplit(c, s.vd))); }
     } else {
       evie::YView y;
-      { PROF(P_GEMM); TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2, &y)); }
+      { PROF(P_GEMM_ATT_IN); TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2, &y)); }
       const float scale = 1.0f / sqrtf((float)s.hd);
       if (c->kv_f32) {
         float* kc = (float*)c->k_cache + (size_t)L.idx * kv_layer;
@@ -753,19 +807,19 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
                                                     scale, c->attn_scratch, c->max_rows, st));
         }
       }
-      { PROF(P_GEMM); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2, &yo, residual_ksplit(c, s.nh * s.hd))); }
+      { PROF(P_GEMM_ATT_OUT); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2, &yo, residual_ksplit(c, s.nh * s.hd))); }
     }
     // model.rs:246-248: residual add after the mixer, then the pre-MLP norm
     { PROF(P_NORM); TRY(evie::k_add_norm(c->x, yo, s.d, R, L.ln2, s.eps, s.d, c->X2, nullptr, 0, s.L, st)); }
     evie::YView yg, yd;
-    { PROF(P_GEMM); TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2, &yg)); }
+    { PROF(P_GEMM_GATE_UP); TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2, &yg)); }
     {
       PROF(P_SWIGLU);
       if (c->gate_layers[li]) TRY(evie::k_gate_detect(yg, 2 * s.n, c->d_segs, nseq, li, s, gt, st));
       TRY(evie::k_swiglu(yg, 2 * s.n, R, c->d_rows, li, s, steer, c->scale, fr, c->track ? c->maxbuf : nullptr,
                          c->X2, st));
     }
-    { PROF(P_GEMM); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2, &yd, residual_ksplit(c, s.n))); }
+    { PROF(P_GEMM_DOWN); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2, &yd, residual_ksplit(c, s.n))); }
     {
       PROF(P_NORM);
       if (li + 1 < s.L) {
@@ -908,9 +962,11 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
   // all steps, the first included, are the same work on device-resident inputs. They replay one captured CUDA
   // graph, cached across calls like the forward graphs (key: sequences, capture, tracking, and a context bound
   // that covers every step, rounded up to a multiple of 2048, from which the attention takes its split count).
-  // The profiling mode (events around kernel groups) runs the steps eagerly, as does a context created with
-  // EVIE_NO_GRAPH=1.
+  // The profiling mode (events around kernel groups) captures each step into a graph of its own, the events as
+  // event-record nodes between the groups, so that every group is timed as the replayed step runs it (no host
+  // launch gaps inside an event pair). A context created with EVIE_NO_GRAPH=1 runs the steps eagerly.
   const bool use_graph = !c->prof && !c->no_graph;
+  const bool prof_graph = c->prof && !c->no_graph;
   const int bound = std::min(c->max_ctx, (max_ctx_rows + steps - 1 + 2047) / 2048 * 2048);
   cudaGraphExec_t exec = nullptr;
   if (use_graph) {
@@ -941,9 +997,40 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
     }
     exec = it->second;
   }
+  struct StepExec {  // the profiling mode's per-step graph, released once its replay has finished
+    cudaStream_t st;
+    cudaGraphExec_t e = nullptr;
+    ~StepExec() { reset(); }
+    void reset() {
+      if (!e) return;
+      cudaStreamSynchronize(st);
+      cudaGraphExecDestroy(e);
+      e = nullptr;
+    }
+  } pexec{st};
   for (int i = 0; i < steps; i++) {
     if (exec) {
       EVIE_CUDA_TRY(cudaGraphLaunch(exec, st));
+    } else if (prof_graph) {
+      c->prof_reserve(2048);
+      cudaGraph_t g = nullptr;
+      EVIE_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      evie_status rc = enqueue_layers(c, R, nseq, bound, capture);
+      if (rc == EVIE_OK) rc = enqueue_head(c, nseq, false);
+      if (rc == EVIE_OK) {
+        PROF(P_OTHER);
+        rc = evie::k_advance_rows(c->d_rows, nseq, c->next, st);
+      }
+      const cudaError_t ce = cudaStreamEndCapture(st, &g);
+      if (rc != EVIE_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      EVIE_CUDA_TRY(ce);
+      const cudaError_t ie = cudaGraphInstantiate(&pexec.e, g, 0);
+      cudaGraphDestroy(g);
+      EVIE_CUDA_TRY(ie);
+      EVIE_CUDA_TRY(cudaGraphLaunch(pexec.e, st));
     } else {
       TRY(enqueue_layers(c, R, nseq, max_ctx_rows + i, capture));
       TRY(enqueue_head(c, nseq, false));
@@ -957,10 +1044,16 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
     if (capture && resid)
       EVIE_CUDA_TRY(cudaMemcpyAsync(resid + (size_t)i * nseq * s.L * s.d, c->resid, (size_t)nseq * s.L * s.d * 2,
                                     cudaMemcpyDeviceToHost, st));
+    if (pexec.e) {
+      pexec.reset();
+      prof_resolve(c);
+    }
   }
   if (out_tokens) EVIE_CUDA_TRY(cudaMemcpyAsync(out_tokens, c->hist, need * 4, cudaMemcpyDeviceToHost, st));
   EVIE_CUDA_TRY(cudaStreamSynchronize(st));
   prof_resolve(c);
+  if (c->prof && c->prof_failed)
+    return evie::fail(EVIE_ERR_CUDA, "decode: the profiling events could not be recorded or timed");
   if (capture) c->cap_rows = nseq;
   return EVIE_OK;
 }
@@ -1171,6 +1264,7 @@ void* evie_stream(const evie_ctx* c) { return c ? (void*)c->stream : nullptr; }
 evie_status evie_profile(evie_ctx* c, int on) {
   if (!c) return evie::fail(EVIE_ERR_ARG, "evie_profile: null context");
   c->prof = on != 0;
+  c->prof_failed = false;
   for (int i = 0; i < P_COUNT; i++) c->prof_ms[i] = 0.0, c->prof_n[i] = 0;
   return EVIE_OK;
 }

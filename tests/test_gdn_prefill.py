@@ -3,7 +3,7 @@
 
 Tolerances: the final state within 1e-3 relative (Frobenius); outputs are bf16, so within one bf16 rounding of the
 oracle's f32 output plus 1e-3 relative of the row norm. Cases cover a single token, ragged last chunks, several
-sequences and heads, a non-zero entering state, an empty prompt and the full config-2 size (B=8, T=8192, H=16),
+sequences and heads, a non-zero entering state, an empty prompt and the full benchmark size (B=8, T=8192, H=16),
 whose heads are checked against the oracle on a sample."""
 import numpy as np
 import pytest
@@ -48,7 +48,7 @@ def test_prefill_matches_oracle(B, T, H, s0, impl, cuda):
 
 
 @pytest.mark.gpu
-def test_prefill_config2_size_sampled_heads(cuda):
+def test_prefill_b8_t8192_h16_sampled_heads(cuda):
     """B=8, T=8192, H=16 (S0 = 0) through the chunked kernel; four (sequence, head) pairs against the
     oracle over the whole 8192-token sequence."""
     from evie_b200 import ops

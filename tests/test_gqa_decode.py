@@ -36,7 +36,7 @@ def test_gqa_decode_group2_and_small_pages(cuda):
 
 
 @pytest.mark.gpu
-def test_gqa_decode_config3_sample(cuda):
+def test_gqa_decode_ctx1k_32k_sample(cuda):
     """The B=64 attention shapes (16 q / 4 kv heads, hd 256, 256-token pages) with contexts drawn from U[1024, 32768]."""
     g = torch.Generator().manual_seed(4)
     ctx = torch.randint(1024, 32769, (8,), generator=g).tolist()

@@ -196,6 +196,35 @@ def test_device_decode_loop_matches_step_calls(tiny_ckpt, cuda):
     assert np.array_equal(results[0][1], results[1][1])
 
 
+@pytest.mark.gpu
+def test_profiled_decode_matches_graph_replay(tiny_ckpt, cuda):
+    """The profiling mode (each decode step captured with event-record nodes between the kernel groups) runs the
+    same work as the cached step graph: identical tokens and frames, and a positive time for every group it saw."""
+    from evie_b200.gpu import GpuSeq
+
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, 2048, n).astype(np.uint32) for n in (9, 21)]
+    results = []
+    for prof in (False, True):
+        m = _gpu_model(tiny_ckpt, False, max_ctx=128, slots=2, max_rows=64)
+        out = m.forward([GpuSeq(i, 0, p) for i, p in enumerate(prompts)], want_logits=False)
+        first = out.next_tokens.copy()
+        seqs = [GpuSeq(i, len(p), first[i:i + 1]) for i, p in enumerate(prompts)]
+        frames = np.zeros((4, 2, m.layers * m.neurons), np.int8)
+        m.profile(prof)
+        toks = m.decode_greedy(seqs, 4, capture=True, frames=frames)
+        groups = m.profile_read()
+        m.profile(False)
+        m.close()
+        results.append((toks, frames))
+        if prof:
+            seen = {k: v for k, v in groups.items() if v[1] > 0}
+            assert {"gemm_mlp_gate_up", "gemm_linear_in", "gdn_mixer", "gqa_attention", "swiglu"} <= set(seen)
+            assert all(ms > 0 for ms, _ in seen.values())
+    assert np.array_equal(results[0][0], results[1][0])
+    assert np.array_equal(results[0][1], results[1][1])
+
+
 @pytest.fixture(scope="module")
 def group4_ckpt(tmp_path_factory):
     """GQA group 4 (the Qwen3.5 sizes' grouping), which selects the flash prefill attention for multi-row calls."""
