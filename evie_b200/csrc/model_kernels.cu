@@ -198,6 +198,74 @@ __global__ void __launch_bounds__(128) conv_silu_norm_kernel(YView y, int ldy,
   act[(size_t)r * conv_dim + c] = out;
 }
 
+// Decode form of the same conv (one row per segment, 4 taps): one warp per 128-channel head block, four consecutive
+// channels per lane (float4 loads and stores), so the q/k head norm reduces with warp shuffles and no CTA barrier.
+// Same products and sums as conv_silu_norm_kernel, bit for bit: the taps are accumulated in the same order, and the
+// shuffle tree below adds the squares in the order of block_sum<128> over one channel per thread. There, channel i of
+// a 32-channel group is lane i and the butterfly pairs i ^ 16, i ^ 8, i ^ 4, i ^ 2, i ^ 1. Here, channel i of the
+// group is element i % 4 of lane i / 4, so the first three levels are lane xors 4, 2, 1 and the last two are inside
+// the lane. The four group sums are then added in group order.
+__global__ void __launch_bounds__(128) conv_decode4_kernel(YView y, int ldy, const RowInfo* __restrict__ rows,
+                                                           const SegInfo* __restrict__ segs,
+                                                           float* __restrict__ conv_state, size_t cs_slot,
+                                                           const float* __restrict__ conv_w, int conv_dim, int hk,
+                                                           float qscale, float* __restrict__ act) {
+  constexpr int K = 4;
+  const int lane = threadIdx.x & 31;
+  const int blk = blockIdx.x * 4 + (threadIdx.x >> 5);  // 128-channel block of this warp
+  if (blk * 128 >= conv_dim) return;                    // the whole warp leaves together
+  const int c = blk * 128 + lane * 4;
+  const int r = blockIdx.y;
+  const SegInfo sg = segs[rows[r].seg];
+  const int t = r - sg.start;
+  float* cs = conv_state + (size_t)sg.slot * cs_slot;
+  float4 win[K];  // [state ; rows] inputs of this output, oldest first
+#pragma unroll
+  for (int j = 0; j < K; j++) {
+    const int tt = t - (K - 1) + j;
+    win[j] = tt >= 0 ? y.at4((size_t)(sg.start + tt) * ldy + c)
+                     : *reinterpret_cast<const float4*>(cs + (size_t)(K - 1 + tt) * conv_dim + c);
+  }
+  float4 w4[K];  // taps of channels c .. c + 3: w4[e] = conv_w[(c + e) * K + 0 .. 3]
+#pragma unroll
+  for (int e = 0; e < 4; e++) w4[e] = *reinterpret_cast<const float4*>(conv_w + (size_t)(c + e) * K);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < K; j++) {
+    const float u[4] = {win[j].x, win[j].y, win[j].z, win[j].w};
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float w = j == 0 ? w4[e].x : j == 1 ? w4[e].y : j == 2 ? w4[e].z : w4[e].w;
+      acc[e] += w * u[e];
+    }
+  }
+  // model.rs:339: the window keeps the last K-1 raw inputs; this lane is the only reader of its four channels
+#pragma unroll
+  for (int j = 1; j < K; j++) *reinterpret_cast<float4*>(cs + (size_t)(j - 1) * conv_dim + c) = win[j];
+  float out[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) out[e] = siluf_(acc[e]);
+  if (blk < 2 * hk) {  // q or k head: L2 normalise (kernels.rs dot + 1e-6), q also by 1/sqrt(dk)
+    float sq[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      sq[e] = out[e] * out[e];
+      sq[e] += __shfl_xor_sync(0xffffffffu, sq[e], 4);
+      sq[e] += __shfl_xor_sync(0xffffffffu, sq[e], 2);
+      sq[e] += __shfl_xor_sync(0xffffffffu, sq[e], 1);
+    }
+    const float grp = (sq[0] + sq[2]) + (sq[1] + sq[3]);  // one 32-channel group, in every lane of its 8
+    const float g0 = __shfl_sync(0xffffffffu, grp, 0), g1 = __shfl_sync(0xffffffffu, grp, 8);
+    const float g2 = __shfl_sync(0xffffffffu, grp, 16), g3 = __shfl_sync(0xffffffffu, grp, 24);
+    const float ss = ((g0 + g1) + g2) + g3;
+    const float inv = 1.0f / sqrtf(ss + 1e-6f);
+    const float scl = inv * (blk < hk ? qscale : 1.0f);
+#pragma unroll
+    for (int e = 0; e < 4; e++) out[e] *= scl;
+  }
+  *reinterpret_cast<float4*>(act + (size_t)r * conv_dim + c) = make_float4(out[0], out[1], out[2], out[3]);
+}
+
 // The same conv for segments of many rows (prefill): one CTA per (128-channel block, segment, 64 consecutive rows),
 // one thread per channel walking the rows with its K-1 previous inputs in registers, so every input is read once.
 // Same products, summation order and head-norm reduction as conv_silu_norm_kernel.
@@ -745,6 +813,15 @@ evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const
     conv_rows_kernel<4><<<grid, 128, 0, st>>>(y, ldy, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
                                               1.0f / sqrtf((float)s.dk), act);
     EVIE_CHECK_LAUNCH("conv_rows_kernel");
+    return EVIE_OK;
+  }
+  const auto a16 = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };
+  if (update_window && s.K == 4 && s.conv_dim % 128 == 0 && ldy % 4 == 0 && y.plane % 4 == 0 && cs_slot % 4 == 0 &&
+      a16(y.p) && a16(conv_state) && a16(conv_w) && a16(act)) {
+    dim3 grid((s.conv_dim + 511) / 512, R);
+    conv_decode4_kernel<<<grid, 128, 0, st>>>(y, ldy, rows, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
+                                              1.0f / sqrtf((float)s.dk), act);
+    EVIE_CHECK_LAUNCH("conv_decode4_kernel");
     return EVIE_OK;
   }
   dim3 grid(s.conv_dim / 128, R);
