@@ -927,6 +927,8 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
     EVIE_CUDA_TRY(cudaMemcpyAsync(resid, c->resid, (size_t)R * s.L * s.d * 2, cudaMemcpyDeviceToHost, st));
   EVIE_CUDA_TRY(cudaStreamSynchronize(st));
   prof_resolve(c);
+  if (c->prof && c->prof_failed)
+    return evie::fail(EVIE_ERR_CUDA, "forward: the profiling events could not be recorded or timed");
   if (capture) c->cap_rows = R;
   return EVIE_OK;
 }

@@ -123,9 +123,13 @@ EVIE_API evie_status evie_decode_greedy(evie_ctx* ctx, const evie_seq* seqs, int
 /* The CUDA stream (cudaStream_t) all of the context's work is enqueued on, for timing with CUDA events. */
 EVIE_API void* evie_stream(const evie_ctx* ctx);
 
-/* Profiling mode: when on, every kernel group of later calls is bracketed by CUDA events on the context's stream
- * and its device time accumulated per group (projection GEMMs, LM head, conv, DeltaNet mixer, attention prep,
- * attention, add+norm, SwiGLU, other). Turning it on or off clears the totals. */
+/* Profiling mode: when on, every kernel group of later calls is bracketed by CUDA events on the context's stream,
+ * and its device time is accumulated per group. The groups are: one per projection weight (DeltaNet input and
+ * output, attention input and output, MLP gate/up and down), LM head, conv, DeltaNet mixer, attention prep,
+ * attention, add+norm, SwiGLU, other. In evie_decode_greedy (without EVIE_NO_GRAPH) each step is captured as a
+ * graph of its own, with the events as event-record nodes, so a group is timed as a replayed step runs it. Each
+ * node adds a few microseconds. Other calls run eagerly. A call whose events cannot be recorded or timed returns
+ * EVIE_ERR_CUDA. Turning the mode on or off clears the totals. */
 EVIE_API evie_status evie_profile(evie_ctx* ctx, int on);
 /* Group i's name, accumulated milliseconds and number of bracketed launches; returns the number of groups
  * (0 when i is out of range). */
