@@ -446,8 +446,9 @@ __global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_seq_kernel(
 
   for (int t0 = 0; t0 < sg.count; t0 += kSeqChunk) {
     const int nt = min(kSeqChunk, sg.count - t0);
-    // ---- stage the chunk's inputs (rows of act and y for this head)
-#pragma unroll 1
+    // ---- stage the chunk's inputs (rows of act and y for this head); unrolled so that each thread has several
+    // loads in flight instead of waiting out one load per iteration
+#pragma unroll 4
     for (int i = tid; i < nt * 128; i += kMixThreads) {
       const int t = i >> 7, part = (i >> 5) & 3, j = (i & 31) * 4;  // per token: q, k, v, z, 32 float4 each
       const size_t row = (size_t)sg.start + t0 + t;
@@ -606,10 +607,11 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
   const int j0 = blockIdx.x * 1024 + threadIdx.x * 4;  // n is a multiple of 4
   const bool active = j0 < n;
   const size_t yr = (size_t)r * ldy;
-  float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), u4 = g4;
+  float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), u4 = g4, sc = g4;
   if (active) {  // issued before the row and steering lookups, which then overlap these loads
     g4 = y.at4(yr + j0);
     u4 = y.at4(yr + n + j0);
+    if (frames) sc = *reinterpret_cast<const float4*>(scale + (size_t)layer * n + j0);
   }
   const RowInfo ri = rows[r];
   if (threadIdx.x == 0) {
@@ -643,7 +645,6 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
   }
   store_split4(X2, xplane, (size_t)r * n + j0, make_float4(a[0], a[1], a[2], a[3]));
   if (frames) {
-    const float4 sc = *reinterpret_cast<const float4*>(scale + (size_t)layer * n + j0);
     const uint32_t packed = (uint32_t)(uint8_t)compand(a[0] / sc.x) | ((uint32_t)(uint8_t)compand(a[1] / sc.y) << 8) |
                             ((uint32_t)(uint8_t)compand(a[2] / sc.z) << 16) |
                             ((uint32_t)(uint8_t)compand(a[3] / sc.w) << 24);
