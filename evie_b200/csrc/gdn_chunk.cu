@@ -666,7 +666,43 @@ evie_status launch_gdn_chunk_prefill_bf16(const void* q, const void* k, const vo
   return EVIE_OK;
 }
 
+namespace {
+
+// One thread waits, bounded by `limit_ns`, on an mbarrier that nothing arrives at. That is the path every bounded
+// wait of these kernels takes when a copy or an MMA never completes: the wait gives up and the thread counts it
+// in the device counter that evie_poll_device_errors reads.
+__global__ void bounded_wait_probe_kernel(uint64_t limit_ns, unsigned int* timeouts, int* gave_up) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  tc::mbar_init(&bar, 1);
+  tc::fence_barrier_init();
+  const bool done = tc::mbar_wait_for(&bar, 0, limit_ns);
+  *gave_up = done ? 0 : 1;
+  if (!done) atomicAdd(timeouts, 1u);
+}
+
+}  // namespace
+
 }  // namespace evie
+
+extern "C" evie_status evie_bounded_wait_probe(uint64_t limit_ns, int* gave_up) {
+  if (!gave_up) return evie::fail(EVIE_ERR_ARG, "evie_bounded_wait_probe: null output");
+  if (limit_ns > evie::tc::kWaitNs)
+    return evie::fail(EVIE_ERR_ARG, "evie_bounded_wait_probe: limit above %llu ns",
+                      (unsigned long long)evie::tc::kWaitNs);
+  unsigned int* counter = evie::device_timeout_counter();
+  if (!counter) return evie::fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
+  int* d = nullptr;
+  EVIE_CUDA_TRY(cudaMalloc(&d, sizeof(int)));
+  evie::bounded_wait_probe_kernel<<<1, 32>>>(limit_ns, counter, d);
+  cudaError_t rc = cudaGetLastError();
+  int h = -1;
+  if (rc == cudaSuccess) rc = cudaMemcpy(&h, d, sizeof h, cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (rc != cudaSuccess) return evie::fail(EVIE_ERR_CUDA, "evie_bounded_wait_probe: %s", cudaGetErrorString(rc));
+  *gave_up = h;
+  return EVIE_OK;
+}
 
 extern "C" evie_status evie_poll_device_errors(void) {
   unsigned int* p = evie::device_timeout_counter();

@@ -44,14 +44,15 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with the given parity to complete; false if the deadline passed first.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Waits for the phase with the given parity to complete; false if `limit_ns` of %globaltimer passed first.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_test(bar, parity))
-    if (globaltimer() - t0 > kWaitNs) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   return true;
 }
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) { return mbar_wait_for(bar, parity, kWaitNs); }
 
 // 2-D TMA tile load into shared memory, completing on `bar` (x = innermost coordinate in elements; x times the
 // element size must be a multiple of 16 bytes).

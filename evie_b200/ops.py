@@ -99,6 +99,17 @@ def poll_device_errors() -> None:
     check(lib().evie_poll_device_errors())
 
 
+def bounded_wait_probe(limit_ns: int) -> int:
+    """Runs the failure path of the kernels' bounded waits (evie_bounded_wait_probe): one thread waits at most
+    limit_ns on an mbarrier that nothing completes and counts the give-up for poll_device_errors. Returns 1 if it
+    gave up."""
+    import ctypes as C
+
+    out = C.c_int(-1)
+    check(lib().evie_bounded_wait_probe(C.c_uint64(int(limit_ns)), C.byref(out)))
+    return out.value
+
+
 def gqa_decode_paged(q, gate, k_pages, v_pages, page_table, ctx_lens, scale, out=None):
     """Gated GQA decode attention over a paged bf16 KV cache (evie_gqa_decode_paged).
 

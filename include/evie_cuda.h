@@ -235,6 +235,11 @@ EVIE_API evie_status evie_gdn_prefill_tokenwise(const void* q, const void* k, co
  * count restarts at zero. Such a kernel drained its copies, freed its tensor memory and left its outputs
  * incomplete. */
 EVIE_API evie_status evie_poll_device_errors(void);
+/* Diagnostic for the failure path above (no reference counterpart; evie-core's backends have no device-side waits):
+ * one thread on the current device waits at most limit_ns (<= 2 s) on an mbarrier that nothing completes, gives
+ * up, counts the give-up for evie_poll_device_errors as the kernels do, and returns. *gave_up is 1 when it gave up.
+ * The device stays usable. */
+EVIE_API evie_status evie_bounded_wait_probe(uint64_t limit_ns, int* gave_up);
 
 /* Gated GQA softmax attention decode over a paged bf16 KV cache (the attention core of Model::attention,
  * model.rs:445-464; WGSL attn_scores/attn_out, gpu/kernels.wgsl:508-589), split-KV with an in-kernel combine:
