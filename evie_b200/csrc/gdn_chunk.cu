@@ -23,8 +23,9 @@
 //     that M = 128 runs along dv: TMEM lane j is row dv = j of each accumulator; warp w handles lane quarter w % 4
 //     and column half w / 4. Thread 0 issues their MMAs and all TMA loads.
 //   * Prep warps 8-15 work one chunk ahead on what does not depend on S: the decay sums, [K;Q] K^T (thread 256
-//     issues it), N, P and T. They hand a chunk over through an mbarrier (tp_ready) and wait for the chain to
-//     release the buffers two chunks later (chunk_done).
+//     issues it), N, P and T. They hand a chunk over through two mbarriers, the decays first (BDE, which the
+//     chain's output and state staging need) and then T and P (BTR, awaited just before the MMAs that read them).
+//     They wait for the chain to release the buffers two chunks later (BCD).
 // TMEM columns:
 //   [0,128)   S^T f32 [dv][dk], holding Gam_C S entering each chunk's update
 //   [128,256) the A operands of the chain's MMAs, bf16 pairs: S^T hi | S^T lo (64 + 64 columns) for S^T [K;Q]^T;
@@ -81,7 +82,7 @@ constexpr uint32_t kColRH = 128, kColRL = 160;                              // R
 constexpr uint32_t kColEH = 192, kColEL = 224;                              // (E U)^T planes
 
 // mbarriers
-enum { BK0 = 0, BK1, BQ0, BQ1, BV, BMC, BMP, BTR0, BTR1, BCD0, BCD1, kNumBars };
+enum { BK0 = 0, BK1, BQ0, BQ1, BV, BMC, BMP, BTR0, BTR1, BCD0, BCD1, BDE0, BDE1, kNumBars };
 constexpr uint32_t kChainBar = 1, kPrepBar = 2;  // named barriers of the two warp groups (256 threads each)
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -185,7 +186,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
   if (tid == 0) {
     for (int i = 0; i < kNumBars; i++)
-      tc::mbar_init(&bar[i], (i == BTR0 || i == BTR1 || i == BCD0 || i == BCD1) ? kGroup : 1);
+      tc::mbar_init(&bar[i], (i == BTR0 || i == BTR1 || i == BCD0 || i == BCD1) ? kGroup
+                             : (i == BDE0 || i == BDE1)                           ? 32
+                                                                                  : 1);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&mq);
     tc::prefetch_tmap(&mk);
@@ -274,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     if (nch > 0) {
-      wait(BTR0, 0);
+      wait(BDE0, 0);  // chunk 0's decays
       if (ok) stage_state(true, false, GamB[63]);
     }
     tc::fence_before_sync();
@@ -330,8 +333,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
-      // ---- U^T = R^T T^T (three passes; A from TMEM, B = T^T rows MN-major)
-      if (tid == 0) {
+      // ---- U^T = R^T T^T (three passes; A from TMEM, B = T^T rows MN-major); T and P of this chunk from the prep
+      wait(BTR0 + p, (c >> 1) & 1);
+      if (tid == 0 && ok) {
         if (c + 1 < nch) issue_v(c + 1);  // V has been consumed
         const uint32_t tm = kOffTM + p * 16384;
         int n = 0;
@@ -397,14 +401,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       wait(BMC, nmc & 1);
       nmc++;
+      // K/Q slot p was read by this chunk's MMAs (all complete) and by the prep's [stack] K^T of this chunk
+      // (consumed before it handed over T): refill it now, so the load overlaps the rest of the prep's next chunk.
+      if (tid == 0 && ok && c + 2 < nch) issue_kq(c + 2);
       tc::mbar_arrive(&bar[BCD0 + p]);  // T, P, Ec of this chunk are consumed: prep may refill buffer p
       const bool last = c + 1 == nch;
-      if (!last) wait(BTR0 + (p ^ 1), ((c + 1) >> 1) & 1);  // the next chunk's T, P and decays
+      // The output and the staging of the state need only the next chunk's decays (its T and P are awaited before
+      // they are read), so this stage overlaps the prep's N, P and T of the next chunk.
+      if (!last) wait(BDE0 + (p ^ 1), ((c + 1) >> 1) & 1);
       if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
       // ---- o_t = Gam_t (Q S)^T + (P U)^T for t in [32 hf, 32 hf + 32); the new state staged for the next chunk
-      if (tid == 0 && c + 2 < nch) issue_kq(c + 2);  // slot p: read by this chunk's MMAs, all complete
       {
         __nv_bfloat16* og = a.o + (((size_t)b * T + t0) * H + h) * kD + dv;
         const int nt = min(kC, T - t0);
@@ -485,6 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         Gam[2 * lane + 1] = ex2(e1);
         Ec[2 * lane] = ex2(lst - e0);
         Ec[2 * lane + 1] = ex2(lst - e1);
+        tc::mbar_arrive(&bar[BDE0 + p]);  // this chunk's decays are ready for the chain
         if (c + 1 < nch) fetch(c + 1);
       }
 
@@ -576,10 +585,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         store_row16(TM, 8192, lane, 3, x + 16);
       }
       tc::fence_proxy_async();
-      tc::mbar_arrive(&bar[BTR0 + p]);  // T, P and the decays of chunk c are ready
+      tc::mbar_arrive(&bar[BTR0 + p]);  // T and P of chunk c are ready
       // The A accumulator was consumed by this chunk's N/P: start the next chunk's [stack] K^T now, so that it runs
-      // while the buffers are awaited and the decays summed. (Its K/Q tiles are loaded by the chain only after it has
-      // taken this chunk's T, hence after the hand-over above.)
+      // while the buffers are awaited and the decays summed. (The chain loads its K/Q tiles once chunk c-1's MMAs
+      // are complete, which needs only chunk c-1's hand-over: no wait here depends on the prep itself.)
       if (c + 1 < nch) issue_a(c + 1);
     }
     if (!ok && pt == 0 && ((pend >> BMP) & 1u)) tc::mbar_wait(&bar[BMP], (ppar >> BMP) & 1u);
