@@ -453,7 +453,8 @@ class ModelDecode(Workload):
     every SwiGLU activation captured. A step is one greedy decode step of all B sequences."""
     name = "model_decode"
     kernel = "decode step (all kernels)"
-    dtype = "f32 activations x bf16 weights (split-bf16 operands), fp32 DeltaNet state, bf16 KV"
+    dtype = "f32"  # the arithmetic type; operands below
+    dtype_detail = "f32 activations x bf16 weights (split-bf16 operands), fp32 DeltaNet state, bf16 KV"
 
     def __init__(self, B=64, prompt=4096, rank=0):
         assert B % 2 == 0
@@ -848,6 +849,7 @@ def run_ours(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": w.dtype,
+        **({"dtype_detail": w.dtype_detail} if getattr(w, "dtype_detail", None) else {}),
         "data": "synthetic",
         "config": dict(w.config(), parallelism=f"dp{world}"),
         "clocks": clocks,
