@@ -143,6 +143,21 @@ def max_over_ranks(values, device=None):
     return t.tolist()
 
 
+def gather_to_rank0(arr, device=None):
+    """The equal-shaped int32 arrays of all ranks, stacked in rank order on rank 0 ([world, ...]); None on the other
+    ranks; arr[None] with one rank. One all-gather, the same step on every rank (NCCL on the GPUs, gloo on CPU)."""
+    import torch
+    import torch.distributed as dist
+
+    a = np.ascontiguousarray(arr, dtype=np.int32)
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return a[None].copy()
+    t = torch.from_numpy(a).to(device) if device is not None else torch.from_numpy(a)
+    parts = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, t)
+    return np.stack([x.cpu().numpy() for x in parts]) if dist.get_rank() == 0 else None
+
+
 # ------------------------------------------------------------------------------------------------------------
 # workloads
 
@@ -612,9 +627,15 @@ class ModelDecode(Workload):
     def run_device_steps(self, k):
         """k greedy decode steps kept on the device (evie_decode_greedy), captures written on the device."""
         toks = self.m.decode_greedy(self.seqs(), k, capture=True)
+        self.last_tokens = toks
         self.next = toks[-1].copy()
         self.pos += k
         return k
+
+    def results(self):
+        """What rank 0 collects after the timed region: the timed steps' token ids [steps, B] and, as the reduced
+        capture, the 16 most active neurons of each sequence's last timed step [B, 16]."""
+        return {"token_ids": self.last_tokens.view(np.int32), "top_active": self.m.top_active(16)}
 
     def step(self):
         return self.run_device_steps(1)
@@ -825,6 +846,10 @@ def run_ours(args):
             torch.cuda.profiler.stop()
     clocks = clk.summary()
     barrier()
+    # results to rank 0 (token ids and reduced captures), outside the timed region; every rank takes this step
+    gathered = None
+    if hasattr(w, "results"):
+        gathered = {k: gather_to_rank0(v, device=dev) for k, v in w.results().items()}
     e2e_ms, h2d, d2h = w.e2e(args.steps)
     kernels = None
     if hasattr(w, "profile_pass"):
@@ -882,6 +907,8 @@ def run_ours(args):
         line["roofline"] = {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                             "frac": ach / pk["bf16_tflops"], "traffic": profiled_traffic(w.kernel),
                             "kernel": w.kernel, "algorithmic_flops": alg, "peak_source": pk["source"]}
+    if rank == 0 and gathered:
+        line["gathered"] = {k: list(v.shape) for k, v in gathered.items()}
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = w.cpu_sample(int(os.environ.get("EVIE_CPU_THREADS", os.cpu_count() or 1)))
     if rank == 0:
