@@ -637,6 +637,9 @@ class ModelDecode(Workload):
         capture, the 16 most active neurons of each sequence's last timed step [B, 16]."""
         return {"token_ids": self.last_tokens.view(np.int32), "top_active": self.m.top_active(16)}
 
+    def result_shapes(self, steps):
+        return {"token_ids": (steps, self.B), "top_active": (self.B, 16)}
+
     def step(self):
         return self.run_device_steps(1)
 
@@ -849,7 +852,12 @@ def run_ours(args):
     # results to rank 0 (token ids and reduced captures), outside the timed region; every rank takes this step
     gathered = None
     if hasattr(w, "results"):
-        gathered = {k: gather_to_rank0(v, device=dev) for k, v in w.results().items()}
+        try:
+            res = w.results()
+        except Exception as e:  # still take the collective steps, with -1 in place of this rank's results
+            print(f"results unavailable on rank {rank}: {e}", file=sys.stderr)
+            res = {k: np.full(shp, -1, np.int32) for k, shp in w.result_shapes(args.steps).items()}
+        gathered = {k: gather_to_rank0(v, device=dev) for k, v in res.items()}
     e2e_ms, h2d, d2h = w.e2e(args.steps)
     kernels = None
     if hasattr(w, "profile_pass"):
