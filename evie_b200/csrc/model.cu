@@ -336,7 +336,12 @@ struct ProfScope {
     if (c->prof) {
       cudaEvent_t b = c->prof_event();
       prof_record(c, b);
-      if (a && b) c->prof_pending.push_back({cat, {a, b}});
+      if (a && b) {
+        c->prof_pending.push_back({cat, {a, b}});
+      } else {  // one of the pair could not be created: return the other to the pool
+        if (a) c->prof_free.push_back(a);
+        if (b) c->prof_free.push_back(b);
+      }
     }
   }
 };
