@@ -129,3 +129,27 @@ def test_chunked_forms_match_token_recurrence(T, H, s0, form):
             S, o = run(S0, q[:, h], k[:, h], v[:, h], g[:, h], beta[:, h], split)
             assert _rel(S, S_ref[0, h]) < tol, (form, split, _rel(S, S_ref[0, h]))
             assert _rel(o, o_ref[0, :, h]) < tol, (form, split, _rel(o, o_ref[0, :, h]))
+
+
+def test_blocked_triangular_solve_forms_agree():
+    """T = (I + N)^-1 diag(beta) in 32-row blocks. The diagonal blocks T11, T22 come from forward substitution.
+    The off-diagonal block either comes from (I + N22) T21 = -N21 T11 by substitution, as the kernel solves it, or
+    is the product -T22 (M21 T11). Here M21 is N21 without its beta_t factors (the rows of (I + N22)^-1 = T22
+    diag(1/beta_2)), so that form needs no division by beta. Both equal the corresponding block of the direct
+    inverse."""
+    x = gdn_prefill_inputs(1, 64, 1, 11)
+    K = x["k"].float().numpy()[0, :, 0].astype(np.float64)
+    g, beta = x["g"].numpy()[0, :, 0].astype(np.float64), x["beta"].numpy()[0, :, 0].astype(np.float64)
+    G = np.cumsum(g)
+    t, s = np.meshgrid(np.arange(64), np.arange(64), indexing="ij")
+    M = np.where(s < t, (K @ K.T) * np.exp(np.minimum(G[:, None] - G[None, :], 0.0)), 0.0)  # without beta
+    N = beta[:, None] * M
+    T = np.linalg.solve(np.eye(64) + N, np.diag(beta))
+    h = slice(0, 32), slice(32, 64)
+    T11 = np.linalg.solve(np.eye(32) + N[h[0], h[0]], np.diag(beta[h[0]]))
+    T22 = np.linalg.solve(np.eye(32) + N[h[1], h[1]], np.diag(beta[h[1]]))
+    T21_sub = np.linalg.solve(np.eye(32) + N[h[1], h[1]], -N[h[1], h[0]] @ T11)
+    T21_prod = -T22 @ (M[h[1], h[0]] @ T11)
+    ref = T[h[1], h[0]]
+    assert np.allclose(T11, T[h[0], h[0]], rtol=0, atol=1e-12) and np.allclose(T22, T[h[1], h[1]], rtol=0, atol=1e-12)
+    assert _rel(T21_sub, ref) < 1e-12 and _rel(T21_prod, ref) < 1e-12
