@@ -78,9 +78,10 @@ evie_status k_add_final(float* x, YView y, int ldy, int R, const RowInfo* rows, 
                         int cap_layer, int L, cudaStream_t st);
 // Causal depthwise conv over [conv state ; new rows] + SiLU, then L2 norm of the q and k heads (q also 1/sqrt(dk)).
 // conv_state points at this layer's window of slot 0; cs_slot is the element stride between slots.
-// update_window: every segment has exactly one row (decode); each thread then also shifts its channel's conv window
-// (replacing k_conv_state_update). With max_seg_rows > 1 (and a 4-tap conv) a sliding-window kernel walks each
-// segment's rows in blocks of 64.
+// update_window: every segment has exactly one row (decode); the kernel then also shifts the conv windows in place
+// (replacing k_conv_state_update). For a 4-tap conv with 16-byte aligned operands that is a warp per 128-channel
+// head block with four channels per lane; otherwise one thread per channel. With max_seg_rows > 1 (and a 4-tap
+// conv) a sliding-window kernel walks each segment's rows in blocks of 64.
 evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
                              float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
                              float* act, cudaStream_t st, bool update_window, int nseg = 0, int max_seg_rows = 0);
