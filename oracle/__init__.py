@@ -72,6 +72,7 @@ def _declare(L):
         "oracle_gqa_decode": (None, [I, I, I, I, I, P, P, P, P, I, P, P, F, P]),
         "oracle_model_new": (P, [P, P]),
         "oracle_model_free": (None, [P]),
+        "oracle_model_kv_bf16": (None, [P, I, F]),
         "oracle_model_set": (I, [P, I, I, P, I, LG, LG]),
         "oracle_cache_new": (P, [P]),
         "oracle_cache_free": (None, [P]),
@@ -351,7 +352,12 @@ _VECS = {
 class Model:
     """model.rs:137-203 over the oracle engine."""
 
-    def __init__(self, ckpt_dir: str):
+    def __init__(self, ckpt_dir: str, kv_bf16: bool = False, kv_perturb: float = 0.0):
+        """kv_bf16: round every appended key and value to bf16 (the GPU's paged-cache format), the oracle's one
+        documented deviation from model.rs:441-442, which appends f32 rows. Off by default.
+        kv_perturb (with kv_bf16): scale each key and value by 1 + kv_perturb * r, r uniform in [-1, 1) from a fixed
+        generator, before rounding. A test aid that measures how far the bf16 rounding alone moves the logits when
+        the values before rounding differ at the level of f32 reordering."""
         self.cfg = load_config(os.path.join(ckpt_dir, "config.json"))
         self.st = SafeTensors(ckpt_dir)
         if self.st.has("model.language_model.embed_tokens.weight"):
@@ -365,6 +371,7 @@ class Model:
                   c.rotary_dim, c.rope_theta, c.conv_kernel, c.lin_k_heads, c.lin_v_heads, c.lin_k_dim, c.lin_v_dim)
         kinds = (C.c_int * c.n_layers)(*[0 if k == "linear" else 1 for k in c.layer_kinds])
         self._h = lib().oracle_model_new(C.byref(cc), kinds)
+        lib().oracle_model_kv_bf16(self._h, 1 if kv_bf16 else 0, float(kv_perturb))
         self._keep = []
         embed = self.st.mat16(prefix + "embed_tokens.weight")
         if embed.shape[0] < c.vocab or embed.shape[1] != c.hidden:

@@ -570,7 +570,23 @@ struct Model {
   Mat embed, lm_head;
   std::vector<LayerW> layers;
   std::vector<float> final_norm, inv_freq;
+  // The one documented deviation from model.rs, off by default: round each appended key and value to bf16
+  // (round to nearest even), the storage format of the GPU's paged KV cache. model.rs:441-442 appends f32 rows.
+  bool kv_bf16 = false;
+  // Test aid for the bf16 cache's sensitivity: before rounding, scale each appended key and value by
+  // (1 + kv_perturb * r), r uniform in [-1, 1) from a fixed generator. 0 (the default) leaves the values as they are.
+  float kv_perturb = 0.0f;
+  uint64_t kv_rng = 0x9E3779B97F4A7C15ull;
 };
+
+// f32 -> bf16 -> f32, round to nearest even (the rounding of the GPU cache's __float2bfloat16_rn); finite inputs.
+inline float round_bf16(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
+  memcpy(&x, &u, 4);
+  return x;
+}
 
 struct LayerCache {
   std::vector<float> conv, state;  // linear
@@ -789,6 +805,19 @@ void attention(const Model& m, const AttnW& at, int li, const float* h, long tot
       }
     });
     LayerCache& lc = seqs[s].cache->layers[li];
+    if (m.kv_bf16) {
+      Model& mm = const_cast<Model&>(m);
+      auto jitter = [&](float x) {
+        if (mm.kv_perturb == 0.0f) return x;
+        mm.kv_rng = mm.kv_rng * 6364136223846793005ull + 1442695040888963407ull;
+        const float r = (float)((mm.kv_rng >> 40) & 0xffffff) / 8388608.0f - 1.0f;
+        return x * (1.0f + mm.kv_perturb * r);
+      };
+      for (size_t i = (size_t)r0 * nkv * hd; i < (size_t)(r0 + nrows) * nkv * hd; i++) {
+        kk[i] = round_bf16(jitter(kk[i]));
+        vv[i] = round_bf16(jitter(vv[i]));
+      }
+    }
     lc.k.insert(lc.k.end(), kk.begin() + (size_t)r0 * nkv * hd, kk.begin() + (size_t)(r0 + nrows) * nkv * hd);
     lc.v.insert(lc.v.end(), vv.begin() + (size_t)r0 * nkv * hd, vv.begin() + (size_t)(r0 + nrows) * nkv * hd);
     const float* kc = lc.k.data();
@@ -1092,6 +1121,12 @@ EXPORT void* oracle_model_new(const oracle_cfg* c, const int* kinds) {
   return m;
 }
 EXPORT void oracle_model_free(void* p) { delete (Model*)p; }
+// Switches the bf16 rounding of appended keys and values (Model::kv_bf16) on or off, with the optional relative
+// jitter before rounding (Model::kv_perturb).
+EXPORT void oracle_model_kv_bf16(void* p, int on, float perturb) {
+  ((Model*)p)->kv_bf16 = on != 0;
+  ((Model*)p)->kv_perturb = perturb;
+}
 
 // Registers one tensor. Matrices are bf16 views (the caller keeps the memory alive); vectors are copied
 // as f32 with the load-time transforms of model.rs:148,171 (1+w norms, -exp(A_log)).
