@@ -70,6 +70,7 @@ SIGNATURES = {
     "evie_gdn_decode_step": (I, [P, P, P, P, P, P, P, I, I, I, I, P]),
     "evie_gdn_chunk_prefill": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, P]),
     "evie_gdn_prefill_tokenwise": (I, [P, P, P, P, P, P, P, I, I, I, I, I, P]),
+    "evie_proj_gemm": (I, [P, P, P, SZ, I, I, I, I, P, P]),
     "evie_poll_device_errors": (I, []),
     "evie_bounded_wait_probe": (I, [C.c_uint64, P]),
     "evie_gqa_decode_paged": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, F, P]),

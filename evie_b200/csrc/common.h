@@ -14,6 +14,9 @@
 
 namespace evie {
 
+// Device ordinals the library's per-device tables cover (0 .. kMaxDevices - 1).
+constexpr int kMaxDevices = 64;
+
 // Message of the last failure on this host thread (calls without a context, and context creation).
 std::string& thread_error();
 
@@ -41,10 +44,27 @@ inline evie_status fail(evie_status code, const char* fmt, ...) {
     if (e_ != cudaSuccess) return ::evie::fail(EVIE_ERR_CUDA, "launch of %s: %s", name, cudaGetErrorString(e_)); \
   } while (0)
 
+#define EVIE_TRY(expr)                  \
+  do {                                  \
+    evie_status s_ = (expr);            \
+    if (s_ != EVIE_OK) return s_;       \
+  } while (0)
+
 #define EVIE_ARG(cond, ...)                                  \
   do {                                                       \
     if (!(cond)) return ::evie::fail(EVIE_ERR_ARG, __VA_ARGS__); \
   } while (0)
+
+// Lets the next kernel in the stream start early when it was launched with programmatic stream serialisation (the
+// projection GEMM, which streams its first weight tiles before it waits for this grid to complete). Kernels call it
+// first; a kernel launched without that attribute after this one is unaffected.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Raises the dynamic shared-memory limit of kernel `fn` to `bytes` on the current device, once per (kernel, device);
+// safe to call from several host threads.
+evie_status max_dynamic_smem(const void* fn, int bytes);
+// Sets kernel attribute `attr` of `fn` to `value` on the current device, once per (kernel, device, attribute, value).
+evie_status func_attr(const void* fn, cudaFuncAttribute attr, int value);
 
 __device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ float bfbits2f(uint32_t bits16) { return __uint_as_float(bits16 << 16); }

@@ -1,7 +1,25 @@
-// Error-message storage behind evie_last_global_error().
+// Error-message storage behind evie_last_global_error(), and the per-device kernel attribute cache.
+#include <mutex>
+#include <set>
+#include <tuple>
+
 #include "common.h"
 
 namespace evie {
+evie_status func_attr(const void* fn, cudaFuncAttribute attr, int value) {
+  int dev = 0;
+  EVIE_CUDA_TRY(cudaGetDevice(&dev));
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int, int>> done;  // (kernel, device, attribute, value) already set
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({fn, dev, (int)attr, value})) return EVIE_OK;
+  EVIE_CUDA_TRY(cudaFuncSetAttribute(fn, attr, value));
+  done.insert({fn, dev, (int)attr, value});
+  return EVIE_OK;
+}
+evie_status max_dynamic_smem(const void* fn, int bytes) {
+  return func_attr(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
 std::string& thread_error() {
   thread_local std::string msg;
   return msg;

@@ -638,8 +638,8 @@ evie_status token_major_map(CUtensorMap* m, const void* base, int B, int T, int 
 
 unsigned int* device_timeout_counter() {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  static unsigned int* ptrs[64] = {};
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  static unsigned int* ptrs[kMaxDevices] = {};
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
   if (!ptrs[dev]) {
@@ -661,14 +661,7 @@ evie_status launch_gdn_chunk_prefill_bf16(const void* q, const void* k, const vo
   if ((s = token_major_map(&mv, v, B, T, H, 128, CU_TENSOR_MAP_SWIZZLE_NONE)) != EVIE_OK) return s;
   unsigned int* counter = device_timeout_counter();
   if (!counter) return fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
-  int dev = 0;
-  EVIE_CUDA_TRY(cudaGetDevice(&dev));
-  static bool attr_set[64] = {};
-  if (dev < 64 && !attr_set[dev]) {
-    EVIE_CUDA_TRY(
-        cudaFuncSetAttribute(gdn_chunk_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    attr_set[dev] = true;
-  }
+  EVIE_TRY(max_dynamic_smem((const void*)gdn_chunk_prefill_kernel, (int)kSmemBytes));
   ChunkArgs a{g, beta, state, static_cast<__nv_bfloat16*>(o), T, H, counter};
   gdn_chunk_prefill_kernel<<<B * H, kThreads, kSmemBytes, st>>>(mq, mk, mv, a);
   EVIE_CHECK_LAUNCH("gdn_chunk_prefill_kernel");

@@ -127,6 +127,7 @@ template <int GROUP, typename KV, class IO>
 __global__ void __launch_bounds__(kThreads, 2)
     gqa_decode_kernel(IO io, const KV* __restrict__ kp, const KV* __restrict__ vp, int Hkv, int page_size,
                       int max_pages, float scale, Scratch scr) {
+  pdl_trigger();
   constexpr int kTokIter = 32 / GROUP;  // tokens per reduce-scatter round
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
@@ -373,6 +374,7 @@ template <class IO>
 __global__ void __launch_bounds__(kThreads, 2)
     gqa_decode_mma_kernel(IO io, const __nv_bfloat16* __restrict__ kp, const __nv_bfloat16* __restrict__ vp, int Hkv,
                           int page_size, int max_pages, float scale, Scratch scr) {
+  pdl_trigger();
   constexpr int GROUP = 4;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -642,6 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gqa_decode_bulk_kernel(IO io, const __nv_bfloat16* __restrict__ kp, const __nv_bfloat16* __restrict__ vp,
                            int Hkv, int page_size, int max_pages, float scale, Scratch scr,
                            unsigned int* timeouts) {
+  pdl_trigger();
   constexpr int GROUP = 4;
   extern __shared__ __align__(128) uint8_t ring_all[];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -848,7 +851,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (nt + t + kStages < 2 * nt) issue(nt + t + kStages);
   }
-  // every copy this warp issued has been waited for (consumed == issued); after a give-up, let them land first
+  // Every copy this warp issued has been waited for (consumed == issued). After a give-up the warp waits for the
+  // outstanding ones once more, again bounded by kWaitNs; if that wait gives up too, a copy may still land in the
+  // ring while the warp writes sO below or after the CTA exits, and this split's outputs are undefined (the call
+  // already reports EVIE_ERR_TIMEOUT through the device counter).
   ok = __all_sync(0xffffffffu, ok);
   if (!ok) {
     for (int n = consumed; n < issued; n++) tc::mbar_wait(&bar[n % kStages], (n / kStages) & 1);
@@ -1022,14 +1028,7 @@ evie_status launch_gqa(const IO& io, const KV* kp, const KV* vp, int B, int Hq, 
       if (bulk_enabled()) {
         unsigned int* counter = device_timeout_counter();
         if (!counter) return fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
-        int dev = 0;
-        EVIE_CUDA_TRY(cudaGetDevice(&dev));
-        static bool attr_set[64] = {};
-        if (dev < 64 && !attr_set[dev]) {
-          EVIE_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_bulk_kernel<IO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kRingBytes));
-          attr_set[dev] = true;
-        }
+        EVIE_TRY(max_dynamic_smem((const void*)gqa_decode_bulk_kernel<IO>, kRingBytes));
         gqa_decode_bulk_kernel<IO><<<grid, kThreads, kRingBytes, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale,
                                                                         scr, counter);
         EVIE_CHECK_LAUNCH("gqa_decode_bulk_kernel");
@@ -1094,12 +1093,13 @@ static __device__ __align__(256) unsigned char g_gqa_noalloc_scratch[kNoAllocScr
 // fault (or silently use the wrong memory where the GPU can reach host memory). The device address is looked up once
 // per device, with that device current, on the first call there.
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[128] = {};
+void* g_noalloc_addr[kMaxDevices] = {};
 
 evie_status noalloc_scratch(void** out) {
   int dev = 0;
   EVIE_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 128) return fail(EVIE_ERR_ARG, "evie_gqa_decode_paged_noalloc: device %d out of range", dev);
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(EVIE_ERR_ARG, "evie_gqa_decode_paged_noalloc: device %d out of range (0..%d)", dev, kMaxDevices - 1);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_addr[dev]) {
     void* p = nullptr;
@@ -1132,9 +1132,10 @@ evie_status launch_gqa_decode_bf16_noalloc(const void* q, const void* gate, cons
   if (need > kNoAllocScratchBytes)
     return fail(EVIE_ERR_ARG,
                 "evie_gqa_decode_paged_noalloc: these sizes need %zu bytes of split scratch, more than its fixed %zu "
-                "(B x Hkv x ceil(max_pages x page_size / 512) must stay at most %zu); use evie_gqa_decode_paged",
+                "(sizes with B x Hkv x ceil(max_pages x page_size / 512) at most %zu always fit); use "
+                "evie_gqa_decode_paged",
                 need, kNoAllocScratchBytes,
-                (kNoAllocScratchBytes - 256) / ((size_t)group * (kHD + 2) * sizeof(float)));
+                (kNoAllocScratchBytes - 255) / (sizeof(int) + (size_t)group * (kHD + 2) * sizeof(float)));
   void* base = nullptr;
   evie_status rc = noalloc_scratch(&base);
   if (rc != EVIE_OK) return rc;

@@ -53,6 +53,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        size_t xplane, const RowInfo* __restrict__ rows, const SegInfo* __restrict__ segs,
                        const int* __restrict__ page_table, int pages_per_slot, const __nv_bfloat16* __restrict__ kc,
                        const __nv_bfloat16* __restrict__ vc, int Hq, int Hkv, int page_size, float scale) {
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t sm[];
   const int kvh = blockIdx.z;
   const SegInfo sg = segs[blockIdx.y];
@@ -274,13 +275,7 @@ evie_status launch_gqa_prefill_model(const float* q_rot, YView y, int ldy, __nv_
   if (nseg == 0 || max_seg_rows == 0) return EVIE_OK;
   if (Hq != kGroup * Hkv) return fail(EVIE_ERR_ARG, "prefill attention: GQA group %d not supported (4)", Hq / Hkv);
   if (page_size % kTile != 0) return fail(EVIE_ERR_ARG, "prefill attention: page size must be a multiple of %d", kTile);
-  int dev = 0;
-  EVIE_CUDA_TRY(cudaGetDevice(&dev));
-  static bool attr_set[64] = {};
-  if (dev < 64 && !attr_set[dev]) {
-    EVIE_CUDA_TRY(cudaFuncSetAttribute(gqa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-    attr_set[dev] = true;
-  }
+  EVIE_TRY(max_dynamic_smem((const void*)gqa_prefill_kernel, (int)kSmem));
   dim3 grid((max_seg_rows + kRowsPerCta - 1) / kRowsPerCta, nseg, Hkv);
   gqa_prefill_kernel<<<grid, kThreads, kSmem, st>>>(q_rot, y, ldy, X2, xplane, rows, segs, page_table, pages_per_slot,
                                                     kc, vc, Hq, Hkv, page_size, scale);

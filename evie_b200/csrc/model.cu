@@ -34,6 +34,7 @@
 #include "json.h"
 #include "gdn_chunk.h"
 #include "model_kernels.h"
+#include "proj_gemm.h"
 #include "sampler.h"
 
 using evie::RowInfo;
@@ -230,7 +231,9 @@ struct evie_ctx {
   __nv_bfloat16* X2 = nullptr;
   float* Y2 = nullptr;
   size_t y2_cols = 0;  // Y2 holds 2 * max_rows rows of y2_cols floats
-  int ksplit = 4;      // K slices of the residual-feeding projections (EVIE_GEMM_KSPLIT overrides, 1..8)
+  bool pdl = true;     // projection GEMMs use programmatic dependent launch (EVIE_NO_PDL=1 at creation: off)
+  int max_planes = evie::YView::kMaxPlanes;  // K slices per projection at most (EVIE_GEMM_PLANES=1..16 at creation)
+  size_t y2_cap() const { return (size_t)2 * max_rows * y2_cols; }
   bool attn_rowwise = false;  // EVIE_ATTN_ROWWISE=1 at creation: prefill rows use the per-row split-KV kernel too
   bool no_graph = false;      // EVIE_NO_GRAPH=1 at creation: decode-shaped calls run eagerly
   // Captured decode-shaped forward calls, keyed by (sequences, want logits, head, capture, tracking, context bound).
@@ -614,7 +617,8 @@ evie_status allocate_state(evie_ctx* c) {
   TRY(c->alloc(&c->X2, 2 * R * kmax));
   TRY(c->alloc(&c->Y2, 2 * R * mmax));
   c->y2_cols = mmax;
-  if (const char* e = getenv("EVIE_GEMM_KSPLIT")) c->ksplit = std::min(8, std::max(1, atoi(e)));
+  if (const char* e = getenv("EVIE_NO_PDL")) c->pdl = e[0] != '1';
+  if (const char* e = getenv("EVIE_GEMM_PLANES")) c->max_planes = std::min(evie::YView::kMaxPlanes, std::max(1, atoi(e)));
   if (const char* e = getenv("EVIE_ATTN_ROWWISE")) c->attn_rowwise = e[0] == '1';
   if (const char* e = getenv("EVIE_NO_GRAPH")) c->no_graph = e[0] == '1';
   TRY(c->alloc(&c->act, R * s.conv_dim));
@@ -638,36 +642,17 @@ evie_status allocate_state(evie_ctx* c) {
   return EVIE_OK;
 }
 
-// Y = X . W^T for the R rows of the split operand X2 ([2][R][K] bf16): one cuBLAS GEMM over both planes (fp32
-// accumulation); the result is the two planes of *out, which consumers add. With ksplit > 1 the K range is cut into
-// ksplit slices, computed as one strided-batched GEMM whose 2 * ksplit output planes are contiguous R x M blocks
-// (slice i, operand plane j at plane 2 i + j): ksplit times as many CTAs stream the weight, and the consumer's plane
-// sum is the split-K reduction. Used for the narrow (M = d) projections that feed the residual add.
+// Y = X . W^T for the R rows of the split operand X2 ([2][R][K] bf16) on the tcgen05 projection GEMM (proj_gemm.cu):
+// the hi and lo products accumulate in one f32 accumulator, so each K slice leaves one plane; decode-shaped calls cut
+// K into as many slices as fill the SMs, and the consumer adds the planes in slice order (the split-K reduction).
+// `cap` is the number of floats at Y2. Launched with programmatic stream serialisation (unless EVIE_NO_PDL=1), so
+// that its first weight tiles stream while the previous kernel finishes.
 evie_status gemm(evie_ctx* c, const __nv_bfloat16* W, int M, int K, const __nv_bfloat16* X2, int R, float* Y2,
-                 evie::YView* out, int ksplit = 1) {
-  const float one = 1.0f, zero = 0.0f;
-  cublasStatus_t st;
-  if (ksplit > 1) {
-    const int ks = K / ksplit;
-    st = cublasGemmStridedBatchedEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, M, 2 * R, ks, &one, W, CUDA_R_16BF, K, ks,
-                                    X2, CUDA_R_16BF, K, ks, &zero, Y2, CUDA_R_32F, M, (long long)2 * R * M, ksplit,
-                                    CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-  } else {
-    st = cublasGemmEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, M, 2 * R, K, &one, W, CUDA_R_16BF, K, X2, CUDA_R_16BF, K,
-                      &zero, Y2, CUDA_R_32F, M, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-  }
-  if (st != CUBLAS_STATUS_SUCCESS)
-    return evie::fail(EVIE_ERR_CUDA, "cuBLAS GEMM (%d x %d x %d, %d slices): status %d", M, 2 * R, K, ksplit, (int)st);
-  *out = evie::YView{Y2, (size_t)R * M, 2 * ksplit};
+                 size_t cap, evie::YView* out) {
+  int planes = 0;
+  TRY(evie::launch_proj_gemm(W, M, K, X2, R, Y2, cap, c->max_planes, c->pdl, c->stream, &planes));
+  *out = evie::YView{Y2, (size_t)R * M, planes};
   return EVIE_OK;
-}
-
-// K slices for a residual-feeding projection of depth K: as many as fit the consumer's plane limit and the Y2
-// buffer, with 16-byte aligned slice starts.
-int residual_ksplit(const evie_ctx* c, int K) {
-  int ks = c->ksplit;
-  while (ks > 1 && (K % ks != 0 || (K / ks) % 8 != 0 || (size_t)ks * c->s.d > c->y2_cols)) ks--;
-  return ks;
 }
 
 // gpu/mod.rs:616-634: limits, then the row and segment tables uploaded for the kernels.
@@ -753,7 +738,7 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
     evie::YView yo;  // output projection of the mixer
     if (L.kind == 0) {
       evie::YView y;
-      { PROF(P_GEMM_LIN_IN); TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2, &y)); }
+      { PROF(P_GEMM_LIN_IN); TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2, c->y2_cap(), &y)); }
       float* cs = c->conv_state + (size_t)L.idx * (s.K - 1) * s.conv_dim;
       {
         PROF(P_CONV);
@@ -771,10 +756,10 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
         TRY(evie::k_gdn_mixer(c->act, y, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm,
                               s, c->X2, st));
       }
-      { PROF(P_GEMM_LIN_OUT); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2, &yo, residual_ksplit(c, s.vd))); }
+      { PROF(P_GEMM_LIN_OUT); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2, c->y2_cap(), &yo)); }
     } else {
       evie::YView y;
-      { PROF(P_GEMM_ATT_IN); TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2, &y)); }
+      { PROF(P_GEMM_ATT_IN); TRY(gemm(c, L.w_in, s.in_at, s.d, c->X2, R, c->Y2, c->y2_cap(), &y)); }
       const float scale = 1.0f / sqrtf((float)s.hd);
       if (c->kv_f32) {
         float* kc = (float*)c->k_cache + (size_t)L.idx * kv_layer;
@@ -812,19 +797,19 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
                                                     scale, c->attn_scratch, c->max_rows, st));
         }
       }
-      { PROF(P_GEMM_ATT_OUT); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2, &yo, residual_ksplit(c, s.nh * s.hd))); }
+      { PROF(P_GEMM_ATT_OUT); TRY(gemm(c, L.w_out, s.d, s.nh * s.hd, c->X2, R, c->Y2, c->y2_cap(), &yo)); }
     }
     // model.rs:246-248: residual add after the mixer, then the pre-MLP norm
     { PROF(P_NORM); TRY(evie::k_add_norm(c->x, yo, s.d, R, L.ln2, s.eps, s.d, c->X2, nullptr, 0, s.L, st)); }
     evie::YView yg, yd;
-    { PROF(P_GEMM_GATE_UP); TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2, &yg)); }
+    { PROF(P_GEMM_GATE_UP); TRY(gemm(c, L.w_gu, 2 * s.n, s.d, c->X2, R, c->Y2, c->y2_cap(), &yg)); }
     {
       PROF(P_SWIGLU);
       if (c->gate_layers[li]) TRY(evie::k_gate_detect(yg, 2 * s.n, c->d_segs, nseq, li, s, gt, st));
       TRY(evie::k_swiglu(yg, 2 * s.n, R, c->d_rows, li, s, steer, c->scale, fr, c->track ? c->maxbuf : nullptr,
                          c->X2, st));
     }
-    { PROF(P_GEMM_DOWN); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2, &yd, residual_ksplit(c, s.n))); }
+    { PROF(P_GEMM_DOWN); TRY(gemm(c, L.w_down, s.d, s.n, c->X2, R, c->Y2, c->y2_cap(), &yd)); }
     {
       PROF(P_NORM);
       if (li + 1 < s.L) {
@@ -859,7 +844,7 @@ evie_status join_captures(evie_ctx* c) {
 // model.rs:271-283: LM head on the last row of every sequence; greedy id (sampling.rs:60-62) on device.
 evie_status enqueue_head(evie_ctx* c, int nseq, bool want_logits) {
   evie::YView yl;
-  { PROF(P_LMHEAD); TRY(gemm(c, c->lm_head, c->s.V, c->s.d, c->X2, nseq, c->L2, &yl)); }
+  { PROF(P_LMHEAD); TRY(gemm(c, c->lm_head, c->s.V, c->s.d, c->X2, nseq, c->L2, (size_t)2 * c->slots * c->s.V, &yl)); }
   PROF(P_OTHER);
   TRY(evie::k_logits_argmax(yl, nseq, c->s.V, want_logits ? c->logits : nullptr, c->best, c->next, c->stream));
   if (!c->samp_active) return EVIE_OK;

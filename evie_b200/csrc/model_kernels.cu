@@ -40,6 +40,7 @@ __global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowInfo*
                                                                   float eps, int d, __nv_bfloat16* __restrict__ X2,
                                                                   size_t xplane, uint32_t* __restrict__ seen,
                                                                   int seen_words) {
+  pdl_trigger();
   __shared__ float red[kNormThreads / 32];
   const int r = blockIdx.x;
   const RowInfo ri = rows[r];
@@ -141,6 +142,7 @@ __global__ void __launch_bounds__(1024) add_norm_kernel(float* __restrict__ x, Y
                                                         const float* __restrict__ gain, float eps, int d,
                                                         __nv_bfloat16* __restrict__ X2, size_t xplane,
                                                         uint16_t* __restrict__ resid, int cap_layer, int L) {
+  pdl_trigger();
   __shared__ float red[32];
   const int r = blockIdx.x;
   add_norm_row(x, y, ldy, r, d, gain, eps, X2, xplane, r, true, resid, cap_layer, L, red);
@@ -153,6 +155,7 @@ __global__ void __launch_bounds__(1024) add_final_kernel(float* __restrict__ x, 
                                                          const float* __restrict__ gain, float eps, int d,
                                                          __nv_bfloat16* __restrict__ X2,
                                                          uint16_t* __restrict__ resid, int cap_layer, int L) {
+  pdl_trigger();
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int s = rows[r].seg;
@@ -169,6 +172,7 @@ __global__ void __launch_bounds__(128) conv_silu_norm_kernel(YView y, int ldy,
                                                              const float* __restrict__ conv_w, int K, int conv_dim,
                                                              int hk, float qscale, float* __restrict__ act,
                                                              bool update_window) {
+  pdl_trigger();
   __shared__ float red[4];
   const int c = blockIdx.x * 128 + threadIdx.x;
   const int r = blockIdx.y;
@@ -210,6 +214,7 @@ __global__ void __launch_bounds__(128) conv_decode4_kernel(YView y, int ldy, con
                                                            float* __restrict__ conv_state, size_t cs_slot,
                                                            const float* __restrict__ conv_w, int conv_dim, int hk,
                                                            float qscale, float* __restrict__ act) {
+  pdl_trigger();
   constexpr int K = 4;
   const int lane = threadIdx.x & 31;
   const int blk = blockIdx.x * 4 + (threadIdx.x >> 5);  // 128-channel block of this warp
@@ -275,6 +280,7 @@ __global__ void __launch_bounds__(128) conv_rows_kernel(YView y, int ldy, const 
                                                         const float* __restrict__ conv_state, size_t cs_slot,
                                                         const float* __restrict__ conv_w, int conv_dim, int hk,
                                                         float qscale, float* __restrict__ act) {
+  pdl_trigger();
   __shared__ float red[4];
   const int c = blockIdx.x * 128 + threadIdx.x;
   const SegInfo sg = segs[blockIdx.y];
@@ -313,6 +319,7 @@ __global__ void __launch_bounds__(128) conv_rows_kernel(YView y, int ldy, const 
 __global__ void conv_state_update_kernel(YView y, int ldy,
                                          const SegInfo* __restrict__ segs, float* __restrict__ conv_state,
                                          size_t cs_slot, int K, int conv_dim) {
+  pdl_trigger();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= conv_dim) return;
   const SegInfo sg = segs[blockIdx.y];
@@ -334,6 +341,7 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
     const SegInfo* __restrict__ segs, float* __restrict__ rec_state, size_t rs_slot, const float* __restrict__ neg_a,
     const float* __restrict__ dt_bias, const float* __restrict__ norm_w, int conv_dim, int key_dim, int vd, int hv,
     int ratio, float eps, __nv_bfloat16* __restrict__ X2, size_t xplane) {
+  pdl_trigger();
   constexpr int DK = 128, DV = 128;
   const int head = blockIdx.x;
   const SegInfo sg = segs[blockIdx.y];
@@ -358,6 +366,8 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
     const float4 v4 = *reinterpret_cast<const float4*>(ar + 2 * key_dim + head * DV + lane * 4);
     const float bb = y.at((size_t)row * ldy + conv_dim + vd + head);
     const float aa = y.at((size_t)row * ldy + conv_dim + vd + hv + head);
+    // the output gate is read here, with the other inputs, so its latency is not exposed after the state update
+    const float z = tid < DV ? y.at((size_t)row * ldy + conv_dim + head * DV + tid) : 0.f;
     const float decay = expf(neg_a[head] * softplus_(aa + dt_bias[head]));
     const float beta = sigmoidf_(bb);
     __syncthreads();
@@ -404,7 +414,6 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
     if (tid < DV) {  // gated RMSNorm, model.rs:377-383: o * rsqrt(mean o^2 + eps) * w * silu(z)
       const float ms = (sred[0] + sred[1] + sred[2] + sred[3]) / (float)DV;
       const float inv = 1.0f / sqrtf(ms + eps);
-      const float z = y.at((size_t)row * ldy + conv_dim + head * DV + tid);
       store_split(X2, xplane, (size_t)row * vd + head * DV + tid, s_o[tid] * inv * norm_w[tid] * siluf_(z));
     }
   }
@@ -423,6 +432,7 @@ __global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_seq_kernel(
     const float* __restrict__ act, YView y, int ldy, const SegInfo* __restrict__ segs, float* __restrict__ rec_state,
     size_t rs_slot, const float* __restrict__ neg_a, const float* __restrict__ dt_bias, const float* __restrict__ norm_w,
     int conv_dim, int key_dim, int vd, int hv, int ratio, float eps, __nv_bfloat16* __restrict__ X2, size_t xplane) {
+  pdl_trigger();
   constexpr int DK = 128, DV = 128;
   extern __shared__ __align__(16) float smf[];
   float* sq = smf;                          // [32][128]
@@ -551,6 +561,7 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(YView y, int ldy,
                                                         int rot, float eps, float* __restrict__ q_rot, KV* __restrict__ kc,
                                                         KV* __restrict__ vc, const int* __restrict__ page_table,
                                                         int pages_per_slot, int page_size) {
+  pdl_trigger();
   __shared__ float red[8];
   __shared__ float yn_s[256];
   const int idx = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
@@ -601,6 +612,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
                                                      SteerTables steer, const float* __restrict__ scale,
                                                      int8_t* __restrict__ frames, uint32_t* __restrict__ maxbuf,
                                                      __nv_bfloat16* __restrict__ X2, size_t xplane) {
+  pdl_trigger();
   __shared__ evie_op s_ops[64];
   __shared__ int s_cnt;
   const int r = blockIdx.y;
@@ -661,6 +673,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
 // last row's sum and a closed gate latches at the first row whose sum exceeds the threshold.
 __global__ void __launch_bounds__(256) gate_detect_kernel(YView y, int ldy, const SegInfo* __restrict__ segs,
                                                           int layer, int n, int L, GateTables t) {
+  pdl_trigger();
   __shared__ int s_min[8];
   const SegInfo sg = segs[blockIdx.x];
   const int sl = sg.slot;
@@ -722,6 +735,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
 __global__ void __launch_bounds__(256) logits_argmax_kernel(YView L2, int nseg, int V,
                                                             float* __restrict__ logits,
                                                             unsigned long long* __restrict__ best) {
+  pdl_trigger();
   __shared__ unsigned long long red[8];
   const int s = blockIdx.y;
   unsigned long long key = 0;
@@ -751,6 +765,7 @@ __global__ void __launch_bounds__(256) logits_argmax_kernel(YView L2, int nseg, 
 }
 
 __global__ void argmax_finish_kernel(unsigned long long* best, uint32_t* next_tokens, int nseg) {
+  pdl_trigger();
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= nseg) return;
   next_tokens[s] = 0xFFFFFFFFu - (uint32_t)(best[s] & 0xFFFFFFFFull);
@@ -758,6 +773,7 @@ __global__ void argmax_finish_kernel(unsigned long long* best, uint32_t* next_to
 }
 
 __global__ void advance_rows_kernel(RowInfo* rows, int nseq, const uint32_t* next) {
+  pdl_trigger();
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= nseq) return;
   rows[s].pos += 1;
@@ -849,13 +865,7 @@ evie_status k_gdn_mixer(const float* act, YView y, int ldy, int R, const SegInfo
   dim3 grid(s.hv, nseg);
   if (R > nseg) {  // some segment has several rows: the warp-local sequential kernel
     constexpr int kSmemSeq = (5 * kSeqChunk * 128 + 2 * kSeqChunk) * 4;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    EVIE_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 64 && !attr_set[dev]) {
-      EVIE_CUDA_TRY(cudaFuncSetAttribute(gdn_mixer_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemSeq));
-      attr_set[dev] = true;
-    }
+    EVIE_TRY(max_dynamic_smem((const void*)gdn_mixer_seq_kernel, kSmemSeq));
     gdn_mixer_seq_kernel<<<grid, kMixThreads, kSmemSeq, st>>>(act, y, ldy, segs, rec_state, rs_slot, neg_a, dt_bias,
                                                               norm_w, s.conv_dim, s.key_dim, s.vd, s.hv, s.hv / s.hk,
                                                               s.eps, X2, (size_t)R * s.vd);

@@ -3,8 +3,9 @@
 // Projection operands: the reference multiplies bf16 weights by f32 activations (crates/evie-core/src/kernels.rs
 // :1-4). On tensor cores both operands must be bf16, so every activation matrix X that feeds a projection is
 // written as two stacked bf16 planes, X = hi + lo with hi = bf16(X) and lo = bf16(X - hi) (16 significant bits).
-// One bf16 GEMM over the 2R stacked rows gives Y2 = [X_hi W^T ; X_lo W^T] in f32, and every consumer reads
-// Y = Y2[r] + Y2[R + r]. The weights are read once; the result matches the f32 product to ~2^-16 relative.
+// The projection GEMM (proj_gemm.h) multiplies both planes by the weights it reads once and adds the products in f32;
+// its output is one plane per K slice, which consumers add when they read it (YView). The result matches the f32
+// product to ~2^-16 relative.
 #pragma once
 #include <cublas_v2.h>
 
@@ -29,21 +30,29 @@ __device__ __forceinline__ void store_split(__nv_bfloat16* X2, size_t plane, siz
 }
 __device__ __forceinline__ float load_y(const float* Y2, size_t plane, size_t idx) { return Y2[idx] + Y2[plane + idx]; }
 
-// A projection output as `n` partial planes of `plane` floats each, added in a fixed order when read: 2 planes
-// (hi and lo operand products) from the cuBLAS path, or K-split partials from a tensor-core decode GEMM.
+// A projection output as `n` partial planes of `plane` floats each, added in a fixed order when read: the K-slice
+// partials of the projection GEMM (one plane when K is not sliced).
 struct YView {
+  static constexpr int kMaxPlanes = 16;
   const float* p;
   size_t plane;
   int n;
+  // Planes are loaded two at a time and added in plane order: consumers near their register limit keep few values
+  // live, and two planes (the common K-slice counts are 1 to 3) cost one L2 round trip.
   __device__ __forceinline__ float at(size_t i) const {
     float s = p[i];
-    for (int k = 1; k < n; k++) s += p[(size_t)k * plane + i];
+    int k = 1;
+    for (; k + 1 < n; k += 2) {
+      const float a = p[(size_t)k * plane + i], b = p[(size_t)(k + 1) * plane + i];
+      s += a;
+      s += b;
+    }
+    if (k < n) s += p[(size_t)k * plane + i];
     return s;
   }
   // Four consecutive elements (i a multiple of 4; rows and planes 16-byte aligned), planes added in plane order.
   // Each plane is added as it arrives: the loads are independent, so the compiler still issues them ahead, without
   // holding every plane in registers at once.
-  static constexpr int kMaxPlanes = 16;
   __device__ __forceinline__ float4 at4(size_t i) const {
     float4 s = *reinterpret_cast<const float4*>(p + i);
 #pragma unroll
@@ -69,7 +78,7 @@ struct ModelShape {
 // repetition history; the kernel sets each row's token bit.
 evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed, float* x, const float* gain,
                          float eps, int d, __nv_bfloat16* X2, uint32_t* seen, int seen_words, cudaStream_t st);
-// x += Y (two planes); optional f16 capture of x as the residual leaving `cap_layer`; then X2 = split(rmsnorm(x)).
+// x += Y (its K-slice planes); optional f16 capture of x as the residual leaving `cap_layer`; then X2 = split(rmsnorm(x)).
 evie_status k_add_norm(float* x, YView y, int ldy, int R, const float* gain, float eps, int d,
                        __nv_bfloat16* X2, uint16_t* resid, int cap_layer, int L, cudaStream_t st);
 // Final residual add (+ capture of the last layer) and final norm of each segment's last row into X2 [2][nseg][d].

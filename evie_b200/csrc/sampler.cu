@@ -102,6 +102,7 @@ __device__ __forceinline__ float splitmix_uniform(uint64_t* state) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1) sample_kernel(SampleArgs a) {
+  pdl_trigger();
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);  // [kCand]
   float* prob = reinterpret_cast<float*>(cand + kCand);                   // [kCand]

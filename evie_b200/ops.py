@@ -54,6 +54,28 @@ def gdn_prefill_tokenwise(q, k, v, g, beta, state, o=None):
     return o
 
 
+def split_planes(x: torch.Tensor) -> torch.Tensor:
+    """The split operand of an f32 matrix x [R,K]: [2,R,K] bf16 with hi = bf16(x) and lo = bf16(x - hi)."""
+    hi = x.to(torch.bfloat16)
+    lo = (x - hi.float()).to(torch.bfloat16)
+    return torch.stack([hi, lo]).contiguous()
+
+
+def proj_gemm(w, x2, max_planes: int = 16):
+    """Projection GEMM (evie_proj_gemm): w [M,K] bf16, x2 [2,R,K] bf16 split operand. Returns the K-slice planes
+    [planes,R,M] f32 whose sum (in slice order) is x w^T."""
+    M, K = w.shape
+    R = x2.shape[1]
+    assert w.dtype == x2.dtype == torch.bfloat16 and x2.shape == (2, R, K)
+    y = torch.empty(max_planes, R, M, device=w.device, dtype=torch.float32)
+    import ctypes as C
+
+    planes = C.c_int(0)
+    check(lib().evie_proj_gemm(_ptr(w), _ptr(x2), _ptr(y), y.numel(), M, K, R, max_planes, C.byref(planes),
+                               _stream()))
+    return y[: planes.value]
+
+
 def sampler_seed_state(seed: int) -> int:
     """Sampler::new's generator state for a seed (sampling.rs:27-29)."""
     return int(lib().evie_sampler_seed_state(seed))

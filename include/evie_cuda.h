@@ -230,6 +230,17 @@ EVIE_API evie_status evie_gdn_prefill_tokenwise(const void* q, const void* k, co
                                                 const float* beta, float* state, void* o, int B, int T, int H, int dk,
                                                 int dv, void* stream);
 
+/* Projection GEMM on tcgen05 tensor cores (evie-core's `matmul` with bf16 weights and f32 activations,
+ * crates/evie-core/src/kernels.rs:138-268; the WGSL `matmul_small` / `matmul_tiled`, gpu/kernels.wgsl:112-235), the
+ * kernel behind every projection and the LM head of evie_forward:
+ *   y[s][r][m] = sum over k in K slice s of w[m][k] (hi[r][k] + lo[r][k]),   s = 0 .. *planes - 1,
+ * where x2 = [hi; lo] ([2][R][K] bf16) is an f32 activation matrix split into bf16 planes (hi = bf16(x),
+ * lo = bf16(x - hi)) and w is [M][K] bf16 (both 16-byte aligned, K % 8 == 0). The full product is the sum of the
+ * *planes planes in slice order; R <= 128 cuts K into up to max_planes slices so that the weight stream fills every
+ * SM. y holds y_cap floats (at least R x M; *planes x R x M are written). */
+EVIE_API evie_status evie_proj_gemm(const void* w, const void* x2, float* y, size_t y_cap, int M, int K, int R,
+                                    int max_planes, int* planes, void* stream);
+
 /* Synchronises the current device and reports whether any kernel gave up a bounded device-side wait (an mbarrier
  * that did not complete within 2 s) since the last poll: EVIE_ERR_TIMEOUT with the count in the message, then the
  * count restarts at zero. Such a kernel drained its copies, freed its tensor memory and left its outputs
