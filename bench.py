@@ -44,6 +44,22 @@ def peaks():
     return dict(FALLBACK_PEAKS)
 
 
+def host_cpus() -> int:
+    """Logical CPUs this process may run on (what Rust's available_parallelism reports)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 4
+
+
+def evie_threads() -> int:
+    """evie's default compute threads: half the logical CPUs, clamped to [1, 8] (crates/evie/src/main.rs:111);
+    EVIE_CPU_THREADS overrides."""
+    if os.environ.get("EVIE_CPU_THREADS"):
+        return max(1, int(os.environ["EVIE_CPU_THREADS"]))
+    return max(1, min(8, host_cpus() // 2))
+
+
 def profiled_traffic(kernel: str, algorithmic_per_launch: float | None = None):
     """DRAM bytes per launch of `kernel` from the committed ncu summaries, if one exists: the captured figure, or,
     for a launch too large to capture, the traffic-to-algorithmic ratio captured on a smaller launch of the same
@@ -144,12 +160,14 @@ def max_over_ranks(values, device=None):
 
 
 def gather_to_rank0(arr, device=None):
-    """The equal-shaped int32 arrays of all ranks, stacked in rank order on rank 0 ([world, ...]); None on the other
-    ranks; arr[None] with one rank. One all-gather, the same step on every rank (NCCL on the GPUs, gloo on CPU)."""
+    """The equal-shaped arrays of all ranks, stacked in rank order on rank 0 ([world, ...]); None on the other ranks;
+    arr[None] with one rank. Floating-point arrays (logits) move as float32, integer ones (token ids, neuron
+    indices) as int32. One all-gather, the same step on every rank (NCCL on the GPUs, gloo on CPU)."""
     import torch
     import torch.distributed as dist
 
-    a = np.ascontiguousarray(arr, dtype=np.int32)
+    arr = np.asarray(arr)
+    a = np.ascontiguousarray(arr, dtype=np.float32 if arr.dtype.kind == "f" else np.int32)
     if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
         return a[None].copy()
     t = torch.from_numpy(a).to(device) if device is not None else torch.from_numpy(a)
@@ -262,10 +280,10 @@ class GdnDecode(Workload):
         import torch
         from tests._inputs import gdn_decode_inputs
 
-        x = gdn_decode_inputs(self.B, self.H, 2)
+        x = gdn_decode_inputs(self.B, self.H, 2, device=dev if getattr(self, "gen_on_device", False) else "cpu")
         self.x = {k: v.to(dev) for k, v in x.items()}
         self.o = torch.empty(self.B, self.H, self.d, device=dev)
-        self.host = {k: v.pin_memory() for k, v in x.items() if k != "S"}
+        self.host = {k: v.cpu().pin_memory() for k, v in x.items() if k != "S"}
         self.dev_in = {k: torch.empty_like(v, device=dev) for k, v in self.host.items()}
         self.o_host = torch.empty(self.B, self.H, self.d).pin_memory()
 
@@ -337,11 +355,11 @@ class GdnPrefill(Workload):
         import torch
         from tests._inputs import gdn_prefill_inputs
 
-        x = gdn_prefill_inputs(self.B, self.T, self.H, 3)
+        x = gdn_prefill_inputs(self.B, self.T, self.H, 3, device=dev if getattr(self, "gen_on_device", False) else "cpu")
         self.S0 = x["S"].to(dev)
         self.x = {k: v.to(dev) for k, v in x.items()}
         self.o = torch.empty(self.B, self.T, self.H, self.d, device=dev, dtype=torch.bfloat16)
-        self.host = {k: x[k].pin_memory() for k in ("q", "k", "v", "g", "beta")}
+        self.host = {k: x[k].cpu().pin_memory() for k in ("q", "k", "v", "g", "beta")}
         self.dev_in = {k: torch.empty_like(v, device=dev) for k, v in self.host.items()}
         self.o_host = torch.empty(self.B, self.T, self.H, self.d, dtype=torch.bfloat16).pin_memory()
 
@@ -413,10 +431,11 @@ class GqaDecode(Workload):
         import torch
         from tests._inputs import gqa_inputs
 
-        x = gqa_inputs(self.B, self.Hq, self.Hkv, self.ctx, 4, hd=self.hd, page=self.page)
+        x = gqa_inputs(self.B, self.Hq, self.Hkv, self.ctx, 4, hd=self.hd, page=self.page,
+                       device=dev if getattr(self, "gen_on_device", False) else "cpu")
         self.x = {k: v.to(dev) for k, v in x.items()}
         self.out = torch.empty(self.B, self.Hq, self.hd, device=dev)
-        self.host = {k: x[k].pin_memory() for k in ("q", "gate")}
+        self.host = {k: x[k].cpu().pin_memory() for k in ("q", "gate")}
         self.dev_in = {k: torch.empty_like(v, device=dev) for k, v in self.host.items()}
         self.out_host = torch.empty(self.B, self.Hq, self.hd).pin_memory()
 
@@ -567,6 +586,26 @@ class ModelDecode(Workload):
     def mid_steps(self):
         return getattr(self, "_steps", 0)
 
+    def prefill_flops(self):
+        """Useful FLOPs of the prefill of B prompts of P tokens (what the split operands double is not counted):
+        2 per weight element per row for every projection (the LM head on each prompt's last row only); causal
+        attention, 4 hd FLOPs per (query row, head, earlier position); the DeltaNet recurrence, 7 dk dv FLOPs per
+        (row, value head) (kv = S^T k, the rank-1 update and o = S^T q)."""
+        c = self.cfg
+        d, n, L, V = c["hidden_size"], c["intermediate_size"], c["num_hidden_layers"], c["vocab_size"]
+        hk, hv, dk, dv = (c["linear_num_key_heads"], c["linear_num_value_heads"], c["linear_key_head_dim"],
+                          c["linear_value_head_dim"])
+        nh, nkv, hd = c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"]
+        n_lin = sum(1 for t in c["layer_types"] if t == "linear_attention")
+        n_full = L - n_lin
+        conv_dim = 2 * hk * dk + hv * dv
+        proj = n_lin * ((conv_dim + hv * dv + 2 * hv) * d + d * hv * dv) + n_full * ((2 * nh + 2 * nkv) * hd * d
+                                                                                     + d * nh * hd) + L * 3 * n * d
+        rows = self.B * self.P
+        attn = n_full * nh * 4 * hd * self.B * (self.P * (self.P + 1) // 2)
+        gdn = n_lin * hv * 7 * dk * dv * rows
+        return 2 * proj * rows + 2 * V * d * self.B + attn + gdn
+
     def group_bytes(self, ctx):
         """Algorithmic bytes per decode step of each profiled kernel group (evie_profile groups)."""
         c = self.cfg
@@ -632,13 +671,23 @@ class ModelDecode(Workload):
         self.pos += k
         return k
 
-    def results(self):
+    def results(self, logits=False):
         """What rank 0 collects after the timed region: the timed steps' token ids [steps, B] and, as the reduced
-        capture, the 16 most active neurons of each sequence's last timed step [B, 16]."""
-        return {"token_ids": self.last_tokens.view(np.int32), "top_active": self.m.top_active(16)}
+        capture, the 16 most active neurons of each sequence's last timed step [B, 16]; with logits, also the next
+        step's logits of every sequence [B, V] f32 (one more forward with want_logits)."""
+        res = {"token_ids": self.last_tokens.view(np.int32), "top_active": self.m.top_active(16)}
+        if logits:
+            o = self.m.forward(self.seqs(), want_logits=True)
+            self.next = o.next_tokens.copy()
+            self.pos += 1
+            res["logits"] = o.logits.astype(np.float32)
+        return res
 
-    def result_shapes(self, steps):
-        return {"token_ids": (steps, self.B), "top_active": (self.B, 16)}
+    def result_shapes(self, steps, logits=False):
+        shp = {"token_ids": (steps, self.B), "top_active": (self.B, 16)}
+        if logits:
+            shp["logits"] = (self.B, self.cfg["vocab_size"])
+        return shp
 
     def step(self):
         return self.run_device_steps(1)
@@ -659,13 +708,15 @@ class ModelDecode(Workload):
         return a.elapsed_time(b), k * self.launches_per_step()
 
     def launches_per_step(self):
-        """Our kernels per decode step: embed+norm; per DeltaNet layer conv (which also shifts the conv window),
-        mixer, add-norm x2, SwiGLU; per attention layer prep, attention, add-norm x2, SwiGLU; logits/argmax + finish,
-        row advance. The ncu launch list of the decode step counts the same 164 at 4B shapes."""
+        """Our kernels per decode step: embed+norm; per DeltaNet layer the input projection, conv (which also shifts
+        the conv window), mixer, output projection, add-norm x2, gate/up projection, SwiGLU, down projection; per
+        attention layer the same with prep + attention in place of conv + mixer; the LM head, logits/argmax + finish,
+        row advance. The ncu launch list of the decode step counts the same 293 at 4B shapes (129 of them the
+        projection GEMM)."""
         c = self.cfg
         L = c["num_hidden_layers"]
         n_lin = sum(1 for t in c["layer_types"] if t == "linear_attention")
-        return 1 + n_lin * 5 + (L - n_lin) * 5 + 3
+        return 1 + n_lin * 9 + (L - n_lin) * 9 + 4
 
     def e2e(self, k):
         import torch
@@ -727,34 +778,40 @@ class ModelDecode(Workload):
         self.ops = ops
 
     def cpu_sample(self, threads):
+        """One steered/unsteered pair decoding at the GPU arm's context: the oracle's caches are put at position P
+        (the prompt length) with generator-filled states and key/value rows (oracle_cache_seed), since the oracle's
+        prefill of a P-token prompt at these shapes takes hours; then a few greedy steps with the steering plan and
+        the capture on the steered lane."""
         import oracle
 
         dose_note = ""
         if not hasattr(self, "ops"):
             self.prepare_cpu(threads)
-            dose_note = "; dose unit measured by the oracle on the 64-token sample prompt"
+            dose_note = "; dose unit measured by the oracle on a 64-token prompt"
         oracle.set_threads(threads)
-        m = oracle.Model(self.ckpt)
-        prompt = self.prompts[0][:64]
+        if getattr(self, "_cpu_model", None) is None:
+            self._cpu_model = oracle.Model(self.ckpt)
+        m = self._cpu_model
         plan = oracle.compile_plan([dict(layer=l, neuron=nn, mode="add", value=v) for l, nn, _, v in self.ops],
                                    m.cfg.n_layers, m.cfg.intermediate, lambda l, n: 1.0)
         gate = oracle.GateState()
-        ca, cb = m.new_cache(), m.new_cache()
-        lg, _, _ = m.forward([dict(cache=ca, tokens=prompt, plan=plan, gate=gate), dict(cache=cb, tokens=prompt)])
-        nxt = [oracle.greedy(lg[0]), oracle.greedy(lg[1])]
+        ca, cb = m.seeded_cache(self.P, 1), m.seeded_cache(self.P, 2)
+        nxt = [int(self.prompts[0][-1]), int(self.prompts[0][-1])]
         steps = 0
         t0 = time.perf_counter()
-        while steps < 8 and time.perf_counter() - t0 < 30.0:
+        while steps < 4 and time.perf_counter() - t0 < 30.0:
             lg, _, _ = m.forward([dict(cache=ca, tokens=np.array([nxt[0]], np.uint32), plan=plan, gate=gate,
                                        frames=True),
                                   dict(cache=cb, tokens=np.array([nxt[1]], np.uint32))])
             nxt = [oracle.greedy(lg[0]), oracle.greedy(lg[1])]
             steps += 1
         dt = time.perf_counter() - t0
-        return {"value": 2 * steps / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-                "sample": f"1 steered/unsteered pair, 64-token prompt, {steps} greedy decode steps with capture on the "
-                          f"steered lane, 4B-shaped model (the full 4096-token prefill is ~65 TFLOP per sequence on "
-                          f"the CPU){dose_note}"}
+        return {"value": 2 * steps / dt, "unit": "tokens/s", "cores": threads, "nproc": host_cpus(),
+                "kind": "port", "context": self.P,
+                "sample": f"1 steered/unsteered pair, {steps} greedy decode steps at context {self.P} (caches put at "
+                          f"position {self.P} with generator-filled states and keys/values), steering plan and "
+                          f"capture on the steered lane, 4B-shaped model; evie's default threads "
+                          f"(half the logical CPUs, at most 8){dose_note}"}
 
 
 WORKLOADS = {"gdn_decode": GdnDecode, "gdn_prefill": GdnPrefill, "gqa_decode": GqaDecode,
@@ -788,7 +845,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     w = make_workload(args)
-    threads = os.cpu_count() or 1
+    threads = evie_threads()
     vals = []
     for _ in range(args.warmup):
         w.cpu_sample(threads)
@@ -800,12 +857,57 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * w.tokens_per_step / v,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
         "config": w.config(),
-        "cpu_baseline": {"value": v, "unit": vals[0]["unit"], "cores": threads, "kind": "port",
-                         "sample": vals[0]["sample"]},
+        "cpu_baseline": {"value": v, "unit": vals[0]["unit"], "cores": threads, "nproc": host_cpus(),
+                         "kind": "port", "sample": vals[0]["sample"]},
         "e2e": {"value": v, "unit": vals[0]["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
     return 0
+
+
+ISOLATED = (("gdn_decode", "gdn_decode_step B=64 H=16 dk=dv=128 fp32 state"),
+            ("gdn_prefill", "gdn_chunk_prefill B=8 T=8192 H=16 dk=dv=128 chunk=64"),
+            ("gqa_decode", "gqa_decode B=64 Hq=16 Hkv=4 hd=256 ctx~U[1024,32768] paged bf16 KV"))
+
+
+def isolated_passes(dev, steps=10, warmup=3):
+    """The three isolated ops of the hot path at their full sizes (the single recurrent DeltaNet step, the chunked
+    DeltaNet prefill, the paged attention decode), each timed like a workload of its own after the model's timed
+    region, with its roofline against the measured peaks: HBM for the two decode ops, bf16 tensor for the prefill.
+    Inputs are drawn on the device (the same distributions as the parity tests' host draws, other values); L2 is
+    flushed between steps where the inputs would fit in it."""
+    import torch
+
+    pk = peaks()
+    out = {}
+    for name, label in ISOLATED:
+        try:
+            w = WORKLOADS[name]()
+            w.gen_on_device = True
+            w.setup(dev)
+            w.warmup(warmup)
+            torch.cuda.synchronize()
+            ms, _ = w.timed(steps)
+            per = ms / steps
+            alg = w.algorithmic()
+            e = {"workload": label, "ms_per_step": per, "value": w.tokens_per_step / (per / 1000.0),
+                 "unit": w.unit}
+            if w.bound == "hbm":
+                ach = alg / (per / 1000.0) / 1e9
+                e["roofline"] = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                 "frac": ach / pk["hbm_gbs"], "kernel": w.kernel, "algorithmic_bytes": alg,
+                                 "peak_source": pk["source"]}
+            else:
+                ach = alg / (per / 1000.0) / 1e12
+                e["roofline"] = {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                                 "frac": ach / pk["bf16_tflops"], "kernel": w.kernel, "algorithmic_flops": alg,
+                                 "peak_source": pk["source"]}
+            out[name] = e
+            del w
+            torch.cuda.empty_cache()
+        except Exception as ex:  # the line is still printed without this entry
+            print(f"isolated pass {name} failed: {ex}", file=sys.stderr)
+    return out
 
 
 def run_ours(args):
@@ -818,6 +920,9 @@ def run_ours(args):
     if world > 1:
         import datetime
 
+        # NCCL's communicator lines (rank count, transport) go to standard error with the rest of the log
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     dev = torch.device("cuda", local)
@@ -853,10 +958,11 @@ def run_ours(args):
     gathered = None
     if hasattr(w, "results"):
         try:
-            res = w.results()
+            res = w.results(logits=args.gather_logits)
         except Exception as e:  # still take the collective steps, with -1 in place of this rank's results
             print(f"results unavailable on rank {rank}: {e}", file=sys.stderr)
-            res = {k: np.full(shp, -1, np.int32) for k, shp in w.result_shapes(args.steps).items()}
+            res = {k: np.full(shp, -1, np.float32 if k == "logits" else np.int32)
+                   for k, shp in w.result_shapes(args.steps, args.gather_logits).items()}
         gathered = {k: gather_to_rank0(v, device=dev) for k, v in res.items()}
     e2e_ms, h2d, d2h = w.e2e(args.steps)
     kernels = None
@@ -915,10 +1021,17 @@ def run_ours(args):
         line["roofline"] = {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                             "frac": ach / pk["bf16_tflops"], "traffic": profiled_traffic(w.kernel),
                             "kernel": w.kernel, "algorithmic_flops": alg, "peak_source": pk["source"]}
+    if hasattr(w, "prefill_flops") and getattr(w, "prefill_ms", None):
+        pf = w.prefill_flops() / (w.prefill_ms / 1000.0) / 1e12
+        line["prefill_roofline"] = {"bound": "tensor", "achieved": pf, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                                    "frac": pf / pk["bf16_tflops"], "algorithmic_flops": w.prefill_flops(),
+                                    "tok_s": w.prefill_tok_s, "peak_source": pk["source"]}
     if rank == 0 and gathered:
         line["gathered"] = {k: list(v.shape) for k, v in gathered.items()}
+    if world == 1 and args.workload == DEFAULT_WORKLOAD and not args.no_isolated:
+        line["isolated"] = isolated_passes(dev)
     if rank == 0 and world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = w.cpu_sample(int(os.environ.get("EVIE_CPU_THREADS", os.cpu_count() or 1)))
+        line["cpu_baseline"] = w.cpu_sample(evie_threads())
     if rank == 0:
         emit(line)
     if world > 1:
@@ -952,6 +1065,10 @@ def main():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--gather-logits", action="store_true",
+                    help="after the timed region also gather every sequence's next-step logits to rank 0")
+    ap.add_argument("--no-isolated", action="store_true",
+                    help="skip the isolated passes of the DeltaNet step, chunked prefill and paged attention")
     ap.add_argument("--batch", type=int, default=0, help="override the batch size (small profiling cases)")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length of model_decode")
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length of gdn_prefill")

@@ -256,6 +256,8 @@ struct evie_ctx {
   SegInfo* d_segs = nullptr;
   RowInfo* h_rows = nullptr;  // pinned
   SegInfo* h_segs = nullptr;  // pinned
+  unsigned int* timeouts = nullptr;    // this device's give-up counter (tc.h)
+  unsigned int* h_timeouts = nullptr;  // pinned copy, read after each call's synchronisation
   uint32_t* hist = nullptr;   // device token history of evie_decode_greedy
   size_t hist_cap = 0;
   // profiling: event pairs per kernel group, resolved after each synchronising call
@@ -639,6 +641,8 @@ evie_status allocate_state(evie_ctx* c) {
   TRY(c->alloc(&c->d_segs, S));
   EVIE_CUDA_TRY(cudaMallocHost(&c->h_rows, R * sizeof(RowInfo)));
   EVIE_CUDA_TRY(cudaMallocHost(&c->h_segs, S * sizeof(SegInfo)));
+  EVIE_CUDA_TRY(cudaMallocHost(&c->h_timeouts, sizeof(unsigned int)));
+  *c->h_timeouts = 0;
   return EVIE_OK;
 }
 
@@ -854,6 +858,28 @@ evie_status enqueue_head(evie_ctx* c, int nseq, bool want_logits) {
   return evie::k_sample(a, nseq, c->stream);
 }
 
+// The device's count of bounded waits that gave up (tc.h) is copied to page-locked memory behind a call's work, so
+// that the call can report a give-up among its own kernels with its status. The count is per device: a give-up in
+// another kernel on the device since the last check (or evie_poll_device_errors) is reported here as well.
+evie_status enqueue_timeout_read(evie_ctx* c) {
+  if (!c->timeouts) {
+    c->timeouts = evie::device_timeout_counter();
+    if (!c->timeouts) return evie::fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
+  }
+  EVIE_CUDA_TRY(cudaMemcpyAsync(c->h_timeouts, c->timeouts, sizeof(unsigned int), cudaMemcpyDeviceToHost, c->stream));
+  return EVIE_OK;
+}
+// After the call's synchronisation: EVIE_ERR_TIMEOUT (and the count restarts) when a kernel gave up a wait.
+evie_status check_timeouts(evie_ctx* c, const char* what) {
+  const unsigned int n = *c->h_timeouts;
+  if (!n) return EVIE_OK;
+  *c->h_timeouts = 0;
+  EVIE_CUDA_TRY(cudaMemsetAsync(c->timeouts, 0, sizeof(unsigned int), c->stream));
+  EVIE_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return evie::fail(EVIE_ERR_TIMEOUT, "%s: %u thread(s) gave up a bounded device-side wait; outputs are incomplete",
+                    what, n);
+}
+
 evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_logits, int capture, float* logits,
                          int8_t* frames, uint16_t* resid, uint32_t* next_tokens) {
   auto& s = c->s;
@@ -915,8 +941,10 @@ evie_status forward_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int want_l
     EVIE_CUDA_TRY(cudaMemcpyAsync(frames, c->frames, (size_t)R * s.L * s.n, cudaMemcpyDeviceToHost, st));
   if (capture && resid && !chv.resid)
     EVIE_CUDA_TRY(cudaMemcpyAsync(resid, c->resid, (size_t)R * s.L * s.d * 2, cudaMemcpyDeviceToHost, st));
+  TRY(enqueue_timeout_read(c));
   EVIE_CUDA_TRY(cudaStreamSynchronize(st));
   prof_resolve(c);
+  TRY(check_timeouts(c, "forward"));
   if (c->prof && c->prof_failed)
     return evie::fail(EVIE_ERR_CUDA, "forward: the profiling events could not be recorded or timed");
   if (capture) c->cap_rows = R;
@@ -1042,8 +1070,10 @@ evie_status decode_greedy_impl(evie_ctx* c, const evie_seq* seqs, int nseq, int 
     }
   }
   if (out_tokens) EVIE_CUDA_TRY(cudaMemcpyAsync(out_tokens, c->hist, need * 4, cudaMemcpyDeviceToHost, st));
+  TRY(enqueue_timeout_read(c));
   EVIE_CUDA_TRY(cudaStreamSynchronize(st));
   prof_resolve(c);
+  TRY(check_timeouts(c, "decode"));
   if (c->prof && c->prof_failed)
     return evie::fail(EVIE_ERR_CUDA, "decode: the profiling events could not be recorded or timed");
   if (capture) c->cap_rows = nseq;
@@ -1065,6 +1095,7 @@ void destroy(evie_ctx* c) {
   for (auto e : c->prof_free) cudaEventDestroy(e);
   if (c->h_rows) cudaFreeHost(c->h_rows);
   if (c->h_segs) cudaFreeHost(c->h_segs);
+  if (c->h_timeouts) cudaFreeHost(c->h_timeouts);
   if (c->blas) cublasDestroy(c->blas);
   for (auto e : c->cap_ev) cudaEventDestroy(e);
   if (c->cstream) cudaStreamDestroy(c->cstream);

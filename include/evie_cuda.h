@@ -107,7 +107,9 @@ EVIE_API evie_status evie_info(const evie_ctx* ctx, evie_model_info* out);
  *   next_tokens  [n_seqs] the token each sequence's slot sampler picks from its last row's logits: greedy = the
  *                first index of the maximum logit (topk(logits, 1), sampling.rs:60) unless evie_set_sampler
  *                gave the slot other parameters (Sampler::sample, sampling.rs:41-93).
- * rows are the concatenation of every sequence's new tokens, in call order. */
+ * rows are the concatenation of every sequence's new tokens, in call order.
+ * Returns EVIE_ERR_TIMEOUT when a kernel on this device gave up a bounded device-side wait since the last check
+ * (this call's, or one enqueued earlier on the device): the outputs are then incomplete. The count restarts. */
 EVIE_API evie_status evie_forward(evie_ctx* ctx, const evie_seq* seqs, int n_seqs, int want_logits, int capture, float* logits,
                          int8_t* frames, uint16_t* resid, uint32_t* next_tokens);
 
@@ -117,7 +119,8 @@ EVIE_API evie_status evie_forward(evie_ctx* ctx, const evie_seq* seqs, int n_seq
  * unless evie_set_sampler says otherwise (the name keeps the greedy default).
  *   out_tokens  [steps][n_seqs] host, the token produced by each step (may be NULL);
  *   frames      [steps][n_seqs][layers*intermediate] i8 host, captured activations per step (if capture);
- *   resid       [steps][n_seqs][layers*hidden] f16 bits host (if capture). */
+ *   resid       [steps][n_seqs][layers*hidden] f16 bits host (if capture).
+ * Returns EVIE_ERR_TIMEOUT as evie_forward does. */
 EVIE_API evie_status evie_decode_greedy(evie_ctx* ctx, const evie_seq* seqs, int n_seqs, int steps,
                                         uint32_t* out_tokens, int capture, int8_t* frames, uint16_t* resid);
 /* The CUDA stream (cudaStream_t) all of the context's work is enqueued on, for timing with CUDA events. */

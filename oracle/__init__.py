@@ -76,6 +76,7 @@ def _declare(L):
         "oracle_model_set": (I, [P, I, I, P, I, LG, LG]),
         "oracle_cache_new": (P, [P]),
         "oracle_cache_free": (None, [P]),
+        "oracle_cache_seed": (None, [P, P, LG, C.c_uint64]),
         "oracle_cache_clone": (P, [P]),
         "oracle_cache_pos": (LG, [P]),
         "oracle_cache_read": (LG, [P, I, I, P, LG]),
@@ -420,6 +421,13 @@ class Model:
 
     def new_cache(self) -> "Cache":
         return Cache(lib().oracle_cache_new(self._h))
+
+    def seeded_cache(self, pos: int, seed: int = 0) -> "Cache":
+        """A cache standing at position `pos` with generator-filled states, conv windows and `pos` key/value rows
+        (oracle_cache_seed): a timing aid for decode at long contexts without a prefill."""
+        c = self.new_cache()
+        lib().oracle_cache_seed(self._h, c._h, pos, seed)
+        return c
 
     def col_norms_down(self, layer: int) -> np.ndarray:
         """||W_down[:, n]|| per neuron, in f64 like kernels.rs:79-103, returned as f32."""

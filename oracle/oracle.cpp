@@ -1198,6 +1198,34 @@ EXPORT void* oracle_cache_new(void* p) {
   return cache;
 }
 EXPORT void oracle_cache_free(void* c) { delete (Cache*)c; }
+// Timing aid: puts a cache at position `pos` without running a prefill. Every DeltaNet state and conv window and
+// `pos` rows of every attention layer's keys and values are filled with values of a fixed generator (uniform in
+// [-a, a], a = 0.1 for states and windows, 1 for keys and values), so that a decode step afterwards does the work
+// of a step at that context length. The values carry no meaning; the CPU baseline uses this to time decode at the
+// GPU's context without the hours-long prefill of the 4B-shaped model.
+EXPORT void oracle_cache_seed(void* p, void* cp, long pos, uint64_t seed) {
+  Model* m = (Model*)p;
+  Cache* c = (Cache*)cp;
+  const Cfg& cfg = m->cfg;
+  uint64_t x = seed * 0x9E3779B97F4A7C15ull + 1;
+  auto uni = [&x](float a) {
+    x = x * 6364136223846793005ull + 1442695040888963407ull;
+    return a * ((float)((x >> 40) & 0xffffff) / 8388608.0f - 1.0f);
+  };
+  for (int i = 0; i < cfg.n_layers; i++) {
+    LayerCache& lc = c->layers[i];
+    if (m->layers[i].kind == 0) {
+      for (float& v : lc.conv) v = uni(0.1f);
+      for (float& v : lc.state) v = uni(0.1f);
+    } else {
+      const size_t n = (size_t)pos * cfg.n_kv_heads * cfg.head_dim;
+      lc.k.resize(n);
+      lc.v.resize(n);
+      for (size_t j = 0; j < n; j++) lc.k[j] = uni(1.0f), lc.v[j] = uni(1.0f);
+    }
+  }
+  c->pos = (size_t)pos;
+}
 EXPORT void* oracle_cache_clone(void* c) { return new Cache(*(Cache*)c); }
 EXPORT long oracle_cache_pos(void* c) { return (long)((Cache*)c)->pos; }
 // Copies one linear layer's recurrent state ([hv][dk][dv] f32) or conv window out of a cache.

@@ -1,6 +1,6 @@
 """The multi-GPU host logic of bench.py on two gloo ranks (CPU): each rank draws disjoint steered/unsteered pairs of
 one global set, the timing reduction gives every rank the max over ranks, and the results (token ids, reduced
-captures) are gathered to rank 0 in rank order."""
+captures, and logits on request) are gathered to rank 0 in rank order."""
 import os
 import socket
 
@@ -25,7 +25,8 @@ def _rank_main(rank, world, port, out):
         prompts = bench.rank_prompts(rank, npairs=3, P=16, V=1000)
         times = bench.max_over_ranks([10.0 + rank, 5.0 - rank])
         got = bench.gather_to_rank0(np.arange(6, dtype=np.uint32).reshape(2, 3) + 100 * rank)
-        out[rank] = (np.stack(prompts), times, got)
+        logits = bench.gather_to_rank0(np.linspace(-1.5, 2.5, 8, dtype=np.float32).reshape(2, 4) * (rank + 1))
+        out[rank] = (np.stack(prompts), times, got, logits)
     finally:
         dist.destroy_process_group()
 
@@ -36,12 +37,15 @@ def test_two_ranks_partition_pairs_and_reduce_max():
     world, port = 2, _free_port()
     out = mp.Manager().dict()
     mp.start_processes(_rank_main, args=(world, port, out), nprocs=world, start_method="spawn", join=True)
-    p0, t0, g0 = out[0]
-    p1, t1, g1 = out[1]
+    p0, t0, g0, l0 = out[0]
+    p1, t1, g1, l1 = out[1]
     assert t0 == t1 == [11.0, 5.0]
     # results gathered to rank 0 in rank order (token ids are uint32 on the host, moved as int32)
     want = np.stack([np.arange(6).reshape(2, 3) + 100 * r for r in range(world)]).astype(np.int32)
     assert g1 is None and g0.dtype == np.int32 and np.array_equal(g0, want)
+    # logits (on request) keep their float32 values
+    lw = np.stack([np.linspace(-1.5, 2.5, 8, dtype=np.float32).reshape(2, 4) * (r + 1) for r in range(world)])
+    assert l1 is None and l0.dtype == np.float32 and np.array_equal(l0, lw)
     # the two ranks' pairs are the first six pairs of the one-rank stream, split in order
     whole = np.stack(bench.rank_prompts(0, npairs=6, P=16, V=1000))
     assert np.array_equal(np.concatenate([p0, p1]), whole)

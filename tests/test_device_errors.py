@@ -40,3 +40,32 @@ def test_probe_rejects_limits_above_the_kernels_deadline():
     lib()
     with pytest.raises(EvieError, match="limit above"):
         ops.bounded_wait_probe(3_000_000_000)
+
+
+@pytest.mark.gpu
+def test_model_calls_report_a_give_up(cuda, tmp_path):
+    """evie_forward and evie_decode_greedy read the device's give-up count behind their own work and return
+    EVIE_ERR_TIMEOUT instead of success with incomplete outputs; the count then restarts. The give-up is made on
+    purpose by the probe (a wait on a barrier nothing completes), the way a kernel of the call would count one."""
+    from evie_b200 import EvieError, checkpoint as ck, ops
+    from evie_b200.gpu import GpuModel, GpuSeq
+
+    path = str(tmp_path / "tiny")
+    ck.write_checkpoint(path, ck.tiny_config(vocab_size=512, num_hidden_layers=4), seed=0)
+    m = GpuModel(path, max_ctx=128, slots=1, max_rows=16)
+    toks = np.arange(3, 11, dtype=np.uint32)
+    ops.poll_device_errors()
+    first = m.forward([GpuSeq(0, 0, toks)]).logits.copy()
+    assert ops.bounded_wait_probe(10_000_000) == 1
+    with pytest.raises(EvieError, match="gave up a bounded device-side wait") as e:
+        m.forward([GpuSeq(0, 8, toks[:1])])
+    assert e.value.status == 5
+    m.reset_slot(0)
+    again = m.forward([GpuSeq(0, 0, toks)]).logits  # the count restarted and the context still works
+    assert np.array_equal(again, first)
+    assert ops.bounded_wait_probe(10_000_000) == 1
+    with pytest.raises(EvieError) as e:
+        m.decode_greedy([GpuSeq(0, 8, toks[:1])], 2)
+    assert e.value.status == 5
+    ops.poll_device_errors()
+    m.close()

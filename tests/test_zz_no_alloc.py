@@ -26,13 +26,16 @@ def _call(L, fn, x, out, scale, max_pages=None):
 
 
 @pytest.mark.gpu
-def test_noalloc_matches_allocating_entry_point(cuda):
+@pytest.mark.parametrize("Hq,Hkv", [(16, 4), (8, 4)])
+def test_noalloc_matches_allocating_entry_point(Hq, Hkv, cuda):
+    """GQA group 4 (the bulk-copy kernel) and group 2 (the CUDA-core kernel, whose per-split partials scale with the
+    group), each with contexts of several 512-token splits."""
     import evie_b200
 
     L = evie_b200.lib()
     scale = 1.0 / 16.0
     for call, (ctx, seed) in enumerate([([300, 5000, 1, 12000], 31), ([9000, 0, 700, 2047], 32)]):
-        x = {k: v.to(cuda) for k, v in gqa_inputs(len(ctx), 16, 4, ctx, seed).items()}
+        x = {k: v.to(cuda) for k, v in gqa_inputs(len(ctx), Hq, Hkv, ctx, seed).items()}
         ref = torch.empty(x["q"].shape, device=cuda, dtype=torch.float32)
         got = torch.full(x["q"].shape, float("nan"), device=cuda, dtype=torch.float32)
         assert _call(L, "evie_gqa_decode_paged", x, ref, scale) == 0, L.evie_last_global_error()
