@@ -3,16 +3,22 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
 Workloads (per GPU; with N GPUs each rank runs its own share: weak scaling, no data-path collective):
+  model_decode (default) Qwen3.5-4B-shaped decode, 64 sequences = 32 steered/unsteered pairs, 4096-token prompts,
+               full SwiGLU capture (--model 0.8b: the 0.8B shapes, for small profiling cases)
   gdn_decode   Gated DeltaNet decode step, B=64 sequences x 16 heads, dk=dv=128, fp32 state
   gqa_decode   gated GQA decode attention, B=64, 16 q / 4 kv heads, hd 256, ctx ~ U[1024, 32768], 256-token pages
   gdn_prefill  Gated DeltaNet prefill, B=8, T=8192, 16 heads
+  proj_gemm    one projection GEMM (the 4B gate/up weight, R=64 rows; --batch sets R)
+The default run also times the three isolated ops (gdn_decode, gdn_prefill, gqa_decode) after the model's timed
+region and reports them under `isolated`.
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the launching stream; L2 is
 flushed (a 256 MiB write) between timed steps whenever a step's working set fits in L2. The K-step region is
 bracketed by a barrier and torch.cuda.synchronize() on both sides; the reported time is the max over ranks.
 `e2e` repeats the step through the C ABI from pinned host buffers with the host<->device copies inside the timed
 region. `cpu_baseline` (rank 0, N=1) times the CPU oracle (a C++ restatement of evie-core's CPU path) on a
-bounded sample of the same workload. `--impl reference` times that CPU path alone, with every host thread.
+bounded sample of the same workload, on evie's default thread count (half the logical CPUs, at most 8).
+`--impl reference` times that CPU path alone.
 """
 from __future__ import annotations
 
@@ -481,6 +487,87 @@ class GqaDecode(Workload):
                           f"scaled to the batch by context length"}
 
 
+class ProjGemm(Workload):
+    """One projection of the model: y = x W^T for bf16 weights W [M][K] and f32 activations x [R][K] as split bf16
+    planes, through evie_proj_gemm. Default shape: the 4B MLP gate/up projection (M = 18432, K = 2560) at the decode
+    batch R = 64; --batch sets R (R > 128 runs the prefill tiles). Weights are rotated over copies that together
+    exceed L2, so every step streams its weight from HBM."""
+    name = "proj_gemm"
+    kernel = "proj_gemm_kernel"
+
+    def __init__(self, B=64, M=18432, K=2560):
+        self.R, self.M, self.K = B, M, K
+        self.tokens_per_step = B
+        self.bound = "hbm" if B <= 128 else "tensor"
+
+    def config(self):
+        return {"workload": f"proj_gemm M={self.M} K={self.K} R={self.R} (bf16 weights x split-bf16 f32 operand)",
+                "global_batch": self.R, "l2": "weights rotated over copies larger than L2"}
+
+    def algorithmic(self):
+        """hbm: the weight bytes plus the operand planes and the f32 output; tensor: 2 M K R useful FLOPs."""
+        if self.bound == "hbm":
+            return self.M * self.K * 2 + 2 * self.R * self.K * 2 + self.R * self.M * 4
+        return 2 * self.M * self.K * self.R
+
+    def setup(self, dev):
+        import torch
+
+        from evie_b200 import ops
+
+        g = torch.Generator(device=dev).manual_seed(7)
+        nbytes = self.M * self.K * 2
+        self.ncopy = max(1, (300 << 20) // nbytes + 1) if self.R <= 128 else 1
+        self.ws = [(torch.randn(self.M, self.K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                   for _ in range(self.ncopy)]
+        self.x2 = ops.split_planes(torch.randn(self.R, self.K, generator=g, device=dev))
+        self.y = torch.empty(16, self.R, self.M, device=dev) if self.R <= 128 else torch.empty(self.R, self.M,
+                                                                                                device=dev)
+        self.i = 0
+
+    def step(self):
+        import ctypes as C
+
+        import torch
+
+        from evie_b200 import check, lib
+
+        planes = C.c_int(0)
+        w = self.ws[self.i % self.ncopy]
+        self.i += 1
+        check(lib().evie_proj_gemm(w.data_ptr(), self.x2.data_ptr(), self.y.data_ptr(), self.y.numel(), self.M,
+                                   self.K, self.R, 16, C.byref(planes), torch.cuda.current_stream().cuda_stream))
+        return 1
+
+    def e2e_step(self):
+        import torch
+
+        if not hasattr(self, "x_host"):
+            self.x_host = self.x2.cpu().pin_memory()
+            self.y_host = torch.empty(self.R, self.M).pin_memory()
+        self.x2.copy_(self.x_host, non_blocking=True)
+        self.step()
+        self.y_host.copy_(self.y[0] if self.y.dim() == 3 else self.y, non_blocking=True)
+        return self.x_host.numel() * 2, self.R * self.M * 4
+
+    def cpu_sample(self, threads):
+        import oracle
+
+        oracle.set_threads(threads)
+        rng = np.random.default_rng(7)
+        R = min(self.R, 64)
+        w = rng.integers(0, 1 << 15, (self.M, self.K), dtype=np.uint16)
+        x = rng.standard_normal((R, self.K), dtype=np.float32)
+        oracle.matmul(w[:64], x)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 and n < 50:
+            oracle.matmul(w, x)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        return {"value": R / dt, "unit": "tokens/s", "cores": threads, "nproc": host_cpus(), "kind": "port",
+                "sample": f"{n} calls of the oracle's matmul (kernels.rs:138-268) at M={self.M} K={self.K} R={R}"}
+
+
 class ModelDecode(Workload):
     """Per GPU: Qwen3.5-4B shapes, random bf16 weights (seed 5), B sequences = B/2 steered/unsteered pairs,
     P-token uniform-random prompts, +0.6 dose Add steering on 32 seeded (layer, neuron) pairs on the steered half,
@@ -490,20 +577,30 @@ class ModelDecode(Workload):
     dtype = "f32"  # the arithmetic type; operands below
     dtype_detail = "f32 activations x bf16 weights (split-bf16 operands), fp32 DeltaNet state, bf16 KV"
 
-    def __init__(self, B=64, prompt=4096, rank=0):
-        assert B % 2 == 0
-        self.B, self.P, self.rank = B, prompt, rank
+    def __init__(self, B=64, prompt=4096, rank=0, model="4b"):
+        assert B % 2 == 0 and model in ("4b", "0.8b")
+        self.B, self.P, self.rank, self.model = B, prompt, rank, model
         self.tokens_per_step = B
         self.n_pairs_total = None
 
     def config(self):
-        return {"workload": f"Qwen3.5-4B-shaped decode, {self.B} sequences ({self.B // 2} steered/unsteered pairs) per "
-                            f"GPU, {self.P}-token prompts, greedy, steering +0.6 dose on 32 (layer, neuron) pairs, "
+        tag = "4B" if self.model == "4b" else "0.8B"
+        return {"workload": f"Qwen3.5-{tag}-shaped decode, {self.B} sequences ({self.B // 2} steered/unsteered pairs) "
+                            f"per GPU, {self.P}-token prompts, greedy, steering +0.6 dose on 32 (layer, neuron) pairs, "
                             f"full SwiGLU capture",
-                "model": "qwen3.5-4b-shaped (random init, seed 5)", "global_batch": self.B, "seq_len": self.P,
+                "model": f"qwen3.5-{self.model}-shaped (random init, seed 5)", "global_batch": self.B, "seq_len": self.P,
                 "l2": "inputs larger than L2 (8.4 GB weights + caches per step)",
                 "prefill_tok_s": getattr(self, "prefill_tok_s", None),
                 "prefill_ms": getattr(self, "prefill_ms", None)}
+
+    def checkpoint(self, device):
+        """The synthetic checkpoint (seed 5), written once per machine (shared by every rank and both arms)."""
+        from evie_b200 import checkpoint as ck
+
+        base = os.environ.get("EVIE_CKPT_DIR", tempfile.gettempdir())
+        shape = ck.QWEN35_4B if self.model == "4b" else ck.QWEN35_0_8B
+        name = "evie_qwen35_4b_seed5" if self.model == "4b" else "evie_qwen35_0p8b_seed5"
+        return ck.ensure_checkpoint(os.path.join(base, name), ck.text_config(shape), seed=5, device=device)
 
     def setup(self, dev):
         import torch
@@ -511,9 +608,7 @@ class ModelDecode(Workload):
         from evie_b200 import checkpoint as ck
         from evie_b200.gpu import GpuModel, GpuSeq
 
-        base = os.environ.get("EVIE_CKPT_DIR", tempfile.gettempdir())
-        self.ckpt = ck.ensure_checkpoint(os.path.join(base, "evie_qwen35_4b_seed5"), ck.text_config(ck.QWEN35_4B),
-                                         seed=5, device="cuda")
+        self.ckpt = self.checkpoint("cuda")
         self.cfg = json.load(open(os.path.join(self.ckpt, "config.json")))
         L, n, V = self.cfg["num_hidden_layers"], self.cfg["intermediate_size"], self.cfg["vocab_size"]
         self.max_ctx = self.P + 1024
@@ -756,9 +851,7 @@ class ModelDecode(Workload):
         import oracle
         from evie_b200 import checkpoint as ck
 
-        base = os.environ.get("EVIE_CKPT_DIR", tempfile.gettempdir())
-        self.ckpt = ck.ensure_checkpoint(os.path.join(base, "evie_qwen35_4b_seed5"), ck.text_config(ck.QWEN35_4B),
-                                         seed=5, device="cuda" if torch.cuda.is_available() else "cpu")
+        self.ckpt = self.checkpoint("cuda" if torch.cuda.is_available() else "cpu")
         self.cfg = json.load(open(os.path.join(self.ckpt, "config.json")))
         L, n, V = self.cfg["num_hidden_layers"], self.cfg["intermediate_size"], self.cfg["vocab_size"]
         g = torch.Generator().manual_seed(5)
@@ -815,7 +908,7 @@ class ModelDecode(Workload):
 
 
 WORKLOADS = {"gdn_decode": GdnDecode, "gdn_prefill": GdnPrefill, "gqa_decode": GqaDecode,
-             "model_decode": ModelDecode}
+             "model_decode": ModelDecode, "proj_gemm": ProjGemm}
 
 
 def make_workload(args):
@@ -825,6 +918,7 @@ def make_workload(args):
         kw["T"] = args.seq
     if cls is ModelDecode:
         kw["rank"] = dist_env()[0]
+        kw["model"] = args.model
         if args.prompt:
             kw["prompt"] = args.prompt
     return cls(**kw)
@@ -1071,6 +1165,8 @@ def main():
                     help="skip the isolated passes of the DeltaNet step, chunked prefill and paged attention")
     ap.add_argument("--batch", type=int, default=0, help="override the batch size (small profiling cases)")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length of model_decode")
+    ap.add_argument("--model", default="4b", choices=["4b", "0.8b"],
+                    help="model_decode shapes: Qwen3.5-4B (the benchmark) or 0.8B (small profiling cases)")
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length of gdn_prefill")
     args = ap.parse_args()
     if args.impl == "reference":

@@ -14,7 +14,10 @@ from evie_b200 import checkpoint as ck
 # 2e-3 holds with the f32 KV cache (EVIE_KV_F32=1, the oracle keeps f32 keys and values); the bf16 paged cache
 # rounds keys and values to 8 significant bits, measured up to 1.5e-2 here, and is held to 3e-2 with identical ids.
 LOGIT_TOL = 2e-3
-LOGIT_TOL_BF16_KV = 3e-2
+# The bf16 KV cache against the oracle that rounds its appended keys and values the same way (kv_bf16): keys and
+# values near a bf16 rounding boundary round differently after f32 reordering, which moves logits by a few 1e-3
+# (the 0.8B parity test measures that band); 1e-2 is the bound used there as well.
+LOGIT_TOL_BF16_KV = 1e-2
 
 
 @pytest.fixture(scope="module")
@@ -27,6 +30,12 @@ def tiny_ckpt(tmp_path_factory):
 @pytest.fixture(scope="module")
 def ref_model(tiny_ckpt):
     return oracle.Model(tiny_ckpt)
+
+
+@pytest.fixture(scope="module")
+def ref_model_bf16(tiny_ckpt):
+    """The oracle with bf16 rounding of appended keys and values, the storage of the default GPU cache."""
+    return oracle.Model(tiny_ckpt, kv_bf16=True)
 
 
 def _gpu_model(path, kv_f32, **kw):
@@ -45,10 +54,11 @@ def _gpu_model(path, kv_f32, **kw):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("kv_f32", [True, False])
-def test_prefill_and_greedy_decode(tiny_ckpt, ref_model, kv_f32, cuda):
+def test_prefill_and_greedy_decode(tiny_ckpt, ref_model, ref_model_bf16, kv_f32, cuda):
     from evie_b200.gpu import GpuSeq
 
     tol = LOGIT_TOL if kv_f32 else LOGIT_TOL_BF16_KV
+    ref_model = ref_model if kv_f32 else ref_model_bf16
     m = _gpu_model(tiny_ckpt, kv_f32, max_ctx=512, slots=2, max_rows=128)
     rng = np.random.default_rng(1)
     prompt = rng.integers(0, 2048, 40).astype(np.uint32)
