@@ -74,6 +74,7 @@ SIGNATURES = {
     "evie_poll_device_errors": (I, []),
     "evie_bounded_wait_probe": (I, [C.c_uint64, P]),
     "evie_gqa_decode_paged": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, F, P]),
+    "evie_gqa_prefill_paged": (I, [P, P, P, P, I, P, I, P, P, I, P, I, I, I, I, F, P]),
     "evie_gqa_decode_paged_noalloc": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, F, P]),
 }
 

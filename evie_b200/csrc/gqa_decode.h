@@ -27,4 +27,12 @@ evie_status launch_gqa_prefill_model(const float* q_rot, YView y, int ldy, __nv_
                                      const int* page_table, int pages_per_slot, const __nv_bfloat16* kc,
                                      const __nv_bfloat16* vc, int Hq, int Hkv, int page_size, float scale,
                                      cudaStream_t st);
+// The same rows on tcgen05 tensor cores (gqa_prefill_tc.cu): blocks of 32 rows x the 4 query heads of a KV head,
+// 64-token K/V tiles by TMA, S and O accumulated in tensor memory. cache_rows = pages x Hkv x page_size (the rows of
+// the cache viewed as [rows][256]); page size a multiple of 64.
+evie_status launch_gqa_prefill_tc_model(const float* q_rot, YView y, int ldy, __nv_bfloat16* X2, size_t xplane,
+                                        const SegInfo* segs, int nseg, int max_seg_rows, const int* page_table,
+                                        int pages_per_slot, const __nv_bfloat16* kc, const __nv_bfloat16* vc,
+                                        long cache_rows, int Hq, int Hkv, int page_size, float scale,
+                                        cudaStream_t st);
 }  // namespace evie

@@ -235,6 +235,7 @@ struct evie_ctx {
   int max_planes = evie::YView::kMaxPlanes;  // K slices per projection at most (EVIE_GEMM_PLANES=1..16 at creation)
   size_t y2_cap() const { return (size_t)2 * max_rows * y2_cols; }
   bool attn_rowwise = false;  // EVIE_ATTN_ROWWISE=1 at creation: prefill rows use the per-row split-KV kernel too
+  bool attn_prefill_mma = false;  // EVIE_ATTN_PREFILL_MMA=1 at creation: prefill attention on the mma.sync kernel
   bool no_graph = false;      // EVIE_NO_GRAPH=1 at creation: decode-shaped calls run eagerly
   // Captured decode-shaped forward calls, keyed by (sequences, want logits, head, capture, tracking, context bound).
   // The host capture destinations are part of the key: their copies are nodes of the graph.
@@ -622,6 +623,7 @@ evie_status allocate_state(evie_ctx* c) {
   if (const char* e = getenv("EVIE_NO_PDL")) c->pdl = e[0] != '1';
   if (const char* e = getenv("EVIE_GEMM_PLANES")) c->max_planes = std::min(evie::YView::kMaxPlanes, std::max(1, atoi(e)));
   if (const char* e = getenv("EVIE_ATTN_ROWWISE")) c->attn_rowwise = e[0] == '1';
+  if (const char* e = getenv("EVIE_ATTN_PREFILL_MMA")) c->attn_prefill_mma = e[0] == '1';
   if (const char* e = getenv("EVIE_NO_GRAPH")) c->no_graph = e[0] == '1';
   TRY(c->alloc(&c->act, R * s.conv_dim));
   TRY(c->alloc(&c->q_rot, R * s.nh * s.hd));
@@ -791,9 +793,15 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
           // prefill: blocks of 16 rows of a segment share every K/V tile (gqa_prefill.cu)
           int max_seg_rows = 0;
           for (int i = 0; i < nseq; i++) max_seg_rows = std::max(max_seg_rows, c->h_segs[i].count);
-          TRY(evie::launch_gqa_prefill_model(c->q_rot, y, s.in_at, c->X2, (size_t)R * s.nh * s.hd, c->d_rows,
-                                             c->d_segs, nseq, max_seg_rows, c->page_table, c->pages_per_slot, kc, vc,
-                                             s.nh, s.nkv, kPage, scale, st));
+          if (c->attn_prefill_mma)
+            TRY(evie::launch_gqa_prefill_model(c->q_rot, y, s.in_at, c->X2, (size_t)R * s.nh * s.hd, c->d_rows,
+                                               c->d_segs, nseq, max_seg_rows, c->page_table, c->pages_per_slot, kc,
+                                               vc, s.nh, s.nkv, kPage, scale, st));
+          else
+            TRY(evie::launch_gqa_prefill_tc_model(c->q_rot, y, s.in_at, c->X2, (size_t)R * s.nh * s.hd, c->d_segs,
+                                                  nseq, max_seg_rows, c->page_table, c->pages_per_slot, kc, vc,
+                                                  (long)c->slots * c->pages_per_slot * s.nkv * kPage, s.nh, s.nkv,
+                                                  kPage, scale, st));
         } else {
           TRY(evie::launch_gqa_model<__nv_bfloat16>(c->q_rot, y, s.in_at, c->X2,
                                                     (size_t)R * s.nh * s.hd, c->d_rows, R, c->page_table,

@@ -54,6 +54,25 @@ def gdn_prefill_tokenwise(q, k, v, g, beta, state, o=None):
     return o
 
 
+def gqa_prefill_paged(q, gate, k_pages, v_pages, page_table, seq_rows, seq_pos0, scale, out=None):
+    """Gated GQA attention for prefill rows (evie_gqa_prefill_paged). q, gate: [R,Hq,256] f32; k_pages, v_pages:
+    [P,Hkv,page,256] bf16; page_table [n_seqs,max_pages] int32 (device); seq_rows, seq_pos0: lists of n_seqs ints
+    (sequence s owns the next seq_rows[s] rows, at positions seq_pos0[s] ...). Returns out [R,Hq,256] f32."""
+    import ctypes as C
+
+    R, Hq, hd = q.shape
+    P, Hkv, page, _ = k_pages.shape
+    n = len(seq_rows)
+    if out is None:
+        out = torch.empty(R, Hq, hd, device=q.device, dtype=torch.float32)
+    rows = (C.c_int32 * n)(*seq_rows)
+    pos0 = (C.c_int32 * n)(*seq_pos0)
+    check(lib().evie_gqa_prefill_paged(_ptr(q), _ptr(gate), _ptr(k_pages), _ptr(v_pages), P, _ptr(page_table),
+                                       page_table.shape[1], rows, pos0, n, _ptr(out), Hq, Hkv, hd, page,
+                                       float(scale), _stream()))
+    return out
+
+
 def split_planes(x: torch.Tensor) -> torch.Tensor:
     """The split operand of an f32 matrix x [R,K]: [2,R,K] bf16 with hi = bf16(x) and lo = bf16(x - hi)."""
     hi = x.to(torch.bfloat16)

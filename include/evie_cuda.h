@@ -266,6 +266,21 @@ EVIE_API evie_status evie_gqa_decode_paged(const void* q, const void* gate, cons
                                   const int32_t* page_table, const int32_t* ctx_lens, float* out, int B, int Hq,
                                   int Hkv, int hd, int page_size, int max_pages, float scale, void* stream);
 
+/* Gated GQA softmax attention for prefill rows (the attention core of Model::attention, model.rs:445-464, for every
+ * new row of a prompt; WGSL attn_scores/attn_out, gpu/kernels.wgsl:508-589) on tcgen05 tensor cores:
+ *   out[r,h] = softmax(scale * q[r,h] . K[s, 0..pos_r]) V[s, 0..pos_r] * sigmoid(gate[r,h]),
+ * where sequence s owns rows [start_s, start_s + seq_rows[s]) (sequences in order), row i of it at position
+ * pos_r = seq_pos0[s] + i, whose keys and values (those of the row itself included) are already in its pages.
+ *   q, gate (logits), out: [rows][Hq][hd] f32 device (q, gate 16-byte aligned);
+ *   k_pages, v_pages: [num_pages][Hkv][page_size][hd] bf16 device (16-byte aligned);
+ *   page_table: [n_seqs][max_pages] int32 device; seq_rows, seq_pos0: [n_seqs] int32 host.
+ * hd = 256, Hq = 4 Hkv, page_size a multiple of 64. The segment table is copied to a device buffer the library keeps
+ * per (device, stream); the call waits for that copy. */
+EVIE_API evie_status evie_gqa_prefill_paged(const float* q, const float* gate, const void* k_pages, const void* v_pages,
+                                            int num_pages, const int32_t* page_table, int max_pages,
+                                            const int32_t* seq_rows, const int32_t* seq_pos0, int n_seqs, float* out,
+                                            int Hq, int Hkv, int hd, int page_size, float scale, void* stream);
+
 /* The same attention as evie_gqa_decode_paged, for callers that cannot let the library allocate device memory:
  * serving engines that reserve nearly all GPU memory for their own allocator at start-up, and latency-critical
  * callers that cannot afford cudaMalloc's device synchronisation. It calls no cudaMalloc, cudaFree or allocating

@@ -70,6 +70,7 @@ def _declare(L):
         "oracle_gdn_decode": (None, [I, I, I, I, P, P, P, P, P, P, P]),
         "oracle_gdn_prefill": (None, [I, I, I, I, I, P, P, P, P, P, P, P]),
         "oracle_gqa_decode": (None, [I, I, I, I, I, P, P, P, P, I, P, P, F, P]),
+        "oracle_gqa_rows": (None, [I, I, I, I, I, P, P, P, P, I, P, P, P, F, P]),
         "oracle_model_new": (P, [P, P]),
         "oracle_model_free": (None, [P]),
         "oracle_model_kv_bf16": (None, [P, I, F]),
@@ -204,6 +205,24 @@ def gdn_prefill(S, q, k, v, g, beta):
     args = [np.ascontiguousarray(a) for a in (q, k, v, g, beta)]
     lib().oracle_gdn_prefill(B, T, H, dk, dv, _p(S), *[_p(a) for a in args], _p(o))
     return o
+
+
+def gqa_rows(q, kpages, vpages, page_table, row_seq, row_pos, gate, scale):
+    """model.rs:445-464 for prefill rows: q, gate f32 [R, Hq, hd]; pages bf16 bits [P, Hkv, page, hd]; page_table
+    [n_seqs, max_pages]; row r attends to positions 0..row_pos[r] of sequence row_seq[r]. Returns [R, Hq, hd]."""
+    q = np.ascontiguousarray(q, np.float32)
+    gate = np.ascontiguousarray(gate, np.float32)
+    kpages = np.ascontiguousarray(kpages, np.uint16)
+    vpages = np.ascontiguousarray(vpages, np.uint16)
+    pt = np.ascontiguousarray(page_table, np.int32)
+    rs = np.ascontiguousarray(row_seq, np.int32)
+    rp = np.ascontiguousarray(row_pos, np.int32)
+    R, Hq, hd = q.shape
+    _, Hkv, page, _ = kpages.shape
+    out = np.zeros((R, Hq, hd), np.float32)
+    lib().oracle_gqa_rows(R, Hq, Hkv, hd, page, _p(q), _p(kpages), _p(vpages), _p(pt), pt.shape[1], _p(rs), _p(rp),
+                          _p(gate), scale, _p(out))
+    return out
 
 
 def gqa_decode(q, kpages, vpages, page_table, ctx, gate, scale):

@@ -1098,6 +1098,40 @@ EXPORT void oracle_gqa_decode(int B, int Hq, int Hkv, int hd, int page_size, con
   });
 }
 
+// The attention core of Model::attention (model.rs:445-464) for prefill rows with f32 queries and gate logits over a
+// paged bf16 cache: row r belongs to sequence row_seq[r] (its page-table row) and sits at position row_pos[r], so
+// its context is positions 0..row_pos[r]. q, gate, out: [R][Hq][hd]; pages: [num_pages][Hkv][page_size][hd].
+EXPORT void oracle_gqa_rows(int R, int Hq, int Hkv, int hd, int page_size, const float* q, const uint16_t* kp,
+                            const uint16_t* vp, const int32_t* page_table, int max_pages, const int32_t* row_seq,
+                            const int32_t* row_pos, const float* gate, float scale, float* out) {
+  int group = Hq / Hkv;
+  par_for((long)R * Hq, [&](long rh) {
+    long r = rh / Hq;
+    int head = (int)(rh % Hq), kvh = head / group;
+    long s = row_seq[r], n = (long)row_pos[r] + 1;
+    std::vector<float> kf(hd), sc(n);
+    auto row_of = [&](const uint16_t* pages, long j) {
+      long page = page_table[s * max_pages + j / page_size];
+      return pages + (((size_t)page * Hkv + kvh) * page_size + (size_t)(j % page_size)) * hd;
+    };
+    const float* qr = q + (size_t)rh * hd;
+    for (long j = 0; j < n; j++) {
+      const uint16_t* kr = row_of(kp, j);
+      for (int i = 0; i < hd; i++) kf[i] = bf16_to_f32(kr[i]);
+      sc[j] = dot(qr, kf.data(), hd) * scale;
+    }
+    softmax_inplace(sc.data(), n);
+    float* oh = out + (size_t)rh * hd;
+    for (int i = 0; i < hd; i++) oh[i] = 0.0f;
+    for (long j = 0; j < n; j++) {
+      const uint16_t* vr = row_of(vp, j);
+      float p = sc[j];
+      for (int i = 0; i < hd; i++) oh[i] += p * bf16_to_f32(vr[i]);
+    }
+    for (int i = 0; i < hd; i++) oh[i] *= sigmoid(gate[(size_t)rh * hd + i]);
+  });
+}
+
 // ---- model ----
 
 struct oracle_cfg {

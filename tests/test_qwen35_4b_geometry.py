@@ -8,8 +8,8 @@ all eight sequences per call, with the SwiGLU capture on. Against the oracle (ev
 greedy ids identical; logits within 2e-3 with the f32 KV cache, and within 1e-2 with the default bf16 KV cache
 against the oracle that stores keys and values in bf16 too (the bound of the 0.8B parity test, which measures why);
 captured frames within one companding step or, near zero where the square-root companding (q = round(127
-sqrt|a|)) turns a 1e-4 difference into two steps, within the run's logit tolerance in activation units; fewer
-than 1 in 1000 entries differ at all."""
+sqrt|a|)) turns a 1e-4 difference into two steps, within the run's logit tolerance in activation units. Fewer than 1 in 100 entries differ at all: near zero the
+companding's slope, 127 / (2 sqrt|a|), turns absolute differences of ~1e-6 into a flip of the rounding."""
 import os
 import tempfile
 
@@ -100,7 +100,7 @@ def test_4b_geometry_steered_pairs(ckpt_4b4, kv_f32, cuda):
         da = np.abs(dec(g) - dec(r))
         bad = (d > 1) & (da > TOL[kv_f32])
         assert not bad.any(), (i, int(d.max()), float(da[d > 1].max()))
-        assert (d != 0).mean() < 1e-3, (i, float((d != 0).mean()))
+        assert (d != 0).mean() < 1e-2, (i, float((d != 0).mean()))
     # the steering acted: the set op holds neuron 9000 of layer 2 at -2.0 on every steered row
     n = ck.QWEN35_4B["intermediate_size"]
     g0 = fr_steps[0][0].reshape(2 * PAIRS, PROMPT, -1)
