@@ -1,4 +1,5 @@
 // Error-message storage behind evie_last_global_error(), and the per-device kernel attribute cache.
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <tuple>
@@ -20,6 +21,14 @@ evie_status func_attr(const void* fn, cudaFuncAttribute attr, int value) {
 evie_status max_dynamic_smem(const void* fn, int bytes) {
   return func_attr(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("EVIE_PDL_ALL");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 std::string& thread_error() {
   thread_local std::string msg;
   return msg;

@@ -128,6 +128,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     gqa_decode_kernel(IO io, const KV* __restrict__ kp, const KV* __restrict__ vp, int Hkv, int page_size,
                       int max_pages, float scale, Scratch scr) {
   pdl_trigger();
+  pdl_wait();
   constexpr int kTokIter = 32 / GROUP;  // tokens per reduce-scatter round
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
@@ -375,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     gqa_decode_mma_kernel(IO io, const __nv_bfloat16* __restrict__ kp, const __nv_bfloat16* __restrict__ vp, int Hkv,
                           int page_size, int max_pages, float scale, Scratch scr) {
   pdl_trigger();
+  pdl_wait();
   constexpr int GROUP = 4;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -645,6 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                            int Hkv, int page_size, int max_pages, float scale, Scratch scr,
                            unsigned int* timeouts) {
   pdl_trigger();
+  pdl_wait();
   constexpr int GROUP = 4;
   extern __shared__ __align__(128) uint8_t ring_all[];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -1029,19 +1032,19 @@ evie_status launch_gqa(const IO& io, const KV* kp, const KV* vp, int B, int Hq, 
         unsigned int* counter = device_timeout_counter();
         if (!counter) return fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
         EVIE_TRY(max_dynamic_smem((const void*)gqa_decode_bulk_kernel<IO>, kRingBytes));
-        gqa_decode_bulk_kernel<IO><<<grid, kThreads, kRingBytes, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale,
-                                                                        scr, counter);
+        EVIE_CUDA_TRY(launch_k(gqa_decode_bulk_kernel<IO>, dim3(grid), dim3(kThreads), kRingBytes, st, io, kp, vp, Hkv, page_size, max_pages, scale,
+                                                                        scr, counter));
         EVIE_CHECK_LAUNCH("gqa_decode_bulk_kernel");
         return EVIE_OK;
       }
-      gqa_decode_mma_kernel<IO><<<grid, kThreads, 0, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale, scr);
+      EVIE_CUDA_TRY(launch_k(gqa_decode_mma_kernel<IO>, dim3(grid), dim3(kThreads), 0, st, io, kp, vp, Hkv, page_size, max_pages, scale, scr));
       EVIE_CHECK_LAUNCH("gqa_decode_mma_kernel");
       return EVIE_OK;
     }
   }
   switch (group) {
-    case 2: gqa_decode_kernel<2, KV, IO><<<grid, kThreads, 0, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale, scr); break;
-    case 4: gqa_decode_kernel<4, KV, IO><<<grid, kThreads, 0, st>>>(io, kp, vp, Hkv, page_size, max_pages, scale, scr); break;
+    case 2: EVIE_CUDA_TRY(launch_k(gqa_decode_kernel<2, KV, IO>, dim3(grid), dim3(kThreads), 0, st, io, kp, vp, Hkv, page_size, max_pages, scale, scr)); break;
+    case 4: EVIE_CUDA_TRY(launch_k(gqa_decode_kernel<4, KV, IO>, dim3(grid), dim3(kThreads), 0, st, io, kp, vp, Hkv, page_size, max_pages, scale, scr)); break;
     default: return fail(EVIE_ERR_ARG, "GQA group %d not supported (2, 4)", group);
   }
   EVIE_CHECK_LAUNCH("gqa_decode_kernel");

@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const int* __restrict__ page_table, int pages_per_slot, const __nv_bfloat16* __restrict__ kc,
                        const __nv_bfloat16* __restrict__ vc, int Hq, int Hkv, int page_size, float scale) {
   pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t sm[];
   const int kvh = blockIdx.z;
   const SegInfo sg = segs[blockIdx.y];
@@ -277,8 +278,8 @@ evie_status launch_gqa_prefill_model(const float* q_rot, YView y, int ldy, __nv_
   if (page_size % kTile != 0) return fail(EVIE_ERR_ARG, "prefill attention: page size must be a multiple of %d", kTile);
   EVIE_TRY(max_dynamic_smem((const void*)gqa_prefill_kernel, (int)kSmem));
   dim3 grid((max_seg_rows + kRowsPerCta - 1) / kRowsPerCta, nseg, Hkv);
-  gqa_prefill_kernel<<<grid, kThreads, kSmem, st>>>(q_rot, y, ldy, X2, xplane, rows, segs, page_table, pages_per_slot,
-                                                    kc, vc, Hq, Hkv, page_size, scale);
+  EVIE_CUDA_TRY(launch_k(gqa_prefill_kernel, dim3(grid), dim3(kThreads), kSmem, st, q_rot, y, ldy, X2, xplane, rows, segs, page_table, pages_per_slot,
+                                                    kc, vc, Hq, Hkv, page_size, scale));
   EVIE_CHECK_LAUNCH("gqa_prefill_kernel");
   return EVIE_OK;
 }

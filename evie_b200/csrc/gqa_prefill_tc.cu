@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const SegInfo* __restrict__ segs, const int* __restrict__ page_table, int pages_per_slot,
                           int Hkv, int page_size, float qscale, unsigned int* timeouts) {
   pdl_trigger();
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   const int kvh = blockIdx.z;
@@ -396,8 +397,8 @@ evie_status launch(const IO& io, const SegInfo* segs, int nseg, int max_seg_rows
   auto* kern = gqa_prefill_tc_kernel<IO>;
   EVIE_TRY(max_dynamic_smem((const void*)kern, (int)kSmem));
   dim3 grid((max_seg_rows + kRows - 1) / kRows, nseg, Hkv);
-  kern<<<grid, kThreads, kSmem, st>>>(mk, mv, io, segs, page_table, pages_per_slot, Hkv, page_size, scale * kLog2e,
-                                      counter);
+  EVIE_CUDA_TRY(launch_k(kern, dim3(grid), dim3(kThreads), kSmem, st, mk, mv, io, segs, page_table, pages_per_slot, Hkv, page_size, scale * kLog2e,
+                                      counter));
   EVIE_CHECK_LAUNCH("gqa_prefill_tc_kernel");
   return EVIE_OK;
 }

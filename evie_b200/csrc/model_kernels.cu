@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(const RowInfo*
                                                                   size_t xplane, uint32_t* __restrict__ seen,
                                                                   int seen_words) {
   pdl_trigger();
+  pdl_wait();
   __shared__ float red[kNormThreads / 32];
   const int r = blockIdx.x;
   const RowInfo ri = rows[r];
@@ -143,6 +144,7 @@ __global__ void __launch_bounds__(1024) add_norm_kernel(float* __restrict__ x, Y
                                                         __nv_bfloat16* __restrict__ X2, size_t xplane,
                                                         uint16_t* __restrict__ resid, int cap_layer, int L) {
   pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int r = blockIdx.x;
   add_norm_row(x, y, ldy, r, d, gain, eps, X2, xplane, r, true, resid, cap_layer, L, red);
@@ -156,6 +158,7 @@ __global__ void __launch_bounds__(1024) add_final_kernel(float* __restrict__ x, 
                                                          __nv_bfloat16* __restrict__ X2,
                                                          uint16_t* __restrict__ resid, int cap_layer, int L) {
   pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int s = rows[r].seg;
@@ -173,6 +176,7 @@ __global__ void __launch_bounds__(128) conv_silu_norm_kernel(YView y, int ldy,
                                                              int hk, float qscale, float* __restrict__ act,
                                                              bool update_window) {
   pdl_trigger();
+  pdl_wait();
   __shared__ float red[4];
   const int c = blockIdx.x * 128 + threadIdx.x;
   const int r = blockIdx.y;
@@ -215,6 +219,7 @@ __global__ void __launch_bounds__(128) conv_decode4_kernel(YView y, int ldy, con
                                                            const float* __restrict__ conv_w, int conv_dim, int hk,
                                                            float qscale, float* __restrict__ act) {
   pdl_trigger();
+  pdl_wait();
   constexpr int K = 4;
   const int lane = threadIdx.x & 31;
   const int blk = blockIdx.x * 4 + (threadIdx.x >> 5);  // 128-channel block of this warp
@@ -281,6 +286,7 @@ __global__ void __launch_bounds__(128) conv_rows_kernel(YView y, int ldy, const 
                                                         const float* __restrict__ conv_w, int conv_dim, int hk,
                                                         float qscale, float* __restrict__ act) {
   pdl_trigger();
+  pdl_wait();
   __shared__ float red[4];
   const int c = blockIdx.x * 128 + threadIdx.x;
   const SegInfo sg = segs[blockIdx.y];
@@ -320,6 +326,7 @@ __global__ void conv_state_update_kernel(YView y, int ldy,
                                          const SegInfo* __restrict__ segs, float* __restrict__ conv_state,
                                          size_t cs_slot, int K, int conv_dim) {
   pdl_trigger();
+  pdl_wait();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= conv_dim) return;
   const SegInfo sg = segs[blockIdx.y];
@@ -342,6 +349,7 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
     const float* __restrict__ dt_bias, const float* __restrict__ norm_w, int conv_dim, int key_dim, int vd, int hv,
     int ratio, float eps, __nv_bfloat16* __restrict__ X2, size_t xplane) {
   pdl_trigger();
+  pdl_wait();
   constexpr int DK = 128, DV = 128;
   const int head = blockIdx.x;
   const SegInfo sg = segs[blockIdx.y];
@@ -358,19 +366,23 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
 #pragma unroll
   for (int r = 0; r < 16; r++) s[r] = *reinterpret_cast<const float4*>(Sh + (size_t)(warp + 8 * r) * DV);
 
+  __shared__ float s_db[2];  // this row's decay and beta
   for (int t = 0; t < sg.count; t++) {
     const int row = sg.start + t;
     const float* ar = act + (size_t)row * conv_dim;
     if (tid < DK) sq[tid] = ar[kh * DK + tid];
     else sk[tid - DK] = ar[key_dim + kh * DK + (tid - DK)];
     const float4 v4 = *reinterpret_cast<const float4*>(ar + 2 * key_dim + head * DV + lane * 4);
-    const float bb = y.at((size_t)row * ldy + conv_dim + vd + head);
-    const float aa = y.at((size_t)row * ldy + conv_dim + vd + hv + head);
+    if (tid == DK) {  // one thread reads the head's b and a logits (all K-slice planes) for the whole CTA
+      const float bb = y.at((size_t)row * ldy + conv_dim + vd + head);
+      const float aa = y.at((size_t)row * ldy + conv_dim + vd + hv + head);
+      s_db[0] = expf(neg_a[head] * softplus_(aa + dt_bias[head]));
+      s_db[1] = sigmoidf_(bb);
+    }
     // the output gate is read here, with the other inputs, so its latency is not exposed after the state update
     const float z = tid < DV ? y.at((size_t)row * ldy + conv_dim + head * DV + tid) : 0.f;
-    const float decay = expf(neg_a[head] * softplus_(aa + dt_bias[head]));
-    const float beta = sigmoidf_(bb);
     __syncthreads();
+    const float decay = s_db[0], beta = s_db[1];
     float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int r = 0; r < 16; r++) {
@@ -433,6 +445,7 @@ __global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_seq_kernel(
     size_t rs_slot, const float* __restrict__ neg_a, const float* __restrict__ dt_bias, const float* __restrict__ norm_w,
     int conv_dim, int key_dim, int vd, int hv, int ratio, float eps, __nv_bfloat16* __restrict__ X2, size_t xplane) {
   pdl_trigger();
+  pdl_wait();
   constexpr int DK = 128, DV = 128;
   extern __shared__ __align__(16) float smf[];
   float* sq = smf;                          // [32][128]
@@ -562,6 +575,7 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(YView y, int ldy,
                                                         KV* __restrict__ vc, const int* __restrict__ page_table,
                                                         int pages_per_slot, int page_size) {
   pdl_trigger();
+  pdl_wait();
   __shared__ float red[8];
   __shared__ float yn_s[256];
   const int idx = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
@@ -613,6 +627,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
                                                      int8_t* __restrict__ frames, uint32_t* __restrict__ maxbuf,
                                                      __nv_bfloat16* __restrict__ X2, size_t xplane) {
   pdl_trigger();
+  pdl_wait();
   __shared__ evie_op s_ops[64];
   __shared__ int s_cnt;
   const int r = blockIdx.y;
@@ -674,6 +689,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
 __global__ void __launch_bounds__(256) gate_detect_kernel(YView y, int ldy, const SegInfo* __restrict__ segs,
                                                           int layer, int n, int L, GateTables t) {
   pdl_trigger();
+  pdl_wait();
   __shared__ int s_min[8];
   const SegInfo sg = segs[blockIdx.x];
   const int sl = sg.slot;
@@ -736,6 +752,7 @@ __global__ void __launch_bounds__(256) logits_argmax_kernel(YView L2, int nseg, 
                                                             float* __restrict__ logits,
                                                             unsigned long long* __restrict__ best) {
   pdl_trigger();
+  pdl_wait();
   __shared__ unsigned long long red[8];
   const int s = blockIdx.y;
   unsigned long long key = 0;
@@ -766,6 +783,7 @@ __global__ void __launch_bounds__(256) logits_argmax_kernel(YView L2, int nseg, 
 
 __global__ void argmax_finish_kernel(unsigned long long* best, uint32_t* next_tokens, int nseg) {
   pdl_trigger();
+  pdl_wait();
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= nseg) return;
   next_tokens[s] = 0xFFFFFFFFu - (uint32_t)(best[s] & 0xFFFFFFFFull);
@@ -774,6 +792,7 @@ __global__ void argmax_finish_kernel(unsigned long long* best, uint32_t* next_to
 
 __global__ void advance_rows_kernel(RowInfo* rows, int nseq, const uint32_t* next) {
   pdl_trigger();
+  pdl_wait();
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= nseq) return;
   rows[s].pos += 1;
@@ -790,7 +809,7 @@ static int norm_threads(int d) {
 }
 
 evie_status k_advance_rows(RowInfo* rows, int nseq, const uint32_t* next, cudaStream_t st) {
-  advance_rows_kernel<<<(nseq + 127) / 128, 128, 0, st>>>(rows, nseq, next);
+  EVIE_CUDA_TRY(launch_k(advance_rows_kernel, dim3((nseq + 127) / 128), dim3(128), 0, st, rows, nseq, next));
   EVIE_CHECK_LAUNCH("advance_rows_kernel");
   return EVIE_OK;
 }
@@ -798,7 +817,7 @@ evie_status k_advance_rows(RowInfo* rows, int nseq, const uint32_t* next, cudaSt
 evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed, float* x, const float* gain,
                          float eps, int d, __nv_bfloat16* X2, uint32_t* seen, int seen_words, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
-  embed_norm_kernel<<<R, kNormThreads, 0, st>>>(rows, embed, x, gain, eps, d, X2, (size_t)R * d, seen, seen_words);
+  EVIE_CUDA_TRY(launch_k(embed_norm_kernel, dim3(R), dim3(kNormThreads), 0, st, rows, embed, x, gain, eps, d, X2, (size_t)R * d, seen, seen_words));
   EVIE_CHECK_LAUNCH("embed_norm_kernel");
   return EVIE_OK;
 }
@@ -806,7 +825,7 @@ evie_status k_embed_norm(const RowInfo* rows, int R, const __nv_bfloat16* embed,
 evie_status k_add_norm(float* x, YView y, int ldy, int R, const float* gain, float eps, int d,
                        __nv_bfloat16* X2, uint16_t* resid, int cap_layer, int L, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
-  add_norm_kernel<<<R, norm_threads(d), 0, st>>>(x, y, ldy, gain, eps, d, X2, (size_t)R * d, resid, cap_layer, L);
+  EVIE_CUDA_TRY(launch_k(add_norm_kernel, dim3(R), dim3(norm_threads(d)), 0, st, x, y, ldy, gain, eps, d, X2, (size_t)R * d, resid, cap_layer, L));
   EVIE_CHECK_LAUNCH("add_norm_kernel");
   return EVIE_OK;
 }
@@ -815,8 +834,8 @@ evie_status k_add_final(float* x, YView y, int ldy, int R, const RowInfo* rows, 
                         int nseg, const float* gain, float eps, int d, __nv_bfloat16* X2, uint16_t* resid,
                         int cap_layer, int L, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
-  add_final_kernel<<<R, norm_threads(d), 0, st>>>(x, y, ldy, rows, segs, nseg, gain, eps, d, X2, resid, cap_layer,
-                                                  L);
+  EVIE_CUDA_TRY(launch_k(add_final_kernel, dim3(R), dim3(norm_threads(d)), 0, st, x, y, ldy, rows, segs, nseg, gain, eps, d, X2, resid, cap_layer,
+                                                  L));
   EVIE_CHECK_LAUNCH("add_final_kernel");
   return EVIE_OK;
 }
@@ -827,8 +846,8 @@ evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const
   if (R == 0) return EVIE_OK;
   if (max_seg_rows > 1 && s.K == 4 && !update_window) {
     dim3 grid(s.conv_dim / 128, nseg, (max_seg_rows + kConvRows - 1) / kConvRows);
-    conv_rows_kernel<4><<<grid, 128, 0, st>>>(y, ldy, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
-                                              1.0f / sqrtf((float)s.dk), act);
+    EVIE_CUDA_TRY(launch_k(conv_rows_kernel<4>, dim3(grid), dim3(128), 0, st, y, ldy, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
+                                              1.0f / sqrtf((float)s.dk), act));
     EVIE_CHECK_LAUNCH("conv_rows_kernel");
     return EVIE_OK;
   }
@@ -836,14 +855,14 @@ evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const
   if (update_window && s.K == 4 && s.conv_dim % 128 == 0 && ldy % 4 == 0 && y.plane % 4 == 0 && cs_slot % 4 == 0 &&
       a16(y.p) && a16(conv_state) && a16(conv_w) && a16(act)) {
     dim3 grid((s.conv_dim + 511) / 512, R);
-    conv_decode4_kernel<<<grid, 128, 0, st>>>(y, ldy, rows, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
-                                              1.0f / sqrtf((float)s.dk), act);
+    EVIE_CUDA_TRY(launch_k(conv_decode4_kernel, dim3(grid), dim3(128), 0, st, y, ldy, rows, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
+                                              1.0f / sqrtf((float)s.dk), act));
     EVIE_CHECK_LAUNCH("conv_decode4_kernel");
     return EVIE_OK;
   }
   dim3 grid(s.conv_dim / 128, R);
-  conv_silu_norm_kernel<<<grid, 128, 0, st>>>(y, ldy, rows, segs, conv_state, cs_slot, conv_w, s.K,
-                                              s.conv_dim, s.hk, 1.0f / sqrtf((float)s.dk), act, update_window);
+  EVIE_CUDA_TRY(launch_k(conv_silu_norm_kernel, dim3(grid), dim3(128), 0, st, y, ldy, rows, segs, conv_state, cs_slot, conv_w, s.K,
+                                              s.conv_dim, s.hk, 1.0f / sqrtf((float)s.dk), act, update_window));
   EVIE_CHECK_LAUNCH("conv_silu_norm_kernel");
   return EVIE_OK;
 }
@@ -852,8 +871,8 @@ evie_status k_conv_state_update(YView y, int ldy, int R, const SegInfo* segs, in
                                 size_t cs_slot, const ModelShape& s, cudaStream_t st) {
   if (nseg == 0) return EVIE_OK;
   dim3 grid((s.conv_dim + 255) / 256, nseg);
-  conv_state_update_kernel<<<grid, 256, 0, st>>>(y, ldy, segs, conv_state, cs_slot, s.K,
-                                                 s.conv_dim);
+  EVIE_CUDA_TRY(launch_k(conv_state_update_kernel, dim3(grid), dim3(256), 0, st, y, ldy, segs, conv_state, cs_slot, s.K,
+                                                 s.conv_dim));
   EVIE_CHECK_LAUNCH("conv_state_update_kernel");
   return EVIE_OK;
 }
@@ -866,15 +885,15 @@ evie_status k_gdn_mixer(const float* act, YView y, int ldy, int R, const SegInfo
   if (R > nseg) {  // some segment has several rows: the warp-local sequential kernel
     constexpr int kSmemSeq = (5 * kSeqChunk * 128 + 2 * kSeqChunk) * 4;
     EVIE_TRY(max_dynamic_smem((const void*)gdn_mixer_seq_kernel, kSmemSeq));
-    gdn_mixer_seq_kernel<<<grid, kMixThreads, kSmemSeq, st>>>(act, y, ldy, segs, rec_state, rs_slot, neg_a, dt_bias,
+    EVIE_CUDA_TRY(launch_k(gdn_mixer_seq_kernel, dim3(grid), dim3(kMixThreads), kSmemSeq, st, act, y, ldy, segs, rec_state, rs_slot, neg_a, dt_bias,
                                                               norm_w, s.conv_dim, s.key_dim, s.vd, s.hv, s.hv / s.hk,
-                                                              s.eps, X2, (size_t)R * s.vd);
+                                                              s.eps, X2, (size_t)R * s.vd));
     EVIE_CHECK_LAUNCH("gdn_mixer_seq_kernel");
     return EVIE_OK;
   }
-  gdn_mixer_kernel<<<grid, kMixThreads, 0, st>>>(act, y, ldy, segs, rec_state, rs_slot, neg_a,
+  EVIE_CUDA_TRY(launch_k(gdn_mixer_kernel, dim3(grid), dim3(kMixThreads), 0, st, act, y, ldy, segs, rec_state, rs_slot, neg_a,
                                                  dt_bias, norm_w, s.conv_dim, s.key_dim, s.vd, s.hv, s.hv / s.hk, s.eps,
-                                                 X2, (size_t)R * s.vd);
+                                                 X2, (size_t)R * s.vd));
   EVIE_CHECK_LAUNCH("gdn_mixer_kernel");
   return EVIE_OK;
 }
@@ -885,8 +904,8 @@ evie_status k_attn_prep(YView y, int ldy, int R, const RowInfo* rows, const floa
                         KV* vc, const int* page_table, int pages_per_slot, int page_size, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
   dim3 grid(s.nh + s.nkv, R);
-  attn_prep_kernel<KV><<<grid, 256, 0, st>>>(y, ldy, rows, q_norm, k_norm, inv_freq, s.nh, s.nkv,
-                                             s.hd, s.rot, s.eps, q_rot, kc, vc, page_table, pages_per_slot, page_size);
+  EVIE_CUDA_TRY(launch_k(attn_prep_kernel<KV>, dim3(grid), dim3(256), 0, st, y, ldy, rows, q_norm, k_norm, inv_freq, s.nh, s.nkv,
+                                             s.hd, s.rot, s.eps, q_rot, kc, vc, page_table, pages_per_slot, page_size));
   EVIE_CHECK_LAUNCH("attn_prep_kernel");
   return EVIE_OK;
 }
@@ -902,8 +921,8 @@ evie_status k_swiglu(YView y, int ldy, int R, const RowInfo* rows, int layer, co
                      cudaStream_t st) {
   if (R == 0) return EVIE_OK;
   dim3 grid((s.n + 1023) / 1024, R);
-  swiglu_kernel<<<grid, 256, 0, st>>>(y, ldy, rows, layer, s.n, s.L, steer, scale, frames, maxbuf,
-                                      X2, (size_t)R * s.n);
+  EVIE_CUDA_TRY(launch_k(swiglu_kernel, dim3(grid), dim3(256), 0, st, y, ldy, rows, layer, s.n, s.L, steer, scale, frames, maxbuf,
+                                      X2, (size_t)R * s.n));
   EVIE_CHECK_LAUNCH("swiglu_kernel");
   return EVIE_OK;
 }
@@ -911,7 +930,7 @@ evie_status k_swiglu(YView y, int ldy, int R, const RowInfo* rows, int layer, co
 evie_status k_gate_detect(YView y, int ldy, const SegInfo* segs, int nseg, int layer, const ModelShape& s,
                           GateTables t, cudaStream_t st) {
   if (nseg == 0) return EVIE_OK;
-  gate_detect_kernel<<<nseg, 256, 0, st>>>(y, ldy, segs, layer, s.n, s.L, t);
+  EVIE_CUDA_TRY(launch_k(gate_detect_kernel, dim3(nseg), dim3(256), 0, st, y, ldy, segs, layer, s.n, s.L, t));
   EVIE_CHECK_LAUNCH("gate_detect_kernel");
   return EVIE_OK;
 }
@@ -920,9 +939,9 @@ evie_status k_logits_argmax(YView L2, int nseg, int V, float* logits, unsigned l
                             uint32_t* next_tokens, cudaStream_t st) {
   if (nseg == 0) return EVIE_OK;
   dim3 grid((V + 1023) / 1024, nseg);
-  logits_argmax_kernel<<<grid, 256, 0, st>>>(L2, nseg, V, logits, best);
+  EVIE_CUDA_TRY(launch_k(logits_argmax_kernel, dim3(grid), dim3(256), 0, st, L2, nseg, V, logits, best));
   EVIE_CHECK_LAUNCH("logits_argmax_kernel");
-  argmax_finish_kernel<<<(nseg + 127) / 128, 128, 0, st>>>(best, next_tokens, nseg);
+  EVIE_CUDA_TRY(launch_k(argmax_finish_kernel, dim3((nseg + 127) / 128), dim3(128), 0, st, best, next_tokens, nseg));
   EVIE_CHECK_LAUNCH("argmax_finish_kernel");
   return EVIE_OK;
 }

@@ -25,9 +25,10 @@
 // lanes (weight rows) of lane quarter w % 4 and one half of the tile's activation columns, 128 contiguous bytes
 // per activation row.
 //
-// Work units are (K slice, M tile, R tile), K slice fastest, so that consecutive CTAs read the same activation tile
-// from L2. Decode-shaped calls (R <= 128) cut K into slices until the units fill the SMs: each slice writes its own
-// plane and the consumer adds the planes in slice order. Larger R runs one slice over a persistent grid.
+// Work units are (K slice, M tile, R tile), K slice fastest. Decode-shaped calls (R <= 128, one R tile) cut K into
+// slices until the units fill the SMs: each slice writes its own plane and the consumer adds the planes in slice
+// order. Larger R runs one slice over a persistent grid, in bands of ~40 MB of weight tiles (M fastest, then R), so
+// that a band's weights stay in L2 while every operand tile passes through it.
 //
 // Programmatic dependent launch: the weights do not depend on the previous kernel, so the producer issues the weight
 // half of its first ring fill, then waits (griddepcontrol.wait) for the previous grid, then loads the activations.
@@ -38,6 +39,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -59,7 +61,7 @@ constexpr uint32_t kRingBudget = 196608;
 struct GemmArgs {
   float* y;      // [planes][R][M]
   size_t plane;  // R * M
-  int M, R, K, kc, ksplit, n_mt, units;
+  int M, R, K, kc, ksplit, n_mt, n_rt, band, units;
   int gchunks;  // K steps of 64 per accumulation group
   unsigned int* timeouts;
   int evict_first;  // weights read once per call (decode): L2 evict-first; otherwise evict-last
@@ -96,12 +98,18 @@ struct Cfg {
 struct Unit {
   int ks, mt, rt, c0, c1;
 };
+// Unit u -> (K slice, M tile, R tile). Tiles go in bands of `band` M tiles: within a band the M tile is fastest and
+// the R tile next, so the CTAs working at the same time share a band's weights (sized to stay in L2) and a few
+// operand tiles, and the weights are read from DRAM once per call, the operand once per band.
 __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u) {
   Unit x;
   x.ks = u % a.ksplit;
   const int t = u / a.ksplit;
-  x.mt = t % a.n_mt;
-  x.rt = t / a.n_mt;
+  const int per_band = a.band * a.n_rt;
+  const int b = t / per_band, v = t - b * per_band;
+  const int cnt = min(a.band, a.n_mt - b * a.band);
+  x.rt = v / cnt;
+  x.mt = b * a.band + v % cnt;
   x.c0 = (int)((long)x.ks * a.kc / a.ksplit);
   x.c1 = (int)((long)(x.ks + 1) * a.kc / a.ksplit);
   return x;
@@ -402,7 +410,9 @@ evie_status launch_tiles(const __nv_bfloat16* W, const __nv_bfloat16* X2, float*
   // Accumulation group: 4 K steps of 64 for decode tiles (drift -2e-7 relative, within 2% of the fastest setting),
   // 8 for the 256 x 128 prefill tiles (-9e-7). EVIE_GEMM_GROUP overrides both.
   const int gchunks = group_env ? group_env : (BR == 128 && R > 128 ? 8 : 4);
-  GemmArgs a{y, (size_t)R * M, M, R, K, (K + kKC - 1) / kKC, p.ksplit, (M + BM - 1) / BM, p.units,
+  const int n_mt = (M + BM - 1) / BM, n_rt = (R + BR - 1) / BR;
+  const int band = std::max(1, std::min(n_mt, (int)((40u << 20) / ((size_t)BM * K * 2))));  // ~40 MB of weights
+  GemmArgs a{y, (size_t)R * M, M, R, K, (K + kKC - 1) / kKC, p.ksplit, n_mt, n_rt, band, p.units,
              gchunks, counter, R <= 128 ? 1 : 0};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
@@ -461,12 +471,25 @@ ProjGemmPlan plan_proj_gemm(int M, int K, int R, int max_planes, size_t y_cap, i
 
 evie_status launch_proj_gemm(const __nv_bfloat16* W, int M, int K, const __nv_bfloat16* X2, int R, float* y,
                              size_t y_cap, int max_planes, bool pdl, cudaStream_t st, int* planes) {
+  // EVIE_GEMM_TILE=<bm>x<slices> (decode-shaped calls, e.g. 128x1) pins the tile plan, for measurements
+  static const std::pair<int, int> force = [] {
+    const char* e = getenv("EVIE_GEMM_TILE");
+    int bm = 0, ks = 0;
+    if (e && sscanf(e, "%dx%d", &bm, &ks) == 2 && (bm == 128 || bm == 256) && ks >= 1) return std::make_pair(bm, ks);
+    return std::make_pair(0, 0);
+  }();
   if (M <= 0 || K <= 0 || R <= 0) return fail(EVIE_ERR_ARG, "proj_gemm: empty shape %d x %d x %d", M, R, K);
   if (K % 8 != 0) return fail(EVIE_ERR_ARG, "proj_gemm: K = %d must be a multiple of 8 (16-byte rows)", K);
   if (((uintptr_t)W | (uintptr_t)X2) & 15) return fail(EVIE_ERR_ARG, "proj_gemm: W and X2 must be 16-byte aligned");
   if (max_planes < 1) return fail(EVIE_ERR_ARG, "proj_gemm: max_planes must be >= 1");
   if ((size_t)R * M > y_cap) return fail(EVIE_ERR_ARG, "proj_gemm: output of %d x %d floats exceeds its buffer", R, M);
-  const ProjGemmPlan p = plan_proj_gemm(M, K, R, max_planes, y_cap, sm_count());
+  ProjGemmPlan p = plan_proj_gemm(M, K, R, max_planes, y_cap, sm_count());
+  if (force.first && R <= 128 && p.br != 128 && (size_t)force.second * R * M <= y_cap) {
+    p.bm = force.first;
+    p.ksplit = std::min(force.second, std::max(1, (K + kKC - 1) / kKC));
+    p.units = ((M + p.bm - 1) / p.bm) * p.ksplit;
+    p.grid = std::min(p.units, sm_count());
+  }
   evie_status s;
   if (p.bm == 256 && p.br == 128) s = launch_tiles<256, 128>(W, X2, y, p, M, K, R, pdl, st);
   else if (p.bm == 256 && p.br == 64) s = launch_tiles<256, 64>(W, X2, y, p, M, K, R, pdl, st);

@@ -103,6 +103,7 @@ __device__ __forceinline__ float splitmix_uniform(uint64_t* state) {
 
 __global__ void __launch_bounds__(kThreads, 1) sample_kernel(SampleArgs a) {
   pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);  // [kCand]
   float* prob = reinterpret_cast<float*>(cand + kCand);                   // [kCand]
@@ -296,7 +297,7 @@ evie_status k_sample(const SampleArgs& a, int nseq, cudaStream_t st) {
         cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(EVIE_ERR_CUDA, "sampler: %s", cudaGetErrorString(e));
   }
-  sample_kernel<<<nseq, kThreads, smem, st>>>(a);
+  EVIE_CUDA_TRY(launch_k(sample_kernel, dim3(nseq), dim3(kThreads), smem, st, a));
   EVIE_CHECK_LAUNCH("sample_kernel");
   return EVIE_OK;
 }
