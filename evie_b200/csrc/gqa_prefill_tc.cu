@@ -21,9 +21,13 @@
 // The last tile's V rows past the block's last position are zeroed in shared memory before P V reads them (the
 // cache there may hold anything); its K rows need no zeroing (their scores are masked).
 //
-// Roles (192 threads): warp 0 lane 0 issues the K and V tile copies; warp 1 owns tensor memory and lane 0 issues
-// the MMAs; warps 2-5 run the softmax and the epilogue (O / l x sigmoid(gate), staged through shared memory so that
-// the stores are coalesced). Every mbarrier wait is bounded (2 s); a thread that gives up stops, the CTA drains its
+// Buffers: K single (its next copy waits for this tile's S MMAs, which are issued a tile ahead), V and P double,
+// so the softmax of tile j + 1 overlaps P V of tile j and only a rescale of O waits for it.
+//
+// Roles (224 threads): warp 0 lane 0 issues the K and V tile copies; warp 1 owns tensor memory and lane 0 issues
+// the S MMAs; warp 6 lane 0 issues the P V MMAs (a second issuing thread, so they never queue behind a wait for the
+// next K tile); warps 2-5 run the softmax and the epilogue (O / l x sigmoid(gate), staged through shared memory so
+// that the stores are coalesced). Every mbarrier wait is bounded (2 s); a thread that gives up stops, the CTA drains its
 // copies and MMAs (bounded again), frees TMEM and counts the give-up for the host.
 #include <cudaTypedefs.h>
 
@@ -44,7 +48,7 @@ constexpr int kHD = 256;
 constexpr int kGroup = 4;
 constexpr int kRows = 32;     // query rows per CTA (x 4 heads = M 128)
 constexpr int kTok = 64;      // tokens per K / V tile
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;  // warp 0 copies, warp 1 S MMAs (and TMEM), warps 2-5 softmax, warp 6 P V MMAs
 constexpr int kSoftThreads = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;  // log2 of the largest P value allowed before the running max is raised
@@ -53,16 +57,21 @@ constexpr float kRescale = 8.0f;  // log2 of the largest P value allowed before 
 constexpr uint32_t kQPlane = 65536;                  // 4 dim blocks x 128 rows x 128 B
 constexpr uint32_t kOffQH = 0, kOffQL = kQPlane;
 constexpr uint32_t kOffK = 2 * kQPlane;              // 4 dim blocks x 64 tokens x 128 B
-constexpr uint32_t kOffV = kOffK + 32768;
-constexpr uint32_t kOffBar = kOffV + 32768;
+constexpr uint32_t kOffV = kOffK + 32768;            // two buffers of 32 KB
+constexpr uint32_t kOffBar = kOffV + 65536;
 constexpr uint32_t kSmem = kOffBar + 256 + 1024;
+static_assert(kSmem <= 232448, "shared memory");
 constexpr int kStageStride = 260;                    // floats per staged output row (1040 B: conflict-free float4)
 static_assert(128 * kStageStride * 4 <= (int)kOffBar, "output staging must fit below the barriers");
 
-// TMEM columns
-constexpr uint32_t kColO = 0, kColS = 256, kColPH = 384, kColPL = 416;
+// TMEM columns: O, two S buffers, two P buffers (hi plane then lo plane, 32 columns each)
+constexpr uint32_t kColO = 0, kColS = 256, kColP = 384;
 
-enum { B_KFULL = 0, B_KFREE, B_VFULL, B_S0, B_S1, B_SF0, B_SF1, B_PFULL, B_PVDONE, B_DRAIN, kNumBars };
+// mbarriers; the double-buffered ones have one barrier per buffer, so that a wait never aliases a later phase
+enum {
+  B_KFULL = 0, B_KFREE, B_VF0, B_VF1, B_S0, B_S1, B_SF0, B_SF1, B_PF0, B_PF1, B_PV0, B_PV1, B_DRAIN, B_DRAIN2,
+  kNumBars
+};
 
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4); }
 
@@ -129,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < kNumBars; i++)
-      tc::mbar_init(&bar[i], (i == B_SF0 || i == B_SF1 || i == B_PFULL) ? kSoftThreads : 1);
+      tc::mbar_init(&bar[i], (i == B_SF0 || i == B_SF1 || i == B_PF0 || i == B_PF1) ? kSoftThreads : 1);
     s_fail = 0;
     tc::fence_barrier_init();
     tc::prefetch_tmap(&mk);
@@ -138,30 +147,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
 
   // ---- Q: rows m = 32 head + row (head of the group), 256 dims, scaled by scale log2 e, split into bf16 hi + lo,
-  // K-major 128-byte-swizzled tiles of 64 dims. Rows past the block are zero.
-  for (int u = tid; u < 128 * 32; u += kThreads) {
-    const int m = u >> 5, k16 = u & 31, hq = m >> 5, r = m & 31;  // k16: 8-dim unit of the row
-    float x[8];
-    if (r < nr) {
-      const float* qp = io.qrow(row0 + r, kvh * kGroup + hq) + 8 * k16;
-      const float4 a = *reinterpret_cast<const float4*>(qp);
-      const float4 b = *reinterpret_cast<const float4*>(qp + 4);
-      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-    } else {
+  // K-major 128-byte-swizzled tiles of 64 dims. Rows past the block are zero. Eight 8-dim units per thread are
+  // loaded before any is converted, so their global loads overlap.
+  constexpr int kQUnits = 128 * 32;
+  for (int u0 = tid; u0 < kQUnits; u0 += 8 * kThreads) {
+    float x[8][8];
 #pragma unroll
-      for (int i = 0; i < 8; i++) x[i] = 0.f;
-    }
-    uint32_t hi[4], lo[4];
+    for (int k = 0; k < 8; k++) {
+      const int u = u0 + k * kThreads, m = u >> 5, k16 = u & 31, hq = m >> 5, r = m & 31;
+      if (u < kQUnits && r < nr) {
+        const float* qp = io.qrow(row0 + r, kvh * kGroup + hq) + 8 * k16;
+        const float4 a = *reinterpret_cast<const float4*>(qp);
+        const float4 b = *reinterpret_cast<const float4*>(qp + 4);
+        x[k][0] = a.x; x[k][1] = a.y; x[k][2] = a.z; x[k][3] = a.w;
+        x[k][4] = b.x; x[k][5] = b.y; x[k][6] = b.z; x[k][7] = b.w;
+      } else {
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const float v0 = x[2 * i] * qscale, v1 = x[2 * i + 1] * qscale;
-      const float h0 = __bfloat162float(__float2bfloat16_rn(v0)), h1 = __bfloat162float(__float2bfloat16_rn(v1));
-      hi[i] = pack_rn(h0, h1);
-      lo[i] = pack_rn(v0 - h0, v1 - h1);
+        for (int i = 0; i < 8; i++) x[k][i] = 0.f;
+      }
     }
-    const uint32_t off = (uint32_t)(k16 >> 3) * 16384u + swz(m, k16 & 7);
-    *reinterpret_cast<uint4*>(sm + kOffQH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(sm + kOffQL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int u = u0 + k * kThreads, m = u >> 5, k16 = u & 31;
+      if (u >= kQUnits) break;
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float v0 = x[k][2 * i] * qscale, v1 = x[k][2 * i + 1] * qscale;
+        const float h0 = __bfloat162float(__float2bfloat16_rn(v0)), h1 = __bfloat162float(__float2bfloat16_rn(v1));
+        hi[i] = pack_rn(h0, h1);
+        lo[i] = pack_rn(v0 - h0, v1 - h1);
+      }
+      const uint32_t off = (uint32_t)(k16 >> 3) * 16384u + swz(m, k16 & 7);
+      *reinterpret_cast<uint4*>(sm + kOffQH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(sm + kOffQL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
   }
   tc::fence_proxy_async();
   tc::fence_before_sync();
@@ -169,11 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
-  int kfills = 0, vfills = 0;  // producer: copies armed
+  int kfills = 0, vfills[2] = {0, 0};  // producer: copies armed
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- K / V tile copies
+      // ---- K (one buffer) and V (two buffers) tile copies
       for (int j = 0; j < ntiles && ok; j++) {
         const int tok0 = j * kTok;
         const int krow = (pt[tok0 / page_size] * Hkv + kvh) * page_size + tok0 % page_size;
@@ -181,23 +201,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mbar_arrive_expect_tx(&bar[B_KFULL], 32768);
         kfills++;
         for (int c = 0; c < 4; c++) tc::tma_load_2d(sm + kOffK + c * 8192, &mk, &bar[B_KFULL], c * 64, krow);
-        if (j >= 1 && !tc::mbar_wait(&bar[B_PVDONE], (j - 1) & 1)) { ok = false; break; }
-        tc::mbar_arrive_expect_tx(&bar[B_VFULL], 32768);
-        vfills++;
-        for (int c = 0; c < 4; c++) tc::tma_load_2d(sm + kOffV + c * 8192, &mv, &bar[B_VFULL], c * 64, krow);
+        const int vb = j & 1;  // V buffer of tile j was read by P V of tile j - 2
+        if (j >= 2 && !tc::mbar_wait(&bar[B_PV0 + vb], ((j - 2) >> 1) & 1)) { ok = false; break; }
+        tc::mbar_arrive_expect_tx(&bar[B_VF0 + vb], 32768);
+        vfills[vb]++;
+        for (int c = 0; c < 4; c++)
+          tc::tma_load_2d(sm + kOffV + vb * 32768 + c * 8192, &mv, &bar[B_VF0 + vb], c * 64, krow);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---- MMA issue
+      // ---- S MMAs, running ahead of the softmax as far as the S buffers and the K copies allow
       constexpr uint32_t idS = tc::idesc(1, 1, 128, kTok);
-      constexpr uint32_t idO = tc::idesc(1, 1, 128, kHD, false, true);
       const uint64_t dQH = tc::sdesc_k_sw128(sm + kOffQH), dQL = tc::sdesc_k_sw128(sm + kOffQL);
       const uint64_t dK = tc::sdesc_k_sw128(sm + kOffK);
-      const uint64_t dV = tc::sdesc_mn_sw128(sm + kOffV, 8192, 1024);
-      auto issue_s = [&](int j) -> bool {
-        if (!tc::mbar_wait(&bar[B_KFULL], j & 1)) return false;
-        if (j >= 2 && !tc::mbar_wait(&bar[B_SF0 + (j & 1)], ((j - 2) >> 1) & 1)) return false;
+      for (int j = 0; j < ntiles; j++) {
+        if (!tc::mbar_wait(&bar[B_KFULL], j & 1)) { ok = false; break; }
+        if (j >= 2 && !tc::mbar_wait(&bar[B_SF0 + (j & 1)], ((j - 2) >> 1) & 1)) { ok = false; break; }
         tc::fence_after_sync();
         const uint32_t d = tmem + kColS + (uint32_t)(j & 1) * kTok;
         int n = 0;
@@ -211,46 +231,54 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         tc::mma_commit(&bar[B_KFREE]);
         tc::mma_commit(&bar[B_S0 + (j & 1)]);
-        return true;
-      };
-      ok = issue_s(0);
-      for (int j = 0; j < ntiles && ok; j++) {
-        if (j + 1 < ntiles && !issue_s(j + 1)) { ok = false; break; }
-        if (!tc::mbar_wait(&bar[B_PFULL], j & 1) || !tc::mbar_wait(&bar[B_VFULL], j & 1)) { ok = false; break; }
-        tc::fence_after_sync();
-#pragma unroll
-        for (int kk = 0; kk < kTok / 16; kk++) {
-          tc::mma_f16_ts(tmem + kColO, tmem + kColPH + kk * 8, dV + ((kk * 2048) >> 4), idO, (j > 0 || kk > 0));
-          tc::mma_f16_ts(tmem + kColO, tmem + kColPL + kk * 8, dV + ((kk * 2048) >> 4), idO, 1u);
-        }
-        tc::mma_commit(&bar[B_PVDONE]);
       }
       tc::mma_commit(&bar[B_DRAIN]);
       if (!tc::mbar_wait(&bar[B_DRAIN], 0)) ok = false;
     }
-  } else {
+  } else if (warp == 6) {
+    if (lane == 0) {
+      // ---- P V MMAs (another issuing thread: they never wait behind a K copy)
+      constexpr uint32_t idO = tc::idesc(1, 1, 128, kHD, false, true);
+      const uint64_t dV = tc::sdesc_mn_sw128(sm + kOffV, 8192, 1024);
+      for (int j = 0; j < ntiles; j++) {
+        const int b = j & 1;
+        if (!tc::mbar_wait(&bar[B_PF0 + b], (j >> 1) & 1) || !tc::mbar_wait(&bar[B_VF0 + b], (j >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t ph = tmem + kColP + (uint32_t)b * 64, pl = ph + 32;
+        const uint64_t dvb = dV + ((uint32_t)(b * 32768) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kTok / 16; kk++) {
+          tc::mma_f16_ts(tmem + kColO, ph + kk * 8, dvb + ((kk * 2048) >> 4), idO, (j > 0 || kk > 0));
+          tc::mma_f16_ts(tmem + kColO, pl + kk * 8, dvb + ((kk * 2048) >> 4), idO, 1u);
+        }
+        tc::mma_commit(&bar[B_PV0 + b]);
+      }
+      tc::mma_commit(&bar[B_DRAIN2]);
+      if (!tc::mbar_wait(&bar[B_DRAIN2], 0)) ok = false;
+    }
+  } else if (warp < 6) {
     // ---- softmax: thread = (head q of the group, row `lane`) in TMEM lane quarter q
     const int q = warp & 3;
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
     const int pr = min(pos_first + lane, pmax);  // rows past the block take the last position (outputs unused)
     float m_run = -INFINITY, l = 0.f;
     for (int j = 0; j < ntiles; j++) {
-      if (!tc::mbar_wait(&bar[B_S0 + (j & 1)], (j >> 1) & 1)) { ok = false; break; }
+      const int b = j & 1;
+      if (!tc::mbar_wait(&bar[B_S0 + b], (j >> 1) & 1)) { ok = false; break; }
       tc::fence_after_sync();
       float s[kTok];
-      tc::tmem_ld32(tl + kColS + (j & 1) * kTok, s);
-      tc::tmem_ld32(tl + kColS + (j & 1) * kTok + 32, s + 32);
+      tc::tmem_ld32(tl + kColS + b * kTok, s);
+      tc::tmem_ld32(tl + kColS + b * kTok + 32, s + 32);
       tc::fence_before_sync();
-      tc::mbar_arrive(&bar[B_SF0 + (j & 1)]);  // S buffer free for tile j + 2
+      tc::mbar_arrive(&bar[B_SF0 + b]);  // S buffer free for tile j + 2
       float mt = -INFINITY;
 #pragma unroll
       for (int i = 0; i < kTok; i++) {
         if (j * kTok + i > pr) s[i] = -INFINITY;
         mt = fmaxf(mt, s[i]);
-      }
-      if (j >= 1) {  // P V of the previous tile is complete: the P columns and O may be rewritten
-        if (!tc::mbar_wait(&bar[B_PVDONE], (j - 1) & 1)) { ok = false; break; }
-        tc::fence_after_sync();
       }
       const bool raise = mt > m_run + kRescale;
       float alpha = 1.f;
@@ -259,7 +287,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_run = mt;
         l *= alpha;
       }
-      if (j >= 1 && __any_sync(0xffffffffu, raise)) {  // rescale this warp's O rows (warp-wide TMEM access)
+      if (j >= 1 && __any_sync(0xffffffffu, raise)) {
+        // rescale this warp's O rows once P V of the previous tile has landed (warp-wide TMEM access)
+        if (!tc::mbar_wait(&bar[B_PV0 + (b ^ 1)], ((j - 1) >> 1) & 1)) { ok = false; break; }
+        tc::fence_after_sync();
 #pragma unroll 1
         for (int c0 = 0; c0 < kHD; c0 += 32) {
           float o[32];
@@ -279,28 +310,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         ph[i] = pack_rn(h0, h1);
         pl[i] = pack_rn(p0 - h0, p1 - h1);
       }
-      tc::tmem_st16u(tl + kColPH, ph);
-      tc::tmem_st16u(tl + kColPH + 16, ph + 16);
-      tc::tmem_st16u(tl + kColPL, pl);
-      tc::tmem_st16u(tl + kColPL + 16, pl + 16);
+      if (j >= 2) {  // P buffer b was read by P V of tile j - 2
+        if (!tc::mbar_wait(&bar[B_PV0 + b], ((j - 2) >> 1) & 1)) { ok = false; break; }
+        tc::fence_after_sync();
+      }
+      const uint32_t pcol = tl + kColP + (uint32_t)b * 64;
+      tc::tmem_st16u(pcol, ph);
+      tc::tmem_st16u(pcol + 16, ph + 16);
+      tc::tmem_st16u(pcol + 32, pl);
+      tc::tmem_st16u(pcol + 48, pl + 16);
       if (j == ntiles - 1) {  // zero the V rows past the block's last position (after their copy has landed)
         const int first_bad = pmax - j * kTok + 1;
         if (first_bad < kTok) {
-          if (!tc::mbar_wait(&bar[B_VFULL], j & 1)) { ok = false; break; }
+          if (!tc::mbar_wait(&bar[B_VF0 + b], (j >> 1) & 1)) { ok = false; break; }
           const int units = (kTok - first_bad) * 4 * 8;  // rows x dim blocks x 16-byte units
           for (int u = tid - 64; u < units; u += kSoftThreads) {
             const int row = first_bad + u / 32, c = (u >> 3) & 3, k = u & 7;
-            *reinterpret_cast<uint4*>(sm + kOffV + c * 8192 + row * 128 + k * 16) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(sm + kOffV + b * 32768 + c * 8192 + row * 128 + k * 16) = make_uint4(0, 0, 0, 0);
           }
           tc::fence_proxy_async();
         }
       }
       tc::tmem_st_wait();
       tc::fence_before_sync();
-      tc::mbar_arrive(&bar[B_PFULL]);
+      tc::mbar_arrive(&bar[B_PF0 + b]);
     }
-    // ---- epilogue: O / l, staged row-major through shared memory (the Q tiles are no longer read)
-    if (ok && !tc::mbar_wait(&bar[B_PVDONE], (ntiles - 1) & 1)) ok = false;
+    // ---- epilogue: O / l, staged row-major through shared memory (the Q tiles and K, V are no longer read)
+    if (ok && !tc::mbar_wait(&bar[B_PV0 + ((ntiles - 1) & 1)], ((ntiles - 1) >> 1) & 1)) ok = false;
     tc::fence_after_sync();
     const bool soft_ok = tc::group_sync_or(1, kSoftThreads, !ok) == false;
     if (soft_ok) {
@@ -317,16 +353,28 @@ __global__ void __launch_bounds__(kThreads, 1)
               make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
       }
       tc::group_sync_or(1, kSoftThreads, false);
-      // warp w writes rows m = w', w' + 4, ...: 256 contiguous dims of one (row, head) per pass
+      // warp w writes rows m = w', w' + 4, ...: 256 contiguous dims of one (row, head) per pass; the gate logits
+      // of four rows are loaded before any is used, so their latencies overlap
       const int sw = warp - 2;
-      for (int mm = sw; mm < 128; mm += 4) {
-        const int hq = mm >> 5, r = mm & 31;
-        if (r >= nr) continue;
-        const int row = row0 + r, head = kvh * kGroup + hq;
+#pragma unroll 1
+      for (int mm0 = sw; mm0 < 128; mm0 += 16) {
+        float gv[4][kHD / 32];
 #pragma unroll
-        for (int i = 0; i < kHD / 32; i++) {
-          const int d = lane + 32 * i;
-          io.store(row, head, d, stage[mm * kStageStride + d] * sigmoidf_(io.gate(row, head, d)));
+        for (int k = 0; k < 4; k++) {
+          const int mm = mm0 + 4 * k, hq = mm >> 5, r = mm & 31;
+#pragma unroll
+          for (int i = 0; i < kHD / 32; i++)
+            gv[k][i] = r < nr ? io.gate(row0 + r, kvh * kGroup + hq, lane + 32 * i) : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const int mm = mm0 + 4 * k, hq = mm >> 5, r = mm & 31;
+          if (r >= nr) continue;
+#pragma unroll
+          for (int i = 0; i < kHD / 32; i++) {
+            const int d = lane + 32 * i;
+            io.store(row0 + r, kvh * kGroup + hq, d, stage[mm * kStageStride + d] * sigmoidf_(gv[k][i]));
+          }
         }
       }
     } else {
@@ -340,7 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) atomicAdd(timeouts, 1u);
     if (tid == 0) {  // copies still in flight land before the CTA exits (bounded)
       if (kfills) tc::mbar_wait(&bar[B_KFULL], (kfills - 1) & 1);
-      if (vfills) tc::mbar_wait(&bar[B_VFULL], (vfills - 1) & 1);
+      for (int b = 0; b < 2; b++)
+        if (vfills[b]) tc::mbar_wait(&bar[B_VF0 + b], (vfills[b] - 1) & 1);
     }
   }
   tc::fence_before_sync();
