@@ -105,6 +105,7 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float* f) {
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float softplus_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
 // Streaming (evict-first) vector accesses for data touched exactly once per step.
 __device__ __forceinline__ float4 ld_stream4(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }

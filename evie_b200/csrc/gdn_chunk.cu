@@ -45,12 +45,28 @@
 // Every mbarrier wait is bounded (2 s of %globaltimer) and every group barrier ORs a failure flag, so both warp
 // groups leave together. A wait that gives up bumps a device counter (read by evie_poll_device_errors); the CTA
 // then drains its outstanding copies and MMAs (bounded again), frees its TMEM and returns.
+//
+// Model form (the forward pass's prefill, kModel = true). The model's q, k, v are f32 (conv + SiLU + L2 norm); bf16
+// q and k move the 0.8B prefill logits by 0.13, so they enter the tensor core split, hi + lo, like every f32
+// operand above: the conv kernel writes the two bf16 planes into the bytes of the q/k columns of its f32 output row
+// ([2 planes][2 key_dim] bf16 is exactly 2 key_dim floats), and each K/Q tile is loaded in both planes (the lo plane
+// 64 KB above the hi plane in shared memory). Every product with K or Q then takes one more MMA: [K;Q] K^T three
+// (hi.hi + lo.hi + hi.lo), S^T [K;Q]^T and (E U)^T K three instead of two. V is read in f32 by the chain threads
+// straight from the activation rows (the lane that needs V[t][dv] loads it, coalesced along dv, issued at the top of
+// the chunk so that the loads overlap the first MMA), which frees the V tile's 16 KB; the output o[t][dv] is written
+// in f32 over V[t][dv] by the same thread after it has read it, and the gated RMSNorm runs as a separate row kernel.
+// Work items are (segment, value head); value head h reads key head h / ratio. A segment's last chunk loads up to
+// 63 rows past its end (rows of the next segment; rows past the call's last row read as zero): they enter only
+// through products with exact zeros (beta = 0 past the end zeroes their rows of N and their rows and columns of T,
+// so their U rows are 0; the log decay is 0 there, so G and the state's decay stop at the last row; their V reads
+// are skipped; their outputs are not stored), so finite neighbours cannot reach this segment's results.
 #include <cudaTypedefs.h>
 
 #include <mutex>
 
 #include "common.h"
 #include "gdn_chunk.h"
+#include "model_kernels.h"
 #include "tc.h"
 
 namespace evie {
@@ -68,14 +84,23 @@ constexpr uint32_t kKQHalf = 32768;
 __device__ __forceinline__ uint32_t kslot(int p) { return p ? 24576u : 0u; }
 __device__ __forceinline__ uint32_t qslot(int p) { return p ? 16384u : 8192u; }
 __device__ __forceinline__ uint32_t stack_off(int p) { return p ? 16384u : 0u; }  // [K0;Q0] or [Q1;K1]
-constexpr uint32_t kOffV = 65536;
-constexpr uint32_t kOffTM = 81920;   // buffers 16 KB apart, planes 8 KB apart
-constexpr uint32_t kOffPM = 114688;  // buffers 16 KB apart, planes 8 KB apart
-constexpr uint32_t kOffNT = 147456;
-constexpr uint32_t kOffSmall = 163840;
 constexpr uint32_t kSmallBytes = 2048;
-constexpr uint32_t kSmemBytes = kOffSmall + kSmallBytes + 1024;  // + slack to align the base to 1024
-static_assert(kSmemBytes <= 232448, "shared memory map exceeds 227 KB");
+// Shared-memory map of the two forms. The model form keeps the lo plane of every K/Q tile 64 KB above its hi plane
+// and has no V tile: [0, 128K) K/Q, then T^T, P, N^T and the small arrays as in the isolated form.
+template <bool kModel>
+struct Map {
+  static constexpr uint32_t kPlane = kModel ? 65536u : 0u;  // hi -> lo plane of a K/Q tile
+  static constexpr uint32_t kOffV = 65536;                   // isolated form only
+  static constexpr uint32_t kOffTM = kModel ? 131072u : 81920u;  // buffers 16 KB apart, planes 8 KB apart
+  static constexpr uint32_t kOffPM = kOffTM + 32768;            // buffers 16 KB apart, planes 8 KB apart
+  static constexpr uint32_t kOffNT = kOffPM + 32768;
+  static constexpr uint32_t kOffSmall = kOffNT + 16384;
+  static constexpr uint32_t kSmemBytes = kOffSmall + kSmallBytes + 1024;  // + slack to align the base to 1024
+  static_assert(kSmemBytes <= 232448, "shared memory map exceeds 227 KB");
+  // MMA terms of the products with K or Q: [K;Q] K^T; S^T [K;Q]^T and (E U)^T K (S and E U are split)
+  static constexpr int kPrepTerms = kModel ? 3 : 1;
+  static constexpr int kChainTerms = kModel ? 3 : 2;
+};
 
 constexpr uint32_t kColS = 0, kColSH = 128, kColSL = 192, kColA = 256, kColKQS = 320, kColU = 448;
 constexpr uint32_t kColRH = 128, kColRL = 160;                              // R^T, then U^T planes
@@ -154,34 +179,66 @@ __device__ __forceinline__ void forward32(const float* NT, int base, float* x) {
 }
 
 struct ChunkArgs {
+  // isolated form: [B][T][H] log decays and betas, [B][H][128][128] states, [B][T][H][128] bf16 outputs
   const float* g;
   const float* beta;
   float* state;
   __nv_bfloat16* o;
   int T;
   int H;
+  // model form
+  const SegInfo* segs;
+  YView y;               // the DeltaNet input projection: b and a logits of head h at columns conv_dim + vd + h, + hv
+  int ldy;
+  const float* neg_a;    // -exp(A_log) per value head
+  const float* dt_bias;
+  float* act;            // [R][conv_dim]: split q/k planes in the q/k columns, v in f32 (overwritten by o)
+  float* rec_state;      // this layer's [hv][128][128] state of slot 0
+  size_t rs_slot;        // element stride between slots
+  int conv_dim, key_dim, vd, hv, ratio;
   unsigned int* timeouts;
 };
 
+template <bool kModel>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_chunk_prefill_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                              const __grid_constant__ CUtensorMap mv, const ChunkArgs a) {
+  using L = Map<kModel>;
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q4 = warp & 3, hf = (warp >> 2) & 1;  // TMEM lane quarter, column half
-  const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
-  const int T = a.T, H = a.H;
+  // Work item: (sequence b, head h) in the isolated form; (segment, value head h) in the model form, whose q and k
+  // are key head kh = h / ratio's and whose rows start at row0 of the activation rows.
+  const int bh = blockIdx.x;
+  int b = 0, h, kh, T, row0 = 0;
+  float* Sg;  // the head's [dk][dv] state
+  if constexpr (kModel) {
+    const SegInfo sg = a.segs[bh / a.hv];
+    h = bh % a.hv;
+    kh = h / a.ratio;
+    T = sg.count;
+    row0 = sg.start;
+    Sg = a.rec_state + (size_t)sg.slot * a.rs_slot + (size_t)h * kD * kD;
+  } else {
+    b = bh / a.H;
+    h = kh = bh % a.H;
+    T = a.T;
+    Sg = a.state + (size_t)bh * kD * kD;
+  }
+  const int H = a.H;
   const int nch = (T + kC - 1) / kC;
 
-  float* GamB = reinterpret_cast<float*>(sm + kOffSmall);  // [2][64] exp(G_t)
+  float* GamB = reinterpret_cast<float*>(sm + L::kOffSmall);  // [2][64] exp(G_t)
   float* EcB = GamB + 128;                                  // [2][64] exp(G_63 - G_t)
   float* G2 = GamB + 256;                                   // [64] G_t * log2(e) (prep only)
   float* Bs = GamB + 320;                                   // [64] beta_t, 0 past the end of the sequence
   float* GamC = GamB + 384;                                 // [64] the chain's copy of exp(G_t)
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffSmall + 1792);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffSmall + 1792 + 8 * kNumBars);
-  float* NT = reinterpret_cast<float*>(sm + kOffNT);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::kOffSmall + 1792);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::kOffSmall + 1792 + 8 * kNumBars);
+  float* NT = reinterpret_cast<float*>(sm + L::kOffNT);
 
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
   if (tid == 0) {
@@ -191,8 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                                                   : 1);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&mq);
-    tc::prefetch_tmap(&mk);
-    tc::prefetch_tmap(&mv);
+    if constexpr (!kModel) {  // the model form reads q and k through one map and v by plain loads
+      tc::prefetch_tmap(&mk);
+      tc::prefetch_tmap(&mv);
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -221,26 +280,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int dv = q4 * 32 + lane;
     auto issue_kq = [&](int c) {
       const int p = c & 1;
-      tc::mbar_arrive_expect_tx(&bar[BK0 + p], 16384);
-      tc::mbar_arrive_expect_tx(&bar[BQ0 + p], 16384);
+      tc::mbar_arrive_expect_tx(&bar[BK0 + p], kModel ? 32768 : 16384);
+      tc::mbar_arrive_expect_tx(&bar[BQ0 + p], kModel ? 32768 : 16384);
       for (int hh = 0; hh < 2; hh++) {
-        tc::tma_load_4d(sm + hh * kKQHalf + kslot(p), &mk, &bar[BK0 + p], hh * 64, h, c * kC, b);
-        tc::tma_load_4d(sm + hh * kKQHalf + qslot(p), &mq, &bar[BQ0 + p], hh * 64, h, c * kC, b);
+        if constexpr (kModel) {
+          // q/k columns of the activation rows as bf16 [row][plane][2 key_dim]: q of key head kh at kh * 128, its k
+          // at key_dim + kh * 128
+#pragma unroll
+          for (int pl = 0; pl < 2; pl++) {
+            uint8_t* dst = sm + pl * L::kPlane + hh * kKQHalf;
+            tc::tma_load_3d(dst + kslot(p), &mq, &bar[BK0 + p], a.key_dim + kh * kD + hh * 64, pl, row0 + c * kC);
+            tc::tma_load_3d(dst + qslot(p), &mq, &bar[BQ0 + p], kh * kD + hh * 64, pl, row0 + c * kC);
+          }
+        } else {
+          tc::tma_load_4d(sm + hh * kKQHalf + kslot(p), &mk, &bar[BK0 + p], hh * 64, h, c * kC, b);
+          tc::tma_load_4d(sm + hh * kKQHalf + qslot(p), &mq, &bar[BQ0 + p], hh * 64, h, c * kC, b);
+        }
       }
       mark(BK0 + p, (c >> 1) & 1);
       mark(BQ0 + p, (c >> 1) & 1);
     };
     auto issue_v = [&](int c) {
-      tc::mbar_arrive_expect_tx(&bar[BV], 16384);
-      tc::tma_load_4d(sm + kOffV, &mv, &bar[BV], 0, h, c * kC, b);
-      mark(BV, c & 1);
+      if constexpr (!kModel) {
+        tc::mbar_arrive_expect_tx(&bar[BV], 16384);
+        tc::tma_load_4d(sm + L::kOffV, &mv, &bar[BV], 0, h, c * kC, b);
+        mark(BV, c & 1);
+      }
     };
     if (tid == 0 && nch > 0) {
       issue_kq(0);
       if (nch > 1) issue_kq(1);
       issue_v(0);
     }
-    float* Sg = a.state + (size_t)bh * kD * kD;
+    // Model form: V[t][dv] (f32, in the activation rows) for t in [32 hf, 32 hf + 32) of the current chunk, 0 past
+    // the segment; the same thread later writes o[t][dv] over it.
+    float vr[kModel ? 32 : 1];
+    const size_t vcol = kModel ? (size_t)2 * a.key_dim + (size_t)h * kD + dv : 0;
+    auto load_v = [&](int c) {
+      if constexpr (kModel) {
+        const int t0 = c * kC + 32 * hf;
+        const float* vp = a.act + (size_t)(row0 + t0) * a.conv_dim + vcol;
+#pragma unroll
+        for (int i = 0; i < 32; i++) vr[i] = t0 + i < T ? vp[(size_t)i * a.conv_dim] : 0.f;
+      }
+    };
     uint32_t nmc = 0;  // completions of the chain's MMA barrier seen
     constexpr uint32_t id64 = tc::idesc(1, 1, 128, 64);
     constexpr uint32_t id128 = tc::idesc(1, 1, 128, 128);
@@ -290,38 +373,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* Ec = EcB + 64 * p;
       if (tid < 64) GamC[tid] = GamB[64 * p + tid];  // the chain's own copy: buffer p is released before the outputs
       const uint32_t ks_col = kColKQS + (p ? 64u : 0u), qs_col = kColKQS + (p ? 0u : 64u);
+      load_v(c);
 
-      // ---- (K S)^T | (Q S)^T = S^T [stack]^T, A = S^T hi/lo from TMEM
+      // ---- (K S)^T | (Q S)^T = S^T [stack]^T, A = S^T hi/lo from TMEM; terms (S hi, KQ hi), (S lo, KQ hi) and,
+      // with split K/Q, (S hi, KQ lo)
       if (tid == 0) {
         wait(BK0 + p, (c >> 1) & 1);
         wait(BQ0 + p, (c >> 1) & 1);
         tc::fence_after_sync();
         if (ok) {
 #pragma unroll
-          for (int pl = 0; pl < 2; pl++)
+          for (int tm = 0; tm < L::kChainTerms; tm++)
 #pragma unroll
             for (int s = 0; s < 8; s++)
-              tc::mma_f16_ts(tmem + kColKQS, tmem + (pl ? kColSL : kColSH) + s * 8,
-                             dK + (((s >> 2) * kKQHalf + stack_off(p) + (s & 3) * 32) >> 4), id128, (pl | s) > 0);
+              tc::mma_f16_ts(tmem + kColKQS, tmem + (tm == 1 ? kColSL : kColSH) + s * 8,
+                             dK + (((s >> 2) * kKQHalf + stack_off(p) + (s & 3) * 32 + (tm == 2 ? L::kPlane : 0u)) >> 4),
+                             id128, (tm | s) > 0);
           tc::mma_commit(&bar[BMC]);
           mark(BMC, nmc & 1);
         }
       }
       wait(BMC, nmc & 1);
       nmc++;
-      wait(BV, c & 1);
+      if constexpr (!kModel) wait(BV, c & 1);
       if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
       // ---- R^T row dv, t in [32 hf, 32 hf + 32): V[t][dv] - Gam_t (K S)^T[dv][t], split into TMEM
       {
-        const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + kOffV);
+        const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + L::kOffV);
         float r[32];
         tc::tmem_ld32(tl + ks_col + 32 * hf, r);
 #pragma unroll
         for (int i = 0; i < 32; i++) {
           const int t = 32 * hf + i;
-          r[i] = fmaf(-GamC[t], r[i], __bfloat162float(V[t * kD + dv]));
+          float v;
+          if constexpr (kModel) v = vr[i];
+          else v = __bfloat162float(V[t * kD + dv]);
+          r[i] = fmaf(-GamC[t], r[i], v);
         }
         uint32_t hi[16], lo[16];
         split_pairs<16>(r, hi, lo);
@@ -337,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait(BTR0 + p, (c >> 1) & 1);
       if (tid == 0 && ok) {
         if (c + 1 < nch) issue_v(c + 1);  // V has been consumed
-        const uint32_t tm = kOffTM + p * 16384;
+        const uint32_t tm = L::kOffTM + p * 16384;
         int n = 0;
 #pragma unroll
         for (int pa = 0; pa < 2; pa++)
@@ -376,9 +465,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (tc::group_sync_or(kChainBar, kGroup, !ok)) { ok = false; break; }
       tc::fence_after_sync();
 
-      // ---- (P U)^T = U^T P^T (three passes, into the (K S)^T half); S^T += (E U)^T K (K as MN-major operand)
+      // ---- (P U)^T = U^T P^T (three passes, into the (K S)^T half); S^T += (E U)^T K (K as MN-major operand;
+      // terms (E U hi, K hi), (E U lo, K hi) and, with split K, (E U hi, K lo))
       if (tid == 0) {
-        const uint32_t pm = kOffPM + p * 16384;
+        const uint32_t pm = L::kOffPM + p * 16384;
         int n = 0;
 #pragma unroll
         for (int pa = 0; pa < 2; pa++)
@@ -391,11 +481,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                              dK + ((pm + pb * 8192 + s * 32) >> 4), id64, n > 0);
           }
 #pragma unroll
-        for (int pa = 0; pa < 2; pa++)
+        for (int tm = 0; tm < L::kChainTerms; tm++)
 #pragma unroll
           for (int s = 0; s < 4; s++)
-            tc::mma_f16_ts(tmem + kColS, tmem + (pa ? kColEL : kColEH) + s * 8,
-                           dMnK + ((kslot(p) + s * 2048) >> 4), idS, 1);
+            tc::mma_f16_ts(tmem + kColS, tmem + (tm == 1 ? kColEL : kColEH) + s * 8,
+                           dMnK + ((kslot(p) + s * 2048 + (tm == 2 ? L::kPlane : 0u)) >> 4), idS, 1);
         tc::mma_commit(&bar[BMC]);
         mark(BMC, nmc & 1);
       }
@@ -414,14 +504,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // ---- o_t = Gam_t (Q S)^T + (P U)^T for t in [32 hf, 32 hf + 32); the new state staged for the next chunk
       {
-        __nv_bfloat16* og = a.o + (((size_t)b * T + t0) * H + h) * kD + dv;
         const int nt = min(kC, T - t0);
         float ov[32], qs[32];
         tc::tmem_ld32x2(tl + ks_col + 32 * hf, tl + qs_col + 32 * hf, ov, qs);
+        if constexpr (kModel) {
+          float* og = a.act + (size_t)(row0 + t0) * a.conv_dim + vcol;  // over V[t][dv], which this thread read
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-          const int t = 32 * hf + i;
-          if (t < nt) reinterpret_cast<uint16_t*>(og)[(size_t)t * H * kD] = bf16_rne(fmaf(GamC[t], qs[i], ov[i]));
+          for (int i = 0; i < 32; i++) {
+            const int t = 32 * hf + i;
+            if (t < nt) og[(size_t)t * a.conv_dim] = fmaf(GamC[t], qs[i], ov[i]);
+          }
+        } else {
+          __nv_bfloat16* og = a.o + (((size_t)b * T + t0) * H + h) * kD + dv;
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            const int t = 32 * hf + i;
+            if (t < nt) reinterpret_cast<uint16_t*>(og)[(size_t)t * H * kD] = bf16_rne(fmaf(GamC[t], qs[i], ov[i]));
+          }
         }
         stage_state(false, last, last ? 1.f : GamB[64 * (p ^ 1) + 63]);
       }
@@ -440,11 +539,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;  // warp 8: decay and beta of the next chunk, 2 tokens a lane
     auto fetch = [&](int c) {
       const int t = c * kC + 2 * lane;
-      const size_t r = ((size_t)b * T + t) * H + h;
-      gn0 = t < T ? __ldg(a.g + r) : 0.f;
-      bn0 = t < T ? __ldg(a.beta + r) : 0.f;
-      gn1 = t + 1 < T ? __ldg(a.g + r + H) : 0.f;
-      bn1 = t + 1 < T ? __ldg(a.beta + r + H) : 0.f;
+      if constexpr (kModel) {
+        // model.rs:374-375: log decay g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)
+        const float na = a.neg_a[h], dtb = a.dt_bias[h];
+        const size_t col = (size_t)a.conv_dim + a.vd + h, r = (size_t)(row0 + t) * a.ldy + col;
+        gn0 = t < T ? na * softplus_(a.y.at(r + a.hv) + dtb) : 0.f;
+        bn0 = t < T ? sigmoidf_(a.y.at(r)) : 0.f;
+        gn1 = t + 1 < T ? na * softplus_(a.y.at(r + a.ldy + a.hv) + dtb) : 0.f;
+        bn1 = t + 1 < T ? sigmoidf_(a.y.at(r + a.ldy)) : 0.f;
+      } else {
+        const size_t r = ((size_t)b * T + t) * H + h;
+        gn0 = t < T ? __ldg(a.g + r) : 0.f;
+        bn0 = t < T ? __ldg(a.beta + r) : 0.f;
+        gn1 = t + 1 < T ? __ldg(a.g + r + H) : 0.f;
+        bn1 = t + 1 < T ? __ldg(a.beta + r + H) : 0.f;
+      }
     };
     if (pw == 0 && nch > 0) fetch(0);
     constexpr uint32_t idA = tc::idesc(1, 1, 128, 64);
@@ -455,11 +564,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait(BQ0 + p, (c >> 1) & 1);
       tc::fence_after_sync();
       if (!ok) return;
+      // terms (stack hi, K hi) and, with split K/Q, (stack lo, K hi), (stack hi, K lo)
 #pragma unroll
-      for (int s = 0; s < 8; s++) {
-        const uint32_t kb = (s >> 2) * kKQHalf + (s & 3) * 32;
-        tc::mma_f16(tmem + kColA, dK + ((kb + stack_off(p)) >> 4), dK + ((kb + kslot(p)) >> 4), idA, s > 0);
-      }
+      for (int tm = 0; tm < L::kPrepTerms; tm++)
+#pragma unroll
+        for (int s = 0; s < 8; s++) {
+          const uint32_t kb = (s >> 2) * kKQHalf + (s & 3) * 32;
+          const uint32_t pa = tm == 1 ? L::kPlane : 0u, pb = tm == 2 ? L::kPlane : 0u;
+          tc::mma_f16(tmem + kColA, dK + ((kb + stack_off(p) + pa) >> 4), dK + ((kb + kslot(p) + pb) >> 4), idA,
+                      (tm | s) > 0);
+        }
       tc::mma_commit(&bar[BMP]);
       mark(BMP, c & 1);
     };
@@ -470,8 +584,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int p = c & 1;
       float* Gam = GamB + 64 * p;  // chunk c's decays, read by the chain
       float* Ec = EcB + 64 * p;
-      uint8_t* TM = sm + kOffTM + p * 16384;
-      uint8_t* PM = sm + kOffPM + p * 16384;
+      uint8_t* TM = sm + L::kOffTM + p * 16384;
+      uint8_t* PM = sm + L::kOffPM + p * 16384;
       if (c >= 2) wait(BCD0 + p, ((c >> 1) - 1) & 1);  // the chain is done with chunk c-2's buffers
 
       // ---- decay sums (log2 units) and beta; warp 8, two tokens a lane
@@ -661,10 +775,62 @@ evie_status launch_gdn_chunk_prefill_bf16(const void* q, const void* k, const vo
   if ((s = token_major_map(&mv, v, B, T, H, 128, CU_TENSOR_MAP_SWIZZLE_NONE)) != EVIE_OK) return s;
   unsigned int* counter = device_timeout_counter();
   if (!counter) return fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
-  EVIE_TRY(max_dynamic_smem((const void*)gdn_chunk_prefill_kernel, (int)kSmemBytes));
-  ChunkArgs a{g, beta, state, static_cast<__nv_bfloat16*>(o), T, H, counter};
-  gdn_chunk_prefill_kernel<<<B * H, kThreads, kSmemBytes, st>>>(mq, mk, mv, a);
+  constexpr uint32_t smem = Map<false>::kSmemBytes;
+  EVIE_TRY(max_dynamic_smem((const void*)gdn_chunk_prefill_kernel<false>, (int)smem));
+  ChunkArgs a{};
+  a.g = g;
+  a.beta = beta;
+  a.state = state;
+  a.o = static_cast<__nv_bfloat16*>(o);
+  a.T = T;
+  a.H = H;
+  a.timeouts = counter;
+  gdn_chunk_prefill_kernel<false><<<B * H, kThreads, smem, st>>>(mq, mk, mv, a);
   EVIE_CHECK_LAUNCH("gdn_chunk_prefill_kernel");
+  return EVIE_OK;
+}
+
+evie_status launch_gdn_chunk_model(float* act, YView y, int ldy, int R, const SegInfo* segs, int nseg,
+                                   float* rec_state, size_t rs_slot, const float* neg_a, const float* dt_bias,
+                                   int conv_dim, int key_dim, int vd, int hv, int hk, cudaStream_t st) {
+  if (nseg == 0 || R == 0) return EVIE_OK;
+  if (hk <= 0 || hv % hk != 0 || key_dim != hk * kD || vd != hv * kD || conv_dim != 2 * key_dim + vd)
+    return fail(EVIE_ERR_ARG, "chunked DeltaNet prefill: head dims must be 128 with value heads a multiple of key heads");
+  if (((uintptr_t)act & 15u) != 0)
+    return fail(EVIE_ERR_ARG, "chunked DeltaNet prefill: activation rows must be 16-byte aligned");
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(EVIE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  // The q/k columns of the activation rows as bf16 [R][2 planes][2 key_dim]; box = 64 elements x 1 plane x 64 rows.
+  CUtensorMap m;
+  const cuuint64_t dims[3] = {(cuuint64_t)2 * key_dim, 2, (cuuint64_t)R};
+  const cuuint64_t strides[2] = {(cuuint64_t)2 * key_dim * 2, (cuuint64_t)conv_dim * 4};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)kC};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, act, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EVIE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  unsigned int* counter = device_timeout_counter();
+  if (!counter) return fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
+  constexpr uint32_t smem = Map<true>::kSmemBytes;
+  EVIE_TRY(max_dynamic_smem((const void*)gdn_chunk_prefill_kernel<true>, (int)smem));
+  ChunkArgs a{};
+  a.segs = segs;
+  a.y = y;
+  a.ldy = ldy;
+  a.neg_a = neg_a;
+  a.dt_bias = dt_bias;
+  a.act = act;
+  a.rec_state = rec_state;
+  a.rs_slot = rs_slot;
+  a.conv_dim = conv_dim;
+  a.key_dim = key_dim;
+  a.vd = vd;
+  a.hv = hv;
+  a.ratio = hv / hk;
+  a.timeouts = counter;
+  EVIE_CUDA_TRY(launch_k(gdn_chunk_prefill_kernel<true>, dim3(nseg * hv), dim3(kThreads), smem, st, m, m, m, a));
+  EVIE_CHECK_LAUNCH("gdn_chunk_prefill_kernel<model>");
   return EVIE_OK;
 }
 

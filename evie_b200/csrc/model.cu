@@ -236,6 +236,7 @@ struct evie_ctx {
   size_t y2_cap() const { return (size_t)2 * max_rows * y2_cols; }
   bool attn_rowwise = false;  // EVIE_ATTN_ROWWISE=1 at creation: prefill rows use the per-row split-KV kernel too
   bool attn_prefill_mma = false;  // EVIE_ATTN_PREFILL_MMA=1 at creation: prefill attention on the mma.sync kernel
+  bool gdn_seq = false;  // EVIE_GDN_SEQ=1 at creation: prefill DeltaNet on the token-sequential CUDA-core kernel
   bool no_graph = false;      // EVIE_NO_GRAPH=1 at creation: decode-shaped calls run eagerly
   // Captured decode-shaped forward calls, keyed by (sequences, want logits, head, capture, tracking, context bound).
   // The host capture destinations are part of the key: their copies are nodes of the graph.
@@ -624,6 +625,7 @@ evie_status allocate_state(evie_ctx* c) {
   if (const char* e = getenv("EVIE_GEMM_PLANES")) c->max_planes = std::min(evie::YView::kMaxPlanes, std::max(1, atoi(e)));
   if (const char* e = getenv("EVIE_ATTN_ROWWISE")) c->attn_rowwise = e[0] == '1';
   if (const char* e = getenv("EVIE_ATTN_PREFILL_MMA")) c->attn_prefill_mma = e[0] == '1';
+  if (const char* e = getenv("EVIE_GDN_SEQ")) c->gdn_seq = e[0] == '1';
   if (const char* e = getenv("EVIE_NO_GRAPH")) c->no_graph = e[0] == '1';
   TRY(c->alloc(&c->act, R * s.conv_dim));
   TRY(c->alloc(&c->q_rot, R * s.nh * s.hd));
@@ -746,21 +748,30 @@ evie_status enqueue_layers(evie_ctx* c, int R, int nseq, int max_ctx_rows, int c
       evie::YView y;
       { PROF(P_GEMM_LIN_IN); TRY(gemm(c, L.w_in, s.in_dn, s.d, c->X2, R, c->Y2, c->y2_cap(), &y)); }
       float* cs = c->conv_state + (size_t)L.idx * (s.K - 1) * s.conv_dim;
+      const bool single_rows = R == nseq && s.K <= 8;  // decode: one row per segment, the conv kernel shifts the window
+      int max_seg_rows = 1;
+      if (!single_rows)
+        for (int i = 0; i < nseq; i++) max_seg_rows = std::max(max_seg_rows, c->h_segs[i].count);
+      // Prefill calls run the recurrence chunked on tensor cores (gdn_chunk.cu); the conv then writes q and k as
+      // split bf16 planes, the chunk kernel's operand format.
+      const bool chunked = !c->gdn_seq && max_seg_rows > 1 && s.K == 4 && s.dk == 128 && s.dv == 128;
       {
         PROF(P_CONV);
-        const bool single_rows = R == nseq && s.K <= 8;  // decode: one row per segment, the conv kernel shifts the window
-        int max_seg_rows = 1;
-        if (!single_rows)
-          for (int i = 0; i < nseq; i++) max_seg_rows = std::max(max_seg_rows, c->h_segs[i].count);
         TRY(evie::k_conv_silu_norm(y, s.in_dn, R, c->d_rows, c->d_segs, cs, cs_slot, L.conv, s, c->act, st,
-                                   single_rows, nseq, max_seg_rows));
+                                   single_rows, nseq, max_seg_rows, chunked));
         if (!single_rows) TRY(evie::k_conv_state_update(y, s.in_dn, R, c->d_segs, nseq, cs, cs_slot, s, st));
       }
       float* rsb = c->rec_state + (size_t)L.idx * s.hv * s.dk * s.dv;
       {
         PROF(P_MIXER);
-        TRY(evie::k_gdn_mixer(c->act, y, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm,
-                              s, c->X2, st));
+        if (chunked) {
+          TRY(evie::launch_gdn_chunk_model(c->act, y, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a,
+                                           L.dt_bias, s.conv_dim, s.key_dim, s.vd, s.hv, s.hk, st));
+          TRY(evie::k_gdn_gated_norm(c->act, y, s.in_dn, R, L.norm, s, c->X2, st));
+        } else {
+          TRY(evie::k_gdn_mixer(c->act, y, s.in_dn, R, c->d_segs, nseq, rsb, rs_slot, L.neg_a, L.dt_bias, L.norm,
+                                s, c->X2, st));
+        }
       }
       { PROF(P_GEMM_LIN_OUT); TRY(gemm(c, L.w_out, s.d, s.vd, c->X2, R, c->Y2, c->y2_cap(), &yo)); }
     } else {

@@ -23,8 +23,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-__device__ __forceinline__ float softplus_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
-
 // worker.rs:97-112: q = round(127 sqrt(min(|v|, 1))) with the sign of v.
 __device__ __forceinline__ int8_t compand(float v) {
   const float q = roundf(sqrtf(fminf(fabsf(v), 1.0f)) * 127.0f);
@@ -279,12 +277,15 @@ __global__ void __launch_bounds__(128) conv_decode4_kernel(YView y, int ldy, con
 // The same conv for segments of many rows (prefill): one CTA per (128-channel block, segment, 64 consecutive rows),
 // one thread per channel walking the rows with its K-1 previous inputs in registers, so every input is read once.
 // Same products, summation order and head-norm reduction as conv_silu_norm_kernel.
+// split_qk: the q and k channels are written as two bf16 planes, hi = bf16(x) and lo = bf16(x - hi), into the bytes
+// of the row's q/k columns (bf16 [2][2 key_dim] in place of f32 [2 key_dim]), the operand format of the chunked
+// prefill's tensor-core tiles; v stays f32.
 constexpr int kConvRows = 64;
 template <int K>
 __global__ void __launch_bounds__(128) conv_rows_kernel(YView y, int ldy, const SegInfo* __restrict__ segs,
                                                         const float* __restrict__ conv_state, size_t cs_slot,
                                                         const float* __restrict__ conv_w, int conv_dim, int hk,
-                                                        float qscale, float* __restrict__ act) {
+                                                        float qscale, float* __restrict__ act, bool split_qk) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red[4];
@@ -317,7 +318,14 @@ __global__ void __launch_bounds__(128) conv_rows_kernel(YView y, int ldy, const 
       const float ss = block_sum<128>(out * out, red);
       out *= (1.0f / sqrtf(ss + 1e-6f)) * scl;
     }
-    act[row * conv_dim + c] = out;
+    if (split_qk && head_norm) {
+      __nv_bfloat16* qk = reinterpret_cast<__nv_bfloat16*>(act + row * conv_dim);
+      const __nv_bfloat16 hi = __float2bfloat16_rn(out);
+      qk[c] = hi;
+      qk[(size_t)256 * hk + c] = __float2bfloat16_rn(out - __bfloat162float(hi));  // 2 key_dim = 256 hk channels
+    } else {
+      act[row * conv_dim + c] = out;
+    }
   }
 }
 
@@ -561,6 +569,30 @@ __global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_seq_kernel(
   }
 #pragma unroll
   for (int r = 0; r < 16; r++) *reinterpret_cast<float4*>(Sh + (size_t)(rg + 8 * r) * DV) = s[r];
+}
+
+// Gated RMSNorm (model.rs:377-383) of the chunked prefill's outputs: o (f32, written over the v columns of act)
+// * rsqrt(mean o^2 + eps) * w * silu(z) -> X2 planes. One warp per (row, value head), four columns per lane.
+__global__ void __launch_bounds__(256) gdn_gated_norm_kernel(const float* __restrict__ act, YView y, int ldy, int R,
+                                                             int conv_dim, int key_dim, int hv,
+                                                             const float* __restrict__ norm_w, float eps,
+                                                             __nv_bfloat16* __restrict__ X2, size_t xplane, int vd) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int DV = 128;
+  const int pair = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (pair >= R * hv) return;  // whole warps leave together
+  const int row = pair / hv, head = pair % hv, c = lane * 4;
+  const float4 o = *reinterpret_cast<const float4*>(act + (size_t)row * conv_dim + 2 * key_dim + head * DV + c);
+  const float4 z = y.at4((size_t)row * ldy + conv_dim + head * DV + c);
+  const float4 w = *reinterpret_cast<const float4*>(norm_w + c);
+  float ss = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float inv = 1.0f / sqrtf(ss / (float)DV + eps);
+  store_split4(X2, xplane, (size_t)row * vd + head * DV + c,
+               make_float4(o.x * inv * w.x * siluf_(z.x), o.y * inv * w.y * siluf_(z.y),
+                           o.z * inv * w.z * siluf_(z.z), o.w * inv * w.w * siluf_(z.w)));
 }
 
 // model.rs:419-442, rope model.rs:470-479: q_norm / k_norm (gains 1+w) + rotate-half RoPE on the first `rot` dims;
@@ -842,12 +874,15 @@ evie_status k_add_final(float* x, YView y, int ldy, int R, const RowInfo* rows, 
 
 evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
                              float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
-                             float* act, cudaStream_t st, bool update_window, int nseg, int max_seg_rows) {
+                             float* act, cudaStream_t st, bool update_window, int nseg, int max_seg_rows,
+                             bool split_qk) {
   if (R == 0) return EVIE_OK;
+  if (split_qk && !(max_seg_rows > 1 && s.K == 4 && !update_window && s.dk == 128))
+    return fail(EVIE_ERR_ARG, "conv: split q/k output needs the 4-tap multi-row form with 128-wide key heads");
   if (max_seg_rows > 1 && s.K == 4 && !update_window) {
     dim3 grid(s.conv_dim / 128, nseg, (max_seg_rows + kConvRows - 1) / kConvRows);
     EVIE_CUDA_TRY(launch_k(conv_rows_kernel<4>, dim3(grid), dim3(128), 0, st, y, ldy, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
-                                              1.0f / sqrtf((float)s.dk), act));
+                                              1.0f / sqrtf((float)s.dk), act, split_qk));
     EVIE_CHECK_LAUNCH("conv_rows_kernel");
     return EVIE_OK;
   }
@@ -895,6 +930,17 @@ evie_status k_gdn_mixer(const float* act, YView y, int ldy, int R, const SegInfo
                                                  dt_bias, norm_w, s.conv_dim, s.key_dim, s.vd, s.hv, s.hv / s.hk, s.eps,
                                                  X2, (size_t)R * s.vd));
   EVIE_CHECK_LAUNCH("gdn_mixer_kernel");
+  return EVIE_OK;
+}
+
+evie_status k_gdn_gated_norm(const float* act, YView y, int ldy, int R, const float* norm_w, const ModelShape& s,
+                             __nv_bfloat16* X2, cudaStream_t st) {
+  if (R == 0) return EVIE_OK;
+  if (s.dv != 128) return fail(EVIE_ERR_ARG, "gated norm: value heads must be 128 wide");
+  const long pairs = (long)R * s.hv;
+  EVIE_CUDA_TRY(launch_k(gdn_gated_norm_kernel, dim3((unsigned)((pairs + 7) / 8)), dim3(256), 0, st, act, y, ldy, R,
+                         s.conv_dim, s.key_dim, s.hv, norm_w, s.eps, X2, (size_t)R * s.vd, s.vd));
+  EVIE_CHECK_LAUNCH("gdn_gated_norm_kernel");
   return EVIE_OK;
 }
 

@@ -90,10 +90,12 @@ evie_status k_add_final(float* x, YView y, int ldy, int R, const RowInfo* rows, 
 // update_window: every segment has exactly one row (decode); the kernel then also shifts the conv windows in place
 // (replacing k_conv_state_update). For a 4-tap conv with 16-byte aligned operands that is a warp per 128-channel
 // head block with four channels per lane; otherwise one thread per channel. With max_seg_rows > 1 (and a 4-tap
-// conv) a sliding-window kernel walks each segment's rows in blocks of 64.
+// conv) a sliding-window kernel walks each segment's rows in blocks of 64; split_qk (that form only) writes the q
+// and k channels as split bf16 planes in place of their f32 values, the chunked prefill's operand format.
 evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
                              float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
-                             float* act, cudaStream_t st, bool update_window, int nseg = 0, int max_seg_rows = 0);
+                             float* act, cudaStream_t st, bool update_window, int nseg = 0, int max_seg_rows = 0,
+                             bool split_qk = false);
 evie_status k_conv_state_update(YView y, int ldy, int R, const SegInfo* segs, int nseg, float* conv_state,
                                 size_t cs_slot, const ModelShape& s, cudaStream_t st);
 // Gated delta rule over each segment's rows (state resident in registers) + gated RMSNorm -> X2 [R][vd].
@@ -101,6 +103,9 @@ evie_status k_conv_state_update(YView y, int ldy, int R, const SegInfo* segs, in
 evie_status k_gdn_mixer(const float* act, YView y, int ldy, int R, const SegInfo* segs, int nseg,
                         float* rec_state, size_t rs_slot, const float* neg_a, const float* dt_bias,
                         const float* norm_w, const ModelShape& s, __nv_bfloat16* X2, cudaStream_t st);
+// Gated RMSNorm of the chunked prefill's outputs (f32 over the v columns of act) -> X2 [R][vd].
+evie_status k_gdn_gated_norm(const float* act, YView y, int ldy, int R, const float* norm_w, const ModelShape& s,
+                             __nv_bfloat16* X2, cudaStream_t st);
 // q/k RMSNorm (1+w gains) + partial RoPE; q -> q_rot f32 [R][nh][hd]; k, v -> paged cache (bf16 or f32).
 template <typename KV>
 evie_status k_attn_prep(YView y, int ldy, int R, const RowInfo* rows, const float* q_norm,
