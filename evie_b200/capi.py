@@ -60,6 +60,11 @@ SIGNATURES = {
     "evie_set_sampler": (I, [P, I, P]),
     "evie_read_top_active": (I, [P, I, P, P]),
     "evie_neuron_sigma": (I, [P, P, SZ, P, P]),
+    "evie_set_lens": (I, [P, P, I, I, I]),
+    "evie_clear_lens": (I, [P]),
+    "evie_lens_logits": (I, [P, I, P, I, P]),
+    "evie_neuron_logits": (I, [P, P, P, I, P]),
+    "evie_search_scores": (I, [P, P, I, P, P, P, P]),
     "evie_top_active": (I, [P, I, C.c_longlong, I, P, P]),
     "evie_sampler_seed_state": (C.c_uint64, [C.c_uint64]),
     "evie_sample": (I, [P, I, I, P, P, P, P, P, P]),

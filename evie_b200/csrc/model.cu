@@ -11,7 +11,6 @@
 //             KV pages [full layer][slot * pages_per_slot][nkv][256][hd] (bf16, or f32 with EVIE_KV_F32=1),
 //             a fixed page table per slot (slot s owns pages s*pps .. s*pps+pps-1)
 //   activations sized for max_rows: residual x f32, split operand planes X2 bf16, projection outputs Y2 f32
-#include <cublas_v2.h>
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -32,6 +31,7 @@
 #include "common.h"
 #include "gqa_decode.h"
 #include "json.h"
+#include "analysis.h"
 #include "gdn_chunk.h"
 #include "model_kernels.h"
 #include "proj_gemm.h"
@@ -180,8 +180,7 @@ struct evie_ctx {
   // forked from the compute stream after each layer and joined at the end of the call (cap_ev: one per layer + 1).
   cudaStream_t cstream = nullptr;
   std::vector<cudaEvent_t> cap_ev;
-  cublasHandle_t blas = nullptr;
-  void* blas_ws = nullptr;
+  evie::LensDev lens;  // evie_set_lens: the lens of the analysis calls
   evie::ModelShape s{};
   std::vector<int> kinds;
   int n_lin = 0, n_full = 0;
@@ -1115,7 +1114,7 @@ void destroy(evie_ctx* c) {
   if (c->h_rows) cudaFreeHost(c->h_rows);
   if (c->h_segs) cudaFreeHost(c->h_segs);
   if (c->h_timeouts) cudaFreeHost(c->h_timeouts);
-  if (c->blas) cublasDestroy(c->blas);
+  evie::lens_free(c->lens);
   for (auto e : c->cap_ev) cudaEventDestroy(e);
   if (c->cstream) cudaStreamDestroy(c->cstream);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -1252,17 +1251,11 @@ evie_status evie_create(const char* ckpt_dir, int device, int slots, int max_ctx
     if (cudaSetDevice(device) != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "cudaSetDevice(%d) failed", device); break; }
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "stream creation failed"); break; }
     if (cudaStreamCreateWithFlags(&c->cstream, cudaStreamNonBlocking) != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "stream creation failed"); break; }
-    if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) { rc = evie::fail(EVIE_ERR_CUDA, "cublasCreate failed"); break; }
-    cublasSetStream(c->blas, c->stream);
-    cublasSetMathMode(c->blas, CUBLAS_DEFAULT_MATH);
     // the device's timeout counter of the bounded-wait kernels, looked up now rather than inside a graph capture
     if (!evie::device_timeout_counter()) { rc = evie::fail(EVIE_ERR_CUDA, "device timeout counter unavailable"); break; }
     if ((rc = read_config(c, ckpt_dir)) != EVIE_OK) break;
     if ((rc = load_weights(c, ckpt_dir)) != EVIE_OK) break;
     if ((rc = allocate_state(c)) != EVIE_OK) break;
-    void* ws = nullptr;
-    if ((rc = c->alloc((char**)&ws, 64u << 20)) != EVIE_OK) break;
-    cublasSetWorkspace(c->blas, ws, 64u << 20);
     if (cudaDeviceSynchronize() != cudaSuccess) { rc = evie::fail(EVIE_ERR_CUDA, "initialisation failed"); break; }
   } while (0);
   if (rc != EVIE_OK) {
@@ -1360,7 +1353,23 @@ evie_status evie_reset_gates(evie_ctx* c, int slot) {
   return EVIE_OK;
 }
 
-// analysis.rs:129-201 (no lens) on the context's weights.
+namespace {
+evie::AnalysisModel analysis_model(evie_ctx* c) {
+  evie::AnalysisModel am;
+  am.lm_head = c->lm_head;
+  am.V = c->s.V;
+  am.d = c->s.d;
+  am.n = c->s.n;
+  am.final_norm = c->final_norm;
+  am.eps = c->s.eps;
+  for (const Layer& L : c->layers) am.w_down.push_back(L.w_down);
+  am.lens = &c->lens;
+  am.st = c->stream;
+  return am;
+}
+}  // namespace
+
+// analysis.rs:129-201 on the context's weights, through the lens set by evie_set_lens (if any).
 evie_status evie_neuron_sigma(evie_ctx* c, float* sigma, size_t n, float* mean, float* m_scale) {
   if (!c) return evie::fail(EVIE_ERR_ARG, "evie_neuron_sigma: null context");
   auto& s = c->s;
@@ -1368,10 +1377,52 @@ evie_status evie_neuron_sigma(evie_ctx* c, float* sigma, size_t n, float* mean, 
     return remember(c, evie::fail(EVIE_ERR_ARG, "evie_neuron_sigma: expected %zu outputs, got %zu",
                                   (size_t)s.L * s.n, n));
   if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
-  std::vector<const __nv_bfloat16*> downs;
-  for (const Layer& L : c->layers) downs.push_back(L.w_down);
-  return remember(c, evie::neuron_sigma_run(c->blas, c->stream, c->lm_head, s.V, s.d, c->final_norm, downs, s.n,
-                                            sigma, mean, m_scale));
+  return remember(c, evie::neuron_sigma_run(analysis_model(c), sigma, mean, m_scale));
+}
+
+// lens.rs:20-54 once the file is read: maps[l] = [hidden][hidden] 16-bit values or NULL.
+evie_status evie_set_lens(evie_ctx* c, const uint16_t* const* maps, int n_layers, int kind, int target_layer) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_set_lens: null context");
+  if (!maps || n_layers != c->s.L)
+    return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_lens: expected %d layer maps, got %d", c->s.L, n_layers));
+  if (target_layer < 0 || target_layer >= c->s.L)
+    return remember(c, evie::fail(EVIE_ERR_ARG, "evie_set_lens: target layer %d out of range", target_layer));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  return remember(c, evie::lens_upload(c->lens, maps, n_layers, c->s.d, kind, target_layer, c->stream));
+}
+
+evie_status evie_clear_lens(evie_ctx* c) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_clear_lens: null context");
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  evie::lens_free(c->lens);
+  return EVIE_OK;
+}
+
+// analysis.rs:28-34
+evie_status evie_lens_logits(evie_ctx* c, int layer, const float* vecs, int n, float* logits) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_lens_logits: null context");
+  if (n < 0 || (n > 0 && (!vecs || !logits))) return remember(c, evie::fail(EVIE_ERR_ARG, "evie_lens_logits: bad buffers"));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  return remember(c, evie::lens_logits_run(analysis_model(c), layer, vecs, n, logits));
+}
+
+// analysis.rs:37-67
+evie_status evie_neuron_logits(evie_ctx* c, const int32_t* layers, const int32_t* neurons, int n, float* logits) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_neuron_logits: null context");
+  if (n < 0 || (n > 0 && (!layers || !neurons || !logits)))
+    return remember(c, evie::fail(EVIE_ERR_ARG, "evie_neuron_logits: bad buffers"));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  return remember(c, evie::neuron_logits_run(analysis_model(c), layers, neurons, n, logits));
+}
+
+// analysis.rs:213-240 (the per-neuron best z of both poles; the ranking is the caller's)
+evie_status evie_search_scores(evie_ctx* c, const uint32_t* tokens, int n_tokens, const float* mean,
+                               const float* sigma, float* z_up, float* z_dn) {
+  if (!c) return evie::fail(EVIE_ERR_ARG, "evie_search_scores: null context");
+  if (n_tokens < 1 || !tokens || !mean || !sigma || !z_up || !z_dn)
+    return remember(c, evie::fail(EVIE_ERR_ARG, "evie_search_scores: bad buffers"));
+  if (cudaSetDevice(c->device) != cudaSuccess) return remember(c, evie::fail(EVIE_ERR_CUDA, "cudaSetDevice failed"));
+  return remember(c, evie::search_scores_run(analysis_model(c), tokens, n_tokens, mean, sigma, z_up, z_dn));
 }
 
 // mcp.rs:242-256 over the frames the last capturing call left on the device.

@@ -7,8 +7,6 @@
 // its output is one plane per K slice, which consumers add when they read it (YView). The result matches the f32
 // product to ~2^-16 relative.
 #pragma once
-#include <cublas_v2.h>
-
 #include <vector>
 
 #include "common.h"
@@ -156,10 +154,6 @@ evie_status k_swiglu(YView y, int ldy, int R, const RowInfo* rows, int layer, co
                      cudaStream_t st);
 // top_active (mcp.rs:242-256) per frame row: the k largest |q|, equal |q| by increasing index -> out [rows][k].
 evie_status k_top_active(const int8_t* frames, int rows, long long width, int k, int32_t* out, cudaStream_t st);
-// analysis.rs:129-201 without a lens (analysis.cu): sigma [L * n], mean [d] and m_scale to the host (synchronous).
-evie_status neuron_sigma_run(cublasHandle_t blas, cudaStream_t st, const __nv_bfloat16* lm_head, int V, int d,
-                             const float* gain, const std::vector<const __nv_bfloat16*>& w_down, int n, float* sigma,
-                             float* mean_out, float* m_scale_out);
 // logits = two planes summed (optional copy out), greedy argmax (first index of the maximum).
 evie_status k_logits_argmax(YView L2, int nseg, int V, float* logits, unsigned long long* best,
                             uint32_t* next_tokens, cudaStream_t st);

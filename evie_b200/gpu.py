@@ -162,12 +162,50 @@ class GpuModel:
         return out[:rows.value].copy()
 
     def neuron_sigma(self):
-        """analysis.rs:129-201 without a lens: (sigma [layers * neurons], unembedding mean [hidden], m_scale)."""
+        """analysis.rs:129-201 through the current lens: (sigma [layers * neurons], unembedding mean [hidden],
+        m_scale)."""
         sig = np.empty(self.layers * self.neurons, np.float32)
         mean = np.empty(self.hidden, np.float32)
         ms = C.c_float()
         self._check(lib().evie_neuron_sigma(self._h, sig.ctypes.data, sig.size, mean.ctypes.data, C.byref(ms)))
         return sig, mean, ms.value
+
+    def set_lens(self, lens):
+        """Copies a lens (evie_b200.lens.Lens) to the device for the analysis calls; None drops it (logit lens)."""
+        if lens is None:
+            self._check(lib().evie_clear_lens(self._h))
+            return
+        d = self.hidden
+        keep = {l: np.ascontiguousarray(m, np.uint16).reshape(d, d) for l, m in lens.maps.items()}
+        ptrs = (C.c_void_p * self.layers)(*[keep[l].ctypes.data if l in keep else None for l in range(self.layers)])
+        self._check(lib().evie_set_lens(self._h, ptrs, self.layers, 0 if lens.kind == "f16" else 1,
+                                        int(lens.target_layer)))
+
+    def lens_logits(self, layer: int, vecs: np.ndarray) -> np.ndarray:
+        """analysis.rs:28-34: [n][vocab] logits of residual-basis vectors [n][hidden] living at `layer`."""
+        x = np.ascontiguousarray(vecs, np.float32).reshape(-1, self.hidden)
+        out = np.empty((x.shape[0], self.vocab), np.float32)
+        self._check(lib().evie_lens_logits(self._h, int(layer), x.ctypes.data, x.shape[0], out.ctypes.data))
+        return out
+
+    def neuron_logits(self, neurons) -> np.ndarray:
+        """analysis.rs:37-67: [n][vocab] logits of the write directions of (layer, neuron) pairs."""
+        ls = np.ascontiguousarray([l for l, _ in neurons], np.int32)
+        ns = np.ascontiguousarray([n for _, n in neurons], np.int32)
+        out = np.empty((len(neurons), self.vocab), np.float32)
+        self._check(lib().evie_neuron_logits(self._h, ls.ctypes.data, ns.ctypes.data, len(neurons), out.ctypes.data))
+        return out
+
+    def search_scores(self, tokens, mean: np.ndarray, sigma: np.ndarray):
+        """analysis.rs:213-240: per-neuron best z of each pole, ([layers][neurons], [layers][neurons])."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        mean = np.ascontiguousarray(mean, np.float32)
+        sigma = np.ascontiguousarray(sigma, np.float32)
+        up = np.empty((self.layers, self.neurons), np.float32)
+        dn = np.empty((self.layers, self.neurons), np.float32)
+        self._check(lib().evie_search_scores(self._h, t.ctypes.data, t.size, mean.ctypes.data, sigma.ctypes.data,
+                                             up.ctypes.data, dn.ctypes.data))
+        return up, dn
 
     def reset_gates(self, slot: int):
         self._check(lib().evie_reset_gates(self._h, slot))

@@ -172,14 +172,38 @@ EVIE_API evie_status evie_set_sampler(evie_ctx* ctx, int slot, const evie_sample
 EVIE_API evie_status evie_reset_slot(evie_ctx* ctx, int slot);
 /* Per-neuron activation scales used to normalise captured frames, layer-major (gpu/mod.rs:549). */
 EVIE_API evie_status evie_set_scale(evie_ctx* ctx, const float* scale, size_t n);
-/* Offline analysis (crates/evie-core/src/analysis.rs:129-201, without a lens): the unembedding statistics
- * (UnembedStats::compute: mean of the LM-head rows, gain-weighted covariance of a strided subsample stored as f16 with
- * its scale) and every neuron's logit spread sqrt(u^T M u) over its down_proj column u (neuron_sigma).
+/* Offline analysis (crates/evie-core/src/analysis.rs, lens.rs). Every call below is synchronous, allocates its
+ * device scratch and frees it before it returns, and runs its products on the library's tensor-core projection
+ * GEMM. A bounded wait that gives up inside one of them makes the call return EVIE_ERR_TIMEOUT.
+ *
+ * A lens (lens.rs:10-83, Lens::load once the torch file is read): per-layer [hidden][hidden] maps J_l, row-major
+ * 16-bit values (kind 0 = f16, 1 = bf16), maps[l] = NULL where the file has no map for layer l; layers past
+ * target_layer, and layers without a map, read out with the identity (Lens::map). The maps are copied to the device
+ * (as J_l and J_l^T); the host arrays may be freed after the call. Replaces the context's previous lens. */
+EVIE_API evie_status evie_set_lens(evie_ctx* ctx, const uint16_t* const* maps, int n_layers, int kind,
+                                   int target_layer);
+/* Drops the lens: the analysis calls read out through the identity (the logit lens). */
+EVIE_API evie_status evie_clear_lens(evie_ctx* ctx);
+/* The unembedding statistics (analysis.rs:129-171, UnembedStats::compute: mean of the LM-head rows, gain-weighted
+ * covariance of a strided subsample stored as f16 with its scale) and every neuron's logit spread sqrt(u^T M u)
+ * over its down_proj column u carried through the lens (analysis.rs:183-201, neuron_sigma).
  *   sigma    [layers * intermediate] host, layer-major (n must equal that count);
- *   mean     [hidden] host or NULL;  m_scale  host or NULL.
- * Allocates and frees ~(hidden x min(vocab, 16384) x 8 + hidden x intermediate x 8) bytes of device memory per call;
- * synchronous. */
+ *   mean     [hidden] host or NULL;  m_scale  host or NULL. */
 EVIE_API evie_status evie_neuron_sigma(evie_ctx* ctx, float* sigma, size_t n, float* mean, float* m_scale);
+/* lens_logits (analysis.rs:28-34): logits [n][vocab] (host) of n residual-basis vectors vecs [n][hidden] (host)
+ * living at `layer`: the lens map of the layer, then the final RMSNorm and the LM head (model.rs:287-294). */
+EVIE_API evie_status evie_lens_logits(evie_ctx* ctx, int layer, const float* vecs, int n, float* logits);
+/* neuron_logits (analysis.rs:37-67): logits [n][vocab] (host) of the write directions W_down[:, neurons[i]] of
+ * layers[i] through the lens and the unembedding. neuron_readouts / token_ranks (analysis.rs:70-105) rank these rows. */
+EVIE_API evie_status evie_neuron_logits(evie_ctx* ctx, const int32_t* layers, const int32_t* neurons, int n,
+                                        float* logits);
+/* search (analysis.rs:213-240) up to the ranking: for every neuron the best standardized score over the tokens of
+ * each pole, z = (W_down^T J_l^T a_t)_n / sigma_n with a_t = (W_U[t] - mean) * g (analysis.rs:173-179):
+ *   z_up[l][n] = max_t z, z_dn[l][n] = max_t -z  (host, [layers * intermediate] each);
+ *   mean, sigma: evie_neuron_sigma's outputs under the same lens. The caller sorts (stable, z descending; per
+ *   layer, then merged) and keeps the top `limit` (analysis.rs:241-250). */
+EVIE_API evie_status evie_search_scores(evie_ctx* ctx, const uint32_t* tokens, int n_tokens, const float* mean,
+                                        const float* sigma, float* z_up, float* z_dn);
 /* Track the max |activation| of every neuron over positions > 0 across later calls (gpu/mod.rs:578). */
 EVIE_API evie_status evie_track_max(evie_ctx* ctx, int on);
 /* Reads the tracked maxima, layer-major (gpu/mod.rs:590). */

@@ -91,6 +91,11 @@ def _declare(L):
         "oracle_gate_state_open": (I, [P, I]),
         "oracle_top_active": (I, [P, LG, I, P]),
         "oracle_neuron_sigma": (F, [P, P, P]),
+        "oracle_lens_set": (None, [P, P, I, I, LG]),
+        "oracle_lens_clear": (None, [P]),
+        "oracle_lens_logits": (None, [P, I, P, LG, P]),
+        "oracle_neuron_logits": (None, [P, P, P, LG, P]),
+        "oracle_search": (LG, [P, P, LG, P, P, LG, P, P, P, P]),
         "oracle_sampler_new": (P, [F, F, F, F, C.c_uint64]),
         "oracle_sampler_free": (None, [P]),
         "oracle_sampler_rng": (C.c_uint64, [P]),
@@ -432,11 +437,49 @@ class Model:
             self._h = None
 
     def neuron_sigma(self):
-        """analysis.rs:129-201 without a lens: (sigma [layers * intermediate], unembedding mean [hidden], m_scale)."""
+        """analysis.rs:129-201 (through the lens when one is set): (sigma [layers * intermediate], unembedding mean
+        [hidden], m_scale)."""
         sig = np.zeros(self.cfg.n_layers * self.cfg.intermediate, np.float32)
         mean = np.zeros(self.cfg.hidden, np.float32)
         ms = lib().oracle_neuron_sigma(self._h, _p(sig), _p(mean))
         return sig, mean, float(ms)
+
+    def set_lens(self, maps: dict, kind: str, target_layer: int):
+        """A loaded lens (lens.rs:10-54): maps {layer: [hidden][hidden] uint16 bits}, kind "f16" or "bf16"."""
+        d, L = self.cfg.hidden, self.cfg.n_layers
+        self._lens = {l: np.ascontiguousarray(m, dtype=np.uint16).reshape(d, d) for l, m in maps.items()}
+        ptrs = (C.c_void_p * L)(*[self._lens[l].ctypes.data if l in self._lens else None for l in range(L)])
+        lib().oracle_lens_set(self._h, ptrs, L, 0 if kind == "f16" else 1, int(target_layer))
+
+    def clear_lens(self):
+        lib().oracle_lens_clear(self._h)
+        self._lens = {}
+
+    def lens_logits(self, layer: int, vecs: np.ndarray) -> np.ndarray:
+        """analysis.rs:28-34: [n][vocab] logits of residual-basis vectors [n][hidden] at `layer`."""
+        x = np.ascontiguousarray(vecs, dtype=np.float32).reshape(-1, self.cfg.hidden)
+        out = np.zeros((x.shape[0], self.cfg.vocab), np.float32)
+        lib().oracle_lens_logits(self._h, int(layer), _p(x), x.shape[0], _p(out))
+        return out
+
+    def neuron_logits(self, neurons) -> np.ndarray:
+        """analysis.rs:37-67: [n][vocab] logits of the write directions of (layer, neuron) pairs."""
+        ls = np.ascontiguousarray([l for l, _ in neurons], np.int32)
+        ns = np.ascontiguousarray([n for _, n in neurons], np.int32)
+        out = np.zeros((len(neurons), self.cfg.vocab), np.float32)
+        lib().oracle_neuron_logits(self._h, _p(ls), _p(ns), len(neurons), _p(out))
+        return out
+
+    def search(self, tokens, mean: np.ndarray, sigma: np.ndarray, limit: int):
+        """analysis.rs:213-251: the top `limit` hits (layer, neuron, sign, z) for the token ids."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        mean = np.ascontiguousarray(mean, np.float32)
+        sigma = np.ascontiguousarray(sigma, np.float32)
+        hl, hn, hs = (np.zeros(limit, np.int32) for _ in range(3))
+        hz = np.zeros(limit, np.float32)
+        k = lib().oracle_search(self._h, _p(t), len(t), _p(mean), _p(sigma), int(limit), _p(hl), _p(hn), _p(hs),
+                                _p(hz))
+        return [(int(hl[i]), int(hn[i]), int(hs[i]), float(hz[i])) for i in range(k)]
 
     def new_cache(self) -> "Cache":
         return Cache(lib().oracle_cache_new(self._h))

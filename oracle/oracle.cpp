@@ -292,7 +292,8 @@ uint32_t sampler_sample(Sampler& s, const float* logits_in, size_t n, const uint
 }
 
 // ------------------------------------------------------------------------------------------------
-// AVX2 matmul (kernels.rs:138-268, 270-522), bf16 weights only
+// AVX2 matmul (kernels.rs:138-268, 270-522). Weights are bf16 bits (uint16_t) or f32 widenings of 16-bit values
+// (float: the f16 matrices of a lens, widened once; widening is exact, so the products and orders are the reference's).
 
 constexpr size_t KC = 256;
 constexpr size_t NR = 16;
@@ -301,6 +302,10 @@ __attribute__((target("avx2,fma,f16c"))) inline __m256 load8(const uint16_t* p) 
   __m128i v = _mm_loadu_si128((const __m128i*)p);
   return _mm256_castsi256_ps(_mm256_slli_epi32(_mm256_cvtepu16_epi32(v), 16));
 }
+
+__attribute__((target("avx2,fma"))) inline __m256 load8(const float* p) { return _mm256_loadu_ps(p); }
+inline float widen(uint16_t x);
+inline float widen(float x) { return x; }
 
 __attribute__((target("avx2,fma"))) inline float hsum(__m256 v) {
   __m128 lo = _mm256_castps256_ps128(v);
@@ -312,12 +317,13 @@ __attribute__((target("avx2,fma"))) inline float hsum(__m256 v) {
 }
 
 // kernels.rs:303-362
-__attribute__((target("avx2,fma,f16c"))) void dot_rows(const uint16_t* w, size_t cols, size_t r0,
+template <typename WT>
+__attribute__((target("avx2,fma,f16c"))) void dot_rows(const WT* w, size_t cols, size_t r0,
                                                          const float* x, float* ys, size_t n) {
   size_t i = 0;
   while (i + 4 <= n) {
-    const uint16_t* p0 = w + (r0 + i) * cols;
-    const uint16_t *p1 = p0 + cols, *p2 = p0 + 2 * cols, *p3 = p0 + 3 * cols;
+    const WT* p0 = w + (r0 + i) * cols;
+    const WT *p1 = p0 + cols, *p2 = p0 + 2 * cols, *p3 = p0 + 3 * cols;
     __m256 z = _mm256_setzero_ps();
     __m256 a0 = z, a1 = z, a2 = z, a3 = z, b0 = z, b1 = z, b2 = z, b3 = z;
     size_t k = 0;
@@ -337,17 +343,17 @@ __attribute__((target("avx2,fma,f16c"))) void dot_rows(const uint16_t* w, size_t
                   hsum(_mm256_add_ps(a3, b3))};
     while (k < cols) {
       float xv = x[k];
-      s[0] += bf16_to_f32(p0[k]) * xv;
-      s[1] += bf16_to_f32(p1[k]) * xv;
-      s[2] += bf16_to_f32(p2[k]) * xv;
-      s[3] += bf16_to_f32(p3[k]) * xv;
+      s[0] += widen(p0[k]) * xv;
+      s[1] += widen(p1[k]) * xv;
+      s[2] += widen(p2[k]) * xv;
+      s[3] += widen(p3[k]) * xv;
       k++;
     }
     memcpy(ys + i, s, sizeof s);
     i += 4;
   }
   while (i < n) {
-    const uint16_t* p = w + (r0 + i) * cols;
+    const WT* p = w + (r0 + i) * cols;
     __m256 a = _mm256_setzero_ps();
     size_t k = 0;
     while (k + 8 <= cols) {
@@ -356,7 +362,7 @@ __attribute__((target("avx2,fma,f16c"))) void dot_rows(const uint16_t* w, size_t
     }
     float s = hsum(a);
     while (k < cols) {
-      s += bf16_to_f32(p[k]) * x[k];
+      s += widen(p[k]) * x[k];
       k++;
     }
     ys[i] = s;
@@ -365,11 +371,11 @@ __attribute__((target("avx2,fma,f16c"))) void dot_rows(const uint16_t* w, size_t
 }
 
 // kernels.rs:365-396
-template <int T>
-__attribute__((target("avx2,fma,f16c"))) void multi_dot(const uint16_t* w, size_t cols, size_t r0, size_t nr,
+template <int T, typename WT>
+__attribute__((target("avx2,fma,f16c"))) void multi_dot(const WT* w, size_t cols, size_t r0, size_t nr,
                                                           const float* x, float* y, size_t ldy) {
   for (size_t r = r0; r < r0 + nr; r++) {
-    const uint16_t* p = w + r * cols;
+    const WT* p = w + r * cols;
     __m256 acc[T];
     for (int t = 0; t < T; t++) acc[t] = _mm256_setzero_ps();
     size_t k = 0;
@@ -380,7 +386,7 @@ __attribute__((target("avx2,fma,f16c"))) void multi_dot(const uint16_t* w, size_
     }
     for (int t = 0; t < T; t++) {
       float s = hsum(acc[t]);
-      for (size_t kk = k; kk < cols; kk++) s += bf16_to_f32(p[kk]) * x[t * cols + kk];
+      for (size_t kk = k; kk < cols; kk++) s += widen(p[kk]) * x[t * cols + kk];
       y[t * ldy + r] = s;
     }
   }
@@ -389,7 +395,6 @@ __attribute__((target("avx2,fma,f16c"))) void multi_dot(const uint16_t* w, size_
 // kernels.rs:427-464 (the packed values are exact f32 widenings; the 8x8 transpose only moves them). The float
 // form packs a matrix already widened from f16 (Kind16::F16), which the same micro-kernel then multiplies.
 inline float widen(uint16_t x) { return bf16_to_f32(x); }
-inline float widen(float x) { return x; }
 template <typename WT>
 __attribute__((target("avx2,fma,f16c"))) void pack_panel(const WT* w, size_t cols, size_t rows, size_t r0,
                                                            size_t k0, size_t kc, float* pack) {
@@ -433,7 +438,8 @@ __attribute__((target("avx2,fma"))) void micro(const float* pack, size_t kc, con
 int n_threads() { return pool().size(); }
 
 // kernels.rs:138-143
-void matvec(const uint16_t* w, size_t rows, size_t cols, const float* x, float* y) {
+template <typename WT>
+void matvec(const WT* w, size_t rows, size_t cols, const float* x, float* y) {
   long chunk = (long)std::min<size_t>(512, std::max<size_t>(4, rows / (n_threads() * 6))) & ~3L;
   if (chunk < 4) chunk = 4;
   long nch = (long)((rows + chunk - 1) / chunk);
@@ -478,7 +484,8 @@ void packed_gemm(const WT* w, size_t rows, size_t cols, const float* x, size_t n
 }
 
 // kernels.rs:163-268
-void matmul(const uint16_t* w, size_t rows, size_t cols, const float* x, size_t n, float* y) {
+template <typename WT>
+void matmul(const WT* w, size_t rows, size_t cols, const float* x, size_t n, float* y) {
   if (n == 0) return;
   if (n == 1) return matvec(w, rows, cols, x, y);
   if (n < 8) {
@@ -577,6 +584,9 @@ struct Model {
   // (1 + kv_perturb * r), r uniform in [-1, 1) from a fixed generator. 0 (the default) leaves the values as they are.
   float kv_perturb = 0.0f;
   uint64_t kv_rng = 0x9E3779B97F4A7C15ull;
+  // lens.rs:10-16: per-layer [d][d] maps (16-bit values widened to f32; empty = no map) and the target layer
+  std::vector<std::vector<float>> lens;
+  long lens_target = -1;
 };
 
 // f32 -> bf16 -> f32, round to nearest even (the rounding of the GPU cache's __float2bfloat16_rn); finite inputs.
@@ -969,10 +979,11 @@ EXPORT int oracle_top_active(const int8_t* f, long n, int k, int32_t* out) {
   for (int i = 0; i < k; i++) out[i] = idx[i];
   return k;
 }
-// crates/evie-core/src/analysis.rs:129-175 (UnembedStats::compute) and 183-201 (neuron_sigma without a lens):
-// mean of the unembedding rows (f64 sums), the gain-weighted covariance of a strided subsample of at most 16384
-// rows (the centred rows scaled by 64 and rounded to f16 as the GEMM's weight operand), normalised to its largest
-// magnitude and stored as f16; then sigma = sqrt(max(u . (M u) * m_scale, 1e-30)) for every down_proj column u.
+// crates/evie-core/src/analysis.rs:129-175 (UnembedStats::compute) and 183-201 (neuron_sigma): mean of the
+// unembedding rows (f64 sums), the gain-weighted covariance of a strided subsample of at most 16384 rows (the
+// centred rows scaled by 64 and rounded to f16 as the GEMM's weight operand), normalised to its largest magnitude
+// and stored as f16; then sigma = sqrt(max(u . (M u) * m_scale, 1e-30)) for every down_proj column u (carried
+// through the lens map of its layer first when a lens is set).
 struct UnembedStats {
   std::vector<float> mean;
   std::vector<float> m;  // d x d, the f16 values widened
@@ -1009,6 +1020,50 @@ UnembedStats unembed_stats(const Model& m) {
   for (size_t i = 0; i < d * d; i++) st.m[i] = f16_to_f32(f32_to_f16(cov[i] / st.m_scale));
   return st;
 }
+// lens.rs:57-62 (map: none past the target layer or where the file has no map) and 64-73 (transport: J_l @ x for n
+// row vectors, the identity without a map).
+const float* lens_map(const Model& m, size_t layer) {
+  if ((long)layer > m.lens_target || layer >= m.lens.size() || m.lens[layer].empty()) return nullptr;
+  return m.lens[layer].data();
+}
+std::vector<float> transport(const Model& m, size_t layer, const float* x, size_t n) {
+  const size_t d = m.cfg.hidden;
+  const float* j = lens_map(m, layer);
+  if (!j) return std::vector<float>(x, x + n * d);
+  std::vector<float> y(n * d);
+  matmul(j, d, d, x, n, y.data());
+  return y;
+}
+// kernels.rs:525-552 (matvec_t): out[c] = sum over rows r (in order, rows with x[r] == 0 skipped) of x[r] w[r][c],
+// each product and sum separately rounded.
+template <typename WT>
+void matvec_t(const WT* w, size_t rows, size_t cols, const float* x, float* out) {
+  for (size_t c = 0; c < cols; c++) out[c] = 0.0f;
+  for (size_t r = 0; r < rows; r++) {
+    const float xr = x[r];
+    if (xr == 0.0f) continue;
+    const WT* row = w + r * cols;
+    for (size_t c = 0; c < cols; c++) out[c] += xr * widen(row[c]);
+  }
+}
+// lens.rs:76-82 (pullback: J_l^T a, the identity without a map)
+std::vector<float> pullback(const Model& m, size_t layer, const float* a) {
+  const size_t d = m.cfg.hidden;
+  const float* j = lens_map(m, layer);
+  if (!j) return std::vector<float>(a, a + d);
+  std::vector<float> out(d);
+  matvec_t(j, d, d, a, out.data());
+  return out;
+}
+// model.rs:287-294 (unembed: final RMSNorm of each row, then the LM head)
+std::vector<float> unembed(const Model& m, const float* x, size_t n) {
+  const size_t d = m.cfg.hidden, v = m.lm_head.rows;
+  std::vector<float> normed(n * d), out(n * v);
+  rmsnorm_rows(x, m.final_norm.data(), m.cfg.eps, normed.data(), d, (long)n);
+  matmul(m.lm_head.p, v, d, normed.data(), n, out.data());
+  return out;
+}
+
 void neuron_sigma(const Model& m, const UnembedStats& st, float* sigma) {
   const size_t nl = m.layers.size(), n = m.cfg.intermediate, d = m.cfg.hidden;
   std::vector<float> u(n * d), mu(n * d);
@@ -1016,6 +1071,7 @@ void neuron_sigma(const Model& m, const UnembedStats& st, float* sigma) {
     const Mat& dn = m.layers[l].down;  // [d][n]
     for (size_t k = 0; k < d; k++)
       for (size_t i = 0; i < n; i++) u[i * d + k] = bf16_to_f32(dn.p[k * n + i]);  // transpose_to_f32
+    if (lens_map(m, l)) u = transport(m, l, u.data(), n);                      // analysis.rs:188-191
     packed_gemm(st.m.data(), d, d, u.data(), n, mu.data());
     for (size_t i = 0; i < n; i++)
       sigma[l * n + i] = std::sqrt(std::max(dot(u.data() + i * d, mu.data() + i * d, d) * st.m_scale, 1e-30f));
@@ -1027,6 +1083,105 @@ EXPORT float oracle_neuron_sigma(void* model, float* sigma, float* mean) {
   if (mean) memcpy(mean, st.mean.data(), st.mean.size() * sizeof(float));
   neuron_sigma(m, st, sigma);
   return st.m_scale;
+}
+// lens.rs:20-54 after the file is read: maps[l] = [d][d] 16-bit values (kind 0 = f16, 1 = bf16) or NULL.
+EXPORT void oracle_lens_set(void* model, const uint16_t* const* maps, int n_layers, int kind, long target_layer) {
+  Model& m = *(Model*)model;
+  const size_t d = m.cfg.hidden;
+  m.lens.assign(n_layers, {});
+  for (int l = 0; l < n_layers; l++) {
+    if (!maps[l]) continue;
+    m.lens[l].resize(d * d);
+    for (size_t i = 0; i < d * d; i++) m.lens[l][i] = kind == 0 ? f16_to_f32(maps[l][i]) : bf16_to_f32(maps[l][i]);
+  }
+  m.lens_target = target_layer;
+}
+EXPORT void oracle_lens_clear(void* model) {
+  Model& m = *(Model*)model;
+  m.lens.clear();
+  m.lens_target = -1;
+}
+// analysis.rs:28-34 (lens_logits): [n][V] logits of n residual-basis vectors at `layer`
+EXPORT void oracle_lens_logits(void* model, int layer, const float* vecs, long n, float* logits) {
+  const Model& m = *(const Model*)model;
+  const std::vector<float> t = transport(m, layer, vecs, n);
+  const std::vector<float> out = unembed(m, t.data(), n);
+  memcpy(logits, out.data(), out.size() * sizeof(float));
+}
+// analysis.rs:37-67 (write_dirs + neuron_logits): the write directions W_down[:, neuron] of each neuron's layer,
+// transported in blocks of one layer (ascending layers), then unembedded in the given order.
+EXPORT void oracle_neuron_logits(void* model, const int32_t* layers, const int32_t* neurons, long n, float* logits) {
+  const Model& m = *(const Model*)model;
+  const size_t d = m.cfg.hidden, ni = m.cfg.intermediate;
+  std::vector<float> dirs(n * d), moved(n * d);
+  for (long i = 0; i < n; i++) {
+    const Mat& dn = m.layers[layers[i]].down;
+    for (size_t k = 0; k < d; k++) dirs[i * d + k] = bf16_to_f32(dn.p[k * ni + neurons[i]]);  // col_to_f32
+  }
+  std::vector<int32_t> ls(layers, layers + n);
+  std::sort(ls.begin(), ls.end());
+  ls.erase(std::unique(ls.begin(), ls.end()), ls.end());
+  for (int32_t l : ls) {
+    std::vector<long> idx;
+    for (long i = 0; i < n; i++)
+      if (layers[i] == l) idx.push_back(i);
+    std::vector<float> block;
+    for (long i : idx) block.insert(block.end(), dirs.begin() + i * d, dirs.begin() + (i + 1) * d);
+    const std::vector<float> t = transport(m, l, block.data(), idx.size());
+    for (size_t j = 0; j < idx.size(); j++) memcpy(&moved[idx[j] * d], &t[j * d], d * sizeof(float));
+  }
+  const std::vector<float> out = unembed(m, moved.data(), n);
+  memcpy(logits, out.data(), out.size() * sizeof(float));
+}
+// analysis.rs:213-251 (search): z scores of `tokens` for every neuron and pole against sigma, best token per
+// (neuron, pole); per layer the hits sorted by z descending (stable) and cut to `limit`, then all layers merged the
+// same way. Writes up to `limit` hits (layer, neuron, sign, z) and returns their count.
+EXPORT long oracle_search(void* model, const uint32_t* tokens, long nt, const float* mean, const float* sigma,
+                          long limit, int32_t* hit_layer, int32_t* hit_neuron, int32_t* hit_sign, float* hit_z) {
+  const Model& m = *(const Model*)model;
+  if (nt == 0) return 0;
+  const size_t nl = m.layers.size(), n = m.cfg.intermediate, d = m.cfg.hidden;
+  const float* g = m.final_norm.data();
+  std::vector<std::vector<float>> a(nt, std::vector<float>(d));
+  for (long t = 0; t < nt; t++)  // analysis.rs:173-179 (UnembedStats::centered)
+    for (size_t i = 0; i < d; i++) a[t][i] = (bf16_to_f32(m.lm_head.p[(size_t)tokens[t] * d + i]) - mean[i]) * g[i];
+  struct Hit {
+    int32_t layer, neuron, sign;
+    float z;
+  };
+  auto by_z = [](const Hit& x, const Hit& y) { return x.z > y.z; };
+  std::vector<Hit> all;
+  for (size_t l = 0; l < nl; l++) {
+    const Mat& dn = m.layers[l].down;  // [d][n]
+    std::vector<std::vector<float>> scores(nt, std::vector<float>(n));
+    for (long t = 0; t < nt; t++) {
+      const std::vector<float> pulled = pullback(m, l, a[t].data());
+      matvec_t(dn.p, d, n, pulled.data(), scores[t].data());
+    }
+    std::vector<Hit> best;
+    for (size_t i = 0; i < n; i++) {
+      float up = -INFINITY, dnz = -INFINITY;
+      for (long t = 0; t < nt; t++) {
+        const float z = scores[t][i] / sigma[l * n + i];
+        up = std::max(up, z);
+        dnz = std::max(dnz, -z);
+      }
+      best.push_back({(int32_t)l, (int32_t)i, 1, up});
+      best.push_back({(int32_t)l, (int32_t)i, -1, dnz});
+    }
+    std::stable_sort(best.begin(), best.end(), by_z);
+    if ((long)best.size() > limit) best.resize(limit);
+    all.insert(all.end(), best.begin(), best.end());
+  }
+  std::stable_sort(all.begin(), all.end(), by_z);
+  if ((long)all.size() > limit) all.resize(limit);
+  for (size_t i = 0; i < all.size(); i++) {
+    hit_layer[i] = all[i].layer;
+    hit_neuron[i] = all[i].neuron;
+    hit_sign[i] = all[i].sign;
+    hit_z[i] = all[i].z;
+  }
+  return (long)all.size();
 }
 EXPORT int oracle_topk(const float* v, long n, int k, uint32_t* idx, float* val) { return topk(v, n, k, idx, val); }
 EXPORT void oracle_softmax(float* x, long n) { softmax_inplace(x, n); }
