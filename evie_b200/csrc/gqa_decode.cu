@@ -959,6 +959,381 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) scr.tickets[bh] = 0;
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// The same tensor-core kernel with K and V tiles brought by TMA in the 128-byte swizzle. A 16-token tile is four
+// boxes of 64 dims x 16 rows over the cache viewed as [pages x Hkv x page_size rows][256 dims]; in shared memory
+// each box is 16 rows of 128 bytes whose 16-byte chunks are XORed with the row index (mod 8). The MMA operands are
+// then read with ldmatrix: the 8 rows of each 8 x 8 matrix fall on 8 different chunks, so the fragment loads are
+// free of bank conflicts (the bulk-copy ring above keeps rows 512 bytes apart: 2-way conflicts for K, 4-way for V),
+// and V^T comes from ldmatrix.trans without byte permutes. Head dims are in natural order: QK k-block kb covers
+// dims 16 kb .. 16 kb + 15, PV m-tile i dims 16 i .. 16 i + 15. Rows past the context in the last tile are loaded
+// (the box is whole) and never used: their scores are masked, and their V values are zeroed in the registers before
+// P V (they may hold anything, e.g. NaN). WARPS warps of kSplit / WARPS tokens per CTA; with 4 warps two CTAs share
+// an SM, so one CTA's ring fills while the other streams.
+template <int WARPS>
+struct TmaCfg {
+  static constexpr int kThreads = WARPS * 32;
+  static constexpr int kTokW = kSplit / WARPS;  // tokens per warp
+  static constexpr int kTiles = kTokW / 16;     // K tiles (and V tiles) per warp
+  static constexpr int kStages = 3;
+  static constexpr int kWarpRing = kStages * kTileBytes;
+  static constexpr int kSmem = WARPS * kWarpRing + 1024;  // + slack to align the ring to 1024 bytes
+  static_assert(kTiles <= 32, "one lane per tile for the row lookup");
+};
+
+// Shared address of the 16-byte chunk of dims d .. d + 7 (d % 8 == 0) in row r of a swizzled 16-row tile
+__device__ __forceinline__ uint32_t sw_addr(uint32_t tile, int r, int d) {
+  return tile + (uint32_t)(d >> 6) * 2048u + (uint32_t)r * 128u + ((uint32_t)(((d & 63) >> 3) ^ (r & 7)) << 4);
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <class IO, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 8 / WARPS)
+    gqa_decode_tma_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, IO io,
+                          int Hkv, int page_size, int max_pages, float scale, Scratch scr, unsigned int* timeouts) {
+  using C = TmaCfg<WARPS>;
+  pdl_trigger();
+  pdl_wait();
+  constexpr int GROUP = 4;
+  extern __shared__ uint8_t tma_smem_raw[];
+  uint8_t* ring_all = tma_smem_raw + ((1024u - (tc::smem_u32(tma_smem_raw) & 1023u)) & 1023u);
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int ctx = min(io.ctx_of(b), max_pages * page_size);
+  const int n_splits = (ctx + kSplit - 1) / kSplit;
+  const int h0 = kvh * GROUP;
+  if (ctx <= 0) {
+    if (split == 0)
+      for (int i = tid; i < GROUP * kHD; i += C::kThreads) io.store(b, h0 + i / kHD, i % kHD, 0.0f);
+    return;
+  }
+  if (split >= n_splits) return;
+
+  __shared__ __align__(16) __nv_bfloat16 sP[WARPS][8][16];
+  __shared__ __align__(16) float sQ[GROUP][kHD];
+  auto sO = [&](int w, int h) { return reinterpret_cast<float*>(ring_all + w * C::kWarpRing) + h * kHD; };
+  __shared__ float sM[WARPS][GROUP], sL[WARPS][GROUP];
+  __shared__ float s_w[WARPS][GROUP];
+  __shared__ float s_fin[GROUP][2];
+  __shared__ int s_last;
+  __shared__ __align__(8) uint64_t s_bar[WARPS][C::kStages];
+
+  const int32_t* pt = io.page_row(b);
+  const int wt0 = split * kSplit + warp * C::kTokW;
+  const int nt = min(C::kTiles, max(0, (ctx - wt0 + 15) / 16));
+  // lane t holds the cache row of tile t (K tile t and V tile t cover the same tokens)
+  int my_row = 0;
+  if (lane < nt) {
+    const int j = wt0 + 16 * lane;
+    my_row = (pt[j / page_size] * Hkv + kvh) * page_size + j % page_size;
+  }
+  uint8_t* ring = ring_all + warp * C::kWarpRing;
+  const uint32_t ring_s = tc::smem_u32(ring);
+  uint64_t* bar = s_bar[warp];
+  if (lane == 0) {
+    for (int i = 0; i < C::kStages; i++) tc::mbar_init(&bar[i], 1);
+    tc::fence_barrier_init();
+  }
+  __syncwarp();
+  const uint64_t evict_first = tc::l2_evict_first();
+  bool ok = true;
+  int issued = 0, consumed = 0;
+  auto issue = [&](int n) {  // tile n into stage n % kStages (the warp has finished reading that stage)
+    const bool isv = n >= nt;
+    const int row = __shfl_sync(0xffffffffu, my_row, isv ? n - nt : n);
+    if (!ok) return;
+    if (lane == 0) {
+      uint8_t* dst = ring + (n % C::kStages) * kTileBytes;
+      tc::fence_proxy_async();
+      tc::mbar_arrive_expect_tx(&bar[n % C::kStages], kTileBytes);
+#pragma unroll
+      for (int s = 0; s < 4; s++)
+        tc::tma_load_2d_hint(dst + s * 2048, isv ? &mv : &mk, &bar[n % C::kStages], 64 * s, row, evict_first);
+    }
+    issued = n + 1;
+  };
+  auto take = [&](int n) -> uint32_t {  // wait for tile n; its stage's shared address
+    if (ok && !tc::mbar_wait(&bar[n % C::kStages], (n / C::kStages) & 1)) ok = false;
+    if (ok) consumed = n + 1;
+    return ring_s + (n % C::kStages) * kTileBytes;
+  };
+  for (int n = 0; n < C::kStages && n < 2 * nt; n++) issue(n);
+
+  // q of the 4 heads staged once per CTA, then Q^T fragments: column n = g is head g % 4, half g / 4 (0 = hi,
+  // 1 = lo), pre-scaled into the log2 domain; k-block kb holds dims {16 kb + 2c, +1} and {16 kb + 8 + 2c, +1}.
+  for (int i = tid; i < GROUP * kHD / 8; i += C::kThreads) io.load_q8(b, h0 + i / 32, (i % 32) * 8, &sQ[i / 32][(i % 32) * 8]);
+  __syncthreads();
+  uint32_t qf[16][2];
+  {
+    const float* qh = sQ[g & 3];
+    const bool lo = g >= 4;
+    const float f = scale * kLog2e;
+    auto part = [&](float x) {
+      x *= f;
+      return lo ? x - bf16_round(x) : x;
+    };
+#pragma unroll
+    for (int kb = 0; kb < 16; kb++) {
+      qf[kb][0] = pack_bf16x2(part(qh[16 * kb + 2 * c]), part(qh[16 * kb + 2 * c + 1]));
+      qf[kb][1] = pack_bf16x2(part(qh[16 * kb + 8 + 2 * c]), part(qh[16 * kb + 9 + 2 * c]));
+    }
+  }
+  // ldmatrix row addresses: lane l gives row (l & 7) of matrix l >> 3
+  const int mi = lane >> 3, rr = lane & 7;
+  const int k_row = (mi & 1) * 8 + rr, k_dim = (mi >> 1) * 8;  // K: matrices (rows 0-7 | 8-15) x (dims +0 | +8)
+  const int v_row = (mi >> 1) * 8 + rr, v_dim = (mi & 1) * 8;  // V: matrices (tokens 0-7 | 8-15) x (dims +0 | +8)
+
+  // ---- scores: lane holds heads hh, hh+1 (hh = 2 (c & 1)) for tokens g and g+8 of each tile
+  float sc[C::kTiles][4];
+#pragma unroll
+  for (int t = 0; t < C::kTiles; t++) {
+    const int jA = wt0 + 16 * t + g, jB = jA + 8;
+    if (t < nt) {
+      const uint32_t tile = take(t);
+      float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kb = 0; kb < 16; kb++) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(sw_addr(tile, k_row, 16 * kb + k_dim), a0, a1, a2, a3);
+        mma_bf16_16816((kb & 1) ? acc1 : acc0, a0, a1, a2, a3, qf[kb][0], qf[kb][1]);
+      }
+      __syncwarp();
+      if (t + C::kStages < 2 * nt) issue(t + C::kStages);
+      float acc[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        acc[i] = acc0[i] + acc1[i];
+        acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 2);  // hi + lo columns
+      }
+      sc[t][0] = jA < ctx ? acc[0] : -INFINITY;
+      sc[t][1] = jA < ctx ? acc[1] : -INFINITY;
+      sc[t][2] = jB < ctx ? acc[2] : -INFINITY;
+      sc[t][3] = jB < ctx ? acc[3] : -INFINITY;
+    } else {
+      sc[t][0] = sc[t][1] = sc[t][2] = sc[t][3] = -INFINITY;
+    }
+  }
+  // ---- warp softmax statistics per head (lanes with equal c hold the same heads)
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+  for (int t = 0; t < C::kTiles; t++) {
+    m0 = fmaxf(m0, fmaxf(sc[t][0], sc[t][2]));
+    m1 = fmaxf(m1, fmaxf(sc[t][1], sc[t][3]));
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+  }
+  const float b0m = m0 == -INFINITY ? 0.f : m0, b1m = m1 == -INFINITY ? 0.f : m1;
+  float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+  for (int t = 0; t < C::kTiles; t++) {
+    sc[t][0] = exp2f(sc[t][0] - b0m);
+    sc[t][1] = exp2f(sc[t][1] - b1m);
+    sc[t][2] = exp2f(sc[t][2] - b0m);
+    sc[t][3] = exp2f(sc[t][3] - b1m);
+    l0 += sc[t][0] + sc[t][2];
+    l1 += sc[t][1] + sc[t][3];
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  const int hh = 2 * (c & 1);
+  if (g == 0 && c < 2) {
+    sM[warp][hh] = m0;
+    sM[warp][hh + 1] = m1;
+    sL[warp][hh] = l0;
+    sL[warp][hh + 1] = l1;
+  }
+
+  // ---- P.V over the 16 m-tiles of 16 head dims
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+#pragma unroll 1
+  for (int t = 0; t < nt; t++) {
+    const int base = wt0 + 16 * t;
+    __syncwarp();
+    {  // P^T into shared memory as [h'][token]: lanes c < 2 write the hi halves, c >= 2 the lo halves
+      const int r0 = hh + (c >= 2 ? 4 : 0);
+      float pv[4] = {sc[0][0], sc[0][1], sc[0][2], sc[0][3]};
+#pragma unroll
+      for (int tt = 1; tt < C::kTiles; tt++)
+        if (tt == t) pv[0] = sc[tt][0], pv[1] = sc[tt][1], pv[2] = sc[tt][2], pv[3] = sc[tt][3];
+      if (c >= 2)
+#pragma unroll
+        for (int i = 0; i < 4; i++) pv[i] -= bf16_round(pv[i]);
+      sP[warp][r0][g] = __float2bfloat16_rn(pv[0]);
+      sP[warp][r0 + 1][g] = __float2bfloat16_rn(pv[1]);
+      sP[warp][r0][g + 8] = __float2bfloat16_rn(pv[2]);
+      sP[warp][r0 + 1][g + 8] = __float2bfloat16_rn(pv[3]);
+    }
+    __syncwarp();
+    const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(&sP[warp][g][2 * c]);
+    const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(&sP[warp][g][2 * c + 8]);
+    // V rows past the context: tokens 2c, 2c+1 (low, high half of a0 and a1) and 2c+8, 2c+9 (a2, a3)
+    const int left = ctx - base;  // >= 1
+    const uint32_t m01 = (2 * c < left ? 0x0000FFFFu : 0u) | (2 * c + 1 < left ? 0xFFFF0000u : 0u);
+    const uint32_t m23 = (2 * c + 8 < left ? 0x0000FFFFu : 0u) | (2 * c + 9 < left ? 0xFFFF0000u : 0u);
+    const uint32_t tile = take(nt + t);
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(sw_addr(tile, v_row, 16 * i + v_dim), a0, a1, a2, a3);
+      mma_bf16_16816(o[i], a0 & m01, a1 & m01, a2 & m23, a3 & m23, pb0, pb1);
+    }
+    __syncwarp();
+    if (nt + t + C::kStages < 2 * nt) issue(nt + t + C::kStages);
+  }
+  // Every copy this warp issued has been waited for (consumed == issued). After a give-up the warp waits for the
+  // outstanding ones once more, again bounded by kWaitNs; if that wait gives up too, a copy may still land in the
+  // ring while the warp writes sO below or after the CTA exits, and this split's outputs are undefined (the call
+  // already reports EVIE_ERR_TIMEOUT through the device counter).
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok) {
+    for (int n = consumed; n < issued; n++) tc::mbar_wait(&bar[n % C::kStages], (n / C::kStages) & 1);
+    if (lane == 0) atomicAdd(timeouts, 1u);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; i++)
+#pragma unroll
+    for (int k = 0; k < 4; k++) o[i][k] += __shfl_xor_sync(0xffffffffu, o[i][k], 2);  // hi + lo
+  if (c < 2) {
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const int d0 = 16 * i + g, d1 = d0 + 8;
+      sO(warp, hh)[d0] = o[i][0];
+      sO(warp, hh + 1)[d0] = o[i][1];
+      sO(warp, hh)[d1] = o[i][2];
+      sO(warp, hh + 1)[d1] = o[i][3];
+    }
+  }
+  __syncthreads();
+
+  // ---- merge the warps of this split
+  if (tid < GROUP) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < WARPS; w++) M = fmaxf(M, sM[w][tid]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; w++) {
+      const float wt = sM[w][tid] == -INFINITY ? 0.f : exp2f(sM[w][tid] - M);
+      s_w[w][tid] = wt;
+      L += wt * sL[w][tid];
+    }
+    s_fin[tid][0] = M;
+    s_fin[tid][1] = L;
+  }
+  __syncthreads();
+  constexpr int kOutPerThread = GROUP * kHD / C::kThreads;
+  float osum[kOutPerThread];
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) {
+    const int e = tid + i * C::kThreads;
+    const int h = e / kHD, d = e % kHD;
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; w++) a += s_w[w][h] * sO(w, h)[d];
+    osum[i] = a;
+  }
+  if (n_splits == 1) {
+#pragma unroll
+    for (int i = 0; i < kOutPerThread; i++) {
+      const int e = tid + i * C::kThreads;
+      const int h = e / kHD, d = e % kHD;
+      io.store(b, h0 + h, d, osum[i] / s_fin[h][1] * sigmoidf_(io.gate(b, h0 + h, d)));
+    }
+    return;
+  }
+  const size_t bh = (size_t)b * Hkv + kvh;
+  float* po = scr.o + (bh * scr.max_splits + split) * GROUP * kHD;
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) __stcg(po + tid + i * C::kThreads, osum[i]);
+  if (tid < GROUP) {
+    float* pml = scr.ml + ((bh * scr.max_splits + split) * GROUP + tid) * 2;
+    __stcg(pml, s_fin[tid][0]);
+    __stcg(pml + 1, s_fin[tid][1]);
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(scr.tickets + bh, 1) == n_splits - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float* s_sw = sO(0, 0);  // [GROUP][n_splits] merge weights (n_splits <= 512 fits in warp 0's ring)
+  if (tid < GROUP) {
+    const float* ml = scr.ml + (bh * scr.max_splits) * GROUP * 2;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < n_splits; s2++) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * GROUP + tid) * 2));
+    float L = 0.f;
+    for (int s2 = 0; s2 < n_splits; s2++) {
+      const float w = exp2f(__ldcg(ml + ((size_t)s2 * GROUP + tid) * 2) - M);
+      s_sw[tid * n_splits + s2] = w;
+      L += w * __ldcg(ml + ((size_t)s2 * GROUP + tid) * 2 + 1);
+    }
+    for (int s2 = 0; s2 < n_splits; s2++) s_sw[tid * n_splits + s2] /= L;
+  }
+  __syncthreads();
+  const float* pob = scr.o + bh * scr.max_splits * GROUP * kHD;
+#pragma unroll
+  for (int i = 0; i < kOutPerThread; i++) {
+    const int e = tid + i * C::kThreads;
+    const int h = e / kHD, d = e % kHD;
+    float a = 0.f;
+    for (int s2 = 0; s2 < n_splits; s2++) a += s_sw[h * n_splits + s2] * __ldcg(pob + (size_t)s2 * GROUP * kHD + e);
+    io.store(b, h0 + h, d, a * sigmoidf_(io.gate(b, h0 + h, d)));
+  }
+  if (tid == 0) scr.tickets[bh] = 0;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// The paged cache [pages][Hkv][page_size][256] bf16 as a 2-D tensor (dim, page row), box 64 dims x 16 rows, 128-byte
+// swizzle. The row extent is not known to the isolated op, so the map spans the largest row count a TMA coordinate
+// can address; the page table bounds the rows read, as it bounds the other kernels' loads.
+evie_status kv_tile_map(CUtensorMap* m, const void* base) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(EVIE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {(cuuint64_t)kHD, (cuuint64_t)INT32_MAX};
+  const cuuint64_t strides[1] = {(cuuint64_t)kHD * 2};
+  const cuuint32_t box[2] = {64, 16};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EVIE_ERR_CUDA, "cuTensorMapEncodeTiled (KV tiles) failed (%d)", (int)r);
+  return EVIE_OK;
+}
+
 // Split scratch per (device, stream), grown on demand and kept for the process lifetime, so that calls on
 // different streams never share tickets or partials.
 struct DeviceScratch {
@@ -1011,13 +1386,41 @@ bool mma_disabled() {
   return off;
 }
 
-// EVIE_GQA_BULK=0 keeps the register-fed tensor-core kernel instead of the bulk-copy one (same results).
+// EVIE_GQA_BULK=0 keeps the register-fed tensor-core kernel instead of the shared-memory ring ones (same results).
 bool bulk_enabled() {
   static const bool on = [] {
     const char* e = getenv("EVIE_GQA_BULK");
     return !(e && e[0] == '0');
   }();
   return on;
+}
+
+// Warps per CTA of the TMA kernel: 4 (two CTAs per SM, the default) or 8; EVIE_GQA_TMA=0 keeps the bulk-copy ring.
+int tma_warps() {
+  static const int w = [] {
+    const char* e = getenv("EVIE_GQA_TMA");
+    if (!e) return 4;
+    const int v = atoi(e);
+    return v == 0 || v == 8 ? v : 4;
+  }();
+  return w;
+}
+
+template <class IO, int WARPS>
+evie_status launch_tma(const IO& io, const __nv_bfloat16* kp, const __nv_bfloat16* vp, dim3 grid, int Hkv,
+                       int page_size, int max_pages, float scale, const Scratch& scr, unsigned int* counter,
+                       cudaStream_t st) {
+  using C = TmaCfg<WARPS>;
+  if (page_size % 16 != 0) return fail(EVIE_ERR_ARG, "decode attention: page size must be a multiple of 16");
+  if (((uintptr_t)kp | (uintptr_t)vp) & 15) return fail(EVIE_ERR_ARG, "decode attention: KV pages 16-byte aligned");
+  CUtensorMap mk, mv;
+  EVIE_TRY(kv_tile_map(&mk, kp));
+  EVIE_TRY(kv_tile_map(&mv, vp));
+  EVIE_TRY(max_dynamic_smem((const void*)gqa_decode_tma_kernel<IO, WARPS>, C::kSmem));
+  EVIE_CUDA_TRY(launch_k(gqa_decode_tma_kernel<IO, WARPS>, grid, dim3(C::kThreads), C::kSmem, st, mk, mv, io, Hkv,
+                         page_size, max_pages, scale, scr, counter));
+  EVIE_CHECK_LAUNCH("gqa_decode_tma_kernel");
+  return EVIE_OK;
 }
 
 template <typename KV, class IO>
@@ -1031,6 +1434,8 @@ evie_status launch_gqa(const IO& io, const KV* kp, const KV* vp, int B, int Hq, 
       if (bulk_enabled()) {
         unsigned int* counter = device_timeout_counter();
         if (!counter) return fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
+        if (tma_warps() == 4) return launch_tma<IO, 4>(io, kp, vp, grid, Hkv, page_size, max_pages, scale, scr, counter, st);
+        if (tma_warps() == 8) return launch_tma<IO, 8>(io, kp, vp, grid, Hkv, page_size, max_pages, scale, scr, counter, st);
         EVIE_TRY(max_dynamic_smem((const void*)gqa_decode_bulk_kernel<IO>, kRingBytes));
         EVIE_CUDA_TRY(launch_k(gqa_decode_bulk_kernel<IO>, dim3(grid), dim3(kThreads), kRingBytes, st, io, kp, vp, Hkv, page_size, max_pages, scale,
                                                                         scr, counter));

@@ -8,10 +8,16 @@ import oracle
 from tests._inputs import bf16_bits, gqa_inputs
 
 
-def _check(B, Hq, Hkv, ctx, seed, cuda, page=256):
+def _check(B, Hq, Hkv, ctx, seed, cuda, page=256, nan_tail=False):
     from evie_b200 import ops
 
     x = gqa_inputs(B, Hq, Hkv, ctx, seed, page=page)
+    if nan_tail:  # every cache position past a sequence's context holds NaN; none may reach an output
+        nan = torch.tensor(float("nan"), dtype=torch.bfloat16)
+        for b, c in enumerate(ctx):
+            for j in range(c, (c + page - 1) // page * page):
+                x["kp"][x["pt"][b, j // page], :, j % page] = nan
+                x["vp"][x["pt"][b, j // page], :, j % page] = nan
     scale = 1.0 / 16.0
     ref = oracle.gqa_decode(bf16_bits(x["q"]), bf16_bits(x["kp"]), bf16_bits(x["vp"]), x["pt"].numpy(),
                             x["ctx"].numpy(), bf16_bits(x["gate"]), scale)
@@ -19,6 +25,7 @@ def _check(B, Hq, Hkv, ctx, seed, cuda, page=256):
                                x["pt"].to(cuda), x["ctx"].to(cuda), scale)
     torch.cuda.synchronize()
     out = out.cpu().numpy()
+    assert np.isfinite(out).all()
     # fp32 arithmetic on identical bf16 inputs; differences come from summation order only
     assert np.abs(out - ref).max() < 2e-5, float(np.abs(out - ref).max())
     return out
@@ -28,6 +35,13 @@ def _check(B, Hq, Hkv, ctx, seed, cuda, page=256):
 @pytest.mark.parametrize("ctx", [[1], [0, 5], [63, 64, 65], [255, 256, 257], [511, 512, 513], [1000, 2048, 4097]])
 def test_gqa_decode_edges(ctx, cuda):
     _check(len(ctx), 16, 4, ctx, 11, cuda)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ctx", [[1, 17, 250], [513, 1000, 4097]])
+def test_gqa_decode_garbage_past_context(ctx, cuda):
+    """Tiles are read whole: the rows past each context (here NaN) are masked in the scores and zeroed in V."""
+    _check(len(ctx), 16, 4, ctx, 13, cuda, nan_tail=True)
 
 
 @pytest.mark.gpu
