@@ -70,6 +70,8 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // turns those off too). Kernels that start early and wait hold the SM resources the GEMM's CTAs need to become
 // resident and stream their first weight tiles.
 bool pdl_enabled();
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count();
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                             Args&&... args) {

@@ -1,5 +1,6 @@
 // Error-message storage behind evie_last_global_error(), and the per-device kernel attribute cache.
 #include <cstdlib>
+#include <map>
 #include <mutex>
 #include <set>
 #include <tuple>
@@ -20,6 +21,19 @@ evie_status func_attr(const void* fn, cudaFuncAttribute attr, int value) {
 }
 evie_status max_dynamic_smem(const void* fn, int bytes) {
   return func_attr(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
+  cache[dev] = n;
+  return n;
 }
 bool pdl_enabled() {
   static const bool on = [] {

@@ -2,8 +2,12 @@
 // Each follows the corresponding step of evie-core's CPU engine, crates/evie-core/src/model.rs (line numbers
 // below), in f32 with the same formulas; only summation orders differ.
 #include "model_kernels.h"
+#include "gdn_chunk.h"
+#include "tc.h"
 
+#include <algorithm>
 #include <climits>
+#include <cstdlib>
 
 namespace evie {
 
@@ -348,9 +352,90 @@ __global__ void conv_state_update_kernel(YView y, int ldy,
   }
 }
 
-// model.rs:362-387 (+ recur_body model.rs:503-524): one CTA per (segment, value head), 256 threads, the head's
-// [128][128] state resident in registers across the segment's rows (16 rows x 4 columns per thread).
+// model.rs:362-387 (+ recur_body model.rs:503-524): the rows of one segment for one value head, 256 threads, the
+// head's [128][128] state resident in registers across the rows (thread (warp, lane) holds rows warp + 8 r, columns
+// 4 lane .. 4 lane + 3); gated RMSNorm (model.rs:377-383) of each row's output into X2.
 constexpr int kMixThreads = 256;
+struct MixShared {
+  float sq[128], sk[128];
+  float4 red[8][32];
+  float sred[4];
+  float s_o[128];
+  float s_db[2];  // the row's decay and beta
+};
+__device__ __forceinline__ void mixer_rows(float4 (&s)[16], MixShared& sh, const float* __restrict__ act,
+                                           const YView& y, int ldy, const SegInfo& sg, int head,
+                                           const float* __restrict__ neg_a, const float* __restrict__ dt_bias,
+                                           const float* __restrict__ norm_w, int conv_dim, int key_dim, int vd, int hv,
+                                           int ratio, float eps, __nv_bfloat16* __restrict__ X2, size_t xplane) {
+  constexpr int DK = 128, DV = 128;
+  const int kh = head / ratio;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;  // lane: 4 columns; warp: rows warp + 8 r
+  for (int t = 0; t < sg.count; t++) {
+    const int row = sg.start + t;
+    const float* ar = act + (size_t)row * conv_dim;
+    if (tid < DK) sh.sq[tid] = ar[kh * DK + tid];
+    else sh.sk[tid - DK] = ar[key_dim + kh * DK + (tid - DK)];
+    const float4 v4 = *reinterpret_cast<const float4*>(ar + 2 * key_dim + head * DV + lane * 4);
+    if (tid == DK) {  // one thread reads the head's b and a logits (all K-slice planes) for the whole CTA
+      const float bb = y.at((size_t)row * ldy + conv_dim + vd + head);
+      const float aa = y.at((size_t)row * ldy + conv_dim + vd + hv + head);
+      sh.s_db[0] = expf(neg_a[head] * softplus_(aa + dt_bias[head]));
+      sh.s_db[1] = sigmoidf_(bb);
+    }
+    // the output gate is read here, with the other inputs, so its latency is not exposed after the state update
+    const float z = tid < DV ? y.at((size_t)row * ldy + conv_dim + head * DV + tid) : 0.f;
+    __syncthreads();
+    const float decay = sh.s_db[0], beta = sh.s_db[1];
+    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+      const float kr = sh.sk[warp + 8 * r];
+      kv.x += s[r].x * kr; kv.y += s[r].y * kr; kv.z += s[r].z * kr; kv.w += s[r].w * kr;
+    }
+    sh.red[warp][lane] = kv;
+    __syncthreads();
+    kv = sh.red[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; w++) {
+      const float4 u = sh.red[w][lane];
+      kv.x += u.x; kv.y += u.y; kv.z += u.z; kv.w += u.w;
+    }
+    const float d0 = (v4.x - decay * kv.x) * beta, d1 = (v4.y - decay * kv.y) * beta;
+    const float d2 = (v4.z - decay * kv.z) * beta, d3 = (v4.w - decay * kv.w) * beta;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+      const int i = warp + 8 * r;
+      const float kr = sh.sk[i], qr = sh.sq[i];
+      s[r].x = s[r].x * decay + kr * d0; s[r].y = s[r].y * decay + kr * d1;
+      s[r].z = s[r].z * decay + kr * d2; s[r].w = s[r].w * decay + kr * d3;
+      o.x += s[r].x * qr; o.y += s[r].y * qr; o.z += s[r].z * qr; o.w += s[r].w * qr;
+    }
+    __syncthreads();  // everyone has read red (kv) before it is reused
+    sh.red[warp][lane] = o;
+    __syncthreads();
+    if (tid < DV) {  // thread j finishes output column j
+      const float* rf = reinterpret_cast<const float*>(&sh.red[0][0]);
+      float oj = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; w++) oj += rf[w * DV + tid];
+      sh.s_o[tid] = oj;
+      float ss = oj * oj;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) sh.sred[warp] = ss;
+    }
+    __syncthreads();
+    if (tid < DV) {  // gated RMSNorm, model.rs:377-383: o * rsqrt(mean o^2 + eps) * w * silu(z)
+      const float ms = (sh.sred[0] + sh.sred[1] + sh.sred[2] + sh.sred[3]) / (float)DV;
+      const float inv = 1.0f / sqrtf(ms + eps);
+      store_split(X2, xplane, (size_t)row * vd + head * DV + tid, sh.s_o[tid] * inv * norm_w[tid] * siluf_(z));
+    }
+  }
+}
+
+// One CTA per (segment, value head).
 __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
     const float* __restrict__ act, YView y, int ldy,
     const SegInfo* __restrict__ segs, float* __restrict__ rec_state, size_t rs_slot, const float* __restrict__ neg_a,
@@ -362,83 +447,87 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
   const int head = blockIdx.x;
   const SegInfo sg = segs[blockIdx.y];
   if (sg.count == 0) return;
-  const int kh = head / ratio;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;  // lane: 4 columns; warp: rows warp + 8 r
-  __shared__ float sq[DK], sk[DK];
-  __shared__ float4 red[8][32];
-  __shared__ float sred[4];
-  __shared__ float s_o[DV];
-
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ MixShared sh;
   float* Sh = rec_state + (size_t)sg.slot * rs_slot + (size_t)head * DK * DV + lane * 4;
   float4 s[16];
 #pragma unroll
   for (int r = 0; r < 16; r++) s[r] = *reinterpret_cast<const float4*>(Sh + (size_t)(warp + 8 * r) * DV);
-
-  __shared__ float s_db[2];  // this row's decay and beta
-  for (int t = 0; t < sg.count; t++) {
-    const int row = sg.start + t;
-    const float* ar = act + (size_t)row * conv_dim;
-    if (tid < DK) sq[tid] = ar[kh * DK + tid];
-    else sk[tid - DK] = ar[key_dim + kh * DK + (tid - DK)];
-    const float4 v4 = *reinterpret_cast<const float4*>(ar + 2 * key_dim + head * DV + lane * 4);
-    if (tid == DK) {  // one thread reads the head's b and a logits (all K-slice planes) for the whole CTA
-      const float bb = y.at((size_t)row * ldy + conv_dim + vd + head);
-      const float aa = y.at((size_t)row * ldy + conv_dim + vd + hv + head);
-      s_db[0] = expf(neg_a[head] * softplus_(aa + dt_bias[head]));
-      s_db[1] = sigmoidf_(bb);
-    }
-    // the output gate is read here, with the other inputs, so its latency is not exposed after the state update
-    const float z = tid < DV ? y.at((size_t)row * ldy + conv_dim + head * DV + tid) : 0.f;
-    __syncthreads();
-    const float decay = s_db[0], beta = s_db[1];
-    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int r = 0; r < 16; r++) {
-      const float kr = sk[warp + 8 * r];
-      kv.x += s[r].x * kr; kv.y += s[r].y * kr; kv.z += s[r].z * kr; kv.w += s[r].w * kr;
-    }
-    red[warp][lane] = kv;
-    __syncthreads();
-    kv = red[0][lane];
-#pragma unroll
-    for (int w = 1; w < 8; w++) {
-      const float4 u = red[w][lane];
-      kv.x += u.x; kv.y += u.y; kv.z += u.z; kv.w += u.w;
-    }
-    const float d0 = (v4.x - decay * kv.x) * beta, d1 = (v4.y - decay * kv.y) * beta;
-    const float d2 = (v4.z - decay * kv.z) * beta, d3 = (v4.w - decay * kv.w) * beta;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int r = 0; r < 16; r++) {
-      const int i = warp + 8 * r;
-      const float kr = sk[i], qr = sq[i];
-      s[r].x = s[r].x * decay + kr * d0; s[r].y = s[r].y * decay + kr * d1;
-      s[r].z = s[r].z * decay + kr * d2; s[r].w = s[r].w * decay + kr * d3;
-      o.x += s[r].x * qr; o.y += s[r].y * qr; o.z += s[r].z * qr; o.w += s[r].w * qr;
-    }
-    __syncthreads();  // everyone has read red (kv) before it is reused
-    red[warp][lane] = o;
-    __syncthreads();
-    if (tid < DV) {  // thread j finishes output column j
-      const float* rf = reinterpret_cast<const float*>(&red[0][0]);
-      float oj = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; w++) oj += rf[w * DV + tid];
-      s_o[tid] = oj;
-      float ss = oj * oj;
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if (lane == 0) sred[warp] = ss;
-    }
-    __syncthreads();
-    if (tid < DV) {  // gated RMSNorm, model.rs:377-383: o * rsqrt(mean o^2 + eps) * w * silu(z)
-      const float ms = (sred[0] + sred[1] + sred[2] + sred[3]) / (float)DV;
-      const float inv = 1.0f / sqrtf(ms + eps);
-      store_split(X2, xplane, (size_t)row * vd + head * DV + tid, s_o[tid] * inv * norm_w[tid] * siluf_(z));
-    }
-  }
+  mixer_rows(s, sh, act, y, ldy, sg, head, neg_a, dt_bias, norm_w, conv_dim, key_dim, vd, hv, ratio, eps, X2, xplane);
 #pragma unroll
   for (int r = 0; r < 16; r++) *reinterpret_cast<float4*>(Sh + (size_t)(warp + 8 * r) * DV) = s[r];
+}
+
+// The same units as a persistent kernel (decode): each CTA walks units u = blockIdx.x, blockIdx.x + gridDim.x, ...
+// of (segment, value head). A head's 64 KB state is one contiguous block, so it arrives by one bulk copy into
+// shared memory, in the register layout's row order (thread (warp, lane) reads rows warp + 8 r, columns 4 lane ..
+// 4 lane + 3: 512 consecutive bytes per warp, no bank conflicts). The next unit's copy is issued as soon as every
+// thread has moved the current state into registers, so its HBM read overlaps this unit's recurrence, norm and
+// state store. Same arithmetic per unit as gdn_mixer_kernel. The copy's wait is bounded: a give-up ends the CTA's
+// walk (after one more bounded wait for the copy in flight) and counts in the device counter.
+constexpr int kMixStateBytes = 128 * 128 * 4;
+__global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_persist_kernel(
+    const float* __restrict__ act, YView y, int ldy,
+    const SegInfo* __restrict__ segs, int nseg, float* __restrict__ rec_state, size_t rs_slot,
+    const float* __restrict__ neg_a, const float* __restrict__ dt_bias, const float* __restrict__ norm_w, int conv_dim,
+    int key_dim, int vd, int hv, int ratio, float eps, __nv_bfloat16* __restrict__ X2, size_t xplane,
+    unsigned int* timeouts) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int DK = 128, DV = 128;
+  extern __shared__ __align__(128) float4 mix_state[];  // [128 rows][32 float4]
+  __shared__ MixShared sh;
+  __shared__ __align__(8) uint64_t bar;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int units = nseg * hv;
+  if (tid == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  auto state_of = [&](int u) {
+    return rec_state + (size_t)segs[u / hv].slot * rs_slot + (size_t)(u % hv) * DK * DV;
+  };
+  auto issue = [&](int u) {
+    if (tid == 0) {
+      tc::fence_proxy_async();
+      tc::mbar_arrive_expect_tx(&bar, kMixStateBytes);
+      tc::bulk_load(mix_state, state_of(u), kMixStateBytes, &bar);
+    }
+  };
+  uint32_t phase = 0;
+  bool pending = false;
+  int u = blockIdx.x;
+  if (u < units) {
+    issue(u);
+    pending = true;
+  }
+  for (; u < units; u += gridDim.x) {
+    const bool got = tc::mbar_wait(&bar, phase);
+    float4 s[16];
+#pragma unroll
+    for (int r = 0; r < 16; r++) s[r] = mix_state[(warp + 8 * r) * 32 + lane];
+    if (!__syncthreads_and(got)) break;  // every thread has also read the state out of shared memory
+    phase ^= 1;
+    pending = false;
+    if (u + (int)gridDim.x < units) {
+      issue(u + gridDim.x);
+      pending = true;
+    }
+    const SegInfo sg = segs[u / hv];
+    if (sg.count > 0) {
+      const int head = u % hv;
+      mixer_rows(s, sh, act, y, ldy, sg, head, neg_a, dt_bias, norm_w, conv_dim, key_dim, vd, hv, ratio, eps, X2,
+                 xplane);
+      float* Sh = state_of(u) + lane * 4;
+#pragma unroll
+      for (int r = 0; r < 16; r++) *reinterpret_cast<float4*>(Sh + (size_t)(warp + 8 * r) * DV) = s[r];
+    }
+  }
+  if (pending && tid == 0) {  // the walk ended on a give-up: wait once more for that copy, count the give-up
+    tc::mbar_wait(&bar, phase);
+    atomicAdd(timeouts, 1u);
+  }
 }
 
 // Prefill form of the mixer (segments of many rows): one CTA per (segment, value head), the head's state in registers
@@ -924,6 +1013,24 @@ evie_status k_gdn_mixer(const float* act, YView y, int ldy, int R, const SegInfo
                                                               norm_w, s.conv_dim, s.key_dim, s.vd, s.hv, s.hv / s.hk,
                                                               s.eps, X2, (size_t)R * s.vd));
     EVIE_CHECK_LAUNCH("gdn_mixer_seq_kernel");
+    return EVIE_OK;
+  }
+  // decode: the persistent kernel (state of the next unit prefetched), unless EVIE_MIXER_PER_HEAD=1 keeps one CTA
+  // per (segment, head)
+  static const bool per_head = [] {
+    const char* e = getenv("EVIE_MIXER_PER_HEAD");
+    return e && e[0] == '1';
+  }();
+  if (!per_head) {
+    unsigned int* counter = device_timeout_counter();
+    if (!counter) return fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
+    const int units = nseg * s.hv;
+    const int ctas = std::min(units, 2 * sm_count());
+    EVIE_TRY(max_dynamic_smem((const void*)gdn_mixer_persist_kernel, kMixStateBytes));
+    EVIE_CUDA_TRY(launch_k(gdn_mixer_persist_kernel, dim3(ctas), dim3(kMixThreads), kMixStateBytes, st, act, y, ldy,
+                           segs, nseg, rec_state, rs_slot, neg_a, dt_bias, norm_w, s.conv_dim, s.key_dim, s.vd, s.hv,
+                           s.hv / s.hk, s.eps, X2, (size_t)R * s.vd, counter));
+    EVIE_CHECK_LAUNCH("gdn_mixer_persist_kernel");
     return EVIE_OK;
   }
   EVIE_CUDA_TRY(launch_k(gdn_mixer_kernel, dim3(grid), dim3(kMixThreads), 0, st, act, y, ldy, segs, rec_state, rs_slot, neg_a,

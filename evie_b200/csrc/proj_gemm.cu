@@ -378,20 +378,6 @@ evie_status operand_map(CUtensorMap* m, const void* X2, int R, int K, int br) {
   return EVIE_OK;
 }
 
-int sm_count() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  static std::mutex mu;
-  static std::map<int, int> cache;
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = cache.find(dev);
-  if (it != cache.end()) return it->second;
-  int n = 148;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
-  cache[dev] = n;
-  return n;
-}
-
 template <int BM, int BR>
 evie_status launch_tiles(const __nv_bfloat16* W, const __nv_bfloat16* X2, float* y, const ProjGemmPlan& p, int M,
                          int K, int R, bool pdl, cudaStream_t st) {
