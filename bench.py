@@ -412,7 +412,7 @@ class GdnPrefill(Workload):
 
 class GqaDecode(Workload):
     name = "gqa_decode"
-    kernel = "gqa_decode_kernel"
+    kernel = "gqa_decode_tma_kernel"
 
     def __init__(self, B=64, Hq=16, Hkv=4, hd=256, page=256):
         import torch
