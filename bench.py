@@ -1014,9 +1014,14 @@ def run_ours(args):
     if world > 1:
         import datetime
 
-        # NCCL's communicator lines (rank count, transport) go to standard error with the rest of the log
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        # NCCL's communicator lines (rank count, transport) go to standard error with the rest of the log. A level
+        # below INFO inherited from the environment (e.g. VERSION) would hide them, so it is raised; INFO or TRACE
+        # set by the caller is kept. Standard output carries only the JSON line.
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     dev = torch.device("cuda", local)
