@@ -333,6 +333,102 @@ __global__ void __launch_bounds__(128) conv_rows_kernel(YView y, int ldy, const 
   }
 }
 
+// The rows form with the decode conv's layout: one warp per (128-channel head block, segment, 64 consecutive rows),
+// four consecutive channels per lane, so the q/k head norm of a row reduces with shuffles alone (the tree of
+// conv_decode4_kernel, which adds the squares in block_sum<128>'s order) and no CTA barrier stands between rows.
+// Each lane keeps its channels' last three inputs in registers and loads the next rows' inputs ahead (kAhead rows
+// in flight). Same products, order of operations and outputs as conv_rows_kernel, bit for bit.
+constexpr int kConvAhead = 4;
+__global__ void __launch_bounds__(128) conv_rows4_kernel(YView y, int ldy, const SegInfo* __restrict__ segs,
+                                                         const float* __restrict__ conv_state, size_t cs_slot,
+                                                         const float* __restrict__ conv_w, int conv_dim, int hk,
+                                                         float qscale, float* __restrict__ act, bool split_qk) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int K = 4;
+  const int lane = threadIdx.x & 31;
+  const int blk = blockIdx.x * 4 + (threadIdx.x >> 5);  // 128-channel block of this warp
+  if (blk * 128 >= conv_dim) return;                    // the whole warp leaves together
+  const SegInfo sg = segs[blockIdx.y];
+  const int t0 = blockIdx.z * kConvRows;
+  if (t0 >= sg.count) return;
+  const int nt = min(kConvRows, sg.count - t0);
+  const int c = blk * 128 + lane * 4;
+  const float* cs = conv_state + (size_t)sg.slot * cs_slot;
+  float4 w4[K];  // taps of channels c .. c + 3: w4[e] = conv_w[(c + e) * K + 0 .. 3]
+#pragma unroll
+  for (int e = 0; e < 4; e++) w4[e] = *reinterpret_cast<const float4*>(conv_w + (size_t)(c + e) * K);
+  float4 win[K];  // [state ; rows] inputs, oldest first; win[K - 1] is the current row's
+#pragma unroll
+  for (int j = 0; j < K - 1; j++) {
+    const int tt = t0 - (K - 1) + j;
+    win[j] = tt >= 0 ? y.at4((size_t)(sg.start + tt) * ldy + c)
+                     : *reinterpret_cast<const float4*>(cs + (size_t)(K - 1 + tt) * conv_dim + c);
+  }
+  const bool head_norm = blk < 2 * hk;
+  const float scl0 = blk < hk ? qscale : 1.0f;
+  float4 ahead[kConvAhead];  // inputs of rows t .. t + kConvAhead - 1
+#pragma unroll
+  for (int i = 0; i < kConvAhead; i++)
+    ahead[i] = i < nt ? y.at4((size_t)(sg.start + t0 + i) * ldy + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int t = 0; t < nt; t++) {
+    const size_t row = (size_t)sg.start + t0 + t;
+    win[K - 1] = ahead[0];
+#pragma unroll
+    for (int i = 0; i + 1 < kConvAhead; i++) ahead[i] = ahead[i + 1];
+    const int tn = t + kConvAhead;
+    ahead[kConvAhead - 1] = tn < nt ? y.at4((row + kConvAhead) * ldy + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < K; j++) {
+      const float u[4] = {win[j].x, win[j].y, win[j].z, win[j].w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float w = j == 0 ? w4[e].x : j == 1 ? w4[e].y : j == 2 ? w4[e].z : w4[e].w;
+        acc[e] += w * u[e];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < K - 1; j++) win[j] = win[j + 1];
+    float out[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) out[e] = siluf_(acc[e]);
+    if (head_norm) {  // q or k head: L2 normalise (kernels.rs dot + 1e-6), q also by 1/sqrt(dk)
+      float sq[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        sq[e] = out[e] * out[e];
+        sq[e] += __shfl_xor_sync(0xffffffffu, sq[e], 4);
+        sq[e] += __shfl_xor_sync(0xffffffffu, sq[e], 2);
+        sq[e] += __shfl_xor_sync(0xffffffffu, sq[e], 1);
+      }
+      const float grp = (sq[0] + sq[2]) + (sq[1] + sq[3]);  // one 32-channel group, in every lane of its 8
+      const float g0 = __shfl_sync(0xffffffffu, grp, 0), g1 = __shfl_sync(0xffffffffu, grp, 8);
+      const float g2 = __shfl_sync(0xffffffffu, grp, 16), g3 = __shfl_sync(0xffffffffu, grp, 24);
+      const float ss = ((g0 + g1) + g2) + g3;
+      const float scl = (1.0f / sqrtf(ss + 1e-6f)) * scl0;
+#pragma unroll
+      for (int e = 0; e < 4; e++) out[e] *= scl;
+    }
+    if (split_qk && head_norm) {  // hi and lo bf16 planes in the bytes of the row's q/k columns
+      __nv_bfloat16* qk = reinterpret_cast<__nv_bfloat16*>(act + row * conv_dim);
+      const __nv_bfloat162 h0 = __floats2bfloat162_rn(out[0], out[1]), h1 = __floats2bfloat162_rn(out[2], out[3]);
+      const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+      const __nv_bfloat162 l0 = __floats2bfloat162_rn(out[0] - f0.x, out[1] - f0.y);
+      const __nv_bfloat162 l1 = __floats2bfloat162_rn(out[2] - f1.x, out[3] - f1.y);
+      uint2 hi, lo;
+      hi.x = *reinterpret_cast<const uint32_t*>(&h0);
+      hi.y = *reinterpret_cast<const uint32_t*>(&h1);
+      lo.x = *reinterpret_cast<const uint32_t*>(&l0);
+      lo.y = *reinterpret_cast<const uint32_t*>(&l1);
+      *reinterpret_cast<uint2*>(qk + c) = hi;
+      *reinterpret_cast<uint2*>(qk + (size_t)256 * hk + c) = lo;  // 2 key_dim = 256 hk channels
+    } else {
+      *reinterpret_cast<float4*>(act + row * conv_dim + c) = make_float4(out[0], out[1], out[2], out[3]);
+    }
+  }
+}
+
 // model.rs:339: the conv window keeps the last K-1 raw inputs of [state ; rows].
 __global__ void conv_state_update_kernel(YView y, int ldy,
                                          const SegInfo* __restrict__ segs, float* __restrict__ conv_state,
@@ -803,6 +899,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
     for (int e = 0; e < 4; e++) atomicMax(maxbuf + (size_t)layer * n + j0 + e, __float_as_uint(fabsf(a[e])));
 }
 
+
 // steering.rs:164-187 for one segment (= one sequence and its slot's plan). Each thread owns rows: the gates whose
 // first detector layer is this one restart at 0, then the layer's detector terms are added in plan order
 // (p += w * a, each step rounded as the reference's f32 arithmetic). Then, per gate deciding here, the score is the
@@ -968,6 +1065,16 @@ evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const
   if (R == 0) return EVIE_OK;
   if (split_qk && !(max_seg_rows > 1 && s.K == 4 && !update_window && s.dk == 128))
     return fail(EVIE_ERR_ARG, "conv: split q/k output needs the 4-tap multi-row form with 128-wide key heads");
+  const auto a16 = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };
+  const bool vec4 = s.K == 4 && s.conv_dim % 128 == 0 && ldy % 4 == 0 && y.plane % 4 == 0 && cs_slot % 4 == 0 &&
+                    a16(y.p) && a16(conv_state) && a16(conv_w) && a16(act);
+  if (max_seg_rows > 1 && vec4 && !update_window) {
+    dim3 grid((s.conv_dim + 511) / 512, nseg, (max_seg_rows + kConvRows - 1) / kConvRows);
+    EVIE_CUDA_TRY(launch_k(conv_rows4_kernel, grid, dim3(128), 0, st, y, ldy, segs, conv_state, cs_slot, conv_w,
+                           s.conv_dim, s.hk, 1.0f / sqrtf((float)s.dk), act, split_qk));
+    EVIE_CHECK_LAUNCH("conv_rows4_kernel");
+    return EVIE_OK;
+  }
   if (max_seg_rows > 1 && s.K == 4 && !update_window) {
     dim3 grid(s.conv_dim / 128, nseg, (max_seg_rows + kConvRows - 1) / kConvRows);
     EVIE_CUDA_TRY(launch_k(conv_rows_kernel<4>, dim3(grid), dim3(128), 0, st, y, ldy, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
@@ -975,9 +1082,7 @@ evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const
     EVIE_CHECK_LAUNCH("conv_rows_kernel");
     return EVIE_OK;
   }
-  const auto a16 = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };
-  if (update_window && s.K == 4 && s.conv_dim % 128 == 0 && ldy % 4 == 0 && y.plane % 4 == 0 && cs_slot % 4 == 0 &&
-      a16(y.p) && a16(conv_state) && a16(conv_w) && a16(act)) {
+  if (update_window && vec4) {
     dim3 grid((s.conv_dim + 511) / 512, R);
     EVIE_CUDA_TRY(launch_k(conv_decode4_kernel, dim3(grid), dim3(128), 0, st, y, ldy, rows, segs, conv_state, cs_slot, conv_w, s.conv_dim, s.hk,
                                               1.0f / sqrtf((float)s.dk), act));

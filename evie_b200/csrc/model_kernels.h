@@ -88,7 +88,8 @@ evie_status k_add_final(float* x, YView y, int ldy, int R, const RowInfo* rows, 
 // update_window: every segment has exactly one row (decode); the kernel then also shifts the conv windows in place
 // (replacing k_conv_state_update). For a 4-tap conv with 16-byte aligned operands that is a warp per 128-channel
 // head block with four channels per lane; otherwise one thread per channel. With max_seg_rows > 1 (and a 4-tap
-// conv) a sliding-window kernel walks each segment's rows in blocks of 64; split_qk (that form only) writes the q
+// conv) a sliding-window kernel walks each segment's rows in blocks of 64 (a warp per head block with four channels
+// per lane when the operands are 16-byte aligned, else a thread per channel); split_qk (that form only) writes the q
 // and k channels as split bf16 planes in place of their f32 values, the chunked prefill's operand format.
 evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const SegInfo* segs,
                              float* conv_state, size_t cs_slot, const float* conv_w, const ModelShape& s,
