@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(128) conv_rows_kernel(YView y, int ldy, const 
 // The rows form with the decode conv's layout: one warp per (128-channel head block, segment, 64 consecutive rows),
 // four consecutive channels per lane, so the q/k head norm of a row reduces with shuffles alone (the tree of
 // conv_decode4_kernel, which adds the squares in block_sum<128>'s order) and no CTA barrier stands between rows.
-// Each lane keeps its channels' last three inputs in registers and loads the next rows' inputs ahead (kAhead rows
+// Each lane keeps its channels' last three inputs in registers and loads the next rows' inputs ahead (kConvAhead rows
 // in flight). Same products, order of operations and outputs as conv_rows_kernel, bit for bit.
 constexpr int kConvAhead = 4;
 __global__ void __launch_bounds__(128) conv_rows4_kernel(YView y, int ldy, const SegInfo* __restrict__ segs,
@@ -554,14 +554,20 @@ __global__ void __launch_bounds__(kMixThreads) gdn_mixer_kernel(
   for (int r = 0; r < 16; r++) *reinterpret_cast<float4*>(Sh + (size_t)(warp + 8 * r) * DV) = s[r];
 }
 
-// The same units as a persistent kernel (decode): each CTA walks units u = blockIdx.x, blockIdx.x + gridDim.x, ...
-// of (segment, value head). A head's 64 KB state is one contiguous block, so it arrives by one bulk copy into
-// shared memory, in the register layout's row order (thread (warp, lane) reads rows warp + 8 r, columns 4 lane ..
-// 4 lane + 3: 512 consecutive bytes per warp, no bank conflicts). The next unit's copy is issued as soon as every
-// thread has moved the current state into registers, so its HBM read overlaps this unit's recurrence, norm and
-// state store. Same arithmetic per unit as gdn_mixer_kernel. The copy's wait is bounded: a give-up ends the CTA's
-// walk (after one more bounded wait for the copy in flight) and counts in the device counter.
+// The same units as a persistent kernel (decode, one row per segment): each CTA walks units u = blockIdx.x,
+// blockIdx.x + gridDim.x, ... of (segment, value head). A head's 64 KB state is one contiguous block, so it arrives
+// by one bulk copy into shared memory, in the register layout's row order (thread (warp, lane) reads rows
+// warp + 8 r, columns 4 lane .. 4 lane + 3: 512 consecutive bytes per warp, no bank conflicts). The unit's inputs
+// come with it on the same mbarrier phase, into one of two staging buffers: the q, k and v rows (512 bytes each,
+// from the conv's output row), the output gate z of every K-slice plane of the input projection (512 bytes each),
+// and, per plane, the 16-byte chunks that hold the head's b and a logits. The next unit's copies are issued as soon
+// as every thread has moved the current state into registers, so its HBM and L2 reads overlap this unit's
+// recurrence, norm and state store. Every thread sums the planes of b and a and forms decay and beta itself (same
+// operations in every thread), so the unit starts without a barrier on them. Same arithmetic per unit as
+// gdn_mixer_kernel (planes added in plane order, as YView::at adds them). The copies' wait is bounded: a give-up
+// ends the CTA's walk (after one more bounded wait for the copies in flight) and counts in the device counter.
 constexpr int kMixStateBytes = 128 * 128 * 4;
+__host__ __device__ constexpr int mix_stage_floats(int planes) { return 3 * 128 + planes * 128 + planes * 8; }
 __global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_persist_kernel(
     const float* __restrict__ act, YView y, int ldy,
     const SegInfo* __restrict__ segs, int nseg, float* __restrict__ rec_state, size_t rs_slot,
@@ -571,8 +577,13 @@ __global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_persist_kernel(
   pdl_trigger();
   pdl_wait();
   constexpr int DK = 128, DV = 128;
-  extern __shared__ __align__(128) float4 mix_state[];  // [128 rows][32 float4]
-  __shared__ MixShared sh;
+  extern __shared__ __align__(128) float4 mix_state[];  // [128 rows][32 float4], then two staging buffers
+  float* stage0 = reinterpret_cast<float*>(mix_state + kMixStateBytes / 16);
+  const int np = y.n;
+  const int stage_floats = mix_stage_floats(np);
+  __shared__ float4 red[8][32];
+  __shared__ float sred[4];
+  __shared__ float s_o[DV];
   __shared__ __align__(8) uint64_t bar;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int units = nseg * hv;
@@ -584,21 +595,35 @@ __global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_persist_kernel(
   auto state_of = [&](int u) {
     return rec_state + (size_t)segs[u / hv].slot * rs_slot + (size_t)(u % hv) * DK * DV;
   };
-  auto issue = [&](int u) {
+  auto issue = [&](int u, int buf) {
     if (tid == 0) {
+      const int head = u % hv, kh = head / ratio;
+      const size_t row = (size_t)segs[u / hv].start;
+      float* st = stage0 + buf * stage_floats;
+      const float* ar = act + row * conv_dim;
+      const size_t ib = row * ldy + conv_dim + vd + head, ia = ib + hv, iz = row * ldy + conv_dim + (size_t)head * DV;
       tc::fence_proxy_async();
-      tc::mbar_arrive_expect_tx(&bar, kMixStateBytes);
+      tc::mbar_arrive_expect_tx(&bar, kMixStateBytes + (3 + np) * 512 + np * 32);
       tc::bulk_load(mix_state, state_of(u), kMixStateBytes, &bar);
+      tc::bulk_load(st, ar + kh * DK, 512, &bar);                          // q
+      tc::bulk_load(st + 128, ar + key_dim + kh * DK, 512, &bar);          // k
+      tc::bulk_load(st + 256, ar + 2 * key_dim + head * DV, 512, &bar);    // v
+      for (int p = 0; p < np; p++) {
+        const float* yp = y.p + (size_t)p * y.plane;
+        tc::bulk_load(st + 384 + p * 128, yp + iz, 512, &bar);                           // z
+        tc::bulk_load(st + 384 + np * 128 + p * 4, yp + (ib & ~(size_t)3), 16, &bar);     // b's chunk
+        tc::bulk_load(st + 384 + np * 132 + p * 4, yp + (ia & ~(size_t)3), 16, &bar);     // a's chunk
+      }
     }
   };
   uint32_t phase = 0;
   bool pending = false;
-  int u = blockIdx.x;
+  int u = blockIdx.x, k = 0;
   if (u < units) {
-    issue(u);
+    issue(u, 0);
     pending = true;
   }
-  for (; u < units; u += gridDim.x) {
+  for (; u < units; u += gridDim.x, k++) {
     const bool got = tc::mbar_wait(&bar, phase);
     float4 s[16];
 #pragma unroll
@@ -607,20 +632,79 @@ __global__ void __launch_bounds__(kMixThreads, 2) gdn_mixer_persist_kernel(
     phase ^= 1;
     pending = false;
     if (u + (int)gridDim.x < units) {
-      issue(u + gridDim.x);
+      issue(u + gridDim.x, (k + 1) & 1);
       pending = true;
     }
-    const SegInfo sg = segs[u / hv];
-    if (sg.count > 0) {
-      const int head = u % hv;
-      mixer_rows(s, sh, act, y, ldy, sg, head, neg_a, dt_bias, norm_w, conv_dim, key_dim, vd, hv, ratio, eps, X2,
-                 xplane);
-      float* Sh = state_of(u) + lane * 4;
+    const float* st = stage0 + (k & 1) * stage_floats;
+    const float* sq = st;
+    const float* sk = st + 128;
+    const int head = u % hv;
+    const size_t row = (size_t)segs[u / hv].start;
+    // model.rs:374-375 from the planes of b and a, added in plane order
+    const size_t ib = row * ldy + conv_dim + vd + head, ia = ib + hv;
+    float bb = st[384 + np * 128 + (ib & 3)], aa = st[384 + np * 132 + (ia & 3)];
+    for (int p = 1; p < np; p++) {
+      bb += st[384 + np * 128 + p * 4 + (ib & 3)];
+      aa += st[384 + np * 132 + p * 4 + (ia & 3)];
+    }
+    const float decay = expf(neg_a[head] * softplus_(aa + dt_bias[head]));
+    const float beta = sigmoidf_(bb);
+    float z = 0.f;
+    if (tid < DV) {
+      z = st[384 + tid];
+      for (int p = 1; p < np; p++) z += st[384 + p * 128 + tid];
+    }
+    const float4 v4 = *reinterpret_cast<const float4*>(st + 256 + lane * 4);
+    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int r = 0; r < 16; r++) *reinterpret_cast<float4*>(Sh + (size_t)(warp + 8 * r) * DV) = s[r];
+    for (int r = 0; r < 16; r++) {
+      const float kr = sk[warp + 8 * r];
+      kv.x += s[r].x * kr; kv.y += s[r].y * kr; kv.z += s[r].z * kr; kv.w += s[r].w * kr;
+    }
+    red[warp][lane] = kv;
+    __syncthreads();
+    kv = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; w++) {
+      const float4 t = red[w][lane];
+      kv.x += t.x; kv.y += t.y; kv.z += t.z; kv.w += t.w;
+    }
+    const float d0 = (v4.x - decay * kv.x) * beta, d1 = (v4.y - decay * kv.y) * beta;
+    const float d2 = (v4.z - decay * kv.z) * beta, d3 = (v4.w - decay * kv.w) * beta;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+      const int i = warp + 8 * r;
+      const float kr = sk[i], qr = sq[i];
+      s[r].x = s[r].x * decay + kr * d0; s[r].y = s[r].y * decay + kr * d1;
+      s[r].z = s[r].z * decay + kr * d2; s[r].w = s[r].w * decay + kr * d3;
+      o.x += s[r].x * qr; o.y += s[r].y * qr; o.z += s[r].z * qr; o.w += s[r].w * qr;
+    }
+    float* Sh = state_of(u) + lane * 4;
+#pragma unroll
+    for (int r = 0; r < 16; r++) *reinterpret_cast<float4*>(Sh + (size_t)(warp + 8 * r) * DV) = s[r];
+    __syncthreads();  // everyone has read red (kv) before it is reused
+    red[warp][lane] = o;
+    __syncthreads();
+    if (tid < DV) {  // thread j finishes output column j
+      const float* rf = reinterpret_cast<const float*>(&red[0][0]);
+      float oj = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; w++) oj += rf[w * DV + tid];
+      s_o[tid] = oj;
+      float ss = oj * oj;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) sred[warp] = ss;
+    }
+    __syncthreads();
+    if (tid < DV) {  // gated RMSNorm, model.rs:377-383: o * rsqrt(mean o^2 + eps) * w * silu(z)
+      const float ms = (sred[0] + sred[1] + sred[2] + sred[3]) / (float)DV;
+      const float inv = 1.0f / sqrtf(ms + eps);
+      store_split(X2, xplane, row * vd + head * DV + tid, s_o[tid] * inv * norm_w[tid] * siluf_(z));
     }
   }
-  if (pending && tid == 0) {  // the walk ended on a give-up: wait once more for that copy, count the give-up
+  if (pending && tid == 0) {  // the walk ended on a give-up: wait once more for those copies, count the give-up
     tc::mbar_wait(&bar, phase);
     atomicAdd(timeouts, 1u);
   }
@@ -1126,13 +1210,17 @@ evie_status k_gdn_mixer(const float* act, YView y, int ldy, int R, const SegInfo
     const char* e = getenv("EVIE_MIXER_PER_HEAD");
     return e && e[0] == '1';
   }();
-  if (!per_head) {
+  // the staged inputs are bulk copies: 16-byte aligned rows and planes
+  const bool staged = ldy % 4 == 0 && y.plane % 4 == 0 && s.conv_dim % 4 == 0 && ((uintptr_t)y.p & 15u) == 0 &&
+                      ((uintptr_t)act & 15u) == 0 && y.n >= 1 && y.n <= YView::kMaxPlanes;
+  if (!per_head && staged) {
     unsigned int* counter = device_timeout_counter();
     if (!counter) return fail(EVIE_ERR_CUDA, "device timeout counter unavailable");
     const int units = nseg * s.hv;
     const int ctas = std::min(units, 2 * sm_count());
-    EVIE_TRY(max_dynamic_smem((const void*)gdn_mixer_persist_kernel, kMixStateBytes));
-    EVIE_CUDA_TRY(launch_k(gdn_mixer_persist_kernel, dim3(ctas), dim3(kMixThreads), kMixStateBytes, st, act, y, ldy,
+    const int smem = kMixStateBytes + 2 * mix_stage_floats(y.n) * 4;
+    EVIE_TRY(max_dynamic_smem((const void*)gdn_mixer_persist_kernel, smem));
+    EVIE_CUDA_TRY(launch_k(gdn_mixer_persist_kernel, dim3(ctas), dim3(kMixThreads), smem, st, act, y, ldy,
                            segs, nseg, rec_state, rs_slot, neg_a, dt_bias, norm_w, s.conv_dim, s.key_dim, s.vd, s.hv,
                            s.hv / s.hk, s.eps, X2, (size_t)R * s.vd, counter));
     EVIE_CHECK_LAUNCH("gdn_mixer_persist_kernel");
