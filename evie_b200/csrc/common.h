@@ -67,8 +67,8 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // Launch mode of the forward pass's per-row kernels: ordinary launches unless EVIE_PDL_ALL=1 asks for programmatic
 // dependent launch on every kernel. Measured on one B200 box, in alternating runs: 6.14 ms per 4B decode step with
 // every kernel launched that way against 6.00-6.02 ms with it on the projection GEMMs only (the default; EVIE_NO_PDL=1
-// turns those off too), and 5.51 against 5.26 ms with the later attention and mixer kernels. Kernels that start early and wait hold the SM resources the GEMM's CTAs need to become
-// resident and stream their first weight tiles.
+// turns those off too), and 5.51 against 5.26 ms with the later attention and mixer kernels. Kernels that start
+// early and wait hold the SM resources the GEMM's CTAs need to become resident and stream their first weight tiles.
 bool pdl_enabled();
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
