@@ -35,7 +35,8 @@ def test_projection_groups_cover_every_projection_weight_once():
 def test_traffic_lookup():
     assert bench.profiled_traffic("gdn_chunk_prefill_kernel") == 1019800576  # a captured launch
     # the model's decode attention: the captured traffic-to-algorithmic ratio of the same kernel
-    assert bench.profiled_traffic("gqa_attention", 1.0e9) == pytest.approx(1.014e9)
+    assert bench.profiled_traffic("gqa_attention", 1.0e9) == pytest.approx(1.0083e9)
+    assert bench.profiled_traffic("gqa_decode_tma_kernel") == 4710427332  # the B=16 capture scaled to B=64
     assert bench.profiled_traffic("gqa_attention") is None
     assert bench.profiled_traffic("no_such_kernel") is None
 
