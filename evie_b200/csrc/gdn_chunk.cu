@@ -116,21 +116,18 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
   return (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
 }
 
-// bf16 rounding of f32 bits by integer arithmetic: adding half a bf16 unit to the magnitude bits rounds half away
-// from zero; the high 16 bits are then the bf16 value.
-__device__ __forceinline__ uint32_t round_bf16_bits(float x) { return __float_as_uint(x) + 0x8000u; }
 
-// 2n floats -> n words of bf16 hi = round(x) and n words of lo = round(x - hi), pairs packed low-half-first
-// (x - hi is exact: hi is within half a bf16 unit of x).
+// 2n floats -> n words of bf16 hi = round(x) and n words of lo = round(x - hi) (round to nearest even, two values
+// per conversion), pairs packed low-half-first (x - hi is exact: hi is within half a bf16 unit of x).
 template <int N>
 __device__ __forceinline__ void split_pairs(const float* x, uint32_t* hi, uint32_t* lo) {
 #pragma unroll
   for (int i = 0; i < N; i++) {
-    const uint32_t ua = round_bf16_bits(x[2 * i]), ub = round_bf16_bits(x[2 * i + 1]);
-    const float ra = x[2 * i] - __uint_as_float(ua & 0xFFFF0000u);
-    const float rb = x[2 * i + 1] - __uint_as_float(ub & 0xFFFF0000u);
-    hi[i] = __byte_perm(ua, ub, 0x7632);
-    lo[i] = __byte_perm(round_bf16_bits(ra), round_bf16_bits(rb), 0x7632);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y);
+    hi[i] = *reinterpret_cast<const uint32_t*>(&h);
+    lo[i] = *reinterpret_cast<const uint32_t*>(&l);
   }
 }
 
