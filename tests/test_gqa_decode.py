@@ -45,6 +45,14 @@ def test_gqa_decode_garbage_past_context(ctx, cuda):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("page", [64, 128])
+def test_gqa_decode_group4_small_pages(page, cuda):
+    """Pages no larger than a warp's 128 tokens (the op accepts multiples of 64): a warp's tiles cross pages, and
+    each 16-token tile finds its own page (the tensor-core kernels)."""
+    _check(3, 16, 4, [100, 700, 1300], 14, cuda, page=page, nan_tail=True)
+
+
+@pytest.mark.gpu
 def test_gqa_decode_group2_and_small_pages(cuda):
     _check(3, 8, 4, [100, 700, 1300], 12, cuda, page=64)
 
