@@ -6,6 +6,7 @@
 #include <tuple>
 
 #include "common.h"
+#include "tmap.h"
 
 namespace evie {
 evie_status func_attr(const void* fn, cudaFuncAttribute attr, int value) {
@@ -21,6 +22,18 @@ evie_status func_attr(const void* fn, cudaFuncAttribute attr, int value) {
 }
 evie_status max_dynamic_smem(const void* fn, int bytes) {
   return func_attr(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
 }
 int sm_count() {
   int dev = 0;

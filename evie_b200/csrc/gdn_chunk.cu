@@ -68,6 +68,7 @@
 #include "gdn_chunk.h"
 #include "model_kernels.h"
 #include "tc.h"
+#include "tmap.h"
 
 namespace evie {
 
@@ -712,22 +713,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tc::tmem_dealloc(tmem, 512);
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_tiled() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
 
 // [B][T][H][128] bf16 viewed as a 4-D tensor (d, head, token, sequence); box = (box_d, 1, 64, 1).
 evie_status token_major_map(CUtensorMap* m, const void* base, int B, int T, int H, uint32_t box_d,

@@ -26,6 +26,7 @@
 #include "model_kernels.h"
 #include "mma_sync.h"
 #include "tc.h"
+#include "tmap.h"
 
 namespace evie {
 
@@ -1300,28 +1301,12 @@ __global__ void __launch_bounds__(WARPS * 32, 8 / WARPS)
   if (tid == 0) scr.tickets[bh] = 0;
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
 
 // The paged cache [pages][Hkv][page_size][256] bf16 as a 2-D tensor (dim, page row), box 64 dims x 16 rows, 128-byte
 // swizzle. The row extent is not known to the isolated op, so the map spans the largest row count a TMA coordinate
 // can address; the page table bounds the rows read, as it bounds the other kernels' loads.
 evie_status kv_tile_map(CUtensorMap* m, const void* base) {
-  EncodeTiledFn enc = encode_fn();
+  EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(EVIE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {(cuuint64_t)kHD, (cuuint64_t)INT32_MAX};
   const cuuint64_t strides[1] = {(cuuint64_t)kHD * 2};

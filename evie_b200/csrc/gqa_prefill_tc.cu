@@ -39,6 +39,7 @@
 #include "gqa_decode.h"
 #include "model_kernels.h"
 #include "tc.h"
+#include "tmap.h"
 
 namespace evie {
 
@@ -398,27 +399,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tc::tmem_dealloc(tmem, 512);
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
 
 // The paged cache [pages][Hkv][page_size][256] bf16 as a 2-D tensor (dim, page row); box (64 dims, 64 rows),
 // 128-byte swizzle: one box is one dim block of a 64-token tile.
 evie_status cache_map(CUtensorMap* m, const void* base, long rows) {
-  EncodeTiledFn enc = encode_fn();
+  EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(EVIE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {(cuuint64_t)kHD, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)kHD * 2};

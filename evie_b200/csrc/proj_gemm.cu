@@ -48,6 +48,7 @@
 #include "gdn_chunk.h"
 #include "proj_gemm.h"
 #include "tc.h"
+#include "tmap.h"
 
 namespace evie {
 
@@ -331,26 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tc::tmem_dealloc(tmem, C::kTmemCols);
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
 
 // W [M][K] bf16 as a 2-D tensor (k, m); box (64, bm), 128-byte swizzle, zero fill past M and K.
 evie_status weight_map(CUtensorMap* m, const void* W, int M, int K, int bm) {
-  EncodeTiledFn enc = encode_fn();
+  EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(EVIE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
@@ -365,7 +350,7 @@ evie_status weight_map(CUtensorMap* m, const void* W, int M, int K, int bm) {
 
 // X2 [2][R][K] bf16 as a 3-D tensor (k, r, plane); box (64, br, 1), 128-byte swizzle, zero fill past R and K.
 evie_status operand_map(CUtensorMap* m, const void* X2, int R, int K, int br) {
-  EncodeTiledFn enc = encode_fn();
+  EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(EVIE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)R, 2};
   const cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)R * K * 2};
