@@ -9,8 +9,11 @@
 // next to each other in shared memory; for decode-shaped tiles one MMA per K = 16 step and half covers both
 // (N = 2 BR, hi and lo products in separate accumulator columns, added by the epilogue), so the weight sub-tile is
 // read from shared memory once. Shared-memory bandwidth is what limits these MMAs: with separate hi and lo MMAs the
-// tensor core re-reads every weight sub-tile. The 256 x 128 prefill tiles issue D += W . lo^T and then
-// D += W . hi^T into the same columns. Either way the result leaves as one plane.
+// tensor core re-reads every weight sub-tile. Prefill tiles (128 weight rows x 256 activation rows, N = 256) issue
+// D += W . lo^T and then D += W . hi^T into the same columns; against 256 x 128 tiles they move ~8% fewer
+// shared-memory bytes per FLOP (TMA stores of the tiles plus the MMAs' reads: ~172 against ~187 bytes per
+// tensor-core cycle, of ~128 available), and a prefill call's projections take 8% less time. Either way the result
+// leaves as one plane.
 //
 // Accumulation groups. The tensor core rounds each MMA's addition into the f32 accumulator toward zero, so an
 // accumulator carried over all of K drifts by about (MMA steps) x half an ulp of its own magnitude: -1.8e-5
@@ -27,8 +30,8 @@
 //
 // Work units are (K slice, M tile, R tile), K slice fastest. Decode-shaped calls (R <= 128, one R tile) cut K into
 // slices until the units fill the SMs: each slice writes its own plane and the consumer adds the planes in slice
-// order. Larger R runs one slice over a persistent grid, in bands of ~40 MB of weight tiles (M fastest, then R), so
-// that a band's weights stay in L2 while every operand tile passes through it.
+// order. Larger R runs one slice over a persistent grid of 128 x 256 tiles, in bands of ~40 MB of weight tiles (M
+// fastest, then R), so that a band's weights stay in L2 while every operand tile passes through it.
 //
 // Programmatic dependent launch: the weights do not depend on the previous kernel, so the producer issues the weight
 // half of its first ring fill, then waits (griddepcontrol.wait) for the previous grid, then loads the activations.
@@ -78,7 +81,7 @@ struct Cfg {
   static constexpr int kHalves = BM / 128;
   // Stacked: one MMA per K step and half with N = 2 BR over the adjacent hi and lo tiles (hi products in accumulator
   // columns [0, BR), lo products in [BR, 2 BR)), so the weight sub-tile is read from shared memory once for both
-  // planes. Otherwise (256 x 128 tiles, whose stacked accumulator would not leave room for two buffers) two MMAs
+  // planes. Otherwise (prefill tiles, whose stacked accumulator would not leave room for two buffers) two MMAs
   // per K step accumulate lo and then hi into the same columns.
   static constexpr bool kStack = 2 * kHalves * 2 * BR <= 512;
   static constexpr int kPlaneCols = kStack ? BR : 0;      // column offset of the lo products
@@ -379,8 +382,8 @@ evie_status launch_tiles(const __nv_bfloat16* W, const __nv_bfloat16* X2, float*
     return e ? std::max(1, atoi(e)) : 0;
   }();
   // Accumulation group: 4 K steps of 64 for decode tiles (drift -2e-7 relative, within 2% of the fastest setting),
-  // 8 for the 256 x 128 prefill tiles (-9e-7). EVIE_GEMM_GROUP overrides both.
-  const int gchunks = group_env ? group_env : (BR == 128 && R > 128 ? 8 : 4);
+  // 8 for the prefill tiles (-9e-7). EVIE_GEMM_GROUP overrides both.
+  const int gchunks = group_env ? group_env : (R > 128 ? 8 : 4);
   const int n_mt = (M + BM - 1) / BM, n_rt = (R + BR - 1) / BR;
   const int band = std::max(1, std::min(n_mt, (int)((40u << 20) / ((size_t)BM * K * 2))));  // ~40 MB of weights
   GemmArgs a{y, (size_t)R * M, M, R, K, (K + kKC - 1) / kKC, p.ksplit, n_mt, n_rt, band, p.units,
@@ -409,11 +412,16 @@ evie_status launch_tiles(const __nv_bfloat16* W, const __nv_bfloat16* X2, float*
 ProjGemmPlan plan_proj_gemm(int M, int K, int R, int max_planes, size_t y_cap, int num_sms) {
   ProjGemmPlan best;
   const int kc = (K + kKC - 1) / kKC;
-  if (R > 128) {  // prefill-shaped: persistent 256 x 128 tiles, one K slice
-    best.bm = 256;
-    best.br = 128;
+  // EVIE_GEMM_PREFILL_NARROW=1 keeps the earlier 256 x 128 prefill tiles, for comparison
+  static const bool narrow = [] {
+    const char* e = getenv("EVIE_GEMM_PREFILL_NARROW");
+    return e && e[0] == '1';
+  }();
+  if (R > 128) {  // prefill-shaped: persistent 128 x 256 tiles, one K slice
+    best.bm = narrow ? 256 : 128;
+    best.br = narrow ? 128 : 256;
     best.ksplit = 1;
-    best.units = ((M + 255) / 256) * ((R + 127) / 128);
+    best.units = ((M + best.bm - 1) / best.bm) * ((R + best.br - 1) / best.br);
     best.grid = std::min(best.units, num_sms);
     return best;
   }
@@ -463,6 +471,7 @@ evie_status launch_proj_gemm(const __nv_bfloat16* W, int M, int K, const __nv_bf
   }
   evie_status s;
   if (p.bm == 256 && p.br == 128) s = launch_tiles<256, 128>(W, X2, y, p, M, K, R, pdl, st);
+  else if (p.bm == 128 && p.br == 256) s = launch_tiles<128, 256>(W, X2, y, p, M, K, R, pdl, st);
   else if (p.bm == 256 && p.br == 64) s = launch_tiles<256, 64>(W, X2, y, p, M, K, R, pdl, st);
   else if (p.bm == 256 && p.br == 16) s = launch_tiles<256, 16>(W, X2, y, p, M, K, R, pdl, st);
   else if (p.bm == 128 && p.br == 64) s = launch_tiles<128, 64>(W, X2, y, p, M, K, R, pdl, st);

@@ -11,7 +11,7 @@ namespace evie {
 // same f32 tensor-memory accumulator, so the result is one plane per K slice:
 //   y[s][r][m] = sum over k in slice s of W[m][k] (hi[r][k] + lo[r][k]),   s = 0 .. *planes - 1,
 // and the consumer adds the planes in slice order (YView). Decode-shaped calls (R <= 128) cut K into slices so
-// that the weight stream fills every SM; larger R runs one slice over persistent 256 x 128 tiles.
+// that the weight stream fills every SM; larger R runs one slice over persistent 128 x 256 tiles.
 //   y_cap      floats available at y (the planes must fit: planes * R * M <= y_cap)
 //   max_planes upper bound on the K slices (>= 1)
 //   pdl        launch with programmatic stream serialisation: the kernel streams its first weight tiles before it
