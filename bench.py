@@ -13,8 +13,9 @@ The default run also times the three isolated ops (gdn_decode, gdn_prefill, gqa_
 region and reports them under `isolated`.
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the launching stream; L2 is
-flushed (a 256 MiB write) between timed steps whenever a step's working set fits in L2. The K-step region is
-bracketed by a barrier and torch.cuda.synchronize() on both sides; the reported time is the max over ranks.
+flushed (a 256 MiB write, then a 256 MiB read so that no dirty line is left) between timed steps whenever a step's
+working set fits in L2. The K-step region is bracketed by a barrier and torch.cuda.synchronize() on both sides; the
+reported time is the max over ranks.
 `e2e` repeats the step through the C ABI from pinned host buffers with the host<->device copies inside the timed
 region. `cpu_baseline` (rank 0, N=1) times the CPU oracle (a C++ restatement of evie-core's CPU path) on a
 bounded sample of the same workload, on evie's default thread count (half the logical CPUs, at most 8).
@@ -221,11 +222,23 @@ class Workload:
             self.step()
 
     def _flush(self):
+        """The L2 flush between timed steps: a 256 MiB write, then a 256 MiB read of a second buffer, so that the
+        write's dirty lines are written back before the timed region and L2 holds only clean, unrelated lines
+        (without the read, the timed kernel pays for writing back up to 126 MB of the flush's data)."""
         import torch
 
         if self.flush_l2 and not hasattr(self, "_flushbuf"):
             self._flushbuf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-        return getattr(self, "_flushbuf", None)
+            self._flushread = torch.zeros(64 << 20, dtype=torch.float32, device="cuda")
+            self._flushsum = torch.empty((), dtype=torch.float32, device="cuda")
+        buf = getattr(self, "_flushbuf", None)
+        if buf is None:
+            return None
+
+        def flush(i):
+            buf.fill_(i & 0xFF)
+            torch.sum(self._flushread, dim=0, out=self._flushsum)
+        return flush
 
     def timed(self, k):
         import torch
@@ -236,7 +249,7 @@ class Workload:
         launches = 0
         for i in range(k):
             if flush is not None:
-                flush.fill_(i & 0xFF)
+                flush(i)
             ev[i][0].record(stream)
             launches += self.step()
             ev[i][1].record(stream)
@@ -255,7 +268,7 @@ class Workload:
         h2d = d2h = 0
         for i in range(k):
             if flush is not None:
-                flush.fill_(i & 0xFF)
+                flush(i)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             h2d, d2h = self.e2e_step()
@@ -276,7 +289,7 @@ class GdnDecode(Workload):
 
     def config(self):
         return {"workload": f"gdn_decode_step B={self.B} H={self.H} dk=dv={self.d} fp32 state",
-                "global_batch": self.B, "heads": self.H, "l2": "flushed between timed steps"}
+                "global_batch": self.B, "heads": self.H, "l2": "flushed between timed steps (256 MiB write, then 256 MiB read)"}
 
     def algorithmic(self):
         B, H, d = self.B, self.H, self.d
