@@ -843,12 +843,14 @@ class ModelDecode(Workload):
 
     def e2e_step(self):
         """One decode step through evie_forward with host buffers: the step's tokens go up, the greedy tokens and
-        the captured frames and residual rows come back."""
+        the captured frames and residual rows come back. The batch is passed as arrays (GpuModel.forward_batch: one
+        token per sequence in slot order), as a serving loop over tens of sequences would call it."""
         from evie_b200.gpu import GpuOut
 
         if not hasattr(self, "_out"):
             self._out = GpuOut(frames=self.frames_host.numpy(), resid=self.resid_host.numpy())
-        o = self.m.forward(self.seqs(), want_logits=False, capture=True, out=self._out)
+            self._slots = np.arange(self.B, dtype=np.int32)
+        o = self.m.forward_batch(self._slots, self.pos, self.next, want_logits=False, capture=True, out=self._out)
         self.next = o.next_tokens.copy()
         self.pos += 1
         c = self.cfg

@@ -11,6 +11,10 @@ import numpy as np
 from . import EvieError, capi, lib
 
 MODES = {"add": 1, "mul": 2, "set": 3}
+# evie_seq as a numpy record (the layout of capi.Seq), for sequence tables built by array operations
+_SEQ_DTYPE = np.dtype({"names": ["slot", "pos0", "tokens", "n_tokens"], "formats": ["<i4", "<i4", "<u8", "<i4"],
+                       "offsets": [capi.Seq.slot.offset, capi.Seq.pos0.offset, capi.Seq.tokens.offset,
+                                   capi.Seq.n_tokens.offset], "itemsize": C.sizeof(capi.Seq)})
 
 
 @dataclass
@@ -70,6 +74,34 @@ class GpuModel:
             keep.append(t)
             arr[i] = capi.Seq(s.slot, s.pos0, t.ctypes.data if t.size else None, t.size)
             rows += t.size
+        return self._forward_table(C.addressof(arr), n, rows, want_logits, capture, out)
+
+    def forward_batch(self, slots, pos0, tokens, counts=None, want_logits: bool = True, capture: bool = False,
+                      out: GpuOut | None = None) -> GpuOut:
+        """forward() for a batch given as arrays: sequence i runs in slot slots[i] from position pos0[i] on
+        counts[i] tokens (1 each when counts is None), all tokens concatenated in sequence order in `tokens`. The
+        same evie_forward call; the sequence table is built by array operations, not by a loop over GpuSeq
+        objects, which keeps the host's share of a decode step small (one token per sequence, tens of sequences)."""
+        slots = np.asarray(slots, np.int32).ravel()
+        n = slots.size
+        pos0 = np.broadcast_to(np.asarray(pos0, np.int32), (n,))
+        counts = np.ones(n, np.int32) if counts is None else np.asarray(counts, np.int32).ravel()
+        tokens = np.ascontiguousarray(tokens, np.uint32).ravel()
+        if counts.size != n or (counts < 0).any() or int(counts.sum()) != tokens.size:
+            raise ValueError("forward_batch: counts must give one non-negative count per slot, summing to len(tokens)")
+        tab = np.zeros(max(n, 1), _SEQ_DTYPE)
+        first = np.zeros(n, np.uint64)
+        np.cumsum(counts[:-1], out=first[1:])
+        tab["slot"][:n] = slots
+        tab["pos0"][:n] = pos0
+        tab["n_tokens"][:n] = counts
+        tab["tokens"][:n] = np.where(counts > 0, np.uint64(tokens.ctypes.data) + 4 * first, 0)
+        return self._forward_table(tab.ctypes.data, n, tokens.size, want_logits, capture, out)
+
+    def _forward_table(self, table: int, n: int, rows: int, want_logits: bool, capture: bool,
+                       out: GpuOut | None) -> GpuOut:
+        """evie_forward on a table of n evie_seq records at address `table` holding `rows` tokens in all (the
+        caller keeps the table and the token arrays alive across the call)."""
         o = out or GpuOut()
         if want_logits and (o.logits is None or o.logits.shape != (n, self.vocab)):
             o.logits = np.empty((n, self.vocab), np.float32)
@@ -81,7 +113,7 @@ class GpuModel:
         if o.next_tokens.shape != (n,):
             o.next_tokens = np.empty(n, np.uint32)
         p = lambda a: a.ctypes.data if a is not None else None  # noqa: E731
-        self._check(lib().evie_forward(self._h, arr, n, int(want_logits), int(capture),
+        self._check(lib().evie_forward(self._h, table, n, int(want_logits), int(capture),
                                        p(o.logits) if want_logits else None, p(o.frames) if capture else None,
                                        p(o.resid) if capture else None, p(o.next_tokens)))
         return o

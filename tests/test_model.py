@@ -308,3 +308,65 @@ def test_pinned_capture_matches_pageable(tiny_ckpt, cuda):
         m.close()
     for (fa, ra, la), (fb, rb, lb) in zip(*got):
         assert np.array_equal(fa, fb) and np.array_equal(ra, rb) and np.array_equal(la, lb)
+
+
+def test_forward_batch_builds_the_seq_table():
+    """forward_batch's evie_seq records (built by array operations) carry each sequence's slot, start position, token
+    count and a pointer to its first token in the concatenated token array; sequences without tokens get NULL."""
+    import ctypes as C
+
+    from evie_b200 import capi
+    from evie_b200.gpu import GpuModel
+
+    m = object.__new__(GpuModel)
+    seen = {}
+
+    def fake(table, n, rows, want_logits, capture, out):
+        recs = (capi.Seq * n).from_address(table)
+        seen["recs"] = [(r.slot, r.pos0, r.tokens, r.n_tokens) for r in recs]
+        seen["rows"] = rows
+        seen["vals"] = [list((C.c_uint32 * r.n_tokens).from_address(r.tokens)) if r.tokens else [] for r in recs]
+
+    m._forward_table = fake
+    toks = np.array([5, 6, 7, 8, 9], np.uint32)
+    m.forward_batch([3, 1, 2], [10, 20, 30], toks, counts=[2, 0, 3])
+    assert [(s, p, c) for s, p, _, c in seen["recs"]] == [(3, 10, 2), (1, 20, 0), (2, 30, 3)]
+    assert seen["recs"][1][2] is None and seen["rows"] == 5
+    assert seen["vals"] == [[5, 6], [], [7, 8, 9]]
+    m.forward_batch(np.arange(4), 7, np.array([1, 2, 3, 4], np.uint32))  # one token each, one shared position
+    assert [(s, p, c) for s, p, _, c in seen["recs"]] == [(0, 7, 1), (1, 7, 1), (2, 7, 1), (3, 7, 1)]
+    assert seen["vals"] == [[1], [2], [3], [4]]
+    with pytest.raises(ValueError):
+        m.forward_batch([1, 2], 0, np.zeros(3, np.uint32))
+
+
+@pytest.mark.gpu
+def test_forward_batch_matches_forward(tiny_ckpt, cuda):
+    """forward_batch (array-built sequence table) and forward (GpuSeq list) give identical logits, tokens and
+    captures on the same prefill and decode calls."""
+    from evie_b200.gpu import GpuSeq
+
+    rng = np.random.default_rng(33)
+    prompts = [rng.integers(0, 2048, n).astype(np.uint32) for n in (11, 4, 20)]
+    got = []
+    for batch in (False, True):
+        m = _gpu_model(tiny_ckpt, False, max_ctx=128, slots=3, max_rows=64)
+        m.set_ops(1, [(3, 5, "mul", 1.5)])
+        runs = []
+        if batch:
+            o = m.forward_batch([0, 1, 2], 0, np.concatenate(prompts), counts=[len(p) for p in prompts], capture=True)
+        else:
+            o = m.forward([GpuSeq(i, 0, p) for i, p in enumerate(prompts)], capture=True)
+        runs.append((o.logits.copy(), o.next_tokens.copy(), o.frames.copy()))
+        for step in range(3):
+            pos = np.array([len(p) + step for p in prompts], np.int32)
+            cur = o.next_tokens.copy()
+            if batch:
+                o = m.forward_batch([0, 1, 2], pos, cur, capture=True)
+            else:
+                o = m.forward([GpuSeq(i, int(pos[i]), cur[i:i + 1]) for i in range(3)], capture=True)
+            runs.append((o.logits.copy(), o.next_tokens.copy(), o.frames.copy()))
+        got.append(runs)
+        m.close()
+    for a, b in zip(*got):
+        assert all(np.array_equal(x, y) for x, y in zip(a, b))
