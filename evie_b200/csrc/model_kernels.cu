@@ -336,9 +336,12 @@ __global__ void __launch_bounds__(128) conv_rows_kernel(YView y, int ldy, const 
 // The rows form with the decode conv's layout: one warp per (128-channel head block, segment, 64 consecutive rows),
 // four consecutive channels per lane, so the q/k head norm of a row reduces with shuffles alone (the tree of
 // conv_decode4_kernel, which adds the squares in block_sum<128>'s order) and no CTA barrier stands between rows.
-// Each lane keeps its channels' last three inputs in registers and loads the next rows' inputs ahead (kConvAhead rows
-// in flight). Same products, order of operations and outputs as conv_rows_kernel, bit for bit.
+// Each lane keeps its channels' last three inputs in registers and loads the next rows' inputs ahead (kConvAhead
+// rows in flight; 8 measured slower, 15.9 against 13.7 ms per 4B prefill call: more registers, fewer CTAs per SM).
+// ONE: the input projection has a single plane (no K slices), read by plain float4 loads. Same products, order of
+// operations and outputs as conv_rows_kernel, bit for bit.
 constexpr int kConvAhead = 4;
+template <bool ONE>
 __global__ void __launch_bounds__(128) conv_rows4_kernel(YView y, int ldy, const SegInfo* __restrict__ segs,
                                                          const float* __restrict__ conv_state, size_t cs_slot,
                                                          const float* __restrict__ conv_w, int conv_dim, int hk,
@@ -346,6 +349,7 @@ __global__ void __launch_bounds__(128) conv_rows4_kernel(YView y, int ldy, const
   pdl_trigger();
   pdl_wait();
   constexpr int K = 4;
+  const auto ld4 = [&](size_t i) { return ONE ? *reinterpret_cast<const float4*>(y.p + i) : y.at4(i); };
   const int lane = threadIdx.x & 31;
   const int blk = blockIdx.x * 4 + (threadIdx.x >> 5);  // 128-channel block of this warp
   if (blk * 128 >= conv_dim) return;                    // the whole warp leaves together
@@ -362,7 +366,7 @@ __global__ void __launch_bounds__(128) conv_rows4_kernel(YView y, int ldy, const
 #pragma unroll
   for (int j = 0; j < K - 1; j++) {
     const int tt = t0 - (K - 1) + j;
-    win[j] = tt >= 0 ? y.at4((size_t)(sg.start + tt) * ldy + c)
+    win[j] = tt >= 0 ? ld4((size_t)(sg.start + tt) * ldy + c)
                      : *reinterpret_cast<const float4*>(cs + (size_t)(K - 1 + tt) * conv_dim + c);
   }
   const bool head_norm = blk < 2 * hk;
@@ -370,14 +374,14 @@ __global__ void __launch_bounds__(128) conv_rows4_kernel(YView y, int ldy, const
   float4 ahead[kConvAhead];  // inputs of rows t .. t + kConvAhead - 1
 #pragma unroll
   for (int i = 0; i < kConvAhead; i++)
-    ahead[i] = i < nt ? y.at4((size_t)(sg.start + t0 + i) * ldy + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    ahead[i] = i < nt ? ld4((size_t)(sg.start + t0 + i) * ldy + c) : make_float4(0.f, 0.f, 0.f, 0.f);
   for (int t = 0; t < nt; t++) {
     const size_t row = (size_t)sg.start + t0 + t;
     win[K - 1] = ahead[0];
 #pragma unroll
     for (int i = 0; i + 1 < kConvAhead; i++) ahead[i] = ahead[i + 1];
     const int tn = t + kConvAhead;
-    ahead[kConvAhead - 1] = tn < nt ? y.at4((row + kConvAhead) * ldy + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    ahead[kConvAhead - 1] = tn < nt ? ld4((row + kConvAhead) * ldy + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < K; j++) {
@@ -915,6 +919,103 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(YView y, int ldy,
   }
 }
 
+// The same prep with one warp per (row, head) for head dim 256 and 64 rotary dims: lane l holds dims 8 l .. 8 l + 7
+// (two float4 per vector), so the head norm reduces with shuffles and no CTA barrier. The sum of squares follows
+// block_sum<256>'s order bit for bit: there dim d sits in lane d % 32 of warp d / 32 and the butterfly pairs lanes
+// i ^ 16, i ^ 8, i ^ 4, i ^ 2, i ^ 1; here dim d is element d % 8 of lane d / 8, so the first two levels are lane xors
+// 2 and 1 and the last three are inside the lane; the eight warp sums are then added in warp order. RoPE's partner of
+// dim d (d + 32 or d - 32) is the same element of lane l ^ 4. Outputs equal attn_prep_kernel's.
+__global__ void __launch_bounds__(256) attn_prep_warp_kernel(YView y, int ldy, int R,
+                                                             const RowInfo* __restrict__ rows,
+                                                             const float* __restrict__ q_norm,
+                                                             const float* __restrict__ k_norm,
+                                                             const float* __restrict__ inv_freq, int nh, int nkv,
+                                                             float eps, float* __restrict__ q_rot,
+                                                             __nv_bfloat16* __restrict__ kc,
+                                                             __nv_bfloat16* __restrict__ vc,
+                                                             const int* __restrict__ page_table, int pages_per_slot,
+                                                             int page_size) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int HD = 256, HALF = 32;
+  const int lane = threadIdx.x & 31;
+  const long u = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int heads = nh + nkv;
+  if (u >= (long)R * heads) return;  // the whole warp leaves together
+  const int r = (int)(u / heads), idx = (int)(u % heads);
+  const bool is_q = idx < nh;
+  const int kh = idx - nh;
+  const int d0 = lane * 8;
+  const size_t base = (size_t)r * ldy;
+  const size_t src = is_q ? base + (size_t)idx * 2 * HD : base + (size_t)2 * nh * HD + (size_t)kh * HD;
+  float x[8];
+  {
+    const float4 a = y.at4(src + d0), b = y.at4(src + d0 + 4);
+    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+  }
+  float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
+  if (!is_q) {  // issued with the other loads
+    const size_t vs = base + (size_t)2 * nh * HD + (size_t)nkv * HD + (size_t)kh * HD + d0;
+    va = y.at4(vs);
+    vb = y.at4(vs + 4);
+  }
+  const RowInfo ri = rows[r];
+  float s[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) s[e] = x[e] * x[e];
+#pragma unroll
+  for (int e = 0; e < 8; e++) s[e] += __shfl_xor_sync(0xffffffffu, s[e], 2);  // block_sum's xor 16
+#pragma unroll
+  for (int e = 0; e < 8; e++) s[e] += __shfl_xor_sync(0xffffffffu, s[e], 1);  // xor 8
+#pragma unroll
+  for (int m = 4; m >= 1; m >>= 1) {  // xor 4, 2, 1
+    float t[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) t[e] = s[e] + s[e ^ m];
+#pragma unroll
+    for (int e = 0; e < 8; e++) s[e] = t[e];
+  }
+  float ss = 0.f;  // the eight warp sums of block_sum, in warp order
+#pragma unroll
+  for (int w = 0; w < 8; w++) ss += __shfl_sync(0xffffffffu, s[0], 4 * w);
+  const float inv = 1.0f / sqrtf(ss / (float)HD + eps);
+  const float* nw = (is_q ? q_norm : k_norm) + d0;
+  float yn[8], out[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) yn[e] = x[e] * inv * nw[e];
+  float pr[8];  // the rotary partner of each dim (lanes 0-7)
+#pragma unroll
+  for (int e = 0; e < 8; e++) pr[e] = __shfl_xor_sync(0xffffffffu, yn[e], 4);
+#pragma unroll
+  for (int e = 0; e < 8; e++) out[e] = yn[e];
+  if (lane < 8) {  // dims below 2 HALF = 64
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int d = d0 + e;
+      const int i = d < HALF ? d : d - HALF;
+      float sn, cs;
+      sincosf((float)ri.pos * inv_freq[i], &sn, &cs);
+      out[e] = d < HALF ? yn[e] * cs - pr[e] * sn : yn[e] * cs + pr[e] * sn;
+    }
+  }
+  if (is_q) {
+    float4* q4 = reinterpret_cast<float4*>(q_rot + ((size_t)r * nh + idx) * HD + d0);
+    q4[0] = make_float4(out[0], out[1], out[2], out[3]);
+    q4[1] = make_float4(out[4], out[5], out[6], out[7]);
+  } else {
+    const int page = page_table[(size_t)ri.slot * pages_per_slot + ri.pos / page_size];
+    const size_t off = (((size_t)page * nkv + kh) * page_size + ri.pos % page_size) * HD + d0;
+    const auto pack = [](float a, float b) {  // two bf16, round to nearest even, a in the low half
+      const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+      return *reinterpret_cast<const uint32_t*>(&h);
+    };
+    *reinterpret_cast<uint4*>(kc + off) =
+        make_uint4(pack(out[0], out[1]), pack(out[2], out[3]), pack(out[4], out[5]), pack(out[6], out[7]));
+    *reinterpret_cast<uint4*>(vc + off) = make_uint4(pack(va.x, va.y), pack(va.z, va.w), pack(vb.x, vb.y),
+                                                     pack(vb.z, vb.w));
+  }
+}
+
 // silu(g) * u with the product rounded on its own, so that the gate detectors (which recompute a few of these
 // activations) see exactly the values the SwiGLU kernel steers and captures.
 __device__ __forceinline__ float swiglu_act(float g, float u) { return __fmul_rn(siluf_(g), u); }
@@ -982,6 +1083,92 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
 #pragma unroll
     for (int e = 0; e < 4; e++) atomicMax(maxbuf + (size_t)layer * n + j0 + e, __float_as_uint(fabsf(a[e])));
 }
+
+// The same step for RPC consecutive rows per CTA (many-row calls): every thread issues the gate and up loads of all
+// its rows first, then the rows' steering lookups run once per CTA (thread i < RPC reads row i's RowInfo and op
+// range; then 64 threads per row load its ops), so a CTA keeps RPC rows' inputs in flight behind one lookup chain
+// (4 rows: 39.0 against 40.9 ms per 4B prefill call). ONE: a single input plane, read by plain float4 loads. Per row
+// and neuron: the same activation, ops in the slot's order, capture and max as swiglu_kernel, bit for bit.
+template <int RPC, bool ONE>
+__global__ void __launch_bounds__(256) swiglu_rows_kernel(YView y, int ldy, const RowInfo* __restrict__ rows, int R,
+                                                          int layer, int n, int L, SteerTables steer,
+                                                          const float* __restrict__ scale,
+                                                          int8_t* __restrict__ frames, uint32_t* __restrict__ maxbuf,
+                                                          __nv_bfloat16* __restrict__ X2, size_t xplane) {
+  static_assert(RPC * 64 <= 256, "one op-loading thread per (row, op)");
+  pdl_trigger();
+  pdl_wait();
+  __shared__ evie_op s_ops[RPC][64];
+  __shared__ int s_cnt[RPC], s_first[RPC], s_slot[RPC], s_pos[RPC];
+  const int r0 = blockIdx.y * RPC;
+  const int nr = min(RPC, R - r0);
+  const int j0 = blockIdx.x * 1024 + threadIdx.x * 4;
+  const bool active = j0 < n;
+  float4 g4[RPC], u4[RPC], sc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < RPC; i++) {
+    g4[i] = u4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (active && i < nr) {
+      const size_t yr = (size_t)(r0 + i) * ldy;
+      g4[i] = ONE ? *reinterpret_cast<const float4*>(y.p + yr + j0) : y.at4(yr + j0);
+      u4[i] = ONE ? *reinterpret_cast<const float4*>(y.p + yr + n + j0) : y.at4(yr + n + j0);
+    }
+  }
+  if (active && frames) sc = *reinterpret_cast<const float4*>(scale + (size_t)layer * n + j0);
+  if (threadIdx.x < nr) {
+    const RowInfo ri = rows[r0 + threadIdx.x];
+    const int* rg = steer.range + ((size_t)ri.slot * L + layer) * 2;
+    s_first[threadIdx.x] = rg[0];
+    s_cnt[threadIdx.x] = min(rg[1], 64);
+    s_slot[threadIdx.x] = ri.slot;
+    s_pos[threadIdx.x] = ri.pos;
+  }
+  __syncthreads();
+  {
+    const int i = threadIdx.x >> 6, k = threadIdx.x & 63;
+    if (i < nr && k < s_cnt[i]) {
+      const int slot = s_slot[i];
+      const size_t oi = (size_t)slot * steer.max_ops + s_first[i] + k;
+      evie_op op = steer.ops[oi];
+      const int g = steer.op_gate[oi];
+      if (g >= 0) {  // steering.rs:190-199: closed -> skip; opened in this call -> from the trigger row at/after its layer
+        const size_t gi = (size_t)slot * steer.max_gates + g;
+        const bool on = steer.open[gi] && (layer < steer.gates[gi].last_layer || s_pos[i] >= steer.from[gi]);
+        if (!on) op.mode = 0;
+      }
+      s_ops[i][k] = op;
+    }
+  }
+  __syncthreads();
+  if (!active) return;
+#pragma unroll
+  for (int i = 0; i < RPC; i++) {
+    if (i >= nr) break;
+    const int r = r0 + i;
+    float a[4] = {swiglu_act(g4[i].x, u4[i].x), swiglu_act(g4[i].y, u4[i].y), swiglu_act(g4[i].z, u4[i].z),
+                  swiglu_act(g4[i].w, u4[i].w)};
+    const int cnt = s_cnt[i];
+    for (int k = 0; k < cnt; k++) {  // steering.rs:189-208, in the slot's order
+      const evie_op op = s_ops[i][k];
+      const int e = op.neuron - j0;
+      if (e < 0 || e > 3) continue;
+      if (op.mode == 1) a[e] += op.value;
+      else if (op.mode == 2) a[e] *= op.value;
+      else if (op.mode == 3) a[e] = op.value;
+    }
+    store_split4(X2, xplane, (size_t)r * n + j0, make_float4(a[0], a[1], a[2], a[3]));
+    if (frames) {
+      const uint32_t packed = (uint32_t)(uint8_t)compand(a[0] / sc.x) | ((uint32_t)(uint8_t)compand(a[1] / sc.y) << 8) |
+                              ((uint32_t)(uint8_t)compand(a[2] / sc.z) << 16) |
+                              ((uint32_t)(uint8_t)compand(a[3] / sc.w) << 24);
+      *reinterpret_cast<uint32_t*>(frames + ((size_t)r * L + layer) * n + j0) = packed;
+    }
+    if (maxbuf && s_pos[i] > 0)
+#pragma unroll
+      for (int e = 0; e < 4; e++) atomicMax(maxbuf + (size_t)layer * n + j0 + e, __float_as_uint(fabsf(a[e])));
+  }
+}
+constexpr int kSwigluRows = 4;
 
 
 // steering.rs:164-187 for one segment (= one sequence and its slot's plan). Each thread owns rows: the gates whose
@@ -1154,7 +1341,8 @@ evie_status k_conv_silu_norm(YView y, int ldy, int R, const RowInfo* rows, const
                     a16(y.p) && a16(conv_state) && a16(conv_w) && a16(act);
   if (max_seg_rows > 1 && vec4 && !update_window) {
     dim3 grid((s.conv_dim + 511) / 512, nseg, (max_seg_rows + kConvRows - 1) / kConvRows);
-    EVIE_CUDA_TRY(launch_k(conv_rows4_kernel, grid, dim3(128), 0, st, y, ldy, segs, conv_state, cs_slot, conv_w,
+    auto* kern = y.n == 1 ? conv_rows4_kernel<true> : conv_rows4_kernel<false>;
+    EVIE_CUDA_TRY(launch_k(kern, grid, dim3(128), 0, st, y, ldy, segs, conv_state, cs_slot, conv_w,
                            s.conv_dim, s.hk, 1.0f / sqrtf((float)s.dk), act, split_qk));
     EVIE_CHECK_LAUNCH("conv_rows4_kernel");
     return EVIE_OK;
@@ -1249,6 +1437,22 @@ evie_status k_attn_prep(YView y, int ldy, int R, const RowInfo* rows, const floa
                         const float* k_norm, const float* inv_freq, const ModelShape& s, float* q_rot, KV* kc,
                         KV* vc, const int* page_table, int pages_per_slot, int page_size, cudaStream_t st) {
   if (R == 0) return EVIE_OK;
+  static const bool cta_form = [] {
+    const char* e = getenv("EVIE_ATTN_PREP_CTA");
+    return e && e[0] == '1';
+  }();
+  const auto a16 = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };
+  if constexpr (sizeof(KV) == 2) {
+    if (!cta_form && s.hd == 256 && s.rot == 64 && ldy % 4 == 0 && y.plane % 4 == 0 && a16(y.p) && a16(q_rot) &&
+        a16(kc) && a16(vc) && a16(q_norm) && a16(k_norm)) {
+      const long warps = (long)R * (s.nh + s.nkv);
+      EVIE_CUDA_TRY(launch_k(attn_prep_warp_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, st, y, ldy, R,
+                             rows, q_norm, k_norm, inv_freq, s.nh, s.nkv, s.eps, q_rot, kc, vc, page_table,
+                             pages_per_slot, page_size));
+      EVIE_CHECK_LAUNCH("attn_prep_warp_kernel");
+      return EVIE_OK;
+    }
+  }
   dim3 grid(s.nh + s.nkv, R);
   EVIE_CUDA_TRY(launch_k(attn_prep_kernel<KV>, dim3(grid), dim3(256), 0, st, y, ldy, rows, q_norm, k_norm, inv_freq, s.nh, s.nkv,
                                              s.hd, s.rot, s.eps, q_rot, kc, vc, page_table, pages_per_slot, page_size));
@@ -1266,6 +1470,20 @@ evie_status k_swiglu(YView y, int ldy, int R, const RowInfo* rows, int layer, co
                      SteerTables steer, const float* scale, int8_t* frames, uint32_t* maxbuf, __nv_bfloat16* X2,
                      cudaStream_t st) {
   if (R == 0) return EVIE_OK;
+  // Many-row calls (prefill) take kSwigluRows rows per CTA unless EVIE_SWIGLU_ROWS=1; decode-sized calls keep one
+  // row per CTA (more CTAs for few rows).
+  static const int rpc = [] {
+    const char* e = getenv("EVIE_SWIGLU_ROWS");
+    return e && e[0] == '1' ? 1 : kSwigluRows;
+  }();
+  if (R > 128 && rpc > 1) {
+    dim3 grid((s.n + 1023) / 1024, (R + kSwigluRows - 1) / kSwigluRows);
+    auto* kern = y.n == 1 ? swiglu_rows_kernel<kSwigluRows, true> : swiglu_rows_kernel<kSwigluRows, false>;
+    EVIE_CUDA_TRY(launch_k(kern, grid, dim3(256), 0, st, y, ldy, rows, R, layer, s.n, s.L, steer, scale, frames,
+                           maxbuf, X2, (size_t)R * s.n));
+    EVIE_CHECK_LAUNCH("swiglu_rows_kernel");
+    return EVIE_OK;
+  }
   dim3 grid((s.n + 1023) / 1024, R);
   EVIE_CUDA_TRY(launch_k(swiglu_kernel, dim3(grid), dim3(256), 0, st, y, ldy, rows, layer, s.n, s.L, steer, scale, frames, maxbuf,
                                       X2, (size_t)R * s.n));
