@@ -950,14 +950,14 @@ __global__ void __launch_bounds__(256) attn_prep_warp_kernel(YView y, int ldy, i
   const size_t src = is_q ? base + (size_t)idx * 2 * HD : base + (size_t)2 * nh * HD + (size_t)kh * HD;
   float x[8];
   {
-    const float4 a = y.at4(src + d0), b = y.at4(src + d0 + 4);
+    const float4 a = y.at4_few(src + d0), b = y.at4_few(src + d0 + 4);
     x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
   }
   float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
   if (!is_q) {  // issued with the other loads
     const size_t vs = base + (size_t)2 * nh * HD + (size_t)nkv * HD + (size_t)kh * HD + d0;
-    va = y.at4(vs);
-    vb = y.at4(vs + 4);
+    va = y.at4_few(vs);
+    vb = y.at4_few(vs + 4);
   }
   const RowInfo ri = rows[r];
   float s[8];
@@ -1038,8 +1038,8 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
   const size_t yr = (size_t)r * ldy;
   float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), u4 = g4, sc = g4;
   if (active) {  // issued before the row and steering lookups, which then overlap these loads
-    g4 = y.at4(yr + j0);
-    u4 = y.at4(yr + n + j0);
+    g4 = y.at4_few(yr + j0);
+    u4 = y.at4_few(yr + n + j0);
     if (frames) sc = *reinterpret_cast<const float4*>(scale + (size_t)layer * n + j0);
   }
   const RowInfo ri = rows[r];
