@@ -663,6 +663,20 @@ class ModelDecode(Workload):
         torch.cuda.synchronize()
         self.prefill_ms = e0.elapsed_time(e1)
         self.prefill_tok_s = self.B * self.P / (self.prefill_ms / 1000.0)
+        # Where one prefill call's time goes: the first call again, from reset slots (the same prompts, so the slots
+        # end as before), with the library's profiling events around every kernel group (the eager path: a little
+        # slower than the timed calls). Its greedy tokens must equal the timed call's.
+        first = [GpuSeq(sl, 0, self.prompts[sl // 2]) for sl in range(min(self.B, per_call))]
+        for s in first:
+            self.m.reset_slot(s.slot)
+        self.m.profile(True)
+        o = self.m.forward(first, want_logits=False)
+        groups = self.m.profile_read()
+        self.m.profile(False)
+        self.prefill_groups = {"rows": len(first) * self.P,
+                               "same_tokens": bool(np.array_equal(o.next_tokens, self.first_tokens[:len(first)])),
+                               "ms": {k: round(v[0], 3) for k, v in sorted(groups.items(), key=lambda kv: -kv[1][0])
+                                      if v[1]}}
         self.pos = self.P
         self.next = self.first_tokens.copy()
         self.stream = stream
@@ -1140,6 +1154,8 @@ def run_ours(args):
         line["prefill_roofline"] = {"bound": "tensor", "achieved": pf, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                                     "frac": pf / pk["bf16_tflops"], "algorithmic_flops": w.prefill_flops(),
                                     "tok_s": w.prefill_tok_s, "peak_source": pk["source"]}
+        if getattr(w, "prefill_groups", None):
+            line["prefill_roofline"]["groups_one_call"] = w.prefill_groups
     if rank == 0 and gathered:
         line["gathered"] = {k: list(v.shape) for k, v in gathered.items()}
     if world == 1 and args.workload == DEFAULT_WORKLOAD and not args.no_isolated:
