@@ -1087,8 +1087,9 @@ __global__ void __launch_bounds__(256) swiglu_kernel(YView y, int ldy,
 // The same step for RPC consecutive rows per CTA (many-row calls): every thread issues the gate and up loads of all
 // its rows first, then the rows' steering lookups run once per CTA (thread i < RPC reads row i's RowInfo and op
 // range; then 64 threads per row load its ops), so a CTA keeps RPC rows' inputs in flight behind one lookup chain
-// (4 rows: 39.0 against 40.9 ms per 4B prefill call). ONE: a single input plane, read by plain float4 loads. Per row
-// and neuron: the same activation, ops in the slot's order, capture and max as swiglu_kernel, bit for bit.
+// (4 rows against 1: 39.0 against 40.9 ms per 4B prefill call, measured with the plane-summing loads; with ONE the
+// kernel takes ~18 ms). ONE: a single input plane, read by plain float4 loads. Per row and neuron: the same
+// activation, ops in the slot's order, capture and max as swiglu_kernel, bit for bit.
 template <int RPC, bool ONE>
 __global__ void __launch_bounds__(256) swiglu_rows_kernel(YView y, int ldy, const RowInfo* __restrict__ rows, int R,
                                                           int layer, int n, int L, SteerTables steer,
