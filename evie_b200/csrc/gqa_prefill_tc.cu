@@ -124,7 +124,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   const int kvh = blockIdx.z;
   const SegInfo sg = segs[blockIdx.y];
-  const int r_first = blockIdx.x * kRows;
+  // Row blocks in reverse: CTAs are dispatched x fastest, and a block's causal work grows with its rows, so the
+  // longest blocks of each (segment, KV head) start first and the last CTAs of the launch are short ones.
+  const int r_first = (gridDim.x - 1 - blockIdx.x) * kRows;
   if (r_first >= sg.count) return;  // the whole CTA: before any barrier or TMEM allocation
   const int nr = min(kRows, sg.count - r_first);
   const int row0 = sg.start + r_first;
